@@ -1,0 +1,104 @@
+"""Seeded synthetic inputs with the BASELINE configs' shapes and value distributions.
+
+There is no checkpoint and no dataset on the GPU box; every workload is synthetic:
+
+  * MXFP4 matrices: packed bytes uniform over 0..255 (so each E2M1 code is uniform over
+    all 16 values) and one E8M0 scale byte per 32 input elements, uniform in [118, 124];
+  * activations ~ N(0, 1), rounded to bf16 where the config says bf16;
+  * router weights ~ N(0, 0.02) in bf16;
+  * INT8 trunk weights uniform in [-127, 127] with one fp32 row scale ~ U(1e-3, 1e-2).
+
+numpy's PCG64 stream is the generator, so a seed names the same bytes on every host.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+HIDDEN = 7168
+INTER = 2048
+N_EXPERTS = 384
+TOPK = 8
+GROUP = 32
+SCALE_LO, SCALE_HI = 118, 124
+
+
+def rng(seed: int) -> np.random.Generator:
+    return np.random.Generator(np.random.PCG64(seed))
+
+
+def bf16_bits(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns, round to nearest even (finite inputs)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return r.astype(np.uint16)
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    """bf16 bits -> fp32: a left shift by 16, exact (the reference's k3_bf16f)."""
+    return (np.ascontiguousarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def mxfp4_matrix(g: np.random.Generator, rows: int, cols: int,
+                 scale_lo: int = SCALE_LO, scale_hi: int = SCALE_HI):
+    """(packed [rows][cols/2] u8, scales [rows][cols/32] u8) in the reference layout."""
+    packed = g.integers(0, 256, size=(rows, cols // 2), dtype=np.uint8)
+    scales = g.integers(scale_lo, scale_hi + 1, size=(rows, (cols + GROUP - 1) // GROUP),
+                        dtype=np.uint8)
+    return packed, scales
+
+
+def expert(g: np.random.Generator, hidden: int = HIDDEN, inter: int = INTER, **kw) -> dict:
+    """One routed expert: gate/up [inter][hidden], down [hidden][inter], all MXFP4."""
+    gp, gs = mxfp4_matrix(g, inter, hidden, **kw)
+    up, us = mxfp4_matrix(g, inter, hidden, **kw)
+    dp, ds = mxfp4_matrix(g, hidden, inter, **kw)
+    return dict(gate_p=gp, gate_s=gs, up_p=up, up_s=us, down_p=dp, down_s=ds)
+
+
+def expert_bytes(hidden: int = HIDDEN, inter: int = INTER) -> int:
+    """Algorithmic bytes of one MXFP4 expert: 3 matrices of packed nibbles + scales."""
+    m = inter * hidden // 2 + inter * hidden // GROUP
+    return 3 * m
+
+
+def activations(g: np.random.Generator, ntok: int, hidden: int = HIDDEN, bf16=True):
+    """x ~ N(0,1); returns (fp32 values, bf16 bits or None). With bf16=True the fp32 array
+    holds exactly the bf16 values."""
+    x = g.standard_normal((ntok, hidden), dtype=np.float32)
+    if not bf16:
+        return x, None
+    b = bf16_bits(x)
+    return bf16_to_f32(b), b
+
+
+def router_weights(g: np.random.Generator, n_experts: int = N_EXPERTS,
+                   hidden: int = HIDDEN):
+    """W_r ~ N(0, 0.02) in bf16; returns (fp32 values, bf16 bits)."""
+    w = g.standard_normal((n_experts, hidden), dtype=np.float32) * np.float32(0.02)
+    b = bf16_bits(w)
+    return bf16_to_f32(b), b
+
+
+def q8_matrix(g: np.random.Generator, out: int, in_: int):
+    """INT8 trunk matrix: (int8 [out][in], fp32 scales [out], reference row bytes).
+
+    The reference row layout is [f32 scale][int8 * in], stride 4+in bytes
+    (include/k3/k3.h:265-303)."""
+    w = g.integers(-127, 128, size=(out, in_), dtype=np.int8)
+    s = g.uniform(1e-3, 1e-2, size=out).astype(np.float32)
+    rows = np.empty((out, 4 + in_), np.uint8)
+    rows[:, :4] = s.view(np.uint8).reshape(out, 4)
+    rows[:, 4:] = w.view(np.uint8)
+    return w, s, rows
+
+
+def zipf_bias(n_experts: int, s: float = 1.1, alpha: float = 0.0,
+              perm: np.ndarray | None = None) -> np.ndarray:
+    """Selection bias b_e = alpha * log(rank_e^-s): steers top-k popularity toward a Zipf
+    law over experts (rank 1 most popular). perm maps rank -> expert id."""
+    ranks = np.arange(1, n_experts + 1, dtype=np.float64)
+    b = alpha * (-s) * np.log(ranks)
+    out = np.empty(n_experts, np.float32)
+    ids = np.arange(n_experts) if perm is None else perm
+    out[ids] = b.astype(np.float32)
+    return out

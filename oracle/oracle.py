@@ -1,0 +1,207 @@
+"""ctypes binding for the CPU checker libraries. TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm import
+this module. It binds
+
+  * ``liboracle.so``      -- the CPU restatement (oracle/k3_oracle.c), and
+  * ``_ref/libk3ref.so``  -- the reference's own kernels compiled from its sources plus
+                             oracle/ref_harness.c (present when built in the container that
+                             has the reference tree; it travels with the snapshot).
+
+Arrays are numpy; every call checks dtypes and contiguity so a wrong buffer cannot be
+passed through silently.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libk3ref.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+
+
+class Expert6(C.Structure):
+    """Six (packed, scale) host pointers in the K3ExpertQ order p1,s1,p3,s3,p2,s2
+    (include/k3/k3.h:323-327 of the reference)."""
+
+    _fields_ = [(n, C.c_void_p) for n in ("p1", "s1", "p3", "s3", "p2", "s2")]
+
+
+def expert6(e: dict) -> Expert6:
+    """Build an Expert6 from a dict of numpy uint8 arrays (keys gate_p, gate_s, up_p,
+    up_s, down_p, down_s). The caller keeps the arrays alive."""
+    return Expert6(*(e[k].ctypes.data for k in ("gate_p", "gate_s", "up_p", "up_s",
+                                                 "down_p", "down_s")))
+
+
+def _build():
+    subprocess.run(["make", "-s", "-f", os.path.join(HERE, "Makefile")], check=True)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO):
+            _build()
+        L = C.CDLL(ORACLE_SO)
+        L.ora_mxfp4_dequant.argtypes = [_f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
+        L.ora_matmul_mxfp4.argtypes = [_f32p, _f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
+        L.ora_matmul_f32.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
+        L.ora_matmul_q8.argtypes = [_f32p, _f32p, _u8p, C.c_int, C.c_int]
+        L.ora_router.argtypes = [_i32p, _f32p, _f32p, _f32p, C.c_void_p, C.c_int, C.c_int,
+                                 C.c_int, C.c_int, C.c_float]
+        L.ora_router_select.argtypes = [_i32p, _f32p, _f32p, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_int, C.c_float]
+        L.ora_router_scores.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
+        L.ora_swiglu.argtypes = [_f32p, _f32p, C.c_int]
+        L.ora_situ_glu.argtypes = [_f32p, _f32p, C.c_int, C.c_float, C.c_float]
+        L.ora_expert_ffn.argtypes = [_f32p, _f32p, C.c_int, C.POINTER(Expert6), C.c_int,
+                                     C.c_int, C.c_int]
+        L.ora_moe_layer.argtypes = [_f32p, _f32p, C.c_int, _f32p, C.c_void_p,
+                                    C.POINTER(Expert6), C.c_void_p, C.c_int, C.c_int,
+                                    C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
+                                    _i32p, _f32p]
+        L.ora_e2m1.restype = C.c_float
+        L.ora_e8m0.restype = C.c_float
+        _lib = L
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref():
+    """The reference's own kernels (k3_matmul_mxfp4, k3_router, k3_matmul_q8, ...) plus the
+    BASELINE compositions of oracle/ref_harness.c."""
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise FileNotFoundError(REF_SO)
+        L = C.CDLL(REF_SO)
+        L.k3_mxfp4_dequant.argtypes = [_f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
+        L.k3_matmul_mxfp4.argtypes = [_f32p, _f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
+        L.k3_matmul_q8.argtypes = [_f32p, _f32p, _u8p, C.c_int, C.c_int]
+        L.k3_matmul.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
+        L.k3_router.argtypes = [_i32p, _f32p, _f32p, _f32p, C.c_void_p, C.c_int, C.c_int,
+                                C.c_int, C.c_int, C.c_float]
+        L.refh_expert_ffn.argtypes = [_f32p, _f32p, C.c_int, C.POINTER(Expert6), C.c_int,
+                                      C.c_int, C.c_int]
+        L.refh_moe_layer.argtypes = [_f32p, _f32p, C.c_int, _f32p, C.c_void_p,
+                                     C.POINTER(Expert6), C.c_void_p, C.c_int, C.c_int,
+                                     C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
+                                     _i32p, _f32p]
+        L.refh_threads.restype = C.c_int
+        _ref = L
+    return _ref
+
+
+def _ptr_or_null(a):
+    return None if a is None else a.ctypes.data
+
+
+# ---------------------------------------------------------------- convenience wrappers
+
+
+def mxfp4_dequant(packed, scales, group=32, L=None):
+    L = L or lib()
+    rows, pcols = packed.shape
+    out = np.empty((rows, pcols * 2), np.float32)
+    fn = L.ora_mxfp4_dequant if hasattr(L, "ora_mxfp4_dequant") else L.k3_mxfp4_dequant
+    fn(out, np.ascontiguousarray(packed), np.ascontiguousarray(scales), rows, pcols, group)
+    return out
+
+
+def matmul_mxfp4(x, packed, scales, group=32, use_ref=False):
+    L = ref() if use_ref else lib()
+    fn = L.k3_matmul_mxfp4 if use_ref else L.ora_matmul_mxfp4
+    rows, pcols = packed.shape
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(rows, np.float32)
+    fn(y, x, np.ascontiguousarray(packed), np.ascontiguousarray(scales), pcols * 2, rows,
+       group)
+    return y
+
+
+def matmul_q8(x, W_rows, in_, out, use_ref=False):
+    L = ref() if use_ref else lib()
+    fn = L.k3_matmul_q8 if use_ref else L.ora_matmul_q8
+    y = np.empty(out, np.float32)
+    fn(y, np.ascontiguousarray(x, np.float32), np.ascontiguousarray(W_rows), in_, out)
+    return y
+
+
+def router(x, W, bias, topk, renorm=1, routed_scale=1.0, use_ref=False):
+    L = ref() if use_ref else lib()
+    fn = L.k3_router if use_ref else L.ora_router
+    E, H = W.shape
+    idx = np.empty(topk, np.int32)
+    w = np.empty(topk, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    fn(idx, w, np.ascontiguousarray(x, np.float32), np.ascontiguousarray(W, np.float32),
+       _ptr_or_null(b), H, E, topk, renorm, routed_scale)
+    return idx, w
+
+
+def router_select(score, bias, topk, renorm=1, routed_scale=1.0):
+    idx = np.empty(topk, np.int32)
+    w = np.empty(topk, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().ora_router_select(idx, w, np.ascontiguousarray(score, np.float32), _ptr_or_null(b),
+                            score.shape[0], topk, renorm, routed_scale)
+    return idx, w
+
+
+def router_scores(x, W):
+    E, H = W.shape
+    s = np.empty(E, np.float32)
+    lib().ora_router_scores(s, np.ascontiguousarray(x, np.float32),
+                            np.ascontiguousarray(W, np.float32), H, E)
+    return s
+
+
+def expert_ffn(x, e: dict, hidden, inter, act=0, use_ref=False):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, hidden)
+    y = np.empty_like(x)
+    q = expert6(e)
+    if use_ref:
+        rc = ref().refh_expert_ffn(y, x, x.shape[0], C.byref(q), hidden, inter, act)
+        assert rc == 0
+    else:
+        lib().ora_expert_ffn(y, x, x.shape[0], C.byref(q), hidden, inter, act)
+    return y
+
+
+def moe_layer(x, router_w, router_bias, experts: list, shared, hidden, inter, topk,
+              renorm=1, routed_scale=1.0, act=0, use_ref=False):
+    """experts: list indexed by expert id of expert dicts (None for experts that must never
+    be selected is not allowed -- every entry must be valid)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, hidden)
+    T = x.shape[0]
+    E = router_w.shape[0]
+    arr = (Expert6 * E)(*[expert6(e) for e in experts])
+    sh = expert6(shared) if shared is not None else None
+    out = np.empty_like(x)
+    idx = np.empty((T, topk), np.int32)
+    wt = np.empty((T, topk), np.float32)
+    b = None if router_bias is None else np.ascontiguousarray(router_bias, np.float32)
+    args = (out, x, T, np.ascontiguousarray(router_w, np.float32), _ptr_or_null(b), arr,
+            None if sh is None else C.addressof(sh), hidden, inter, E, topk, renorm,
+            routed_scale, act, idx, wt)
+    if use_ref:
+        assert ref().refh_moe_layer(*args) == 0
+    else:
+        lib().ora_moe_layer(*args)
+    return out, idx, wt
