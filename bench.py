@@ -1,0 +1,367 @@
+"""bench.py -- BASELINE metric "MXFP4 MoE-layer tokens/s" on B200.
+
+Workload: one MoE layer decode on one GPU -- hidden 7168, 384 routed
+MXFP4 experts (gate/up 2048x7168, down 7168x2048, E8M0 bytes uniform in [118,124]) plus
+one shared expert, all HBM-resident; bf16 router W ~ N(0,0.02), sigmoid top-8 with
+renormalised weights; and the INT8 trunk projection 7168x7168 (int8 uniform [-127,127],
+fp32 row scales ~ U(1e-3,1e-2)) on the same bf16 input. A step is one batch of B=16 tokens
+x ~ N(0,1) in bf16 through the INT8 projection and the MoE layer; B=1 and B=4 are reported
+in "batches". Each step uses a different token batch from a rotating pool, so each step
+touches ~110 different experts (~2.6 GB): inputs larger than L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun) runs N independent replicas (decode does not shard; scaling "weak").
+--impl reference times the reference's own CPU kernels (oracle/_ref, built from its
+sources) on the same workload with every host thread.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E, K = 7168, 2048, 384, 8
+METRIC = "MXFP4 MoE-layer tokens/s"
+UNIT = "tokens/s"
+WORKLOAD = "config[1] MoE layer decode: B=16 bf16 tokens, 384 HBM-resident MXFP4 experts " \
+           "(7168->2048->7168) + 1 shared, bf16 sigmoid top-8 router, INT8 7168x7168 trunk"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (clock and throttle reasons)."""
+
+    def __init__(self, gpu_index):
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        self.p = None
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index),
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(5)
+        except Exception:
+            self.p.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            v = [c.strip() for c in line.split(",")]
+            if len(v) < 9:
+                continue
+            try:
+                sm.append(float(v[1]))
+                mx.append(float(v[2]))
+            except ValueError:
+                continue
+            for n, a in zip(names, v[5:9]):
+                if a.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ------------------------------------------------------------------ reference arm
+def host_workload(seed, ndistinct=48):
+    """Host copy of the config[1] workload for the CPU runs: ndistinct random experts tiled
+    over the 384 expert ids, shared expert, fp32 router W (bf16 values), INT8 trunk rows."""
+    import __graft_entry__ as ge
+    synth = ge.load_package().synth
+    g = synth.rng(seed)
+    distinct = [synth.expert(g) for _ in range(ndistinct)]
+    shared = synth.expert(g)
+    wf, _ = synth.router_weights(g, E, H)
+    _, _, q8rows = synth.q8_matrix(g, H, H)
+    batches = [synth.activations(g, 16, H)[0] for _ in range(4)]
+    return distinct, shared, wf, q8rows, batches
+
+
+def cpu_moe_tokens_per_s(budget_s, steps=None, warmup=0, seed=7):
+    """Time the reference's kernels (oracle/_ref) on the config[1] step; returns
+    (tokens/s, threads, steps run, seconds)."""
+    import ctypes as C
+    from oracle import oracle as ora
+    R = ora.ref()
+    distinct, shared, wf, q8rows, batches = host_workload(seed)
+    experts = [distinct[i % len(distinct)] for i in range(E)]
+    arr = (ora.Expert6 * E)(*[ora.expert6(e) for e in experts])
+    sh = ora.expert6(shared)
+    out = np.empty((16, H), np.float32)
+    y8 = np.empty(H, np.float32)
+    idx = np.empty((16, K), np.int32)
+    wt = np.empty((16, K), np.float32)
+
+    def step(b):
+        x = batches[b % len(batches)]
+        for t in range(16):
+            R.k3_matmul_q8(y8, x[t], q8rows, H, H)
+        R.refh_moe_layer(out, x, 16, wf, None, arr, C.addressof(sh), H, I, E, K, 1, 1.0, 0,
+                         idx, wt)
+
+    for w in range(warmup):
+        step(w)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step(n)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= budget_s):
+            break
+    return 16 * n / el, R.refh_threads(), n, el
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    from oracle import oracle as ora
+    if not ora.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libk3ref.so not built (needs the reference tree)"}))
+        return
+    tps, threads, n, el = cpu_moe_tokens_per_s(None, steps=args.steps, warmup=args.warmup)
+    sample = f"{n} steps of 16 tokens, 48 distinct experts tiled over 384 ids"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 * el / n, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp64 accumulate (reference CPU)",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "batch": 16},
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+# ------------------------------------------------------------------------ our arm
+def build_device_workload(k3, dev, seed):
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    lay, run = k3.expert_run_layout(H, I)
+    blob = torch.empty((E + 1) * run, dtype=torch.uint8, device=dev)
+    b2 = blob.view(E + 1, run)
+    for name, (off, nb) in lay.items():
+        seg = b2[:, off:off + nb]
+        if name.endswith("_p"):
+            seg.copy_(torch.randint(0, 256, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+        else:
+            seg.copy_(torch.randint(118, 125, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+    qs = k3.experts_from_blob(blob, E + 1, H, I)
+    W = (torch.randn((E, H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    layer = k3.MoeLayer(qs[:E], qs[E], W, None, H, I, K, device=dev)
+    wq = torch.randint(-127, 128, (H, H), generator=g, device=dev, dtype=torch.int8)
+    ws = torch.rand(H, generator=g, device=dev) * 9e-3 + 1e-3
+    return blob, layer, wq, ws
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    blob, layer, wq, wsc, = build_device_workload(k3, dev, 1234 + rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(99 + rank)
+    B = 16
+    NB = 32
+    xs = [torch.randn((B, H), generator=g, device=dev).to(torch.bfloat16) for _ in range(NB)]
+    host_x = [x.cpu().pin_memory() for x in xs]
+    out = torch.empty((B, H), dtype=torch.float32, device=dev)
+    y8 = torch.empty((B, H), dtype=torch.float32, device=dev)
+    idx_log = [torch.empty((B, K), dtype=torch.int32, device=dev) for _ in range(args.steps)]
+    wt = torch.empty((B, K), dtype=torch.float32, device=dev)
+    h_out = torch.empty((B, H), dtype=torch.float32).pin_memory()
+    h_y8 = torch.empty((B, H), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    import ctypes as C
+    stream = k3._stream()
+
+    def step(i, idx=None, e2e=False):
+        if e2e:
+            x_dev.copy_(host_x[i % NB], non_blocking=True)
+            x = x_dev
+        else:
+            x = xs[i % NB]
+        rc = L.k3c_q8_gemv(C.c_void_p(y8.data_ptr()), H, C.c_void_p(x.data_ptr()), k3.K3C_BF16, H,
+                           B, C.c_void_p(wq.data_ptr()), C.c_void_p(wsc.data_ptr()), H, H, H, stream)
+        assert rc == 0, L.k3c_last_error()
+        layer.decode(x, out=out, idx=idx if idx is not None else idx_log[0], wt=wt)
+        if e2e:
+            h_out.copy_(out, non_blocking=True)
+            h_y8.copy_(y8, non_blocking=True)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def maxed(v):
+        if ws == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    for i in range(args.warmup):
+        step(i)
+    # --- device-resident timed region
+    barrier()
+    clk = Clocks(local)
+    L.k3c_timing_enable(1)
+    ms_buf = (C.c_double * 4)()
+    n_buf = (C.c_longlong * 4)()
+    L.k3c_timing_read(ms_buf, n_buf, 4)          # discard warm-up records
+    launches0 = L.k3c_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i, idx=idx_log[i])
+    e1.record()
+    torch.cuda.synchronize()
+    launches = L.k3c_launch_count() - launches0
+    L.k3c_timing_enable(0)
+    L.k3c_timing_read(ms_buf, n_buf, 4)
+    clocks = clk.stop()
+    dt = maxed(e0.elapsed_time(e1) / 1e3)
+    barrier()
+    # unique experts per step (the algorithmic bytes of the expert stage)
+    uniq = [int(torch.unique(t).numel()) for t in idx_log]
+    run_bytes = k3.expert_run_layout(H, I)[1]
+    expert_bytes = sum((u + 1) * run_bytes for u in uniq)
+    exp_ms = ms_buf[0]
+    achieved = expert_bytes / (exp_ms / 1e3) / 1e9 if exp_ms > 0 else None
+    hbm_peak, _, peak_kind = peaks()
+    router_bytes = E * H * 2
+    layer_bytes = expert_bytes + args.steps * (router_bytes + H * H + 4 * H)
+    # --- end-to-end timed region: pinned host x in, host results out
+    for i in range(min(3, args.warmup)):
+        step(i, e2e=True)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(args.steps):
+        step(args.warmup + i, e2e=True)
+    f1.record()
+    torch.cuda.synchronize()
+    dte = maxed(f0.elapsed_time(f1) / 1e3)
+    # --- B = 1 and B = 4 (same layer, device-resident)
+    batches = {}
+    for b in (1, 4):
+        xb = [x[:b].contiguous() for x in xs]
+        ob = torch.empty((b, H), dtype=torch.float32, device=dev)
+        ib = torch.empty((b, K), dtype=torch.int32, device=dev)
+        wb = torch.empty((b, K), dtype=torch.float32, device=dev)
+        for i in range(args.warmup):
+            layer.decode(xb[i % NB], out=ob, idx=ib, wt=wb)
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for i in range(args.steps):
+            layer.decode(xb[(args.warmup + i) % NB], out=ob, idx=ib, wt=wb)
+        c1.record()
+        torch.cuda.synchronize()
+        tb = maxed(c0.elapsed_time(c1) / 1e3)
+        batches[f"B{b}"] = {"tokens_per_s": ws * b * args.steps / tb, "ms_per_step": 1e3 * tb / args.steps}
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None
+    if ws == 1 and not args.no_cpu:
+        from oracle import oracle as ora
+        if ora.ref_available():
+            tps, threads, n, el = cpu_moe_tokens_per_s(args.cpu_seconds)
+            cpu = {"value": tps, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": f"{n} steps of 16 tokens ({el:.1f} s), 48 distinct experts tiled over 384 ids"}
+    line = {
+        "metric": METRIC, "value": ws * B * args.steps / dt, "unit": UNIT, "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (MXFP4 weights, bf16 inputs widened exactly, fp32 accumulate)",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": B, "hidden": H, "inter": I, "experts": E,
+                   "topk": K, "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                   "l2": "inputs larger than L2: each step reads ~110 different experts (~2.6 GB) "
+                         "from a rotating pool of 32 token batches"},
+        "decode_hbm_gbs": layer_bytes / dt / 1e9,
+        "unique_experts_per_step": float(np.mean(uniq)),
+        "batches": batches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
+                     "kernel": "expert stage (gate/up+act and down MXFP4 GEMV kernels)",
+                     "peak_kind": peak_kind},
+        "cpu_baseline": cpu,
+        "e2e": {"value": ws * B * args.steps / dte, "unit": UNIT,
+                "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": 2 * B * H * 4},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    ws, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+    else:
+        run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

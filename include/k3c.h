@@ -1,0 +1,184 @@
+/* k3c.h -- C ABI of libk3cuda.so, the B200 (sm_100a) routed-expert hot path.
+ *
+ * Two layers:
+ *
+ *   1. DROP-IN entry points with the reference's exact names, signatures and semantics
+ *      (host pointers in, host pointers out, void return, abort on a precondition
+ *      violation). Linking libk3cuda.so in place of the reference's k3_ops.o routes these
+ *      calls through the GPU. Each cites the declaration it replaces in the reference's
+ *      include/k3/k3.h.
+ *
+ *   2. DEVICE entry points (k3c_*): device pointers, an explicit CUDA stream, an int
+ *      status (K3C_OK or a negative K3C_E* code, message in k3c_last_error()). These are
+ *      the performance path; nothing in them synchronises the host unless stated.
+ *
+ * Reference types (K3ExpertQ, K3ExpertSrc) are mirrored field-for-field so the ABI is the
+ * reference's; when the reference's k3.h is included first its definitions are used.
+ */
+#ifndef K3C_H
+#define K3C_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------- mirrored types ---- */
+#ifndef K3_H
+#define K3_MXFP4_GROUP 32   /* include/k3/k3.h:548 */
+#define K3_MAX_TOPK 64      /* include/k3/k3.h:557 */
+enum { K3_WF32 = 0, K3_WBF16 = 1, K3_WI8 = 2 };   /* include/k3/k3.h:270 */
+
+/* One expert as three (packed, scale) pairs: include/k3/k3.h:323-327. In the k3c_* API
+ * these are DEVICE addresses. */
+typedef struct {
+    const unsigned char *p1, *s1;   /* w1 gate */
+    const unsigned char *p3, *s3;   /* w3 up   */
+    const unsigned char *p2, *s2;   /* w2 down */
+} K3ExpertQ;
+
+/* Expert source vtable: include/k3/k3.h:332-355. */
+typedef struct K3ExpertSrc {
+    int (*get)(struct K3ExpertSrc *self, int layer, int expert, K3ExpertQ *out);
+    int (*getmany)(struct K3ExpertSrc *self, int layer, const int *experts, int n);
+    int (*resident)(struct K3ExpertSrc *self, int layer, int expert, K3ExpertQ *out);
+    void *ctx;
+} K3ExpertSrc;
+#endif /* K3_H */
+
+/* Binary-compatible with cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st *k3c_stream_t;
+
+/* --------------------------------------------------------------- status codes ---- */
+enum {
+    K3C_OK = 0,
+    K3C_EINVAL = -1,     /* bad argument (shape, alignment, range)          */
+    K3C_ECUDA = -2,      /* a CUDA call failed                              */
+    K3C_ENOMEM = -3,     /* device or pinned allocation failed              */
+    K3C_ETIMEOUT = -4,   /* a bounded device wait gave up                   */
+    K3C_ENOTFOUND = -5,  /* expert not resident / not registered            */
+    K3C_EFULL = -6       /* every pool slot is pinned or in flight          */
+};
+/* Message for the last failing k3c_* call on this host thread ("" if none). */
+const char *k3c_last_error(void);
+/* Library version string and the compiled device architecture ("sm_100a"). */
+const char *k3c_version(void);
+
+/* Instrumentation (no reference counterpart; the reference times its stages with wall
+ * clocks, src/cache/k3_cache.c:90-102). k3c_launch_count: kernels this library has
+ * launched since load. k3c_timing_enable(1) makes the k3c_* entry points record CUDA
+ * events around their stages on the launching stream; k3c_timing_read sums and resets
+ * the elapsed milliseconds and call counts per stage, in the order
+ * {experts, router, combine, q8}. */
+long long k3c_launch_count(void);
+void k3c_timing_enable(int on);
+int k3c_timing_read(double *ms, long long *count, int nstage);
+
+/* Activation / weight element types used by the k3c_* entry points. */
+enum { K3C_F32 = 0, K3C_BF16 = 1 };
+/* Expert activation functions. */
+enum { K3C_ACT_SWIGLU = 0, K3C_ACT_SITU = 1 };
+
+/* ====================================================================================
+ * 1. DROP-IN ENTRY POINTS (host pointers)
+ * ==================================================================================== */
+
+/* include/k3/k3.h:559-560. out[rows][2*pcols] = E2M1(nibble) * 2^(scale-127); the LOW nibble
+ * is the EVEN element; scale 255 gives 0. Bit-exact with the reference. */
+void k3_mxfp4_dequant(float *out, const unsigned char *packed,
+                      const unsigned char *scales, int rows, int pcols, int group);
+
+/* include/k3/k3.h:565-566. y[rows] = W[rows][in] . x[in] with W read as MXFP4 (packed
+ * [rows][in/2], scales [rows][ceil(in/group)]). Aborts on odd `in` or group > 64, as the
+ * reference does (src/core/k3_ops.c:1366-1384). */
+void k3_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
+                     const unsigned char *scales, int in, int rows, int group);
+
+/* include/k3/k3.h:285. W is `out` rows of [f32 scale][int8 * in] (row stride 4+in). */
+void k3_matmul_q8(float *y, const float *x, const void *W, int in, int out);
+
+/* include/k3/k3.h:241-243. Sigmoid scores, selection on score+bias, weights from the
+ * unbiased score, optional renorm, times routed_scale; idx/w in descending order. */
+void k3_router(int *idx, float *w, const float *x, const float *W,
+               const float *bias, int hidden, int n_experts, int topk,
+               int renorm, float routed_scale);
+
+/* include/k3/k3.h:388: routed experts dropped from a sum because they failed to load. */
+extern long k3_expert_drops;
+
+/* ====================================================================================
+ * 2. DEVICE ENTRY POINTS (device pointers, explicit stream)
+ * ==================================================================================== */
+
+/* Device form of k3_mxfp4_dequant (same layout and semantics). */
+int k3c_mxfp4_dequant(float *out, const uint8_t *packed, const uint8_t *scales,
+                      int rows, int pcols, int group, k3c_stream_t stream);
+
+/* Batched MXFP4 GEMV: y[t*ldy + r] = sum_k W[r][k] * x[t*ldx + k] for t < ntok (fp32 x,
+ * fp32 accumulate). Device form of k3_matmul_mxfp4 for ntok tokens at once. */
+int k3c_mxfp4_gemv(float *y, int ldy, const float *x, int ldx, int ntok,
+                   const uint8_t *packed, const uint8_t *scales, int in, int rows,
+                   int group, k3c_stream_t stream);
+
+/* INT8 per-row trunk projection, pool layout: wq [out][ldw] int8 (ldw >= in, a multiple of
+ * 16) and wscale [out] fp32. k3c_q8_pack converts the reference's inline row layout
+ * ([f32 scale][int8*in], stride 4+in, include/k3/k3.h:265-303), already on the device,
+ * into that layout. k3c_q8_gemv: y[t*ldy + o] = wscale[o] * sum_i wq[o][i] * x[t][i], x of
+ * type x_dtype (K3C_F32 or K3C_BF16) with row stride ldx elements. */
+int k3c_q8_pack(int8_t *wq, float *wscale, int ldw, const void *w_rows, int in, int out,
+                k3c_stream_t stream);
+int k3c_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
+                const int8_t *wq, const float *wscale, int ldw, int in, int out,
+                k3c_stream_t stream);
+
+/* Router for ntok tokens: logits W.x accumulated in double, sigmoid as in the reference,
+ * top-k selection on score+bias with strict-greater first-index ties, renorm, scale.
+ * x: [ntok][hidden] of x_dtype; W: [n_experts][hidden] of w_dtype; bias fp32 or NULL.
+ * idx/w: [ntok][topk]. scores (optional, may be NULL): [ntok][n_experts] fp32. */
+int k3c_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
+               const void *W, int w_dtype, const float *bias, int hidden, int n_experts,
+               int topk, int renorm, float routed_scale, int ntok, k3c_stream_t stream);
+/* Selection stage alone, on given fp32 scores [ntok][n_experts]: the parity boundary at
+ * which indices must match the reference bit-exactly. */
+int k3c_router_select(int *idx, float *w, const float *scores, const float *bias,
+                      int n_experts, int topk, int renorm, float routed_scale, int ntok,
+                      k3c_stream_t stream);
+
+/* One expert FFN for ntok tokens: y[t] = down(act(gate x[t], up x[t])), x fp32
+ * [ntok][hidden], y fp32 [ntok][hidden]; e holds device addresses. scratch: device bytes,
+ * at least k3c_expert_ffn_scratch(ntok, hidden, inter). */
+size_t k3c_expert_ffn_scratch(int ntok, int hidden, int inter);
+int k3c_expert_ffn(float *y, const float *x, int ntok, const K3ExpertQ *e, int hidden,
+                   int inter, int act, void *scratch, size_t scratch_bytes,
+                   k3c_stream_t stream);
+
+/* A non-latent MoE layer (router + routed experts + unweighted shared expert).
+ * `experts` is a DEVICE array [n_experts] of K3ExpertQ holding device addresses; an
+ * entry whose p1 is NULL is not resident and is counted as a drop if selected.
+ * `shared` is a DEVICE pointer to one K3ExpertQ, or NULL. */
+typedef struct {
+    int hidden, inter, n_experts, topk, renorm, act;
+    float routed_scale;
+    const void *router_w;       /* [n_experts][hidden], router_dtype */
+    int router_dtype;           /* K3C_F32 or K3C_BF16 */
+    const float *router_bias;   /* [n_experts] or NULL */
+    const K3ExpertQ *experts;   /* device array [n_experts] */
+    const K3ExpertQ *shared;    /* device pointer or NULL */
+} k3c_moe_layer;
+
+/* Scratch (device bytes) k3c_moe_decode needs for ntok tokens. */
+size_t k3c_moe_decode_scratch(const k3c_moe_layer *L, int ntok);
+/* out[ntok][hidden] fp32 = MoE(x); x [ntok][hidden] of x_dtype. idx/wt (device, may be
+ * NULL) receive the routing [ntok][topk]. drops (device int, may be NULL) is incremented
+ * by the number of selected experts that were not resident. */
+int k3c_moe_decode(float *out, const void *x, int x_dtype, int ntok, const k3c_moe_layer *L,
+                   int *idx, float *wt, int *drops, void *scratch, size_t scratch_bytes,
+                   k3c_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* K3C_H */

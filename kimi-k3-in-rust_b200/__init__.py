@@ -1,2 +1,327 @@
-"""k3b200: B200-native routed-expert hot path (placeholder, filled in below)."""
+"""k3b200 -- B200-native routed-expert hot path of the kimi-k3 engine.
+
+The product is ``libk3cuda.so`` (sources in ``csrc/``, C ABI in ``include/k3c.h``). This
+module is the thin Python host side over that ABI: it binds the ``k3c_*`` device entry
+points with ctypes and uses torch only for device memory and the current CUDA stream.
+There is no CPU fallback: every call goes through the CUDA library, and importing the
+binding fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
 from . import synth  # noqa: F401
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libk3cuda.so")
+
+K3C_F32, K3C_BF16 = 0, 1
+ACT_SWIGLU, ACT_SITU = 0, 1
+
+
+class K3ExpertQ(C.Structure):
+    """Mirror of the reference's K3ExpertQ (include/k3/k3.h:323-327): gate, up, down as
+    (packed, scale) pointer pairs, here device addresses."""
+
+    _fields_ = [(n, C.c_void_p) for n in ("p1", "s1", "p3", "s3", "p2", "s2")]
+
+
+class MoeLayerC(C.Structure):
+    """Mirror of k3c_moe_layer (include/k3c.h)."""
+
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("n_experts", C.c_int),
+                ("topk", C.c_int), ("renorm", C.c_int), ("act", C.c_int),
+                ("routed_scale", C.c_float), ("router_w", C.c_void_p),
+                ("router_dtype", C.c_int), ("router_bias", C.c_void_p),
+                ("experts", C.c_void_p), ("shared", C.c_void_p)]
+
+
+class K3CError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib():
+    """Load libk3cuda.so (building it with make if this checkout has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        import subprocess
+        subprocess.run(["make", "-s", "-C", os.path.join(HERE, "csrc")], check=True)
+    L = C.CDLL(LIB_PATH)
+    vp, i, f, sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+    sig = {
+        "k3c_last_error": ([], C.c_char_p),
+        "k3c_version": ([], C.c_char_p),
+        "k3c_launch_count": ([], C.c_longlong),
+        "k3c_timing_enable": ([i], None),
+        "k3c_timing_read": ([C.POINTER(C.c_double), C.POINTER(C.c_longlong), i], i),
+        "k3c_mxfp4_dequant": ([vp, vp, vp, i, i, i, vp], i),
+        "k3c_mxfp4_gemv": ([vp, i, vp, i, i, vp, vp, i, i, i, vp], i),
+        "k3c_q8_pack": ([vp, vp, i, vp, i, i, vp], i),
+        "k3c_q8_gemv": ([vp, i, vp, i, i, i, vp, vp, i, i, i, vp], i),
+        "k3c_router": ([vp, vp, vp, vp, i, vp, i, vp, i, i, i, i, f, i, vp], i),
+        "k3c_router_select": ([vp, vp, vp, vp, i, i, i, f, i, vp], i),
+        "k3c_expert_ffn_scratch": ([i, i, i], sz),
+        "k3c_expert_ffn": ([vp, vp, i, C.POINTER(K3ExpertQ), i, i, i, vp, sz, vp], i),
+        "k3c_moe_decode_scratch": ([C.POINTER(MoeLayerC), i], sz),
+        "k3c_moe_decode": ([vp, vp, i, i, C.POINTER(MoeLayerC), vp, vp, vp, vp, sz, vp], i),
+        "k3_mxfp4_dequant": ([vp, vp, vp, i, i, i], None),
+        "k3_matmul_mxfp4": ([vp, vp, vp, vp, i, i, i], None),
+        "k3_matmul_q8": ([vp, vp, vp, i, i], None),
+        "k3_router": ([vp, vp, vp, vp, vp, i, i, i, i, f], None),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise K3CError(f"{what} failed ({rc}): {lib().k3c_last_error().decode()}")
+
+
+def _stream():
+    import torch
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _dtype_code(t):
+    import torch
+    if t.dtype == torch.float32:
+        return K3C_F32
+    if t.dtype in (torch.bfloat16, torch.int16, torch.uint16):
+        return K3C_BF16
+    raise K3CError(f"unsupported activation dtype {t.dtype}")
+
+
+# ------------------------------------------------------------------ kernel wrappers
+
+
+def mxfp4_dequant(packed, scales, group=32):
+    import torch
+    rows, pcols = packed.shape
+    out = torch.empty((rows, 2 * pcols), dtype=torch.float32, device=packed.device)
+    _check(lib().k3c_mxfp4_dequant(_ptr(out), _ptr(packed), _ptr(scales), rows, pcols, group,
+                                   _stream()), "k3c_mxfp4_dequant")
+    return out
+
+
+def mxfp4_gemv(x, packed, scales, group=32):
+    """y[t][r] = sum_k W[r][k] x[t][k]; x fp32 [ntok][in] on the device."""
+    import torch
+    x = x.contiguous()
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    ntok, in_ = x.shape
+    rows = packed.shape[0]
+    y = torch.empty((ntok, rows), dtype=torch.float32, device=x.device)
+    _check(lib().k3c_mxfp4_gemv(_ptr(y), rows, _ptr(x), in_, ntok, _ptr(packed), _ptr(scales),
+                                in_, rows, group, _stream()), "k3c_mxfp4_gemv")
+    return y
+
+
+def q8_pack(rows_u8, in_, out):
+    """Reference row layout ([f32 scale][int8*in] per row, on the device) -> pool layout."""
+    import torch
+    ldw = (in_ + 15) // 16 * 16
+    wq = torch.empty((out, ldw), dtype=torch.int8, device=rows_u8.device)
+    ws = torch.empty(out, dtype=torch.float32, device=rows_u8.device)
+    _check(lib().k3c_q8_pack(_ptr(wq), _ptr(ws), ldw, _ptr(rows_u8), in_, out, _stream()),
+           "k3c_q8_pack")
+    return wq, ws, ldw
+
+
+def q8_gemv(x, wq, ws, ldw, in_, out):
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    x = x.contiguous()
+    ntok = x.shape[0]
+    y = torch.empty((ntok, out), dtype=torch.float32, device=x.device)
+    _check(lib().k3c_q8_gemv(_ptr(y), out, _ptr(x), _dtype_code(x), x.shape[1], ntok, _ptr(wq),
+                             _ptr(ws), ldw, in_, out, _stream()), "k3c_q8_gemv")
+    return y
+
+
+def router(x, W, bias, topk, renorm=1, routed_scale=1.0):
+    """Returns (idx [ntok][topk] int32, w [ntok][topk] fp32, scores [ntok][E] fp32)."""
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    x = x.contiguous()
+    ntok, H = x.shape
+    E = W.shape[0]
+    idx = torch.empty((ntok, topk), dtype=torch.int32, device=x.device)
+    w = torch.empty((ntok, topk), dtype=torch.float32, device=x.device)
+    sc = torch.empty((ntok, E), dtype=torch.float32, device=x.device)
+    _check(lib().k3c_router(_ptr(idx), _ptr(w), _ptr(sc), _ptr(x), _dtype_code(x), _ptr(W),
+                            _dtype_code(W), _ptr(bias), H, E, topk, renorm, routed_scale, ntok,
+                            _stream()), "k3c_router")
+    return idx, w, sc
+
+
+def router_select(scores, bias, topk, renorm=1, routed_scale=1.0):
+    import torch
+    ntok, E = scores.shape
+    idx = torch.empty((ntok, topk), dtype=torch.int32, device=scores.device)
+    w = torch.empty((ntok, topk), dtype=torch.float32, device=scores.device)
+    _check(lib().k3c_router_select(_ptr(idx), _ptr(w), _ptr(scores.contiguous()), _ptr(bias), E,
+                                   topk, renorm, routed_scale, ntok, _stream()),
+           "k3c_router_select")
+    return idx, w
+
+
+class DeviceExpert:
+    """One MXFP4 expert resident in device memory (reference layout per matrix)."""
+
+    KEYS = ("gate_p", "gate_s", "up_p", "up_s", "down_p", "down_s")
+
+    def __init__(self, tensors: dict):
+        self.t = tensors
+
+    @classmethod
+    def from_host(cls, e: dict, device):
+        import torch
+        return cls({k: torch.from_numpy(np.ascontiguousarray(e[k])).to(device) for k in cls.KEYS})
+
+    def q(self) -> K3ExpertQ:
+        t = self.t
+        return K3ExpertQ(t["gate_p"].data_ptr(), t["gate_s"].data_ptr(), t["up_p"].data_ptr(),
+                         t["up_s"].data_ptr(), t["down_p"].data_ptr(), t["down_s"].data_ptr())
+
+
+def expert_run_layout(hidden, inter):
+    """Byte offsets of one expert's contiguous run, in the reference checkpoint's order
+    w1.p w1.s w2.p w2.s w3.p w3.s (src/io/k3_load.c:82-105; w1 gate, w2 down, w3 up).
+    Returns (dict name -> (offset, nbytes), total bytes)."""
+    parts = [("gate_p", inter * hidden // 2), ("gate_s", inter * hidden // 32),
+             ("down_p", hidden * inter // 2), ("down_s", hidden * inter // 32),
+             ("up_p", inter * hidden // 2), ("up_s", inter * hidden // 32)]
+    off, lay = 0, {}
+    for name, nb in parts:
+        lay[name] = (off, nb)
+        off += nb
+    return lay, off
+
+
+def experts_from_blob(blob, n, hidden, inter, stride=None):
+    """K3ExpertQ for n expert runs laid out back to back (every `stride` bytes) in one
+    device uint8 tensor."""
+    lay, total = expert_run_layout(hidden, inter)
+    stride = stride or total
+    base = blob.data_ptr()
+    qs = []
+    for i in range(n):
+        b = base + i * stride
+        qs.append(K3ExpertQ(b + lay["gate_p"][0], b + lay["gate_s"][0], b + lay["up_p"][0],
+                            b + lay["up_s"][0], b + lay["down_p"][0], b + lay["down_s"][0]))
+    return qs
+
+
+def expert_table(qs, device):
+    """Device array of K3ExpertQ built from a list of K3ExpertQ (None = not resident)."""
+    import torch
+    arr = np.zeros((len(qs), 6), np.uint64)
+    for i, q in enumerate(qs):
+        if q is not None:
+            arr[i] = [q.p1 or 0, q.s1 or 0, q.p3 or 0, q.s3 or 0, q.p2 or 0, q.s2 or 0]
+    return torch.from_numpy(arr.view(np.int64)).to(device)
+
+
+def expert_ffn(x, expert: DeviceExpert, hidden, inter, act=ACT_SWIGLU):
+    import torch
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    x = x.contiguous()
+    ntok = x.shape[0]
+    L = lib()
+    nbytes = L.k3c_expert_ffn_scratch(ntok, hidden, inter)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    y = torch.empty((ntok, hidden), dtype=torch.float32, device=x.device)
+    q = expert.q()
+    _check(L.k3c_expert_ffn(_ptr(y), _ptr(x), ntok, C.byref(q), hidden, inter, act,
+                            _ptr(scratch), nbytes, _stream()), "k3c_expert_ffn")
+    return y
+
+
+class MoeLayer:
+    """A non-latent MoE layer on the device: router (bf16 or fp32 W), routed MXFP4
+    experts in an expert table, optional shared expert. decode() runs k3c_moe_decode."""
+
+    def __init__(self, experts, shared, router_w, router_bias, hidden, inter, topk,
+                 renorm=1, routed_scale=1.0, act=ACT_SWIGLU, device=None):
+        """experts: list of DeviceExpert, K3ExpertQ (device addresses) or None (not
+        resident); shared likewise or None."""
+        import torch
+        self.device = device
+        self.experts = experts            # kept alive: the table holds their addresses
+        self.shared = shared
+        self.router_w = router_w
+        self.router_bias = router_bias
+
+        def q_of(e):
+            return e.q() if isinstance(e, DeviceExpert) else e
+        self.table = expert_table([q_of(e) for e in experts], device)
+        self.shared_table = expert_table([q_of(shared)], device) if shared is not None else None
+        self.c = MoeLayerC(hidden, inter, len(experts), topk, renorm, act, routed_scale,
+                           router_w.data_ptr(), _dtype_code(router_w),
+                           router_bias.data_ptr() if router_bias is not None else None,
+                           self.table.data_ptr(),
+                           self.shared_table.data_ptr() if shared is not None else None)
+        self._scratch = torch.empty(0, dtype=torch.uint8, device=device)
+
+    @classmethod
+    def from_host(cls, experts, shared, router_w_bits, router_bias, hidden, inter, topk,
+                  device, **kw):
+        """experts/shared: host dicts of numpy arrays (synth.expert); router_w_bits: bf16 bits
+        (uint16) or fp32 numpy array."""
+        import torch
+        dev = [DeviceExpert.from_host(e, device) for e in experts]
+        sh = DeviceExpert.from_host(shared, device) if shared is not None else None
+        if router_w_bits.dtype == np.uint16:
+            W = torch.from_numpy(router_w_bits.view(np.int16)).to(device).view(torch.bfloat16)
+        else:
+            W = torch.from_numpy(np.ascontiguousarray(router_w_bits, np.float32)).to(device)
+        b = None if router_bias is None else torch.from_numpy(
+            np.ascontiguousarray(router_bias, np.float32)).to(device)
+        return cls(dev, sh, W, b, hidden, inter, topk, device=device, **kw)
+
+    def scratch_bytes(self, ntok):
+        return lib().k3c_moe_decode_scratch(C.byref(self.c), ntok)
+
+    def decode(self, x, out=None, idx=None, wt=None, drops=None):
+        """x: [ntok][hidden] bf16 (or int16 bf16 bits) or fp32 device tensor."""
+        import torch
+        import torch as _t
+        if x.dtype == _t.int16:
+            x = x.view(_t.bfloat16)
+        x = x.contiguous()
+        ntok = x.shape[0]
+        need = self.scratch_bytes(ntok)
+        if self._scratch.numel() < need:
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        H, K = self.c.hidden, self.c.topk
+        if out is None:
+            out = torch.empty((ntok, H), dtype=torch.float32, device=x.device)
+        if idx is None:
+            idx = torch.empty((ntok, K), dtype=torch.int32, device=x.device)
+        if wt is None:
+            wt = torch.empty((ntok, K), dtype=torch.float32, device=x.device)
+        _check(lib().k3c_moe_decode(_ptr(out), _ptr(x), _dtype_code(x), ntok, C.byref(self.c),
+                                    _ptr(idx), _ptr(wt), _ptr(drops), _ptr(self._scratch),
+                                    self._scratch.numel(), _stream()), "k3c_moe_decode")
+        return out, idx, wt

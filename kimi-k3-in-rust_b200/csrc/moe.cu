@@ -1,0 +1,391 @@
+// moe.cu -- expert FFN and the non-latent MoE layer for decode-sized batches.
+//
+// Reference semantics (src/core/k3_ops.c:556-656, restated for the BASELINE shapes):
+//   route each token on its full input; run each selected expert as gate/up GEMV, the
+//   activation, and the down GEMV; accumulate acc += w_j * expert_j in float, in top-k
+//   order, from zero; add the shared expert unweighted. A selected expert that is not
+//   resident is skipped and counted as a drop (:616-626).
+//
+// Device schedule (one stream, no host round trip):
+//   plan     group the (token, slot) pairs by expert, deterministically (pairs of one
+//            expert keep token order), so each expert's weights stream from HBM once for
+//            all of its tokens; the shared expert is one more slot holding every token.
+//   gateup   per (slot, 8 rows): gate and up rows read once, SwiGLU/SiTU fused in the
+//            epilogue; act[pair][inter] fp32.
+//   down     per (slot, 16 rows): down rows read once; unweighted expert output written
+//            to contrib[token][k][hidden] (k = topk for the shared expert).
+//   combine  out[t] = sum_j w[t][j] * contrib[t][j] in j order (separately rounded multiply
+//            and add, as the reference compiles with -ffp-contract=off) + contrib[t][topk].
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "gemv_core.cuh"
+
+namespace k3c {
+
+int launch_router_scores(float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
+                         int hidden, int n_experts, int ntok, cudaStream_t s);
+int launch_router_select(int *idx, float *w, const float *scores, const float *bias,
+                         int n_experts, int topk, int renorm, float routed_scale, int ntok,
+                         cudaStream_t s);
+
+struct Slot {
+    K3ExpertQ q;
+    int ntok;       // pairs in this slot
+    int pair_base;  // first pair index
+};
+
+struct Plan {
+    int *n_slots;     // [1]
+    Slot *slots;      // [max_slots]
+    int *pair_tok;    // [max_pairs]
+    int *pair_k;      // [max_pairs]
+    uint8_t *dropped; // [ntok*topk]
+};
+
+__device__ __forceinline__ float sigmoid_ref(float v) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+}
+
+__device__ __forceinline__ float act_fn(float g, float u, int act) {
+    if (act == K3C_ACT_SITU) {  // src/core/k3_ops.c:110-123, b1=4, b2=25
+        const float a = __fmul_rn(__fmul_rn(4.0f, tanhf(__fdiv_rn(g, 4.0f))), sigmoid_ref(g));
+        const float uu = __fmul_rn(25.0f, tanhf(__fdiv_rn(u, 25.0f)));
+        return __fmul_rn(a, uu);
+    }
+    return __fmul_rn(__fmul_rn(g, sigmoid_ref(g)), u);  // silu(g) * u
+}
+
+// ------------------------------------------------------------------------- plan
+// One block. Pairs (t, j) -> slot of expert idx[t][j]; rank within the slot = number of
+// earlier pairs (row-major) with the same expert, so the layout is deterministic.
+__global__ void __launch_bounds__(1024) k_moe_plan(Plan p, const int *__restrict__ idx, int ntok,
+                                                   int topk, const K3ExpertQ *__restrict__ experts,
+                                                   int n_experts, const K3ExpertQ *__restrict__ shared,
+                                                   int *__restrict__ drops) {
+    extern __shared__ int sm[];
+    int *cnt = sm;                 // [n_experts]
+    int *slot_of = sm + n_experts; // [n_experts]
+    __shared__ int s_npairs;
+    const int P = ntok * topk;
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int e = idx[i];
+        const bool ok = e >= 0 && e < n_experts && experts[e].p1 != nullptr;
+        p.dropped[i] = ok ? 0 : 1;
+        if (ok) atomicAdd(&cnt[e], 1);
+        else if (drops) atomicAdd(drops, 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // n_experts is small (hundreds); a serial scan is cheapest here
+        int ns = 0, base = 0;
+        for (int e = 0; e < n_experts; e++) {
+            if (cnt[e] > 0) {
+                slot_of[e] = ns;
+                p.slots[ns].q = experts[e];
+                p.slots[ns].ntok = cnt[e];
+                p.slots[ns].pair_base = base;
+                base += cnt[e];
+                ns++;
+            } else {
+                slot_of[e] = -1;
+            }
+        }
+        if (shared) {
+            p.slots[ns].q = *shared;
+            p.slots[ns].ntok = ntok;
+            p.slots[ns].pair_base = base;
+            ns++;
+        }
+        s_npairs = base;
+        *p.n_slots = ns;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        if (p.dropped[i]) continue;
+        const int e = idx[i];
+        int rank = 0;
+        for (int k = 0; k < i; k++) rank += (idx[k] == e && !p.dropped[k]);
+        const int pos = p.slots[slot_of[e]].pair_base + rank;
+        p.pair_tok[pos] = i / topk;
+        p.pair_k[pos] = i % topk;
+    }
+    if (shared) {
+        for (int t = threadIdx.x; t < ntok; t += blockDim.x) {
+            p.pair_tok[s_npairs + t] = t;
+            p.pair_k[s_npairs + t] = topk;
+        }
+    }
+}
+
+// Single-expert plan for k3c_expert_ffn: slot 0 = e, pairs t -> (t, 0).
+__global__ void k_ffn_plan(Plan p, K3ExpertQ e, int ntok) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        *p.n_slots = 1;
+        p.slots[0].q = e;
+        p.slots[0].ntok = ntok;
+        p.slots[0].pair_base = 0;
+    }
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < ntok; t += gridDim.x * blockDim.x) {
+        p.pair_tok[t] = t;
+        p.pair_k[t] = 0;
+    }
+}
+
+// ---------------------------------------------------------------- gate/up + act
+// grid (inter/8, max_slots): warp w computes gate row r and up row r (r = 8*bx + w) for all
+// tokens of the slot, NT at a time.
+template <int NT>
+__global__ void __launch_bounds__(256) k_moe_gateup(Plan p, const float *__restrict__ xf,
+                                                    int hidden, int inter, int act,
+                                                    float *__restrict__ actbuf) {
+    const int s = blockIdx.y;
+    if (s >= *p.n_slots) return;
+    const Slot sl = p.slots[s];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    if (r >= inter) return;
+    const size_t pitch = (size_t)hidden / 2, spitch = (size_t)hidden / 32;
+    const uint8_t *prow[2] = {sl.q.p1 + r * pitch, sl.q.p3 + r * pitch};
+    const uint8_t *srow[2] = {sl.q.s1 + r * spitch, sl.q.s3 + r * spitch};
+    for (int t0 = 0; t0 < sl.ntok; t0 += NT) {
+        const int nt = sl.ntok - t0 < NT ? sl.ntok - t0 : NT;
+        const float *xrow[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+            xrow[t] = xf + (size_t)p.pair_tok[sl.pair_base + t0 + (t < nt ? t : 0)] * hidden;
+        float acc[2][NT];
+        mx_dot_rows<2, NT>(prow, srow, xrow, nt, hidden / 32, acc);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const float g = warp_sum(acc[0][t]);
+            const float u = warp_sum(acc[1][t]);
+            if (lane == 0 && t < nt)
+                actbuf[(size_t)(sl.pair_base + t0 + t) * inter + r] = act_fn(g, u, act);
+        }
+    }
+}
+
+// -------------------------------------------------------------------------- down
+// grid (hidden/16, max_slots): warp w computes down rows 2*(8*bx+w)+{0,1}.
+template <int NT>
+__global__ void __launch_bounds__(256) k_moe_down(Plan p, const float *__restrict__ actbuf,
+                                                  int hidden, int inter, int kstride,
+                                                  float *__restrict__ contrib) {
+    const int s = blockIdx.y;
+    if (s >= *p.n_slots) return;
+    const Slot sl = p.slots[s];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = (blockIdx.x * 8 + warp) * 2;
+    if (r0 >= hidden) return;
+    const int r1 = r0 + 1 < hidden ? r0 + 1 : r0;
+    const size_t pitch = (size_t)inter / 2, spitch = (size_t)inter / 32;
+    const uint8_t *prow[2] = {sl.q.p2 + r0 * pitch, sl.q.p2 + r1 * pitch};
+    const uint8_t *srow[2] = {sl.q.s2 + r0 * spitch, sl.q.s2 + r1 * spitch};
+    for (int t0 = 0; t0 < sl.ntok; t0 += NT) {
+        const int nt = sl.ntok - t0 < NT ? sl.ntok - t0 : NT;
+        const float *xrow[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+            xrow[t] = actbuf + (size_t)(sl.pair_base + t0 + (t < nt ? t : 0)) * inter;
+        float acc[2][NT];
+        mx_dot_rows<2, NT>(prow, srow, xrow, nt, inter / 32, acc);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const float a0 = warp_sum(acc[0][t]);
+            const float a1 = warp_sum(acc[1][t]);
+            if (lane == 0 && t < nt) {
+                const int pr = sl.pair_base + t0 + t;
+                float *o = contrib + ((size_t)p.pair_tok[pr] * kstride + p.pair_k[pr]) * hidden;
+                o[r0] = a0;
+                if (r1 != r0) o[r1] = a1;
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------------------- combine
+__global__ void k_moe_combine(float *__restrict__ out, const float *__restrict__ contrib,
+                              const float *__restrict__ wt, const uint8_t *__restrict__ dropped,
+                              int ntok, int topk, int hidden, int has_shared) {
+    const int t = blockIdx.y;
+    const int ks = topk + 1;
+    for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < hidden; h += gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (int j = 0; j < topk; j++) {
+            if (dropped[t * topk + j]) continue;
+            acc = __fadd_rn(acc, __fmul_rn(wt[t * topk + j], contrib[((size_t)t * ks + j) * hidden + h]));
+        }
+        if (has_shared) acc = __fadd_rn(acc, contrib[((size_t)t * ks + topk) * hidden + h]);
+        out[(size_t)t * hidden + h] = acc;
+    }
+}
+
+template <typename XT>
+__global__ void k_to_f32(float *__restrict__ y, const XT *__restrict__ x, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        if constexpr (sizeof(XT) == 2) y[i] = bf16_bits_to_f32(x[i]);
+        else y[i] = x[i];
+    }
+}
+
+// ------------------------------------------------------------------- launchers
+static int check_dims(int hidden, int inter) {
+    if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32)
+        return set_error(K3C_EINVAL, "moe: hidden=%d inter=%d must be positive multiples of 32", hidden, inter);
+    return K3C_OK;
+}
+
+static int launch_ffn_kernels(const Plan &p, int max_slots, const float *xf, int hidden,
+                              int inter, int act, float *actbuf, int kstride, float *contrib,
+                              int max_tok_per_slot, cudaStream_t s) {
+    dim3 ga((inter + 7) / 8, max_slots), gd((hidden + 15) / 16, max_slots);
+    if (max_tok_per_slot <= 1) {
+        k_moe_gateup<1><<<ga, 256, 0, s>>>(p, xf, hidden, inter, act, actbuf);
+        K3C_CHECK_LAUNCH();
+        k_moe_down<1><<<gd, 256, 0, s>>>(p, actbuf, hidden, inter, kstride, contrib);
+    } else if (max_tok_per_slot <= 2) {
+        k_moe_gateup<2><<<ga, 256, 0, s>>>(p, xf, hidden, inter, act, actbuf);
+        K3C_CHECK_LAUNCH();
+        k_moe_down<2><<<gd, 256, 0, s>>>(p, actbuf, hidden, inter, kstride, contrib);
+    } else {
+        k_moe_gateup<4><<<ga, 256, 0, s>>>(p, xf, hidden, inter, act, actbuf);
+        K3C_CHECK_LAUNCH();
+        k_moe_down<4><<<gd, 256, 0, s>>>(p, actbuf, hidden, inter, kstride, contrib);
+    }
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
+static bool carve_plan(Carve &cv, Plan &p, int max_slots, int max_pairs, int ntok_topk) {
+    p.n_slots = cv.take<int>(1);
+    p.slots = cv.take<Slot>(max_slots);
+    p.pair_tok = cv.take<int>(max_pairs);
+    p.pair_k = cv.take<int>(max_pairs);
+    p.dropped = cv.take<uint8_t>(ntok_topk > 0 ? ntok_topk : 1);
+    return p.n_slots && p.slots && p.pair_tok && p.pair_k && p.dropped;
+}
+
+// Sizing passes carve from a dummy non-null base: only the offsets matter.
+static char *const kSizingBase = reinterpret_cast<char *>(4096);
+
+size_t ffn_scratch(int ntok, int hidden, int inter) {
+    Carve cv{kSizingBase, (size_t)-1 / 2, 0};
+    Plan p;
+    carve_plan(cv, p, 1, ntok, 0);
+    cv.take<float>((size_t)ntok * inter);
+    return cv.used + 256;
+}
+
+int launch_expert_ffn(float *y, const float *x, int ntok, const K3ExpertQ *e, int hidden,
+                      int inter, int act, void *scratch, size_t scratch_bytes, cudaStream_t s) {
+    K3C_TRY(check_dims(hidden, inter));
+    if (!e || !e->p1 || !e->p2 || !e->p3) return set_error(K3C_EINVAL, "expert_ffn: null expert");
+    if (ntok <= 0) return K3C_OK;
+    if (((uintptr_t)x & 15) != 0) return set_error(K3C_EINVAL, "expert_ffn: x not 16-byte aligned");
+    Carve cv{(char *)scratch, scratch_bytes, 0};
+    Plan p;
+    if (!carve_plan(cv, p, 1, ntok, 0)) return set_error(K3C_EINVAL, "expert_ffn: scratch too small");
+    float *actbuf = cv.take<float>((size_t)ntok * inter);
+    if (!actbuf) return set_error(K3C_EINVAL, "expert_ffn: scratch too small (%zu)", scratch_bytes);
+    k_ffn_plan<<<1, 256, 0, s>>>(p, *e, ntok);
+    K3C_CHECK_LAUNCH();
+    return launch_ffn_kernels(p, 1, x, hidden, inter, act, actbuf, 1, y, ntok, s);
+}
+
+struct DecodeBufs {
+    Plan p;
+    float *xf, *scores, *wt, *actbuf, *contrib;
+    int *idx;
+};
+
+static bool carve_decode(Carve &cv, DecodeBufs &b, const k3c_moe_layer *L, int ntok) {
+    const int P = ntok * L->topk;
+    const int max_slots = (P < L->n_experts ? P : L->n_experts) + 1;
+    const int max_pairs = P + ntok;
+    if (!carve_plan(cv, b.p, max_slots, max_pairs, P)) return false;
+    b.xf = cv.take<float>((size_t)ntok * L->hidden);
+    b.scores = cv.take<float>((size_t)ntok * L->n_experts);
+    b.idx = cv.take<int>(P);
+    b.wt = cv.take<float>(P);
+    b.actbuf = cv.take<float>((size_t)max_pairs * L->inter);
+    b.contrib = cv.take<float>((size_t)ntok * (L->topk + 1) * L->hidden);
+    return b.xf && b.scores && b.idx && b.wt && b.actbuf && b.contrib;
+}
+
+size_t moe_decode_scratch(const k3c_moe_layer *L, int ntok) {
+    Carve cv{kSizingBase, (size_t)-1 / 2, 0};
+    DecodeBufs b;
+    carve_decode(cv, b, L, ntok);
+    return cv.used + 256;
+}
+
+int launch_moe_decode(float *out, const void *x, int x_dtype, int ntok, const k3c_moe_layer *L,
+                      int *idx_out, float *wt_out, int *drops, void *scratch,
+                      size_t scratch_bytes, cudaStream_t s) {
+    if (!L) return set_error(K3C_EINVAL, "moe_decode: null layer");
+    K3C_TRY(check_dims(L->hidden, L->inter));
+    if (L->n_experts <= 0 || L->topk <= 0 || L->topk > K3_MAX_TOPK || L->topk > L->n_experts)
+        return set_error(K3C_EINVAL, "moe_decode: n_experts=%d topk=%d", L->n_experts, L->topk);
+    if (!L->experts || !L->router_w) return set_error(K3C_EINVAL, "moe_decode: null experts/router");
+    if (ntok <= 0) return K3C_OK;
+    if (ntok * L->topk > 4096) return set_error(K3C_EINVAL, "moe_decode: ntok*topk=%d > 4096 (use prefill)", ntok * L->topk);
+    if ((size_t)L->n_experts * 2 * sizeof(int) > 96 * 1024) return set_error(K3C_EINVAL, "moe_decode: n_experts too large");
+    Carve cv{(char *)scratch, scratch_bytes, 0};
+    DecodeBufs b;
+    if (!carve_decode(cv, b, L, ntok)) return set_error(K3C_EINVAL, "moe_decode: scratch too small (%zu)", scratch_bytes);
+    int *idx = idx_out ? idx_out : b.idx;
+    float *wt = wt_out ? wt_out : b.wt;
+    const size_t nx = (size_t)ntok * L->hidden;
+    if (x_dtype == K3C_BF16) k_to_f32<uint16_t><<<(unsigned)((nx + 255) / 256 < 1184 ? (nx + 255) / 256 : 1184), 256, 0, s>>>(b.xf, (const uint16_t *)x, nx);
+    else if (x_dtype == K3C_F32) k_to_f32<float><<<(unsigned)((nx + 255) / 256 < 1184 ? (nx + 255) / 256 : 1184), 256, 0, s>>>(b.xf, (const float *)x, nx);
+    else return set_error(K3C_EINVAL, "moe_decode: x_dtype=%d", x_dtype);
+    K3C_CHECK_LAUNCH();
+    stage_begin(STAGE_ROUTER, s);
+    K3C_TRY(launch_router_scores(b.scores, x, x_dtype, L->router_w, L->router_dtype, L->hidden, L->n_experts, ntok, s));
+    K3C_TRY(launch_router_select(idx, wt, b.scores, L->router_bias, L->n_experts, L->topk, L->renorm, L->routed_scale, ntok, s));
+    stage_end(STAGE_ROUTER, s);
+    const int P = ntok * L->topk;
+    const int max_slots = (P < L->n_experts ? P : L->n_experts) + (L->shared ? 1 : 0);
+    const size_t psmem = (size_t)L->n_experts * 2 * sizeof(int);
+    if (psmem > 48 * 1024) K3C_TRY_CUDA(cudaFuncSetAttribute(k_moe_plan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
+    k_moe_plan<<<1, 1024, psmem, s>>>(b.p, idx, ntok, L->topk, L->experts, L->n_experts, L->shared, drops);
+    K3C_CHECK_LAUNCH();
+    stage_begin(STAGE_EXPERTS, s);
+    K3C_TRY(launch_ffn_kernels(b.p, max_slots, b.xf, L->hidden, L->inter, L->act, b.actbuf,
+                               L->topk + 1, b.contrib, ntok, s));
+    stage_end(STAGE_EXPERTS, s);
+    k_moe_combine<<<dim3((L->hidden + 255) / 256, ntok), 256, 0, s>>>(out, b.contrib, wt, b.p.dropped, ntok, L->topk, L->hidden, L->shared ? 1 : 0);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
+}  // namespace k3c
+
+extern "C" size_t k3c_expert_ffn_scratch(int ntok, int hidden, int inter) {
+    return k3c::ffn_scratch(ntok, hidden, inter);
+}
+
+extern "C" int k3c_expert_ffn(float *y, const float *x, int ntok, const K3ExpertQ *e,
+                              int hidden, int inter, int act, void *scratch,
+                              size_t scratch_bytes, k3c_stream_t stream) {
+    k3c::clear_error();
+    k3c::stage_begin(k3c::STAGE_EXPERTS, (cudaStream_t)stream);
+    int rc = k3c::launch_expert_ffn(y, x, ntok, e, hidden, inter, act, scratch, scratch_bytes,
+                                    (cudaStream_t)stream);
+    k3c::stage_end(k3c::STAGE_EXPERTS, (cudaStream_t)stream);
+    return rc;
+}
+
+extern "C" size_t k3c_moe_decode_scratch(const k3c_moe_layer *L, int ntok) {
+    return L ? k3c::moe_decode_scratch(L, ntok) : 0;
+}
+
+extern "C" int k3c_moe_decode(float *out, const void *x, int x_dtype, int ntok,
+                              const k3c_moe_layer *L, int *idx, float *wt, int *drops,
+                              void *scratch, size_t scratch_bytes, k3c_stream_t stream) {
+    k3c::clear_error();
+    return k3c::launch_moe_decode(out, x, x_dtype, ntok, L, idx, wt, drops, scratch,
+                                  scratch_bytes, (cudaStream_t)stream);
+}

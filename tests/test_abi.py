@@ -1,0 +1,75 @@
+"""CPU-only checks of the C ABI: the library loads, exports every function include/k3c.h
+declares, and the ctypes mirrors of the header's structs have the C layout."""
+import ctypes as C
+import os
+import re
+import subprocess
+import tempfile
+
+from conftest import ROOT
+
+HEADERS = [os.path.join(ROOT, "include", f) for f in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if f.endswith(".h")]
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:extern\s+)?[A-Za-z_][\w\s\*]*?\b(k3c?_\w+)\s*\(", src, re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_dropin_and_device_api():
+    names = declared_functions()
+    for n in ("k3_mxfp4_dequant", "k3_matmul_mxfp4", "k3_matmul_q8", "k3_router",
+              "k3c_mxfp4_gemv", "k3c_moe_decode", "k3c_router_select", "k3c_last_error"):
+        assert n in names, n
+
+
+def test_library_exports_every_declared_symbol(k3):
+    L = k3.lib()
+    missing = [n for n in sorted(declared_functions()) if not hasattr(L, n)]
+    assert not missing, missing
+    assert hasattr(L, "k3_expert_drops")       # extern long, include/k3c.h
+    assert C.c_long.in_dll(L, "k3_expert_drops").value == 0
+    assert L.k3c_version().decode().endswith("sm_100a")
+
+
+def test_library_built_for_sm100a_only():
+    mk = open(os.path.join(ROOT, "kimi-k3-in-rust_b200", "csrc", "Makefile")).read()
+    arch = re.search(r"^ARCH\s*:=\s*(.*)$", mk, re.M).group(1).split()
+    assert arch == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    assert "use_fast_math" not in mk.split("NVFLAGS")[1].split("\n")[0]
+
+
+def test_struct_layouts_match_header(k3):
+    prog = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "k3c.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu\n", sizeof(K3ExpertQ), offsetof(K3ExpertQ, p2),
+         sizeof(k3c_moe_layer), offsetof(k3c_moe_layer, router_w), offsetof(k3c_moe_layer, shared));
+  return 0; }
+"""
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(prog)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        got = [int(v) for v in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
+    want = [C.sizeof(k3.K3ExpertQ), k3.K3ExpertQ.p2.offset, C.sizeof(k3.MoeLayerC),
+            k3.MoeLayerC.router_w.offset, k3.MoeLayerC.shared.offset]
+    assert got == want
+
+
+def test_errors_are_reported_without_a_gpu(k3):
+    """Argument validation runs before any CUDA call, so it is testable here."""
+    L = k3.lib()
+    rc = L.k3c_mxfp4_gemv(None, 4, None, 4, 1, None, None, 7, 4, 32, None)   # odd `in`
+    assert rc == -1 and b"odd" in L.k3c_last_error()
+    rc = L.k3c_mxfp4_gemv(None, 4, None, 64, 1, None, None, 64, 4, 65, None)  # group > 64
+    assert rc == -1 and b"group" in L.k3c_last_error()

@@ -74,11 +74,12 @@ def test_q8_matches_reference_kernel(golden, ora, name):
 
 def test_router_small_matches_reference(golden, ora):
     g = golden("ref_kernels.npz")
+    X, W, bias = g["rt_x"], g["rt_W"], g["rt_bias"]     # keep the arrays alive across calls
     for renorm in (0, 1):
-        for t in range(g["rt_x"].shape[0]):
+        for t in range(X.shape[0]):
             idx = np.empty(6, np.int32)
             w = np.empty(6, np.float32)
-            ora.lib().ora_router(idx, w, g["rt_x"][t], g["rt_W"], g["rt_bias"].ctypes.data,
+            ora.lib().ora_router(idx, w, np.ascontiguousarray(X[t]), W, bias.ctypes.data,
                                  64, 24, 6, renorm, 2.5)
             assert np.array_equal(idx, g[f"rt_idx_r{renorm}"][t])
             assert np.array_equal(w.view(np.uint32), g[f"rt_wt_r{renorm}"][t].view(np.uint32))
