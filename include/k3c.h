@@ -177,6 +177,23 @@ int k3c_moe_decode(float *out, const void *x, int x_dtype, int ntok, const k3c_m
                    int *idx, float *wt, int *drops, void *scratch, size_t scratch_bytes,
                    k3c_stream_t stream);
 
+/* No counterpart in the reference. k3c_moe_decode without caller scratch, for callers that
+ * cannot allocate device memory: an engine that owns all device memory and gives this
+ * library no allocator, or a decode loop whose host code must not call cudaMalloc. The
+ * scratch is a fixed device array inside the library, K3C_NOALLOC_SCRATCH_BYTES (8 MiB)
+ * per GPU that loads it, held until the process exits; that covers the BASELINE decode
+ * batch (hidden 7168, inter 2048, top-8 + shared, 16 tokens: ~5.8 MB). A call whose
+ * k3c_moe_decode_scratch(L, ntok) exceeds the maximum returns K3C_EINVAL without touching
+ * the GPU. The call itself allocates nothing; inputs and outputs are the caller's. The
+ * first call on each device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current: make that first call before any stream capture begins. All
+ * calls on a device share the array and leave the last call's contents in it (none is read
+ * before being written), so calls whose kernels overlap on the GPU race. */
+#define K3C_NOALLOC_SCRATCH_BYTES (8u << 20)
+int k3c_moe_decode_noalloc(float *out, const void *x, int x_dtype, int ntok,
+                           const k3c_moe_layer *L, int *idx, float *wt, int *drops,
+                           k3c_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
