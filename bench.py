@@ -169,22 +169,25 @@ def run_reference(args, ws, rank):
 
 
 # ------------------------------------------------------------------------ our arm
-def build_device_workload(k3, dev, seed):
+def build_device_workload(k3, dev, seed, distinct=E):
+    """distinct < 384 tiles that many random experts over the 384 ids (profiling runs with
+    a smaller device footprint); the default gives every expert id its own weights."""
     import torch
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     lay, run = k3.expert_run_layout(H, I)
-    blob = torch.empty((E + 1) * run, dtype=torch.uint8, device=dev)
-    b2 = blob.view(E + 1, run)
+    blob = torch.empty((distinct + 1) * run, dtype=torch.uint8, device=dev)
+    b2 = blob.view(distinct + 1, run)
     for name, (off, nb) in lay.items():
         seg = b2[:, off:off + nb]
         if name.endswith("_p"):
             seg.copy_(torch.randint(0, 256, seg.shape, generator=g, device=dev, dtype=torch.uint8))
         else:
             seg.copy_(torch.randint(118, 125, seg.shape, generator=g, device=dev, dtype=torch.uint8))
-    qs = k3.experts_from_blob(blob, E + 1, H, I)
+    qs = k3.experts_from_blob(blob, distinct + 1, H, I)
     W = (torch.randn((E, H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    layer = k3.MoeLayer(qs[:E], qs[E], W, None, H, I, K, device=dev)
+    layer = k3.MoeLayer([qs[i % distinct] for i in range(E)], qs[distinct], W, None, H, I, K,
+                        device=dev)
     wq = torch.randint(-127, 128, (H, H), generator=g, device=dev, dtype=torch.int8)
     ws = torch.rand(H, generator=g, device=dev) * 9e-3 + 1e-3
     return blob, layer, wq, ws
@@ -202,7 +205,7 @@ def run_ours(args, ws, rank, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    blob, layer, wq, wsc, = build_device_workload(k3, dev, 1234 + rank)
+    blob, layer, wq, wsc, = build_device_workload(k3, dev, 1234 + rank, args.distinct)
     g = torch.Generator(device=dev)
     g.manual_seed(99 + rank)
     B = 16
@@ -355,6 +358,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--distinct", type=int, default=E,
+                    help="distinct expert weights tiled over the 384 ids (profiling only)")
     args = ap.parse_args()
     ws, rank, local = dist_setup(args)
     if args.impl == "reference":
