@@ -169,13 +169,19 @@ def run_reference(args, ws, rank):
 
 
 # ------------------------------------------------------------------------ our arm
-def build_device_workload(k3, dev, seed, distinct=E):
+def build_device_workload(k3, dev, seed, distinct=E, path="tc", terms=3):
     """distinct < 384 tiles that many random experts over the 384 ids (profiling runs with
-    a smaller device footprint); the default gives every expert id its own weights."""
+    a smaller device footprint); the default gives every expert id its own weights.
+    path "tc": experts generated directly in the pool format of the tensor-core path
+    (random nibbles and scale bytes have the same distribution in any byte order);
+    path "cuda": the reference's expert run layout for the CUDA-core kernels."""
     import torch
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
-    lay, run = k3.expert_run_layout(H, I)
+    if path == "tc":
+        lay, run = k3.pool_layout(H, I)
+    else:
+        lay, run = k3.expert_run_layout(H, I)
     blob = torch.empty((distinct + 1) * run, dtype=torch.uint8, device=dev)
     b2 = blob.view(distinct + 1, run)
     for name, (off, nb) in lay.items():
@@ -184,10 +190,15 @@ def build_device_workload(k3, dev, seed, distinct=E):
             seg.copy_(torch.randint(0, 256, seg.shape, generator=g, device=dev, dtype=torch.uint8))
         else:
             seg.copy_(torch.randint(118, 125, seg.shape, generator=g, device=dev, dtype=torch.uint8))
-    qs = k3.experts_from_blob(blob, distinct + 1, H, I)
     W = (torch.randn((E, H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    layer = k3.MoeLayer([qs[i % distinct] for i in range(E)], qs[distinct], W, None, H, I, K,
-                        device=dev)
+    if path == "tc":
+        run_of = torch.tensor([i % distinct for i in range(E)], dtype=torch.int32, device=dev)
+        layer = k3.PoolMoeLayer(blob, distinct + 1, run_of, distinct, W, None, H, I, K,
+                                terms=terms)
+    else:
+        qs = k3.experts_from_blob(blob, distinct + 1, H, I)
+        layer = k3.MoeLayer([qs[i % distinct] for i in range(E)], qs[distinct], W, None, H, I,
+                            K, device=dev)
     wq = torch.randint(-127, 128, (H, H), generator=g, device=dev, dtype=torch.int8)
     ws = torch.rand(H, generator=g, device=dev) * 9e-3 + 1e-3
     return blob, layer, wq, ws
@@ -205,7 +216,8 @@ def run_ours(args, ws, rank, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    blob, layer, wq, wsc, = build_device_workload(k3, dev, 1234 + rank, args.distinct)
+    blob, layer, wq, wsc, = build_device_workload(k3, dev, 1234 + rank, args.distinct, args.path,
+                                                  args.terms)
     g = torch.Generator(device=dev)
     g.manual_seed(99 + rank)
     B = 16
@@ -328,10 +340,13 @@ def run_ours(args, ws, rank, local):
         "metric": METRIC, "value": ws * B * args.steps / dt, "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp32 (MXFP4 weights, bf16 inputs widened exactly, fp32 accumulate)",
+        "dtype": (f"mxfp4 x e4m3 (activations as {args.terms} E4M3 terms), fp32 accumulate "
+                  "(tcgen05 kind::mxf8f6f4)") if args.path == "tc" else
+                 "fp32 (MXFP4 weights, bf16 inputs widened exactly, fp32 accumulate)",
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "batch": B, "hidden": H, "inter": I, "experts": E,
-                   "topk": K, "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                   "topk": K, "path": args.path, "terms": args.terms if args.path == "tc" else None,
+                   "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
                    "l2": "inputs larger than L2: each step reads ~110 different experts (~2.6 GB) "
                          "from a rotating pool of 32 token batches"},
         "decode_hbm_gbs": layer_bytes / dt / 1e9,
@@ -360,6 +375,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--distinct", type=int, default=E,
                     help="distinct expert weights tiled over the 384 ids (profiling only)")
+    ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
+                    help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
+    ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
     args = ap.parse_args()
     ws, rank, local = dist_setup(args)
     if args.impl == "reference":

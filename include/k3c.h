@@ -194,6 +194,42 @@ int k3c_moe_decode_noalloc(float *out, const void *x, int x_dtype, int ntok,
                            const k3c_moe_layer *L, int *idx, float *wt, int *drops,
                            k3c_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * Tensor-core path (tcgen05 block-scaled MMA, kind::mxf8f6f4).
+ *
+ * Experts live in an HBM arena of "pool-format" runs (no reference counterpart; the
+ * reference's cache holds the checkpoint's byte run, src/cache/k3_cache.c:24-261): the same
+ * bytes as the checkpoint's w1/w2/w3 packed nibbles and E8M0 scales, re-ordered so the
+ * tensor core can read them -- gate and up rows interleaved in blocks of 64 and the scales
+ * in 512-byte 128-row x 4-group atoms. k3c_pool_pack_expert converts one expert given in the
+ * reference layout (device addresses) into a run of k3c_pool_run_bytes bytes (256-byte
+ * aligned). hidden and inter must be multiples of 128.
+ * ------------------------------------------------------------------------------------ */
+size_t k3c_pool_run_bytes(int hidden, int inter);
+int k3c_pool_pack_expert(uint8_t *run, const K3ExpertQ *src, int hidden, int inter,
+                         k3c_stream_t stream);
+
+typedef struct {
+    int hidden, inter, n_experts, topk, renorm, act;
+    float routed_scale;
+    const void *router_w;       /* [n_experts][hidden], router_dtype */
+    int router_dtype;
+    const float *router_bias;   /* [n_experts] or NULL */
+    const uint8_t *arena;       /* device: n_runs pool-format runs, run_stride bytes apart */
+    size_t run_stride;          /* multiple of 256, >= k3c_pool_run_bytes */
+    int n_runs;
+    const int *run_of;          /* device [n_experts]: run index, -1 = not resident (drop) */
+    int shared_run;             /* run index of the shared expert, -1 = none */
+    int terms;                  /* E4M3 terms per activation (1..3): ~4 bits each */
+} k3c_moe_pool_layer;
+
+/* Same contract as k3c_moe_decode (non-latent MoE layer, drops counted), computed with
+ * tcgen05 block-scaled MMAs on pool-format experts; ntok <= 32. */
+size_t k3c_moe_decode_tc_scratch(const k3c_moe_pool_layer *L, int ntok);
+int k3c_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok,
+                      const k3c_moe_pool_layer *L, int *idx, float *wt, int *drops,
+                      void *scratch, size_t scratch_bytes, k3c_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

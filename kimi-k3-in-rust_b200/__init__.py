@@ -39,6 +39,17 @@ class MoeLayerC(C.Structure):
                 ("experts", C.c_void_p), ("shared", C.c_void_p)]
 
 
+class MoePoolLayerC(C.Structure):
+    """Mirror of k3c_moe_pool_layer (include/k3c.h)."""
+
+    _fields_ = [("hidden", C.c_int), ("inter", C.c_int), ("n_experts", C.c_int),
+                ("topk", C.c_int), ("renorm", C.c_int), ("act", C.c_int),
+                ("routed_scale", C.c_float), ("router_w", C.c_void_p),
+                ("router_dtype", C.c_int), ("router_bias", C.c_void_p),
+                ("arena", C.c_void_p), ("run_stride", C.c_size_t), ("n_runs", C.c_int),
+                ("run_of", C.c_void_p), ("shared_run", C.c_int), ("terms", C.c_int)]
+
+
 class K3CError(RuntimeError):
     pass
 
@@ -72,6 +83,10 @@ def lib():
         "k3c_expert_ffn": ([vp, vp, i, C.POINTER(K3ExpertQ), i, i, i, vp, sz, vp], i),
         "k3c_moe_decode_scratch": ([C.POINTER(MoeLayerC), i], sz),
         "k3c_moe_decode": ([vp, vp, i, i, C.POINTER(MoeLayerC), vp, vp, vp, vp, sz, vp], i),
+        "k3c_pool_run_bytes": ([i, i], sz),
+        "k3c_pool_pack_expert": ([vp, C.POINTER(K3ExpertQ), i, i, vp], i),
+        "k3c_moe_decode_tc_scratch": ([C.POINTER(MoePoolLayerC), i], sz),
+        "k3c_moe_decode_tc": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
         "k3_mxfp4_dequant": ([vp, vp, vp, i, i, i], None),
         "k3_matmul_mxfp4": ([vp, vp, vp, vp, i, i, i], None),
         "k3_matmul_q8": ([vp, vp, vp, i, i], None),
@@ -218,6 +233,20 @@ def expert_run_layout(hidden, inter):
     return lay, off
 
 
+def pool_layout(hidden, inter):
+    """Byte offsets of the pool-format run read by the tensor-core path (csrc/moe_tc.cu):
+    GU packed (gate/up rows interleaved per 64), GU scale atoms, D packed, D scale atoms.
+    Returns (dict name -> (offset, nbytes), total bytes)."""
+    H, I = hidden, inter
+    parts = [("gu_p", I * H), ("gu_s", 2 * I * H // 32), ("d_p", H * I // 2),
+             ("d_s", H * I // 32)]
+    off, lay = 0, {}
+    for name, nb in parts:
+        lay[name] = (off, nb)
+        off += nb
+    return lay, off
+
+
 def experts_from_blob(blob, n, hidden, inter, stride=None):
     """K3ExpertQ for n expert runs laid out back to back (every `stride` bytes) in one
     device uint8 tensor."""
@@ -324,4 +353,82 @@ class MoeLayer:
         _check(lib().k3c_moe_decode(_ptr(out), _ptr(x), _dtype_code(x), ntok, C.byref(self.c),
                                     _ptr(idx), _ptr(wt), _ptr(drops), _ptr(self._scratch),
                                     self._scratch.numel(), _stream()), "k3c_moe_decode")
+        return out, idx, wt
+
+
+def pool_run_bytes(hidden, inter):
+    n = lib().k3c_pool_run_bytes(hidden, inter)
+    if n == 0:
+        raise K3CError(f"pool format needs hidden/inter multiples of 128 ({hidden}, {inter})")
+    return n
+
+
+def pool_pack(run, q: K3ExpertQ, hidden, inter):
+    """Pack one expert (reference layout, device addresses) into a pool-format run (a
+    device uint8 tensor view of pool_run_bytes bytes, 256-byte aligned)."""
+    _check(lib().k3c_pool_pack_expert(_ptr(run), C.byref(q), hidden, inter, _stream()),
+           "k3c_pool_pack_expert")
+
+
+class PoolMoeLayer:
+    """A non-latent MoE layer whose experts live in one HBM arena of pool-format runs and
+    run on the tcgen05 block-scaled MMA path (k3c_moe_decode_tc)."""
+
+    def __init__(self, arena, n_runs, run_of, shared_run, router_w, router_bias, hidden, inter,
+                 topk, terms=3, renorm=1, routed_scale=1.0, act=ACT_SWIGLU):
+        import torch
+        self.arena = arena
+        self.run_of = run_of
+        self.router_w = router_w
+        self.router_bias = router_bias
+        self.stride = pool_run_bytes(hidden, inter)
+        self.c = MoePoolLayerC(hidden, inter, run_of.numel(), topk, renorm, act, routed_scale,
+                               router_w.data_ptr(), _dtype_code(router_w),
+                               router_bias.data_ptr() if router_bias is not None else None,
+                               arena.data_ptr(), self.stride, n_runs, run_of.data_ptr(),
+                               shared_run, terms)
+        self._scratch = torch.empty(0, dtype=torch.uint8, device=arena.device)
+
+    @classmethod
+    def pack(cls, experts, shared, router_w, router_bias, hidden, inter, topk, device,
+             expert_map=None, **kw):
+        """experts: list of K3ExpertQ / DeviceExpert (reference layout, distinct runs);
+        expert_map: expert id -> index into `experts` (default identity); shared may be None."""
+        import torch
+        srcs = list(experts) + ([shared] if shared is not None else [])
+        run = pool_run_bytes(hidden, inter)
+        arena = torch.empty(len(srcs) * run, dtype=torch.uint8, device=device)
+        for i, e in enumerate(srcs):
+            q = e.q() if isinstance(e, DeviceExpert) else e
+            pool_pack(arena[i * run:(i + 1) * run], q, hidden, inter)
+        n_exp = len(expert_map) if expert_map is not None else len(experts)
+        m = np.arange(n_exp) if expert_map is None else np.asarray(expert_map)
+        run_of = torch.from_numpy(m.astype(np.int32)).to(device)
+        shared_run = len(experts) if shared is not None else -1
+        return cls(arena, len(srcs), run_of, shared_run, router_w, router_bias, hidden, inter,
+                   topk, **kw)
+
+    def scratch_bytes(self, ntok):
+        return lib().k3c_moe_decode_tc_scratch(C.byref(self.c), ntok)
+
+    def decode(self, x, out=None, idx=None, wt=None, drops=None):
+        import torch
+        if x.dtype == torch.int16:
+            x = x.view(torch.bfloat16)
+        x = x.contiguous()
+        ntok = x.shape[0]
+        need = self.scratch_bytes(ntok)
+        if self._scratch.numel() < need:
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        H, K = self.c.hidden, self.c.topk
+        if out is None:
+            out = torch.empty((ntok, H), dtype=torch.float32, device=x.device)
+        if idx is None:
+            idx = torch.empty((ntok, K), dtype=torch.int32, device=x.device)
+        if wt is None:
+            wt = torch.empty((ntok, K), dtype=torch.float32, device=x.device)
+        _check(lib().k3c_moe_decode_tc(_ptr(out), _ptr(x), _dtype_code(x), ntok,
+                                       C.byref(self.c), _ptr(idx), _ptr(wt), _ptr(drops),
+                                       _ptr(self._scratch), self._scratch.numel(), _stream()),
+               "k3c_moe_decode_tc")
         return out, idx, wt

@@ -222,6 +222,14 @@ __global__ void k_moe_combine(float *__restrict__ out, const float *__restrict__
     }
 }
 
+int launch_moe_combine(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
+                       int ntok, int topk, int hidden, int has_shared, cudaStream_t s) {
+    k_moe_combine<<<dim3((hidden + 255) / 256, ntok), 256, 0, s>>>(out, contrib, wt, dropped, ntok,
+                                                                  topk, hidden, has_shared);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
 template <typename XT>
 __global__ void k_to_f32(float *__restrict__ y, const XT *__restrict__ x, size_t n) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
