@@ -45,51 +45,58 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region (clock and throttle reasons)."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every 5 ms in a
+    background thread while the timed region runs (read-only queries)."""
 
-    def __init__(self, gpu_index):
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
-        self.p = None
+    HW_SLOWDOWN, SW_POWER_CAP, SW_THERMAL, HW_THERMAL, HW_POWER_BRAKE = 0x8, 0x4, 0x20, 0x40, 0x80
+
+    def __init__(self, cuda_index):
+        import threading
+        self.samples, self.reasons, self.max_mhz, self.err = [], 0, None, None
+        self._stop = threading.Event()
         try:
-            self.f = open(self.path, "w")
-            self.p = subprocess.Popen(
-                ["nvidia-smi", "-i", str(gpu_index),
-                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
-                stderr=subprocess.DEVNULL)
-        except Exception:
-            self.p = None
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            p = torch.cuda.get_device_properties(cuda_index)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            get = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._reasons_fn = get
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception as e:  # no NVML: report it rather than inventing clocks
+            self.err = f"nvml unavailable: {e}"
+            self.t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= int(self._reasons_fn(self.h))
+            except Exception as e:
+                self.err = str(e)
+            self._stop.wait(0.005)
 
     def stop(self):
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
-        try:
-            self.p.wait(5)
-        except Exception:
-            self.p.kill()
-        self.f.close()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            v = [c.strip() for c in line.split(",")]
-            if len(v) < 9:
-                continue
-            try:
-                sm.append(float(v[1]))
-                mx.append(float(v[2]))
-            except ValueError:
-                continue
-            for n, a in zip(names, v[5:9]):
-                if a.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.t is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err]}
+        self._stop.set()
+        self.t.join(2)
+        names = {self.HW_SLOWDOWN: "hw_slowdown", self.HW_THERMAL: "hw_thermal_slowdown",
+                 self.SW_THERMAL: "sw_thermal_slowdown", self.SW_POWER_CAP: "sw_power_cap",
+                 self.HW_POWER_BRAKE: "hw_power_brake_slowdown"}
+        reasons = sorted(n for bit, n in names.items() if self.reasons & bit)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": reasons + ["no samples"]}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
 
 
 def dist_setup(args):
@@ -368,8 +375,8 @@ def run_ours(args, ws, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")

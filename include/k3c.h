@@ -123,7 +123,7 @@ int k3c_mxfp4_gemv(float *y, int ldy, const float *x, int ldx, int ntok,
                    int group, k3c_stream_t stream);
 
 /* INT8 per-row trunk projection, pool layout: wq [out][ldw] int8 (ldw >= in, a multiple of
- * 16) and wscale [out] fp32. k3c_q8_pack converts the reference's inline row layout
+ * 32, zero-padded) and wscale [out] fp32. k3c_q8_pack converts the reference's inline row layout
  * ([f32 scale][int8*in], stride 4+in, include/k3/k3.h:265-303), already on the device,
  * into that layout. k3c_q8_gemv: y[t*ldy + o] = wscale[o] * sum_i wq[o][i] * x[t][i], x of
  * type x_dtype (K3C_F32 or K3C_BF16) with row stride ldx elements. */

@@ -152,7 +152,7 @@ def mxfp4_gemv(x, packed, scales, group=32):
 def q8_pack(rows_u8, in_, out):
     """Reference row layout ([f32 scale][int8*in] per row, on the device) -> pool layout."""
     import torch
-    ldw = (in_ + 15) // 16 * 16
+    ldw = (in_ + 31) // 32 * 32
     wq = torch.empty((out, ldw), dtype=torch.int8, device=rows_u8.device)
     ws = torch.empty(out, dtype=torch.float32, device=rows_u8.device)
     _check(lib().k3c_q8_pack(_ptr(wq), _ptr(ws), ldw, _ptr(rows_u8), in_, out, _stream()),

@@ -137,7 +137,7 @@ void k3_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
 void k3_matmul_q8(float *y, const float *x, const void *W, int in, int out) {
     const char *what = "k3_matmul_q8";
     if (in <= 0 || out <= 0) return;
-    const int ldw = (int)align_up((size_t)in, 16);
+    const int ldw = (int)align_up((size_t)in, 32);
     const size_t nb_r = (size_t)out * (4 + (size_t)in), nb_x = (size_t)in * sizeof(float);
     const size_t nb_q = (size_t)out * ldw, nb_sc = (size_t)out * sizeof(float);
     const size_t nb_y = (size_t)out * sizeof(float);

@@ -141,10 +141,11 @@ __device__ __forceinline__ void quantize_block(float a, QF qdst, SF sfdst) {
     }
 }
 
-// x [ntok][H] -> x_q [J][32][H] E4M3 and x_sf [J][H/128] atoms (rows = tokens, < 32).
+// x [ntok][H] -> x_q [J*NT][H] E4M3, row j*NT + t holding term j of token t, and the scale
+// atoms x_sf [H/128][512] over those rows (J*NT <= 96 rows: one atom row).
 template <int J, typename XT>
 __global__ void __launch_bounds__(256) k_quant_x(uint8_t *__restrict__ xq, uint8_t *__restrict__ xsf,
-                                                 const XT *__restrict__ x, int ntok, int H) {
+                                                 const XT *__restrict__ x, int ntok, int H, int NT) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int blk = blockIdx.x * 8 + warp;  // 32-element block index
     const int t = blockIdx.y;
@@ -153,11 +154,10 @@ __global__ void __launch_bounds__(256) k_quant_x(uint8_t *__restrict__ xq, uint8
     float a;
     if constexpr (sizeof(XT) == 2) a = bf16_bits_to_f32(x[(size_t)t * H + k]);
     else a = x[(size_t)t * H + k];
-    const int KT = H / 128;
     quantize_block<J>(
-        a, [&](int j, uint32_t q) { xq[((size_t)j * 32 + t) * H + k] = (uint8_t)q; },
+        a, [&](int j, uint32_t q) { xq[((size_t)j * NT + t) * H + k] = (uint8_t)q; },
         [&](int j, uint32_t sf) {
-            xsf[((size_t)j * KT + blk / 4) * 512 + atom_byte(t, blk % 4)] = (uint8_t)sf;
+            xsf[(size_t)(blk / 4) * 512 + atom_byte(j * NT + t, blk % 4)] = (uint8_t)sf;
         });
 }
 
@@ -223,17 +223,39 @@ __global__ void __launch_bounds__(1024) k_moe_plan_tc(int *__restrict__ n_slots,
     }
 }
 
-// ------------------------------------------------------------------ tcgen05 mainloop
-constexpr int TC_NT = 32;           // N tile: tokens (GU) or pairs of a slot (D)
+// ------------------------------------------------------------------ persistent tcgen05 kernel
+// Persistent CTAs (two per SM) loop over work items (slot, row tile). Six warps:
+//   warp 0      TMA producer: one thread streams A (weights), B (the activation terms) and
+//               their scale atoms through a STAGES-deep ring, continuously across items;
+//   warp 1      MMA issuer: one thread copies the two scale atoms of a K tile into TMEM and
+//               issues one tcgen05 MMA per 32-element K block into one of two accumulators;
+//   warps 2-5   epilogue: wait for an accumulator, read it with tcgen05.ld (warp w owns TMEM
+//               lanes 32*(w%4)..+31), hand it back, then run the item's epilogue while the
+//               MMA warp fills the other accumulator.
+// The J activation terms of each token are stacked as J*NT rows of the B operand (row
+// j*NT + t = term j of token t), each row with its own block scales, so one MMA with
+// N = J*NT covers all terms and the epilogue adds the J partial columns of a token.
+// GU items: 64 gate + 64 up rows for output columns [64*rt, 64*rt+64); the epilogue applies
+// the activation and requantises it into the D stage's operand. D items: 128 down rows x
+// the slot's pairs; the epilogue writes each pair's unweighted expert output to contrib.
 constexpr int TC_A_BYTES = 128 * 128;   // shared-memory footprint of a padded E2M1 tile
 constexpr int TC_A_TX = 128 * 128 / 2;  // its TMA transaction bytes: 4 bits per element
-constexpr int TC_B_BYTES = TC_NT * 128;
-constexpr uint32_t TC_TMEM_COLS = 64;
+constexpr int TC_THREADS = 192;
 
-template <int J, int STAGES>
-struct TcSmem {
-    static constexpr int STAGE = TC_A_BYTES + J * TC_B_BYTES + 512 + J * 512;
-    static constexpr int BYTES = STAGES * STAGE + 1024 /* align */ + 256 /* barriers */;
+__host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
+    return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
+}
+
+template <int J, int NT, int STAGES>
+struct TcCfg {
+    static constexpr int NCOL = J * NT;                   // MMA N
+    static constexpr int B_BYTES = NCOL * 128;
+    static constexpr int STAGE = TC_A_BYTES + B_BYTES + 1024;   // + SFA and SFB atoms
+    static constexpr int TILE = 128 * (NT + 1) * 4;       // epilogue staging [128][NT+1] fp32
+    static constexpr int BYTES = STAGES * STAGE + TILE + 256 + 1024;
+    static constexpr uint32_t SF_COL = 2 * NCOL;          // after the two accumulators
+    static constexpr uint32_t TMEM_COLS = pow2_cols(2 * NCOL + 16);
+    static constexpr uint32_t TX = TC_A_TX + B_BYTES + 1024;
 };
 
 struct TcArgs {
@@ -242,99 +264,14 @@ struct TcArgs {
     const int *pair_tok, *pair_k;
     const uint8_t *arena;
     size_t run_stride;
-    const uint8_t *b_sf;     // GU activation scale atoms [J][H/128][512] (tokens = atom rows 0..31)
-    uint8_t *act_q;          // GU output: [J][S*32][I], slot s owns rows 32s..32s+31
-    uint8_t *act_sf;         // GU output atoms [J][S][I/128][512], one atom per slot (rows 0..31)
-    int act_slots;           // S
+    const uint8_t *x_sf;     // GU B scale atoms [H/128][512] (row j*NT + t)
+    uint8_t *act_q;          // GU output / D operand: [S][J*NT][I]
+    uint8_t *act_sf;         // [S][I/128][512], row j*NT + pair
     float *contrib;          // D output [T][topk+1][H]
     int kstride;             // topk + 1
     int H, I, act;
     int *err;
 };
-
-// Stage layout inside one pipeline stage: A | B[J] | SFA | SFB[J].
-template <int J>
-struct StagePtr {
-    uint8_t *a, *b[J], *sfa, *sfb[J];
-    __device__ StagePtr(uint8_t *base) {
-        a = base;
-#pragma unroll
-        for (int j = 0; j < J; j++) b[j] = base + TC_A_BYTES + j * TC_B_BYTES;
-        sfa = base + TC_A_BYTES + J * TC_B_BYTES;
-#pragma unroll
-        for (int j = 0; j < J; j++) sfb[j] = sfa + 512 + j * 512;
-    }
-};
-
-// Runs the K loop for one M=128 x N=32 tile: warp 0 lane 0 produces (TMA), warp 1 lane 0
-// issues tcgen05 copies and MMAs; returns with the accumulator in TMEM columns [0,32) and
-// the accum barrier armed. kt_count: K tiles of 128. a_* select the weight tile, b_row the
-// activation rows (whose scales sit in rows 0..31 of their atoms).
-// Alignment self-checks: a violated precondition records an error code in *err and the
-// loop stops issuing, instead of handing the hardware a misaligned address.
-__device__ __forceinline__ bool tc_check(bool ok, int *err, int code) {
-    if (!ok && err) atomicExch(err, code);
-    return ok;
-}
-
-template <int J, int STAGES>
-__device__ __forceinline__ void tc_mainloop(uint8_t *smem, uint64_t *full, uint64_t *empty,
-                                            uint64_t *accum, uint32_t tmem, const CUtensorMap *tmA,
-                                            const CUtensorMap *tmB, const uint8_t *sfa_base,
-                                            const uint8_t *sfb_base, size_t sfb_term_stride,
-                                            int a_row, int a_run, int b_row, int kt_count, int *err) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int STAGE = TcSmem<J, STAGES>::STAGE;
-    if (warp == 0 && lane == 0) {
-        if (!tc_check(((uintptr_t)sfa_base & 15) == 0 && ((uintptr_t)sfb_base & 15) == 0 &&
-                          (sfb_term_stride & 15) == 0 && (tc::smem_u32(smem) & 1023) == 0,
-                      err, 10))
-            return;
-        tc::prefetch_tmap(tmA);
-        tc::prefetch_tmap(tmB);
-        for (int kt = 0; kt < kt_count; kt++) {
-            const int st = kt % STAGES;
-            const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-            if (kt >= STAGES && !tc::mbar_wait(&empty[st], ph ^ 1u, err, 1)) return;
-            StagePtr<J> sp(smem + st * STAGE);
-            tc::mbar_expect_tx(&full[st], TC_A_TX + 512 + J * (TC_B_BYTES + 512));
-            tc::tma_load_3d(sp.a, tmA, &full[st], kt * 128, a_row, a_run);
-            tc::bulk_load(sp.sfa, sfa_base + (size_t)kt * 512, 512, &full[st]);
-#pragma unroll
-            for (int j = 0; j < J; j++) {
-                tc::tma_load_3d(sp.b[j], tmB, &full[st], kt * 128, b_row, j);
-                tc::bulk_load(sp.sfb[j], sfb_base + j * sfb_term_stride + (size_t)kt * 512, 512, &full[st]);
-            }
-        }
-    } else if (warp == 1 && lane == 0) {
-        for (int kt = 0; kt < kt_count; kt++) {
-            const int st = kt % STAGES;
-            const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-            if (!tc::mbar_wait(&full[st], ph, err, 2)) return;
-            tc::tc_fence_after();
-            StagePtr<J> sp(smem + st * STAGE);
-            const uint32_t sf_col = 32u + 16u * (uint32_t)(kt & 1);  // double-buffered
-            tc::tc_cp_sf(tmem + sf_col, tc::desc_sf_atom(tc::smem_u32(sp.sfa)));
-#pragma unroll
-            for (int j = 0; j < J; j++)
-                tc::tc_cp_sf(tmem + sf_col + 4 + 4 * j, tc::desc_sf_atom(tc::smem_u32(sp.sfb[j])));
-#pragma unroll
-            for (int kb = 0; kb < 4; kb++) {
-                const uint64_t da = tc::desc_kmajor_sw128(tc::smem_u32(sp.a) + 32 * kb);
-#pragma unroll
-                for (int j = 0; j < J; j++) {
-                    const uint64_t db = tc::desc_kmajor_sw128(tc::smem_u32(sp.b[j]) + 32 * kb);
-                    const uint32_t id = tc::idesc_mxf8f6f4(tc::FMT_E2M1, tc::FMT_E4M3, TC_NT, kb, kb);
-                    const uint32_t sfa = (tmem + sf_col) | ((uint32_t)kb << 30);
-                    const uint32_t sfb = (tmem + sf_col + 4 + 4 * j) | ((uint32_t)kb << 30);
-                    tc::tc_mma_mx(tmem, da, db, id, sfa, sfb, (kt | kb | j) != 0);
-                }
-            }
-            tc::tc_commit(&empty[st]);
-        }
-        tc::tc_commit(accum);
-    }
-}
 
 __device__ __forceinline__ float sigmoid_f(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))); }
 __device__ __forceinline__ float act_apply(float g, float u, int act) {
@@ -345,127 +282,205 @@ __device__ __forceinline__ float act_apply(float g, float u, int act) {
     return __fmul_rn(__fmul_rn(g, sigmoid_f(g)), u);
 }
 
-// Shared prologue: barriers + TMEM; returns the TMEM base.
-template <int STAGES>
-__device__ __forceinline__ uint32_t tc_setup(uint64_t *bars, uint32_t *tmem_slot) {
-    const int warp = threadIdx.x >> 5;
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void tma_load_3d_hint(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
+                                                 int c0, int c1, int c2, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(tc::smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+        "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t *v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+          "=r"(v[14]), "=r"(v[15])
+        : "r"(addr));
+}
+
+__device__ __forceinline__ bool tc_check(bool ok, int *err, int code) {
+    if (!ok && err) atomicExch(err, code);
+    return ok;
+}
+
+template <int J, int NT, int STAGES, bool GU>
+__global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ CUtensorMap tmW,
+                                                      const __grid_constant__ CUtensorMap tmB,
+                                                      TcArgs p) {
+    using Cfg = TcCfg<J, NT, STAGES>;
+    constexpr int NCOL = Cfg::NCOL;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float *tile = reinterpret_cast<float *>(smem + STAGES * Cfg::STAGE);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::STAGE + Cfg::TILE);
+    uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2 * STAGES + 1; i++) tc::mbar_init(&bars[i], 1);
+        for (int i = 0; i < 2 * STAGES; i++) tc::mbar_init(&bars[i], 1);
+        tc::mbar_init(&tfull[0], 1);
+        tc::mbar_init(&tfull[1], 1);
+        tc::mbar_init(&tempty[0], 4);
+        tc::mbar_init(&tempty[1], 4);
         tc::fence_mbar_init();
     }
-    if (warp == 1) tc::tmem_alloc(tmem_slot, TC_TMEM_COLS);
+    if (warp == 1) tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
-    return *tmem_slot;
-}
+    const uint32_t tmem = *tmem_slot;
 
-template <int STAGES>
-__device__ __forceinline__ void tc_teardown(uint32_t tmem) {
-    tc::tc_fence_before();
-    __syncthreads();
-    if ((threadIdx.x >> 5) == 1) tc::tmem_dealloc(tmem, TC_TMEM_COLS);
-}
-
-// GU stage: grid (2I/128, max_slots), 128 threads. Tile rows: 64 gate + 64 up rows of output
-// columns [64*bx, 64*bx+64); N = 32 token columns (all tokens; the slot's pairs pick theirs).
-template <int J, int STAGES>
-__global__ void __launch_bounds__(128) k_tc_gateup(const __grid_constant__ CUtensorMap tmW,
-                                                   const __grid_constant__ CUtensorMap tmX, TcArgs p) {
-    const int s = blockIdx.y;
-    if (s >= *p.n_slots) return;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    constexpr int STAGE = TcSmem<J, STAGES>::STAGE;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE);
-    uint64_t *full = bars, *empty = bars + STAGES, *accum = bars + 2 * STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
-    const uint32_t tmem = tc_setup<STAGES>(bars, tmem_slot);
-
-    const SlotTc sl = p.slots[s];
-    const int rt = blockIdx.x, KT = p.H / 128;
+    const int n_slots = *p.n_slots;
+    const int RT = GU ? (2 * p.I) / 128 : p.H / 128;   // row tiles per slot
+    const int KT = GU ? p.H / 128 : p.I / 128;         // K tiles per item
+    const int n_items = n_slots * RT;
     const PoolGeom g = pool_geom(p.H, p.I);
-    const uint8_t *run = p.arena + (size_t)sl.run * p.run_stride;
-    tc_mainloop<J, STAGES>(smem, full, empty, accum, tmem, &tmW, &tmX,
-                           run + g.gu_s + (size_t)rt * KT * 512, p.b_sf, (size_t)KT * 512,
-                           rt * 128, sl.run, 0, KT, p.err);
-    __syncwarp();
-    const bool ok = tc::mbar_wait(accum, 0, p.err, 3);
-    tc::tc_fence_after();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *tile = reinterpret_cast<float *>(smem);  // [128][33], reuses stage 0
-    if (ok) {
-        uint32_t v[32];
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16), v);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; c++) tile[(32 * warp + lane) * 33 + c] = __uint_as_float(v[c]);
-    }
-    __syncthreads();
-    if (ok && warp < 2) {
-        const int r = 32 * warp + lane;               // gate row within the tile
-        const int col = 64 * rt + r;                  // output column in [0, I)
-        const int KTd = p.I / 128;
-        for (int pl = 0; pl < sl.ntok; pl++) {
-            const int prow = s * 32 + pl;
-            const int tok = p.pair_tok[prow];
-            const float a = act_apply(tile[r * 33 + tok], tile[(r + 64) * 33 + tok], p.act);
-            quantize_block<J>(
-                a,
-                [&](int j, uint32_t q) {
-                    p.act_q[((size_t)j * p.act_slots * 32 + prow) * p.I + col] = (uint8_t)q;
-                },
-                [&](int j, uint32_t sf) {
-                    const size_t atom = ((size_t)j * p.act_slots + s) * KTd + col / 128;
-                    p.act_sf[atom * 512 + atom_byte(pl, (col % 128) / 32)] = (uint8_t)sf;
-                });
+    const size_t sf_off = GU ? g.gu_s : g.d_s;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ producer
+        bool ok = tc_check((tc::smem_u32(smem) & 1023) == 0, p.err, 10);
+        tc::prefetch_tmap(&tmW);
+        tc::prefetch_tmap(&tmB);
+        const uint64_t pol = l2_evict_first_policy();
+        uint32_t kiter = 0;
+        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+            const int s = it / RT, rt = it % RT;
+            const SlotTc sl = p.slots[s];
+            const uint8_t *sfa = p.arena + (size_t)sl.run * p.run_stride + sf_off + (size_t)rt * KT * 512;
+            const uint8_t *sfb = GU ? p.x_sf : p.act_sf + (size_t)s * KT * 512;
+            const int b_row = GU ? 0 : NCOL * s;
+            for (int kt = 0; kt < KT; kt++, kiter++) {
+                const int st = kiter % STAGES;
+                const uint32_t ph = (kiter / STAGES) & 1u;
+                if (kiter >= STAGES && !tc::mbar_wait(&empty[st], ph ^ 1u, p.err, 1)) { ok = false; break; }
+                uint8_t *sa = smem + st * Cfg::STAGE;
+                uint8_t *sb = sa + TC_A_BYTES;
+                uint8_t *ssf = sb + Cfg::B_BYTES;
+                tc::mbar_expect_tx(&full[st], Cfg::TX);
+                tma_load_3d_hint(sa, &tmW, &full[st], kt * 128, rt * 128, sl.run, pol);
+                tc::tma_load_3d(sb, &tmB, &full[st], kt * 128, b_row, 0);
+                tc::bulk_load(ssf, sfa + (size_t)kt * 512, 512, &full[st]);
+                tc::bulk_load(ssf + 512, sfb + (size_t)kt * 512, 512, &full[st]);
+            }
         }
-    }
-    tc_teardown<STAGES>(tmem);
-}
-
-// D stage: grid (H/128, max_slots). A = down rows [128*bx, +128), B = the slot's 32 pair rows
-// of act_q. Epilogue writes the unweighted expert output for each pair to contrib.
-template <int J, int STAGES>
-__global__ void __launch_bounds__(128) k_tc_down(const __grid_constant__ CUtensorMap tmW,
-                                                 const __grid_constant__ CUtensorMap tmA, TcArgs p) {
-    const int s = blockIdx.y;
-    if (s >= *p.n_slots) return;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    constexpr int STAGE = TcSmem<J, STAGES>::STAGE;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE);
-    uint64_t *full = bars, *empty = bars + STAGES, *accum = bars + 2 * STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
-    const uint32_t tmem = tc_setup<STAGES>(bars, tmem_slot);
-
-    const SlotTc sl = p.slots[s];
-    const int rt = blockIdx.x, KT = p.I / 128;
-    const PoolGeom g = pool_geom(p.H, p.I);
-    const uint8_t *run = p.arena + (size_t)sl.run * p.run_stride;
-    const uint8_t *sfb = p.act_sf + (size_t)s * KT * 512;
-    tc_mainloop<J, STAGES>(smem, full, empty, accum, tmem, &tmW, &tmA,
-                           run + g.d_s + (size_t)rt * KT * 512, sfb, (size_t)p.act_slots * KT * 512,
-                           rt * 128, sl.run, s * 32, KT, p.err);
-    __syncwarp();
-    const bool ok = tc::mbar_wait(accum, 0, p.err, 3);
-    tc::tc_fence_after();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (ok) {
-        uint32_t v[32];
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16), v);
-        tc::tmem_ld_wait();
-        const int h = 128 * rt + 32 * warp + lane;
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------ MMA issuer
+        uint32_t kiter = 0, li = 0;
+        bool ok = true;
+        const uint32_t idesc0 = tc::idesc_mxf8f6f4(tc::FMT_E2M1, tc::FMT_E4M3, NCOL, 0, 0);
+        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, li++) {
+            const uint32_t a = li & 1u, use = li >> 1;
+            if (use >= 1 && !tc::mbar_wait(&tempty[a], (use - 1) & 1u, p.err, 4)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint32_t d = tmem + a * NCOL;
+            for (int kt = 0; kt < KT; kt++, kiter++) {
+                const int st = kiter % STAGES;
+                const uint32_t ph = (kiter / STAGES) & 1u;
+                if (!tc::mbar_wait(&full[st], ph, p.err, 2)) { ok = false; break; }
+                tc::tc_fence_after();
+                uint8_t *sa = smem + st * Cfg::STAGE;
+                uint8_t *sb = sa + TC_A_BYTES;
+                uint8_t *ssf = sb + Cfg::B_BYTES;
+                const uint32_t sfc = tmem + Cfg::SF_COL + 8u * (kiter & 1u);
+                tc::tc_cp_sf(sfc, tc::desc_sf_atom(tc::smem_u32(ssf)));
+                tc::tc_cp_sf(sfc + 4, tc::desc_sf_atom(tc::smem_u32(ssf + 512)));
 #pragma unroll
-        for (int pl = 0; pl < 32; pl++) {
-            if (pl < sl.ntok) {
-                const int prow = s * 32 + pl;
-                p.contrib[((size_t)p.pair_tok[prow] * p.kstride + p.pair_k[prow]) * p.H + h] =
-                    __uint_as_float(v[pl]);
+                for (int kb = 0; kb < 4; kb++) {
+                    const uint64_t da = tc::desc_kmajor_sw128(tc::smem_u32(sa) + 32 * kb);
+                    const uint64_t db = tc::desc_kmajor_sw128(tc::smem_u32(sb) + 32 * kb);
+                    const uint32_t id = idesc0 | ((uint32_t)kb << 4) | ((uint32_t)kb << 29);
+                    tc::tc_mma_mx(d, da, db, id, sfc | ((uint32_t)kb << 30), (sfc + 4) | ((uint32_t)kb << 30),
+                                  (kt | kb) != 0);
+                }
+                tc::tc_commit(&empty[st]);
+            }
+            if (ok) tc::tc_commit(&tfull[a]);
+        }
+    } else if (warp >= 2) {
+        // ------------------------------------------------------------ epilogue
+        // Every epilogue warp runs every item and every named barrier even after a failed
+        // wait (it then skips the TMEM read and the work), so the barriers cannot strand a
+        // warp; once an error is recorded the remaining waits return at once.
+        const int q = warp & 3;                 // TMEM lane quadrant
+        const int row = 32 * q + lane;          // row within the 128-row tile
+        uint32_t li = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, li++) {
+            const int s = it / RT, rt = it % RT;
+            const uint32_t a = li & 1u;
+            const bool ok = *(volatile int *)p.err == 0 && tc::mbar_wait(&tfull[a], (li >> 1) & 1u, p.err, 3);
+            float val[NT];
+            if (ok) {
+                tc::tc_fence_after();
+                uint32_t v[NCOL];
+#pragma unroll
+                for (int c = 0; c < NCOL; c += 16)
+                    tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + a * NCOL + c, v + c);
+                tc::tmem_ld_wait();
+                tc::tc_fence_before();
+                if (lane == 0) tc::mbar_arrive(&tempty[a]);
+#pragma unroll
+                for (int c = 0; c < NT; c++) {
+                    float acc = __uint_as_float(v[c]);
+#pragma unroll
+                    for (int j = 1; j < J; j++) acc += __uint_as_float(v[j * NT + c]);
+                    val[c] = acc;
+                }
+            }
+            const SlotTc sl = p.slots[s];
+            if constexpr (GU) {
+                if (ok) {
+#pragma unroll
+                    for (int c = 0; c < NT; c++) tile[row * (NT + 1) + c] = val[c];
+                }
+                named_bar_sync(1, 128);
+                if (ok && q < 2) {               // gate rows 0..63 (warps 4 and 5)
+                    const int col = 64 * rt + row;   // output column in [0, I)
+                    const int KTd = p.I / 128;
+                    for (int pl = 0; pl < sl.ntok; pl++) {
+                        const int tok = p.pair_tok[s * 32 + pl];
+                        const float av = act_apply(tile[row * (NT + 1) + tok], tile[(row + 64) * (NT + 1) + tok], p.act);
+                        quantize_block<J>(
+                            av,
+                            [&](int j, uint32_t qv) {
+                                p.act_q[((size_t)s * NCOL + j * NT + pl) * p.I + col] = (uint8_t)qv;
+                            },
+                            [&](int j, uint32_t sf) {
+                                p.act_sf[((size_t)s * KTd + col / 128) * 512 + atom_byte(j * NT + pl, (col % 128) / 32)] =
+                                    (uint8_t)sf;
+                            });
+                    }
+                }
+                named_bar_sync(1, 128);          // the tile is reused by the next item
+            } else if (ok) {
+                const int h = 128 * rt + row;
+#pragma unroll
+                for (int pl = 0; pl < NT; pl++) {
+                    if (pl < sl.ntok) {
+                        const int prow = s * 32 + pl;
+                        p.contrib[((size_t)p.pair_tok[prow] * p.kstride + p.pair_k[prow]) * p.H + h] = val[pl];
+                    }
+                }
             }
         }
     }
-    tc_teardown<STAGES>(tmem);
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tc::tmem_dealloc(tmem, Cfg::TMEM_COLS);
 }
 
 // ------------------------------------------------------------------ host side
@@ -499,6 +514,17 @@ static int make_map3(CUtensorMap *m, CUtensorMapDataType dt, const void *base, u
     return K3C_OK;
 }
 
+static int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
 struct TcBufs {
     int *n_slots;
     SlotTc *slots;
@@ -526,9 +552,9 @@ static bool carve_tc(Carve &cv, TcBufs &b, const k3c_moe_pool_layer *L, int ntok
     b.wt = cv.take<float>(P);
     b.contrib = cv.take<float>((size_t)ntok * (L->topk + 1) * H);
     b.xq = cv.take<uint8_t>((size_t)J * 32 * H, 1024);
-    b.xsf = cv.take<uint8_t>((size_t)J * (H / 128) * 512, 1024);
-    b.actq = cv.take<uint8_t>((size_t)J * b.max_slots * 32 * I, 1024);
-    b.actsf = cv.take<uint8_t>((size_t)J * b.max_slots * (I / 128) * 512, 1024);
+    b.xsf = cv.take<uint8_t>((size_t)(H / 128) * 512, 1024);
+    b.actq = cv.take<uint8_t>((size_t)b.max_slots * J * 32 * I, 1024);
+    b.actsf = cv.take<uint8_t>((size_t)b.max_slots * (I / 128) * 512, 1024);
     return b.n_slots && b.err && b.slots && b.pair_tok && b.pair_k && b.dropped && b.scores &&
            b.idx && b.wt && b.contrib && b.xq && b.xsf && b.actq && b.actsf;
 }
@@ -542,8 +568,10 @@ size_t moe_decode_tc_scratch(const k3c_moe_pool_layer *L, int ntok) {
     return cv.used + 1024;
 }
 
-template <int J, int STAGES>
-static int launch_tc_stages(const TcBufs &b, const k3c_moe_pool_layer *L, int ntok, cudaStream_t s) {
+template <int J, int NT, int STAGES>
+static int launch_tc_stages(const TcBufs &b, const k3c_moe_pool_layer *L, cudaStream_t s) {
+    using Cfg = TcCfg<J, NT, STAGES>;
+    static_assert(2 * Cfg::BYTES <= 228 * 1024, "two CTAs per SM");
     const int H = L->hidden, I = L->inter;
     const PoolGeom g = pool_geom(H, I);
     CUtensorMap tmGU, tmD, tmX, tmAct;
@@ -551,9 +579,10 @@ static int launch_tc_stages(const TcBufs &b, const k3c_moe_pool_layer *L, int nt
                       H / 2, L->run_stride, 128, 128));
     K3C_TRY(make_map3(&tmD, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->arena + g.d_p, I, H, L->n_runs, I / 2,
                       L->run_stride, 128, 128));
-    K3C_TRY(make_map3(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.xq, H, 32, J, H, (uint64_t)32 * H, 128, 32));
-    K3C_TRY(make_map3(&tmAct, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.actq, I, (uint64_t)b.max_slots * 32, J, I,
-                      (uint64_t)b.max_slots * 32 * I, 128, 32));
+    constexpr int NCOL = Cfg::NCOL;
+    K3C_TRY(make_map3(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.xq, H, NCOL, 1, H, (uint64_t)NCOL * H, 128, NCOL));
+    K3C_TRY(make_map3(&tmAct, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.actq, I, (uint64_t)b.max_slots * NCOL, 1, I,
+                      (uint64_t)b.max_slots * NCOL * I, 128, NCOL));
     TcArgs a;
     a.n_slots = b.n_slots;
     a.slots = b.slots;
@@ -561,25 +590,42 @@ static int launch_tc_stages(const TcBufs &b, const k3c_moe_pool_layer *L, int nt
     a.pair_k = b.pair_k;
     a.arena = L->arena;
     a.run_stride = L->run_stride;
-    a.b_sf = b.xsf;
+    a.x_sf = b.xsf;
     a.act_q = b.actq;
     a.act_sf = b.actsf;
-    a.act_slots = b.max_slots;
     a.contrib = b.contrib;
     a.kstride = L->topk + 1;
     a.H = H;
     a.I = I;
     a.act = L->act;
     a.err = b.err;
-    const int smem = TcSmem<J, STAGES>::BYTES;
-    K3C_TRY_CUDA(cudaFuncSetAttribute(k_tc_gateup<J, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    K3C_TRY_CUDA(cudaFuncSetAttribute(k_tc_down<J, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    auto kgu = k_tc_moe<J, NT, STAGES, true>;
+    auto kd = k_tc_moe<J, NT, STAGES, false>;
+    K3C_TRY_CUDA(cudaFuncSetAttribute(kgu, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
+    K3C_TRY_CUDA(cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
+    // all of the unified L1/shared storage as shared memory, so two CTAs fit per SM
+    K3C_TRY_CUDA(cudaFuncSetAttribute(kgu, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    K3C_TRY_CUDA(cudaFuncSetAttribute(kd, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    // CTAs per SM from the shared-memory budget (228 KB per SM, 1 KB reserved per CTA); the
+    // CTAs are independent, so a CTA that does not fit simply starts when another ends.
+    const int per_sm = (228 * 1024) / (Cfg::BYTES + 1024) >= 2 ? 2 : 1;
+    const int grid = sm_count() * per_sm;
     stage_begin(STAGE_EXPERTS, s);
-    k_tc_gateup<J, STAGES><<<dim3(2 * I / 128, b.max_slots), 128, smem, s>>>(tmGU, tmX, a);
+    kgu<<<grid, TC_THREADS, Cfg::BYTES, s>>>(tmGU, tmX, a);
     K3C_CHECK_LAUNCH();
-    k_tc_down<J, STAGES><<<dim3(H / 128, b.max_slots), 128, smem, s>>>(tmD, tmAct, a);
+    kd<<<grid, TC_THREADS, Cfg::BYTES, s>>>(tmD, tmAct, a);
     K3C_CHECK_LAUNCH();
     stage_end(STAGE_EXPERTS, s);
+    return K3C_OK;
+}
+
+template <int J>
+static int launch_quant_x(const TcBufs &b, const void *x, int x_dtype, int ntok, int H, int NT, cudaStream_t s) {
+    dim3 gq(H / 256 + (H % 256 ? 1 : 0), ntok);
+    if (x_dtype == K3C_BF16) k_quant_x<J, uint16_t><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const uint16_t *)x, ntok, H, NT);
+    else if (x_dtype == K3C_F32) k_quant_x<J, float><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const float *)x, ntok, H, NT);
+    else return set_error(K3C_EINVAL, "moe_decode_tc: x_dtype=%d", x_dtype);
+    K3C_CHECK_LAUNCH();
     return K3C_OK;
 }
 
@@ -615,25 +661,20 @@ int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const
     k_moe_plan_tc<<<1, 1024, psmem, s>>>(b.n_slots, b.slots, b.pair_tok, b.pair_k, b.dropped, idx, ntok,
                                          L->topk, L->run_of, L->n_experts, L->n_runs, L->shared_run, drops);
     K3C_CHECK_LAUNCH();
-    dim3 gq(H / 256 + (H % 256 ? 1 : 0), ntok);
+    const bool n16 = ntok <= 16;
+    const int NT = n16 ? 16 : 32;
     switch (L->terms) {
     case 1:
-        if (x_dtype == K3C_BF16) k_quant_x<1, uint16_t><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const uint16_t *)x, ntok, H);
-        else k_quant_x<1, float><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const float *)x, ntok, H);
-        K3C_CHECK_LAUNCH();
-        K3C_TRY((launch_tc_stages<1, 4>(b, L, ntok, s)));
+        K3C_TRY(launch_quant_x<1>(b, x, x_dtype, ntok, H, NT, s));
+        K3C_TRY(n16 ? (launch_tc_stages<1, 16, 5>(b, L, s)) : (launch_tc_stages<1, 32, 4>(b, L, s)));
         break;
     case 2:
-        if (x_dtype == K3C_BF16) k_quant_x<2, uint16_t><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const uint16_t *)x, ntok, H);
-        else k_quant_x<2, float><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const float *)x, ntok, H);
-        K3C_CHECK_LAUNCH();
-        K3C_TRY((launch_tc_stages<2, 4>(b, L, ntok, s)));
+        K3C_TRY(launch_quant_x<2>(b, x, x_dtype, ntok, H, NT, s));
+        K3C_TRY(n16 ? (launch_tc_stages<2, 16, 4>(b, L, s)) : (launch_tc_stages<2, 32, 3>(b, L, s)));
         break;
     default:
-        if (x_dtype == K3C_BF16) k_quant_x<3, uint16_t><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const uint16_t *)x, ntok, H);
-        else k_quant_x<3, float><<<gq, 256, 0, s>>>(b.xq, b.xsf, (const float *)x, ntok, H);
-        K3C_CHECK_LAUNCH();
-        K3C_TRY((launch_tc_stages<3, 3>(b, L, ntok, s)));
+        K3C_TRY(launch_quant_x<3>(b, x, x_dtype, ntok, H, NT, s));
+        K3C_TRY(n16 ? (launch_tc_stages<3, 16, 4>(b, L, s)) : (launch_tc_stages<3, 32, 3>(b, L, s)));
         break;
     }
     K3C_TRY(launch_moe_combine(out, b.contrib, wt, b.dropped, ntok, L->topk, H, L->shared_run >= 0 ? 1 : 0, s));

@@ -46,50 +46,79 @@ __device__ __forceinline__ float xload<uint16_t>(const uint16_t *x, size_t i) {
     return bf16_bits_to_f32(x[i]);
 }
 
-// One warp per output row, TCH tokens per pass with x staged in shared memory as fp32.
+// Block = 4 warps = 32 output rows; lane l of every warp owns row 32*bx + l, warp w owns the
+// K-quarter [w*KQ, (w+1)*KQ). Each warp stages its own activations for 16 tokens in chunks
+// of 256 K (fp32, exact widening) so every activation is one shared-memory broadcast feeding
+// 32 FMAs (one per row); a lane streams its row 32 int8 weights (two full 16-byte vectors of
+// one 32-byte sector) per step. The four quarter sums are added in a fixed order.
 template <typename XT>
-__global__ void __launch_bounds__(256) k_q8_gemv(float *__restrict__ y, int ldy,
+__global__ void __launch_bounds__(128, 3) k_q8_gemv(float *__restrict__ y, int ldy,
                                                  const XT *__restrict__ x, int ldx, int ntok,
                                                  const int8_t *__restrict__ wq,
                                                  const float *__restrict__ wscale, int ldw,
                                                  int in, int out) {
-    extern __shared__ float xs[];  // [4][ldw]
-    constexpr int TCH = 4;
+    constexpr int TCH = 16, KC = 256;
+    extern __shared__ __align__(16) float q8_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int o = blockIdx.x * 8 + warp;
+    float *xs = q8_smem + (size_t)warp * TCH * KC;    // this warp's [16][256] chunk
+    float *red = q8_smem + (size_t)4 * TCH * KC;       // [4][32][16] quarter sums
+    const int row = blockIdx.x * 32 + lane;
+    const int rowc = row < out ? row : out - 1;
+    const int8_t *wrow = wq + (size_t)rowc * ldw;
+    const int kq = ((ldw / 32 + 3) / 4) * 32;          // K-quarter, a multiple of 32
+    const int kbeg = warp * kq, kend = min(ldw, kbeg + kq);
     for (int t0 = 0; t0 < ntok; t0 += TCH) {
         const int nt = ntok - t0 < TCH ? ntok - t0 : TCH;
-        __syncthreads();
-        for (int i = threadIdx.x; i < TCH * ldw; i += blockDim.x) {
-            const int t = i / ldw, k = i % ldw;
-            xs[i] = (t < nt && k < in) ? xload<XT>(x, (size_t)(t0 + t) * ldx + k) : 0.0f;
-        }
-        __syncthreads();
-        if (o >= out) continue;
-        float acc[TCH] = {0.f, 0.f, 0.f, 0.f};
-        const int8_t *row = wq + (size_t)o * ldw;
-        for (int c = lane; c < ldw / 16; c += 32) {
-            const uint4 v = ldg_nc_v4(row + (size_t)c * 16);
-            const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+        float acc[TCH];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                float f[4];
-                s8x4_to_f32(ws[q], f);
+        for (int t = 0; t < TCH; t++) acc[t] = 0.f;
+        for (int k0 = kbeg; k0 < kend; k0 += KC) {
+            __syncwarp();
+            for (int i = lane; i < TCH * KC; i += 32) {  // coalesced: consecutive k per lane
+                const int t = i / KC, k = k0 + i % KC;
+                xs[i] = (t < nt && k < in && k < kend) ? xload<XT>(x, (size_t)(t0 + t) * ldx + k) : 0.0f;
+            }
+            __syncwarp();
+            const int kk_end = min(KC, kend - k0);
+            for (int kk = 0; kk < kk_end; kk += 32) {
+                const uint4 v0 = ldg_nc_v4(wrow + k0 + kk);
+                const uint4 v1 = ldg_nc_v4(wrow + k0 + kk + 16);
+                float f[32];
+                s8x4_to_f32(v0.x, *reinterpret_cast<float(*)[4]>(f + 0));
+                s8x4_to_f32(v0.y, *reinterpret_cast<float(*)[4]>(f + 4));
+                s8x4_to_f32(v0.z, *reinterpret_cast<float(*)[4]>(f + 8));
+                s8x4_to_f32(v0.w, *reinterpret_cast<float(*)[4]>(f + 12));
+                s8x4_to_f32(v1.x, *reinterpret_cast<float(*)[4]>(f + 16));
+                s8x4_to_f32(v1.y, *reinterpret_cast<float(*)[4]>(f + 20));
+                s8x4_to_f32(v1.z, *reinterpret_cast<float(*)[4]>(f + 24));
+                s8x4_to_f32(v1.w, *reinterpret_cast<float(*)[4]>(f + 28));
 #pragma unroll
                 for (int t = 0; t < TCH; t++) {
-                    const float4 xv = *reinterpret_cast<const float4 *>(xs + t * ldw + 16 * c + 4 * q);
-                    acc[t] = fmaf(f[0], xv.x, acc[t]);
-                    acc[t] = fmaf(f[1], xv.y, acc[t]);
-                    acc[t] = fmaf(f[2], xv.z, acc[t]);
-                    acc[t] = fmaf(f[3], xv.w, acc[t]);
+                    const float4 *xp = reinterpret_cast<const float4 *>(xs + t * KC + kk);
+#pragma unroll
+                    for (int q = 0; q < 8; q++) {
+                        const float4 xv = xp[q];  // same address in every lane: a broadcast
+                        acc[t] = fmaf(f[4 * q + 0], xv.x, acc[t]);
+                        acc[t] = fmaf(f[4 * q + 1], xv.y, acc[t]);
+                        acc[t] = fmaf(f[4 * q + 2], xv.z, acc[t]);
+                        acc[t] = fmaf(f[4 * q + 3], xv.w, acc[t]);
+                    }
                 }
             }
         }
 #pragma unroll
-        for (int t = 0; t < TCH; t++) {
-            const float a = warp_sum(acc[t]);
-            if (lane == 0 && t < nt) y[(size_t)(t0 + t) * ldy + o] = a * wscale[o];
+        for (int t = 0; t < TCH; t++) red[(warp * 32 + lane) * TCH + t] = acc[t];
+        __syncthreads();
+        if (warp == 0 && row < out) {
+            for (int t = 0; t < nt; t++) {
+                float a = red[(0 * 32 + lane) * TCH + t];
+                a += red[(1 * 32 + lane) * TCH + t];
+                a += red[(2 * 32 + lane) * TCH + t];
+                a += red[(3 * 32 + lane) * TCH + t];
+                y[(size_t)(t0 + t) * ldy + row] = a * wscale[row];
+            }
         }
+        __syncthreads();
     }
 }
 
@@ -105,20 +134,17 @@ int launch_q8_pack(int8_t *wq, float *wscale, int ldw, const void *rows, int in,
 int launch_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
                    const int8_t *wq, const float *wscale, int ldw, int in, int out,
                    cudaStream_t s) {
-    if (in <= 0 || out <= 0 || ldw < in || (ldw % 16) || ((uintptr_t)wq & 15))
-        return set_error(K3C_EINVAL, "q8_gemv: in=%d out=%d ldw=%d", in, out, ldw);
+    if (in <= 0 || out <= 0 || ldw < in || (ldw % 32) || ((uintptr_t)wq & 15))
+        return set_error(K3C_EINVAL, "q8_gemv: in=%d out=%d ldw=%d (ldw must be a multiple of 32)", in, out, ldw);
     if (ntok <= 0) return K3C_OK;
-    const size_t smem = (size_t)4 * ldw * sizeof(float);
-    if (smem > 200 * 1024) return set_error(K3C_EINVAL, "q8_gemv: in=%d too large", in);
-    const unsigned blocks = (unsigned)((out + 7) / 8);
+    const size_t smem = (size_t)(4 * 16 * 256 + 4 * 32 * 16) * sizeof(float);  // 72 KB
+    const unsigned blocks = (unsigned)((out + 31) / 32);
     if (x_dtype == K3C_BF16) {
-        if (smem > 48 * 1024)
-            K3C_TRY_CUDA(cudaFuncSetAttribute(k_q8_gemv<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_q8_gemv<uint16_t><<<blocks, 256, smem, s>>>(y, ldy, (const uint16_t *)x, ldx, ntok, wq, wscale, ldw, in, out);
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k_q8_gemv<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_q8_gemv<uint16_t><<<blocks, 128, smem, s>>>(y, ldy, (const uint16_t *)x, ldx, ntok, wq, wscale, ldw, in, out);
     } else if (x_dtype == K3C_F32) {
-        if (smem > 48 * 1024)
-            K3C_TRY_CUDA(cudaFuncSetAttribute(k_q8_gemv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_q8_gemv<float><<<blocks, 256, smem, s>>>(y, ldy, (const float *)x, ldx, ntok, wq, wscale, ldw, in, out);
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k_q8_gemv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_q8_gemv<float><<<blocks, 128, smem, s>>>(y, ldy, (const float *)x, ldx, ntok, wq, wscale, ldw, in, out);
     } else {
         return set_error(K3C_EINVAL, "q8_gemv: x_dtype=%d", x_dtype);
     }

@@ -25,41 +25,82 @@ __device__ __forceinline__ double widen<uint16_t>(const uint16_t *p, size_t i) {
     return (double)bf16_bits_to_f32(p[i]);
 }
 
-// scores[t][e] for one expert row per warp, all tokens. x is staged in shared memory as
-// fp32 (exact widening) in token chunks of TCH.
+// Eight W elements of row `row` from element k (k a multiple of 8, rows 16-byte aligned
+// when vec): exact widening to double.
+template <typename WT>
+__device__ __forceinline__ void load_w8(const WT *row, int k, int hidden, bool vec, double (&w)[8]) {
+    if (vec && k + 8 <= hidden) {
+        if constexpr (sizeof(WT) == 2) {
+            const uint4 u = *reinterpret_cast<const uint4 *>(row + k);
+            const uint32_t p[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                w[2 * q] = (double)__uint_as_float(p[q] << 16);
+                w[2 * q + 1] = (double)__uint_as_float(p[q] & 0xFFFF0000u);
+            }
+        } else {
+            const float4 a = *reinterpret_cast<const float4 *>(row + k);
+            const float4 b = *reinterpret_cast<const float4 *>(row + k + 4);
+            w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+            w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < 8; q++) w[q] = k + q < hidden ? widen<WT>(row, k + q) : 0.0;
+    }
+}
+
+// grid (ceil(E/8), ceil(ntok/4)): warp w owns expert row 8*bx + w and the block's 4 tokens.
+// x is staged in chunks of 2048 elements (fp32, exact) and reused by the 8 rows; each lane
+// owns 8-element segments; products and sums in double, lane partials reduced by a fixed
+// shuffle tree.
 template <typename WT, typename XT>
 __global__ void __launch_bounds__(256) k_router_scores(float *__restrict__ scores,
                                                        const XT *__restrict__ x,
                                                        const WT *__restrict__ W, int hidden,
-                                                       int n_experts, int ntok) {
-    extern __shared__ float xs[];  // [TCH][hidden]
-    const int TCH = 4;
+                                                       int n_experts, int ntok, int vec) {
+    constexpr int TCH = 4, KC = 2048;
+    __shared__ __align__(16) float xs[TCH * KC];  // 32 KB
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * 8 + warp;
-    for (int t0 = 0; t0 < ntok; t0 += TCH) {
-        const int nt = ntok - t0 < TCH ? ntok - t0 : TCH;
+    const int t0 = blockIdx.y * TCH;
+    const int nt = ntok - t0 < TCH ? ntok - t0 : TCH;
+    double acc[TCH] = {0.0, 0.0, 0.0, 0.0};
+    const WT *row = W + (size_t)(e < n_experts ? e : 0) * hidden;
+    for (int k0 = 0; k0 < hidden; k0 += KC) {
         __syncthreads();
-        for (int i = threadIdx.x; i < nt * hidden; i += blockDim.x)
-            xs[i] = (float)widen<XT>(x, (size_t)t0 * hidden + i);
+        for (int i = threadIdx.x; i < TCH * KC; i += blockDim.x) {
+            const int t = i / KC, k = k0 + i % KC;
+            xs[i] = (t < nt && k < hidden) ? (float)widen<XT>(x, (size_t)(t0 + t) * hidden + k) : 0.0f;
+        }
         __syncthreads();
-        if (e < n_experts) {
-            double acc[TCH] = {0.0, 0.0, 0.0, 0.0};
-            const WT *row = W + (size_t)e * hidden;
-            for (int i = lane; i < hidden; i += 32) {
-                const double wv = widen<WT>(row, i);
-#pragma unroll
-                for (int t = 0; t < TCH; t++)
-                    if (t < nt) acc[t] = fma(wv, (double)xs[t * hidden + i], acc[t]);
-            }
+        if (e >= n_experts) continue;
+        for (int seg = lane; seg < KC / 8 && k0 + 8 * seg < hidden; seg += 32) {
+            double w[8];
+            load_w8<WT>(row, k0 + 8 * seg, hidden, vec != 0, w);
 #pragma unroll
             for (int t = 0; t < TCH; t++) {
-                const double a = warp_sum_d(acc[t]);
-                if (lane == 0 && t < nt) {
-                    const float logit = (float)a;
-                    const float ex = (float)exp(-(double)logit);
-                    scores[(size_t)(t0 + t) * n_experts + e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
-                }
+                const float4 a = *reinterpret_cast<const float4 *>(xs + t * KC + 8 * seg);
+                const float4 b = *reinterpret_cast<const float4 *>(xs + t * KC + 8 * seg + 4);
+                acc[t] = fma(w[0], (double)a.x, acc[t]);
+                acc[t] = fma(w[1], (double)a.y, acc[t]);
+                acc[t] = fma(w[2], (double)a.z, acc[t]);
+                acc[t] = fma(w[3], (double)a.w, acc[t]);
+                acc[t] = fma(w[4], (double)b.x, acc[t]);
+                acc[t] = fma(w[5], (double)b.y, acc[t]);
+                acc[t] = fma(w[6], (double)b.z, acc[t]);
+                acc[t] = fma(w[7], (double)b.w, acc[t]);
             }
+        }
+    }
+    if (e >= n_experts) return;
+#pragma unroll
+    for (int t = 0; t < TCH; t++) {
+        const double a = warp_sum_d(acc[t]);
+        if (lane == 0 && t < nt) {
+            const float logit = (float)a;
+            const float ex = (float)exp(-(double)logit);
+            scores[(size_t)(t0 + t) * n_experts + e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
         }
     }
 }
@@ -130,13 +171,9 @@ int launch_router_select(int *idx, float *w, const float *scores, const float *b
 template <typename WT, typename XT>
 static int launch_scores_t(float *scores, const void *x, const void *W, int hidden,
                            int n_experts, int ntok, cudaStream_t s) {
-    const size_t smem = (size_t)4 * hidden * sizeof(float);
-    if (smem > 200 * 1024) return set_error(K3C_EINVAL, "router: hidden=%d too large", hidden);
-    auto kern = k_router_scores<WT, XT>;
-    if (smem > 48 * 1024)
-        K3C_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(n_experts + 7) / 8, 256, smem, s>>>(scores, (const XT *)x, (const WT *)W, hidden,
-                                                n_experts, ntok);
+    const int vec = ((uintptr_t)W % 16 == 0) && ((hidden * (int)sizeof(WT)) % 16 == 0);
+    k_router_scores<WT, XT><<<dim3((n_experts + 7) / 8, (ntok + 3) / 4), 256, 0, s>>>(
+        scores, (const XT *)x, (const WT *)W, hidden, n_experts, ntok, vec);
     K3C_CHECK_LAUNCH();
     return K3C_OK;
 }
