@@ -359,6 +359,9 @@ def run_ours(args, ws, rank, local):
         "decode_hbm_gbs": layer_bytes / dt / 1e9,
         "unique_experts_per_step": float(np.mean(uniq)),
         "batches": batches,
+        "stages_ms_per_step": {name: ms_buf[j] / args.steps
+                               for j, name in enumerate(("experts", "router", "combine", "q8"))},
+        "q8_hbm_gbs": (H * H + 4 * H) * args.steps / (ms_buf[3] / 1e3) / 1e9 if ms_buf[3] > 0 else None,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
                      "kernel": "expert stage (gate/up+act and down MXFP4 GEMV kernels)",

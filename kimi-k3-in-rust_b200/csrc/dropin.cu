@@ -25,11 +25,10 @@ int launch_q8_pack(int8_t *wq, float *wscale, int ldw, const void *rows, int in,
                    cudaStream_t s);
 int launch_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
                    const int8_t *wq, const float *wscale, int ldw, int in, int out, cudaStream_t s);
-int launch_router_scores(float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
-                         int hidden, int n_experts, int ntok, cudaStream_t s);
-int launch_router_select(int *idx, float *w, const float *scores, const float *bias,
-                         int n_experts, int topk, int renorm, float routed_scale, int ntok,
-                         cudaStream_t s);
+int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
+                  const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
+                  int ntok, double *part, cudaStream_t s);
+size_t router_scratch_bytes(int hidden, int n_experts, int ntok);
 
 [[noreturn]] static void fatal(const char *what, const char *detail) {
     fprintf(stderr, "k3c: FATAL, %s: %s\n    Aborting rather than returning with the output "
@@ -162,7 +161,7 @@ void k3_router(int *idx, float *wout, const float *x, const float *W, const floa
     if (n_experts <= 0 || hidden <= 0) fatal(what, "empty router");
     const size_t nb_x = (size_t)hidden * sizeof(float), nb_w = (size_t)n_experts * hidden * sizeof(float);
     const size_t nb_b = bias ? (size_t)n_experts * sizeof(float) : 0;
-    const size_t nb_sc = (size_t)n_experts * sizeof(float);
+    const size_t nb_sc = router_scratch_bytes(hidden, n_experts, 1);   // logit chunks
     const size_t nb_i = (size_t)topk * sizeof(int), nb_o = (size_t)topk * sizeof(float);
     Workspace &w = ws_for_current(what);
     std::lock_guard<std::mutex> lk(w.mu);
@@ -173,11 +172,9 @@ void k3_router(int *idx, float *wout, const float *x, const float *W, const floa
     cuda_ok(cudaMemcpyAsync(b + o_x, x, nb_x, cudaMemcpyHostToDevice, w.stream), what);
     cuda_ok(cudaMemcpyAsync(b + o_w, W, nb_w, cudaMemcpyHostToDevice, w.stream), what);
     if (bias) cuda_ok(cudaMemcpyAsync(b + o_b, bias, nb_b, cudaMemcpyHostToDevice, w.stream), what);
-    rc_ok(launch_router_scores((float *)(b + o_sc), b + o_x, K3C_F32, b + o_w, K3C_F32, hidden,
-                               n_experts, 1, w.stream), what);
-    rc_ok(launch_router_select((int *)(b + o_i), (float *)(b + o_o), (const float *)(b + o_sc),
-                               bias ? (const float *)(b + o_b) : nullptr, n_experts, topk, renorm,
-                               routed_scale, 1, w.stream), what);
+    rc_ok(launch_router((int *)(b + o_i), (float *)(b + o_o), nullptr, b + o_x, K3C_F32, b + o_w, K3C_F32,
+                        bias ? (const float *)(b + o_b) : nullptr, hidden, n_experts, topk, renorm, routed_scale,
+                        1, (double *)(b + o_sc), w.stream), what);
     cuda_ok(cudaMemcpyAsync(idx, b + o_i, nb_i, cudaMemcpyDeviceToHost, w.stream), what);
     cuda_ok(cudaMemcpyAsync(wout, b + o_o, nb_o, cudaMemcpyDeviceToHost, w.stream), what);
     cuda_ok(cudaStreamSynchronize(w.stream), what);

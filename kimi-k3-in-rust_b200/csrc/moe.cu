@@ -23,11 +23,10 @@
 
 namespace k3c {
 
-int launch_router_scores(float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
-                         int hidden, int n_experts, int ntok, cudaStream_t s);
-int launch_router_select(int *idx, float *w, const float *scores, const float *bias,
-                         int n_experts, int topk, int renorm, float routed_scale, int ntok,
-                         cudaStream_t s);
+int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
+                  const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
+                  int ntok, double *part, cudaStream_t s);
+size_t router_scratch_bytes(int hidden, int n_experts, int ntok);
 
 struct Slot {
     K3ExpertQ q;
@@ -304,7 +303,7 @@ int launch_expert_ffn(float *y, const float *x, int ntok, const K3ExpertQ *e, in
 
 struct DecodeBufs {
     Plan p;
-    float *xf, *scores, *wt, *actbuf, *contrib;
+    float *xf, *wt, *actbuf, *contrib;
     int *idx;
 };
 
@@ -314,12 +313,15 @@ static bool carve_decode(Carve &cv, DecodeBufs &b, const k3c_moe_layer *L, int n
     const int max_pairs = P + ntok;
     if (!carve_plan(cv, b.p, max_slots, max_pairs, P)) return false;
     b.xf = cv.take<float>((size_t)ntok * L->hidden);
-    b.scores = cv.take<float>((size_t)ntok * L->n_experts);
     b.idx = cv.take<int>(P);
     b.wt = cv.take<float>(P);
     b.actbuf = cv.take<float>((size_t)max_pairs * L->inter);
-    b.contrib = cv.take<float>((size_t)ntok * (L->topk + 1) * L->hidden);
-    return b.xf && b.scores && b.idx && b.wt && b.actbuf && b.contrib;
+    // contrib is first written by the down kernels, after routing: the router's logit
+    // chunks share its space
+    const size_t nc = (size_t)ntok * (L->topk + 1) * L->hidden;
+    const size_t np = router_scratch_bytes(L->hidden, L->n_experts, ntok) / sizeof(float);
+    b.contrib = cv.take<float>(nc > np ? nc : np);
+    return b.xf && b.idx && b.wt && b.actbuf && b.contrib;
 }
 
 size_t moe_decode_scratch(const k3c_moe_layer *L, int ntok) {
@@ -351,8 +353,9 @@ int launch_moe_decode(float *out, const void *x, int x_dtype, int ntok, const k3
     else return set_error(K3C_EINVAL, "moe_decode: x_dtype=%d", x_dtype);
     K3C_CHECK_LAUNCH();
     stage_begin(STAGE_ROUTER, s);
-    K3C_TRY(launch_router_scores(b.scores, x, x_dtype, L->router_w, L->router_dtype, L->hidden, L->n_experts, ntok, s));
-    K3C_TRY(launch_router_select(idx, wt, b.scores, L->router_bias, L->n_experts, L->topk, L->renorm, L->routed_scale, ntok, s));
+    K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, L->hidden,
+                          L->n_experts, L->topk, L->renorm, L->routed_scale, ntok,
+                          reinterpret_cast<double *>(b.contrib), s));
     stage_end(STAGE_ROUTER, s);
     const int P = ntok * L->topk;
     const int max_slots = (P < L->n_experts ? P : L->n_experts) + (L->shared ? 1 : 0);

@@ -1,4 +1,4 @@
-// moe_tc.cu -- MoE decode on the 5th-generation tensor cores (tcgen05, kind::mxf8f6f4).
+// moe_pool.cu -- MoE decode on the 5th-generation tensor cores (tcgen05, kind::mxf8f6f4).
 //
 // The routed experts stay in MXFP4: TMA streams the packed E2M1 nibbles straight into
 // shared memory (the 16U4_ALIGN16B tensor-map type places each 8-byte group of 16 nibbles
@@ -28,14 +28,14 @@
 
 #include "common.cuh"
 #include "tc_common.cuh"
+#include "tc_host.cuh"
 
 namespace k3c {
 
-int launch_router_scores(float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
-                         int hidden, int n_experts, int ntok, cudaStream_t s);
-int launch_router_select(int *idx, float *w, const float *scores, const float *bias,
-                         int n_experts, int topk, int renorm, float routed_scale, int ntok,
-                         cudaStream_t s);
+int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
+                  const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
+                  int ntok, double *part, cudaStream_t s);
+size_t router_scratch_bytes(int hidden, int n_experts, int ntok);
 int launch_moe_combine(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
                        int ntok, int topk, int hidden, int has_shared, cudaStream_t s);
 
@@ -166,7 +166,10 @@ struct SlotTc {
     int run, ntok;
 };
 
-// Same grouping as the CUDA-core plan, slot-major with 32 pair rows per slot.
+// Same grouping as the CUDA-core plan, slot-major with 32 pair rows per slot: one slot per
+// selected resident expert in expert order, then the shared expert. One block; every step
+// is parallel over pairs or experts (slot numbers by a block-wide prefix count), and a pair's
+// row within its slot is its rank among the earlier pairs of the same expert.
 __global__ void __launch_bounds__(1024) k_moe_plan_tc(int *__restrict__ n_slots, SlotTc *__restrict__ slots,
                                                       int *__restrict__ pair_tok, int *__restrict__ pair_k,
                                                       uint8_t *__restrict__ dropped, const int *__restrict__ idx,
@@ -174,8 +177,11 @@ __global__ void __launch_bounds__(1024) k_moe_plan_tc(int *__restrict__ n_slots,
                                                       int n_experts, int n_runs, int shared_run,
                                                       int *__restrict__ drops) {
     extern __shared__ int sm[];
-    int *cnt = sm, *slot_of = sm + n_experts;
+    int *cnt = sm, *slot_of = sm + n_experts;        // [E], [E]
+    int *pe = slot_of + n_experts;                   // [P] expert of each kept pair, -1 if dropped
+    __shared__ int warp_sum[32];
     const int P = ntok * topk;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
@@ -184,39 +190,50 @@ __global__ void __launch_bounds__(1024) k_moe_plan_tc(int *__restrict__ n_slots,
         // scale addresses from it
         const bool ok = e >= 0 && e < n_experts && run_of[e] >= 0 && run_of[e] < n_runs;
         dropped[i] = ok ? 0 : 1;
+        pe[i] = ok ? e : -1;
         if (ok) atomicAdd(&cnt[e], 1);
         else if (drops) atomicAdd(drops, 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int ns = 0;
-        for (int e = 0; e < n_experts; e++) {
-            if (cnt[e] > 0) {
-                slot_of[e] = ns;
-                slots[ns].run = run_of[e];
-                slots[ns].ntok = cnt[e];
-                ns++;
-            } else {
-                slot_of[e] = -1;
+    // slot numbers: exclusive prefix count of used experts, in chunks of blockDim experts
+    int base = 0;
+    for (int e0 = 0; e0 < n_experts; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        const bool used = e < n_experts && cnt[e] > 0;
+        const unsigned m = __ballot_sync(0xffffffffu, used);
+        if (lane == 0) warp_sum[warp] = __popc(m);
+        __syncthreads();
+        int before = base;
+        for (int w = 0; w < warp; w++) before += warp_sum[w];
+        int total = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) total += warp_sum[w];
+        if (e < n_experts) {
+            const int sl = before + __popc(m & ((1u << lane) - 1u));
+            slot_of[e] = used ? sl : -1;
+            if (used) {
+                slots[sl].run = run_of[e];
+                slots[sl].ntok = cnt[e];
             }
         }
-        if (shared_run >= 0) {
-            slots[ns].run = shared_run;
-            slots[ns].ntok = ntok;
-            for (int t = 0; t < ntok; t++) {
-                pair_tok[ns * 32 + t] = t;
-                pair_k[ns * 32 + t] = topk;
-            }
-            ns++;
-        }
-        *n_slots = ns;
+        base += total;
+        __syncthreads();   // warp_sum is rewritten by the next chunk
     }
-    __syncthreads();
+    if (shared_run >= 0) {
+        for (int t = threadIdx.x; t < ntok; t += blockDim.x) {
+            pair_tok[base * 32 + t] = t;
+            pair_k[base * 32 + t] = topk;
+        }
+        if (threadIdx.x == 0) {
+            slots[base].run = shared_run;
+            slots[base].ntok = ntok;
+        }
+    }
+    if (threadIdx.x == 0) *n_slots = base + (shared_run >= 0 ? 1 : 0);
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        if (dropped[i]) continue;
-        const int e = idx[i];
+        const int e = pe[i];
+        if (e < 0) continue;
         int rank = 0;
-        for (int k = 0; k < i; k++) rank += (idx[k] == e && !dropped[k]);
+        for (int k = 0; k < i; k++) rank += pe[k] == e;
         const int pos = slot_of[e] * 32 + rank;
         pair_tok[pos] = i / topk;
         pair_k[pos] = i % topk;
@@ -282,39 +299,11 @@ __device__ __forceinline__ float act_apply(float g, float u, int act) {
     return __fmul_rn(__fmul_rn(g, sigmoid_f(g)), u);
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__device__ __forceinline__ uint64_t l2_evict_first_policy() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-__device__ __forceinline__ void tma_load_3d_hint(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
-                                                 int c0, int c1, int c2, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(tc::smem_u32(smem_dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
-        "l"(policy)
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t *v) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-          "=r"(v[14]), "=r"(v[15])
-        : "r"(addr));
-}
-
-__device__ __forceinline__ bool tc_check(bool ok, int *err, int code) {
-    if (!ok && err) atomicExch(err, code);
-    return ok;
-}
+using tc::l2_evict_first_policy;
+using tc::named_bar_sync;
+using tc::tc_check;
+using tc::tma_load_3d_hint;
+using tc::tmem_ld16;
 
 template <int J, int NT, int STAGES, bool GU>
 __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ CUtensorMap tmW,
@@ -484,53 +473,12 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
 }
 
 // ------------------------------------------------------------------ host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
-static int make_map3(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t d0, uint64_t d1,
-                     uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return set_error(K3C_ECUDA, "tc: cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[3] = {d0, d1, d2}, strides[2] = {s1, s2};
-    cuuint32_t box[3] = {b0, b1, 1}, es[3] = {1, 1, 1};
-    CUresult r = fn(m, dt, 3, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(K3C_ECUDA, "tc: tensor map encode failed (%d)", (int)r);
-    return K3C_OK;
-}
-
-static int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 struct TcBufs {
     int *n_slots;
     SlotTc *slots;
     int *pair_tok, *pair_k;
     uint8_t *dropped;
-    float *scores, *wt, *contrib;
+    float *wt, *contrib;
     int *idx;
     uint8_t *xq, *xsf, *actq, *actsf;
     int *err;
@@ -547,15 +495,18 @@ static bool carve_tc(Carve &cv, TcBufs &b, const k3c_moe_pool_layer *L, int ntok
     b.pair_tok = cv.take<int>((size_t)b.max_slots * 32);
     b.pair_k = cv.take<int>((size_t)b.max_slots * 32);
     b.dropped = cv.take<uint8_t>(P);
-    b.scores = cv.take<float>((size_t)ntok * L->n_experts);
     b.idx = cv.take<int>(P);
     b.wt = cv.take<float>(P);
-    b.contrib = cv.take<float>((size_t)ntok * (L->topk + 1) * H);
+    // contrib is first written by the down kernel, after routing: the router's logit chunks
+    // share its space
+    const size_t nc = (size_t)ntok * (L->topk + 1) * H;
+    const size_t np = router_scratch_bytes(H, L->n_experts, ntok) / sizeof(float);
+    b.contrib = cv.take<float>(nc > np ? nc : np);
     b.xq = cv.take<uint8_t>((size_t)J * 32 * H, 1024);
     b.xsf = cv.take<uint8_t>((size_t)(H / 128) * 512, 1024);
     b.actq = cv.take<uint8_t>((size_t)b.max_slots * J * 32 * I, 1024);
     b.actsf = cv.take<uint8_t>((size_t)b.max_slots * (I / 128) * 512, 1024);
-    return b.n_slots && b.err && b.slots && b.pair_tok && b.pair_k && b.dropped && b.scores &&
+    return b.n_slots && b.err && b.slots && b.pair_tok && b.pair_k && b.dropped &&
            b.idx && b.wt && b.contrib && b.xq && b.xsf && b.actq && b.actsf;
 }
 
@@ -651,11 +602,11 @@ int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const
     float *wt = wt_out ? wt_out : b.wt;
     K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), s));
     stage_begin(STAGE_ROUTER, s);
-    K3C_TRY(launch_router_scores(b.scores, x, x_dtype, L->router_w, L->router_dtype, H, L->n_experts, ntok, s));
-    K3C_TRY(launch_router_select(idx, wt, b.scores, L->router_bias, L->n_experts, L->topk, L->renorm,
-                                 L->routed_scale, ntok, s));
+    K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, H,
+                          L->n_experts, L->topk, L->renorm, L->routed_scale, ntok,
+                          reinterpret_cast<double *>(b.contrib), s));
     stage_end(STAGE_ROUTER, s);
-    const size_t psmem = (size_t)L->n_experts * 2 * sizeof(int);
+    const size_t psmem = ((size_t)L->n_experts * 2 + (size_t)ntok * L->topk) * sizeof(int);
     if (psmem > 48 * 1024)
         K3C_TRY_CUDA(cudaFuncSetAttribute(k_moe_plan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
     k_moe_plan_tc<<<1, 1024, psmem, s>>>(b.n_slots, b.slots, b.pair_tok, b.pair_k, b.dropped, idx, ntok,

@@ -2,8 +2,10 @@
 //
 // logits  W.x with every product exact in double (bf16 and fp32 operands widen exactly) and
 //         the sum in double, rounded once to float: the reference's double accumulator
-//         (:447-450). Lane-strided summation reassociates exact products, which moves the
-//         double sum by ~1e-16 relative; the float rounding absorbs it.
+//         (:447-450). The sum runs in K chunks of 256 (one kernel, partials in double) that
+//         the select kernel adds in chunk order; the chunked, lane-strided order reassociates
+//         exact products, which moves the double sum by ~1e-16 relative; the float rounding
+//         absorbs it.
 // score   1/(1+e) in float with e = exp(-logit) rounded once from double, i.e. a correctly
 //         rounded expf; the reference calls libm expf (:451).
 // select  repeated strict-greater argmax on score+bias from -INFINITY, lowest index on
@@ -50,143 +52,334 @@ __device__ __forceinline__ void load_w8(const WT *row, int k, int hidden, bool v
     }
 }
 
-// grid (ceil(E/8), ceil(ntok/4)): warp w owns expert row 8*bx + w and the block's 4 tokens.
-// x is staged in chunks of 2048 elements (fp32, exact) and reused by the 8 rows; each lane
-// owns 8-element segments; products and sums in double, lane partials reduced by a fixed
-// shuffle tree.
-template <typename WT, typename XT>
-__global__ void __launch_bounds__(256) k_router_scores(float *__restrict__ scores,
-                                                       const XT *__restrict__ x,
-                                                       const WT *__restrict__ W, int hidden,
-                                                       int n_experts, int ntok, int vec) {
-    constexpr int TCH = 4, KC = 2048;
-    __shared__ __align__(16) float xs[TCH * KC];  // 32 KB
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * 8 + warp;
-    const int t0 = blockIdx.y * TCH;
-    const int nt = ntok - t0 < TCH ? ntok - t0 : TCH;
-    double acc[TCH] = {0.0, 0.0, 0.0, 0.0};
-    const WT *row = W + (size_t)(e < n_experts ? e : 0) * hidden;
-    for (int k0 = 0; k0 < hidden; k0 += KC) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < TCH * KC; i += blockDim.x) {
-            const int t = i / KC, k = k0 + i % KC;
-            xs[i] = (t < nt && k < hidden) ? (float)widen<XT>(x, (size_t)(t0 + t) * hidden + k) : 0.0f;
-        }
-        __syncthreads();
-        if (e >= n_experts) continue;
-        for (int seg = lane; seg < KC / 8 && k0 + 8 * seg < hidden; seg += 32) {
-            double w[8];
-            load_w8<WT>(row, k0 + 8 * seg, hidden, vec != 0, w);
+// Logits in K chunks of RT_KC = 256: grid (ceil(E/32), ceil(hidden/RT_KC), ceil(ntok/NT)),
+// 256 threads. The block stages x[chunk][NT tokens] in shared memory as double (exact,
+// converted once per block). Lane l of every warp takes expert 32*bx + l and streams its own
+// W row, warp w the K slice [32w, 32w+32) of the chunk, so every shared-memory read of x is
+// a broadcast feeding 32 FMAs (one per lane). The eight slice sums are added in warp order
+// and part[chunk][t][e] receives the chunk's double sum; the select kernel adds the chunks
+// in order. NT (1..16 tokens per block) keeps small batches from computing empty slots.
+constexpr int RT_KC = 256;
+constexpr int RT_KW = RT_KC / 8;   // K per warp
+
+template <typename XT>
+__device__ __forceinline__ void load_x8(const XT *p, int n, bool vec, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load_x8<uint16_t>(const uint16_t *p, int n, bool vec, float (&v)[8]) {
+    if (vec && n >= 8) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(p);
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int t = 0; t < TCH; t++) {
-                const float4 a = *reinterpret_cast<const float4 *>(xs + t * KC + 8 * seg);
-                const float4 b = *reinterpret_cast<const float4 *>(xs + t * KC + 8 * seg + 4);
-                acc[t] = fma(w[0], (double)a.x, acc[t]);
-                acc[t] = fma(w[1], (double)a.y, acc[t]);
-                acc[t] = fma(w[2], (double)a.z, acc[t]);
-                acc[t] = fma(w[3], (double)a.w, acc[t]);
-                acc[t] = fma(w[4], (double)b.x, acc[t]);
-                acc[t] = fma(w[5], (double)b.y, acc[t]);
-                acc[t] = fma(w[6], (double)b.z, acc[t]);
-                acc[t] = fma(w[7], (double)b.w, acc[t]);
-            }
+        for (int i = 0; i < 4; i++) {
+            v[2 * i] = __uint_as_float(q[i] << 16);
+            v[2 * i + 1] = __uint_as_float(q[i] & 0xFFFF0000u);
         }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = i < n ? bf16_bits_to_f32(p[i]) : 0.0f;
     }
-    if (e >= n_experts) return;
+}
+template <>
+__device__ __forceinline__ void load_x8<float>(const float *p, int n, bool vec, float (&v)[8]) {
+    if (vec && n >= 8) {
+        const float4 a = *reinterpret_cast<const float4 *>(p);
+        const float4 b = *reinterpret_cast<const float4 *>(p + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
 #pragma unroll
-    for (int t = 0; t < TCH; t++) {
-        const double a = warp_sum_d(acc[t]);
-        if (lane == 0 && t < nt) {
-            const float logit = (float)a;
-            const float ex = (float)exp(-(double)logit);
-            scores[(size_t)(t0 + t) * n_experts + e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
-        }
+        for (int i = 0; i < 8; i++) v[i] = i < n ? p[i] : 0.0f;
     }
 }
 
-// One warp per token: top-k by repeated warp argmax over score+bias.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// A lane's whole RT_KW-element W slice as raw 16-byte vectors, all requested at once.
+template <typename WT>
+struct WSlice {
+    static constexpr int V = RT_KW * (int)sizeof(WT) / 16;
+    uint4 raw[V];
+    __device__ __forceinline__ void load(const WT *row) {
+#pragma unroll
+        for (int i = 0; i < V; i++) raw[i] = *reinterpret_cast<const uint4 *>(row + i * (16 / sizeof(WT)));
+    }
+    // elements [8g, 8g+8) widened to double (exact)
+    __device__ __forceinline__ void get(int g, double (&w)[8]) const {
+        if constexpr (sizeof(WT) == 2) {
+            const uint4 u = raw[g];
+            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                w[2 * i] = (double)__uint_as_float(q[i] << 16);
+                w[2 * i + 1] = (double)__uint_as_float(q[i] & 0xFFFF0000u);
+            }
+        } else {
+            const uint4 a = raw[2 * g], b = raw[2 * g + 1];
+            w[0] = __uint_as_float(a.x); w[1] = __uint_as_float(a.y);
+            w[2] = __uint_as_float(a.z); w[3] = __uint_as_float(a.w);
+            w[4] = __uint_as_float(b.x); w[5] = __uint_as_float(b.y);
+            w[6] = __uint_as_float(b.z); w[7] = __uint_as_float(b.w);
+        }
+    }
+};
+
+template <typename WT, typename XT, int NT>
+__global__ void __launch_bounds__(256) k_router_partial(double *__restrict__ part, const XT *__restrict__ x,
+                                                        const WT *__restrict__ W, int hidden, int n_experts,
+                                                        int ntok, int vec_w, int vec_x) {
+    extern __shared__ __align__(16) double rsm[];   // xs [RT_KC][NT], then red [8][NT][32]
+    double *xs = rsm;
+    double *red = rsm + RT_KC * NT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    grid_dep_launch();   // the select kernel may be scheduled; it waits for this grid's end
+    grid_dep_wait();     // x may come from the previous kernel
+    const int k0 = blockIdx.y * RT_KC, kn = min(RT_KC, hidden - k0);
+    const int t0 = blockIdx.z * NT, nt = min(NT, ntok - t0);
+    // consecutive threads take consecutive tokens, so stores of one k row are contiguous
+#pragma unroll 4
+    for (int i = threadIdx.x; i < NT * (RT_KC / 8); i += 256) {
+        const int t = i % NT, kk = (i / NT) * 8;
+        float v[8];
+        if (t < nt) load_x8<XT>(x + (size_t)(t0 + t) * hidden + k0 + kk, kn - kk, vec_x != 0, v);
+        else
+#pragma unroll
+            for (int q = 0; q < 8; q++) v[q] = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; q++) xs[(kk + q) * NT + t] = (double)v[q];
+    }
+    __syncthreads();
+    const int e = blockIdx.x * 32 + lane;
+    const int kw = warp * RT_KW, kwn = min(RT_KW, kn - kw);   // this warp's slice
+    const WT *row = W + (size_t)(e < n_experts ? e : 0) * hidden + k0 + kw;
+    double acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; t++) acc[t] = 0.0;
+    // acc[t] += w[0..8) . x[kw+k .. kw+k+8)[t]
+    auto step = [&](const double (&w)[8], int k) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const double *xp = xs + (kw + k + q) * NT;   // same address in every lane: broadcast
+            if constexpr (NT % 2 == 0) {
+#pragma unroll
+                for (int t2 = 0; t2 < NT / 2; t2++) {
+                    const double2 xv = reinterpret_cast<const double2 *>(xp)[t2];
+                    acc[2 * t2] = fma(w[q], xv.x, acc[2 * t2]);
+                    acc[2 * t2 + 1] = fma(w[q], xv.y, acc[2 * t2 + 1]);
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < NT; t++) acc[t] = fma(w[q], xp[t], acc[t]);
+            }
+        }
+    };
+    if (kwn == RT_KW && vec_w) {
+        WSlice<WT> ws;
+        ws.load(row);                    // one round trip for the whole slice
+#pragma unroll
+        for (int g = 0; g < RT_KW / 8; g++) {
+            double w[8];
+            ws.get(g, w);
+            step(w, 8 * g);
+        }
+    } else {
+        for (int k = 0; k < kwn; k += 8) {
+            double w[8];
+            load_w8<WT>(row, k, kwn, vec_w != 0, w);
+            step(w, k);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++) red[(warp * NT + t) * 32 + lane] = acc[t];
+    __syncthreads();
+    for (int i = threadIdx.x; i < NT * 32; i += 256) {
+        const int t = i / 32, l = i % 32, ee = blockIdx.x * 32 + l;
+        double sum = red[t * 32 + l];
+#pragma unroll
+        for (int w = 1; w < 8; w++) sum += red[(w * NT + t) * 32 + l];
+        if (t < nt && ee < n_experts) part[((size_t)blockIdx.y * ntok + t0 + t) * n_experts + ee] = sum;
+    }
+}
+
+__device__ __forceinline__ float sigmoid_score(double logit_d) {
+    const float logit = (float)logit_d;
+    const float ex = (float)exp(-(double)logit);
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+}
+
+// One block per token. With `part`, all threads first form the scores from the logit chunks
+// (added in chunk order) and write them to `scores` if that is not null; otherwise `scores`
+// holds them on entry. Warp 0 then takes the top-k by repeated warp argmax over score+bias.
 __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, float *__restrict__ w,
-                                                       const float *__restrict__ scores,
+                                                       float *__restrict__ scores,
+                                                       const double *__restrict__ part, int nchunk,
                                                        const float *__restrict__ bias,
                                                        int n_experts, int topk, int renorm,
                                                        float routed_scale, int ntok) {
-    extern __shared__ float ch[];  // [8 warps][n_experts] choice values
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 8 + warp;
-    if (t >= ntok) return;
-    float *c = ch + (size_t)warp * n_experts;
-    const float *s = scores + (size_t)t * n_experts;
-    for (int e = lane; e < n_experts; e += 32) c[e] = __fadd_rn(s[e], bias ? bias[e] : 0.0f);
-    __syncwarp();
-    int *it = idx + (size_t)t * topk;
-    float *wt = w + (size_t)t * topk;
-    for (int j = 0; j < topk; j++) {
-        float bv = -INFINITY;
-        int bi = -1;
-        for (int e = lane; e < n_experts; e += 32) {
-            const float v = c[e];
-            if (v > bv) { bv = v; bi = e; }  // ascending e per lane: first index wins
+    extern __shared__ float ch[];  // [2][n_experts]: choice values, scores
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x;
+    grid_dep_wait();   // the logit chunks come from the partial kernel
+    float *c = ch;
+    float *sc = ch + n_experts;
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+        float v;
+        if (part) {
+            // chunks in order; up to 16 loads in flight per pass
+            double logit = 0.0;
+            for (int k0 = 0; k0 < nchunk; k0 += 16) {
+                double v16[16];
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    v16[k] = k0 + k < nchunk ? part[((size_t)(k0 + k) * ntok + t) * n_experts + e] : 0.0;
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    if (k0 + k < nchunk) logit += v16[k];
+            }
+            v = sigmoid_score(logit);
+            if (scores) scores[(size_t)t * n_experts + e] = v;
+        } else {
+            v = scores[(size_t)t * n_experts + e];
         }
+        sc[e] = v;
+        c[e] = __fadd_rn(v, bias ? bias[e] : 0.0f);
+    }
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    __shared__ int s_idx[K3_MAX_TOPK];
+    __shared__ float s_w[K3_MAX_TOPK];
+    // warp argmax of (value, index) pairs: largest value, lowest index on ties, -1 if none
+    auto warp_best = [&](float bv, int bi) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
         }
-        if (lane == 0) {
-            if (bi < 0) { it[j] = 0; wt[j] = 0.0f; }
-            else { it[j] = bi; wt[j] = s[bi]; c[bi] = -INFINITY; }
+        return bi;
+    };
+    constexpr int RMAX = 16;   // candidates per lane held in registers (n_experts <= 512)
+    if (n_experts <= 32 * RMAX) {
+        float v[RMAX];
+#pragma unroll
+        for (int j = 0; j < RMAX; j++) v[j] = lane + 32 * j < n_experts ? c[lane + 32 * j] : -INFINITY;
+        for (int j = 0; j < topk; j++) {
+            float bv = -INFINITY;
+            int bj = -1;
+#pragma unroll
+            for (int q = 0; q < RMAX; q++)
+                if (v[q] > bv) { bv = v[q]; bj = q; }   // ascending e per lane: first index wins
+            const int bi = warp_best(bv, bj >= 0 ? lane + 32 * bj : -1);
+            if (bi >= 0 && (bi & 31) == lane) {
+#pragma unroll
+                for (int q = 0; q < RMAX; q++)
+                    if (q == (bi >> 5)) v[q] = -INFINITY;
+            }
+            if (lane == 0) {
+                s_idx[j] = bi < 0 ? 0 : bi;
+                s_w[j] = bi < 0 ? 0.0f : sc[bi];
+            }
         }
-        __syncwarp();
+    } else {
+        for (int j = 0; j < topk; j++) {
+            float bv = -INFINITY;
+            int bi = -1;
+            for (int e = lane; e < n_experts; e += 32) {
+                const float v = c[e];
+                if (v > bv) { bv = v; bi = e; }  // ascending e per lane: first index wins
+            }
+            bi = warp_best(bv, bi);
+            if (lane == 0) {
+                if (bi < 0) { s_idx[j] = 0; s_w[j] = 0.0f; }
+                else { s_idx[j] = bi; s_w[j] = sc[bi]; c[bi] = -INFINITY; }
+            }
+            __syncwarp();
+        }
     }
+    __syncwarp();
     if (lane == 0) {
         if (renorm && topk > 1) {
             double sum = 0.0;
-            for (int j = 0; j < topk; j++) sum += (double)wt[j];
+            for (int j = 0; j < topk; j++) sum += (double)s_w[j];
             const float inv = (float)(1.0 / (sum + 1e-20));
-            for (int j = 0; j < topk; j++) wt[j] = __fmul_rn(wt[j], inv);
+            for (int j = 0; j < topk; j++) s_w[j] = __fmul_rn(s_w[j], inv);
         }
-        for (int j = 0; j < topk; j++) wt[j] = __fmul_rn(wt[j], routed_scale);
+        for (int j = 0; j < topk; j++) s_w[j] = __fmul_rn(s_w[j], routed_scale);
     }
+    __syncwarp();
+    for (int j = lane; j < topk; j += 32) {
+        idx[(size_t)t * topk + j] = s_idx[j];
+        w[(size_t)t * topk + j] = s_w[j];
+    }
+}
+
+static int launch_select(int *idx, float *w, float *scores, const double *part, int nchunk,
+                         const float *bias, int n_experts, int topk, int renorm, float routed_scale,
+                         int ntok, cudaStream_t s) {
+    if (n_experts <= 0 || topk <= 0 || topk > K3_MAX_TOPK || ntok < 0)
+        return set_error(K3C_EINVAL, "router_select: n_experts=%d topk=%d ntok=%d", n_experts,
+                         topk, ntok);
+    if (ntok == 0) return K3C_OK;
+    const size_t smem = (size_t)2 * n_experts * sizeof(float);
+    if (smem > 200 * 1024) return set_error(K3C_EINVAL, "router_select: n_experts=%d too large", n_experts);
+    if (smem > 48 * 1024)
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    count_launch();
+    K3C_TRY_CUDA(launch_pdl(k_router_select, dim3(ntok), dim3(256), smem, s, idx, w, scores, part, nchunk, bias,
+                            n_experts, topk, renorm, routed_scale, ntok));
+    return K3C_OK;
 }
 
 int launch_router_select(int *idx, float *w, const float *scores, const float *bias,
                          int n_experts, int topk, int renorm, float routed_scale, int ntok,
                          cudaStream_t s) {
-    if (n_experts <= 0 || topk <= 0 || topk > K3_MAX_TOPK || ntok < 0)
-        return set_error(K3C_EINVAL, "router_select: n_experts=%d topk=%d ntok=%d", n_experts,
-                         topk, ntok);
-    if (ntok == 0) return K3C_OK;
-    const size_t smem = (size_t)8 * n_experts * sizeof(float);
-    if (smem > 200 * 1024) return set_error(K3C_EINVAL, "router_select: n_experts=%d too large", n_experts);
+    return launch_select(idx, w, const_cast<float *>(scores), nullptr, 0, bias, n_experts, topk, renorm,
+                         routed_scale, ntok, s);
+}
+
+size_t router_scratch_bytes(int hidden, int n_experts, int ntok) {
+    return (size_t)((hidden + RT_KC - 1) / RT_KC) * ntok * n_experts * sizeof(double);
+}
+
+template <typename WT, typename XT, int NT>
+static int launch_partial_nt(double *part, const void *x, const void *W, int hidden, int n_experts, int ntok,
+                             int vec_w, int vec_x, cudaStream_t s) {
+    const int smem = (RT_KC * NT + 8 * NT * 32) * (int)sizeof(double);
     if (smem > 48 * 1024)
-        K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k_router_select<<<(ntok + 7) / 8, 256, smem, s>>>(idx, w, scores, bias, n_experts, topk,
-                                                      renorm, routed_scale, ntok);
-    K3C_CHECK_LAUNCH();
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_partial<WT, XT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const dim3 grid((n_experts + 31) / 32, (hidden + RT_KC - 1) / RT_KC, (ntok + NT - 1) / NT);
+    count_launch();
+    K3C_TRY_CUDA(launch_pdl(k_router_partial<WT, XT, NT>, grid, dim3(256), smem, s, part, (const XT *)x,
+                            (const WT *)W, hidden, n_experts, ntok, vec_w, vec_x));
     return K3C_OK;
 }
 
 template <typename WT, typename XT>
-static int launch_scores_t(float *scores, const void *x, const void *W, int hidden,
-                           int n_experts, int ntok, cudaStream_t s) {
-    const int vec = ((uintptr_t)W % 16 == 0) && ((hidden * (int)sizeof(WT)) % 16 == 0);
-    k_router_scores<WT, XT><<<dim3((n_experts + 7) / 8, (ntok + 3) / 4), 256, 0, s>>>(
-        scores, (const XT *)x, (const WT *)W, hidden, n_experts, ntok, vec);
-    K3C_CHECK_LAUNCH();
-    return K3C_OK;
+static int launch_partial_t(double *part, const void *x, const void *W, int hidden, int n_experts, int ntok,
+                            cudaStream_t s) {
+    const int vec_w = ((uintptr_t)W % 16 == 0) && ((hidden * (int)sizeof(WT)) % 16 == 0);
+    const int vec_x = ((uintptr_t)x % 16 == 0) && ((hidden * (int)sizeof(XT)) % 16 == 0);
+    if (ntok <= 1) return launch_partial_nt<WT, XT, 1>(part, x, W, hidden, n_experts, ntok, vec_w, vec_x, s);
+    if (ntok <= 2) return launch_partial_nt<WT, XT, 2>(part, x, W, hidden, n_experts, ntok, vec_w, vec_x, s);
+    if (ntok <= 4) return launch_partial_nt<WT, XT, 4>(part, x, W, hidden, n_experts, ntok, vec_w, vec_x, s);
+    if (ntok <= 8) return launch_partial_nt<WT, XT, 8>(part, x, W, hidden, n_experts, ntok, vec_w, vec_x, s);
+    return launch_partial_nt<WT, XT, 16>(part, x, W, hidden, n_experts, ntok, vec_w, vec_x, s);
 }
 
-int launch_router_scores(float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
-                         int hidden, int n_experts, int ntok, cudaStream_t s) {
+int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
+                  const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
+                  int ntok, double *part, cudaStream_t s) {
     if (hidden <= 0 || n_experts <= 0) return set_error(K3C_EINVAL, "router: hidden=%d n_experts=%d", hidden, n_experts);
     if (ntok == 0) return K3C_OK;
-    if (w_dtype == K3C_BF16 && x_dtype == K3C_BF16) return launch_scores_t<uint16_t, uint16_t>(scores, x, W, hidden, n_experts, ntok, s);
-    if (w_dtype == K3C_BF16 && x_dtype == K3C_F32) return launch_scores_t<uint16_t, float>(scores, x, W, hidden, n_experts, ntok, s);
-    if (w_dtype == K3C_F32 && x_dtype == K3C_BF16) return launch_scores_t<float, uint16_t>(scores, x, W, hidden, n_experts, ntok, s);
-    if (w_dtype == K3C_F32 && x_dtype == K3C_F32) return launch_scores_t<float, float>(scores, x, W, hidden, n_experts, ntok, s);
-    return set_error(K3C_EINVAL, "router: dtypes x=%d W=%d", x_dtype, w_dtype);
+    int rc;
+    if (w_dtype == K3C_BF16 && x_dtype == K3C_BF16) rc = launch_partial_t<uint16_t, uint16_t>(part, x, W, hidden, n_experts, ntok, s);
+    else if (w_dtype == K3C_BF16 && x_dtype == K3C_F32) rc = launch_partial_t<uint16_t, float>(part, x, W, hidden, n_experts, ntok, s);
+    else if (w_dtype == K3C_F32 && x_dtype == K3C_BF16) rc = launch_partial_t<float, uint16_t>(part, x, W, hidden, n_experts, ntok, s);
+    else if (w_dtype == K3C_F32 && x_dtype == K3C_F32) rc = launch_partial_t<float, float>(part, x, W, hidden, n_experts, ntok, s);
+    else return set_error(K3C_EINVAL, "router: dtypes x=%d W=%d", x_dtype, w_dtype);
+    if (rc) return rc;
+    return launch_select(idx, w, scores, part, (hidden + RT_KC - 1) / RT_KC, bias, n_experts, topk, renorm,
+                         routed_scale, ntok, s);
 }
 
 }  // namespace k3c
@@ -205,14 +398,13 @@ extern "C" int k3c_router(int *idx, float *w, float *scores, const void *x, int 
                           k3c_stream_t stream) {
     k3c::clear_error();
     cudaStream_t s = (cudaStream_t)stream;
-    float *sc = scores;
-    if (!sc) {
-        K3C_TRY_CUDA(cudaMallocAsync((void **)&sc, (size_t)ntok * n_experts * sizeof(float), s));
-    }
-    int rc = k3c::launch_router_scores(sc, x, x_dtype, W, w_dtype, hidden, n_experts, ntok, s);
-    if (rc == K3C_OK)
-        rc = k3c::launch_router_select(idx, w, sc, bias, n_experts, topk, renorm, routed_scale,
-                                       ntok, s);
-    if (!scores) cudaFreeAsync(sc, s);
+    if (ntok <= 0 || hidden <= 0 || n_experts <= 0)
+        return k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk, renorm,
+                                  routed_scale, ntok, nullptr, s);
+    double *part = nullptr;
+    K3C_TRY_CUDA(cudaMallocAsync((void **)&part, k3c::router_scratch_bytes(hidden, n_experts, ntok), s));
+    const int rc = k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk,
+                                      renorm, routed_scale, ntok, part, s);
+    cudaFreeAsync(part, s);
     return rc;
 }

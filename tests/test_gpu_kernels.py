@@ -171,6 +171,37 @@ def test_router_full_shape_matches_reference(golden, k3, ora, dev):
     np.testing.assert_array_max_ulp(sc.cpu().numpy(), sref, maxulp=2)
 
 
+@pytest.mark.parametrize("ntok,hidden,wdt,xdt", [
+    (1, 7168, "bf16", "bf16"), (2, 7168, "bf16", "f32"), (3, 1000, "f32", "bf16"),
+    (7, 7168, "bf16", "bf16"), (16, 700, "f32", "f32"), (21, 7168, "bf16", "bf16"),
+])
+def test_router_token_blockings(k3, ora, dev, ntok, hidden, wdt, xdt):
+    """Every tokens-per-block specialisation (1, 2, 4, 8, 16, and several blocks), ragged
+    hidden sizes (a partial last K chunk, rows not 16-byte aligned) and all dtype pairs:
+    indices exact, scores within 2 ulp of the oracle's correctly rounded ones."""
+    import torch
+    g = k3.synth.rng(500 + ntok)
+    E, K = 384, 8
+    wf = (g.standard_normal((E, hidden)) * 0.02).astype(np.float32)
+    xf = g.standard_normal((ntok, hidden)).astype(np.float32)
+    bias = (g.standard_normal(E) * 0.01).astype(np.float32)
+    dev_t = {}
+    for name, a, dt in (("W", wf, wdt), ("x", xf, xdt)):
+        if dt == "bf16":
+            b = k3.synth.bf16_bits(a)
+            a[...] = k3.synth.bf16_to_f32(b)
+            dev_t[name] = T(b.view(np.int16), dev).view(torch.bfloat16)
+        else:
+            dev_t[name] = T(a, dev)
+    idx, w, sc = k3.router(dev_t["x"], dev_t["W"], T(bias, dev), K)
+    idx, w, sc = idx.cpu().numpy(), w.cpu().numpy(), sc.cpu().numpy()
+    for t in range(ntok):
+        ri, rw = ora.router(xf[t], wf, bias, K)
+        assert np.array_equal(idx[t], ri), t
+        np.testing.assert_allclose(w[t], rw, rtol=1e-6)   # from scores within 2 ulp
+        np.testing.assert_array_max_ulp(sc[t], ora.router_scores(xf[t], wf), maxulp=2)
+
+
 def test_dropin_router_host_pointers(golden, k3, ora):
     g = golden("ref_kernels.npz")
     L = k3.lib()
