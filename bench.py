@@ -10,6 +10,7 @@ in "batches". Each step uses a different token batch from a rotating pool, so ea
 touches ~110 different experts (~2.6 GB): inputs larger than L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload prefill [--steps K] [--warmup W]   (config[2], one line)
 
 N > 1 (torchrun) runs N independent replicas (decode does not shard; scaling "weak").
 --impl reference times the reference's own CPU kernels (oracle/_ref, built from its
@@ -375,6 +376,120 @@ def run_ours(args, ws, rank, local):
     print(json.dumps(line))
 
 
+# ------------------------------------------------------------------ prefill (config[2])
+PF_T = 4096
+PF_WORKLOAD = "config[2] MoE layer prefill: 4096 bf16 tokens, 384 HBM-resident MXFP4 experts " \
+              "(7168->2048->7168) + 1 shared, bf16 sigmoid top-8 router with a Zipf(1.1) selection bias"
+
+
+def run_prefill(args, ws, rank, local):
+    """One step = the whole layer over 4096 tokens through k3c_moe_prefill_tc (router,
+    expert-sorted grouped tcgen05 GEMMs, combine). Routing popularity follows Zipf(1.1) over
+    the expert ids by a selection bias fitted on a separate sample of tokens."""
+    import ctypes as C
+    import torch
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    blob, layer0, _, _ = build_device_workload(k3, dev, 1234 + rank, E, "tc", 2)
+    W = layer0.router_w
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    sample = torch.randn((2048, H), generator=g, device=dev).to(torch.bfloat16)
+    scores = torch.sigmoid(sample.float() @ W.float().T)
+    bias = k3.synth.zipf_fit_bias(scores, s=1.1, topk=K, iters=600)
+    layer = k3.PoolMoeLayer(blob, E + 1, layer0.run_of, E, W, bias, H, I, K, terms=2)
+    NB = 2
+    xs = [torch.randn((PF_T, H), generator=g, device=dev).to(torch.bfloat16) for _ in range(NB)]
+    host_x = xs[0].cpu().pin_memory()
+    out = torch.empty((PF_T, H), dtype=torch.float32, device=dev)
+    idx = torch.empty((PF_T, K), dtype=torch.int32, device=dev)
+    wt = torch.empty((PF_T, K), dtype=torch.float32, device=dev)
+    h_out = torch.empty((PF_T, H), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty((PF_T, H), dtype=torch.bfloat16, device=dev)
+    for i in range(args.warmup):
+        layer.prefill(xs[i % NB], out=out, idx=idx, wt=wt)
+    torch.cuda.synchronize()
+    # routing statistics of the measured batches
+    uniq, counts = [], torch.zeros(E, dtype=torch.int64, device=dev)
+    for b in range(NB):
+        layer.prefill(xs[b], out=out, idx=idx, wt=wt)
+        uniq.append(int(torch.unique(idx).numel()))
+        counts += torch.bincount(idx.reshape(-1).long(), minlength=E)
+    pop = (counts.double() / counts.sum()).sort(descending=True).values
+    target = k3.synth.zipf_topk_marginal(E, 1.1, K, device=dev)
+    clk = Clocks(local)
+    L.k3c_timing_enable(1)
+    ms_buf = (C.c_double * 4)()
+    n_buf = (C.c_longlong * 4)()
+    L.k3c_timing_read(ms_buf, n_buf, 4)
+    launches0 = L.k3c_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(args.steps):
+        layer.prefill(xs[i % NB], out=out, idx=idx, wt=wt)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = L.k3c_launch_count() - launches0
+    L.k3c_timing_enable(0)
+    L.k3c_timing_read(ms_buf, n_buf, 4)
+    clocks = clk.stop()
+    dt = e0.elapsed_time(e1) / 1e3
+    # end to end: pinned host tokens in, host outputs back, every step
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(args.steps):
+        x_dev.copy_(host_x, non_blocking=True)
+        layer.prefill(x_dev, out=out, idx=idx, wt=wt)
+        h_out.copy_(out, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    dte = f0.elapsed_time(f1) / 1e3
+    if rank != 0:
+        return
+    run_bytes = k3.pool_run_bytes(H, I)
+    flop = (PF_T * K + PF_T) * 2 * 3 * I * H          # routed pairs + shared expert
+    exp_s = ms_buf[0] / 1e3 / args.steps
+    wbytes = (np.mean(uniq) + 1) * run_bytes
+    hbm, bf16, kind = peaks()
+    fp4_nominal, fp8_nominal = 9000.0, 4500.0       # dense TFLOP/s, B200 datasheet
+    tflops = flop / exp_s / 1e12 if exp_s > 0 else None
+    bound_s = max(flop / (fp8_nominal * 1e12), wbytes / (hbm * 1e9))
+    print(json.dumps({
+        "metric": METRIC, "value": PF_T * args.steps / dt, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
+        "data": "synthetic",
+        "config": {"workload": PF_WORKLOAD, "tokens": PF_T, "hidden": H, "inter": I, "experts": E,
+                   "topk": K, "parallelism": "single GPU",
+                   "l2": "inputs larger than L2: ~9 GB of expert weights per step"},
+        "routing": {"unique_experts": float(np.mean(uniq)), "top1_share": float(pop[0]),
+                    "top10_share": float(pop[:10].sum()),
+                    "zipf_topk_target": {"top1": float(target[0]), "top10": float(target[:10].sum())},
+                    "l1_to_target": float((pop - target).abs().sum())},
+        "stages_ms_per_step": {name: ms_buf[j] / args.steps
+                               for j, name in enumerate(("experts", "router", "combine", "q8"))},
+        "roofline": {"bound": "tensor", "kernel": "expert stage (GU + D grouped tcgen05 kernels)",
+                     "achieved": tflops, "unit": "TFLOP/s",
+                     "useful_flop_per_step": flop, "weight_bytes_per_step": wbytes,
+                     "frac_of_fp4_dense_nominal": tflops / fp4_nominal if tflops else None,
+                     "frac_of_fp8_dense_nominal": tflops / fp8_nominal if tflops else None,
+                     "frac_of_bf16_measured": tflops / bf16 if (tflops and bf16) else None,
+                     "hbm_gbs": wbytes / exp_s / 1e9 if exp_s > 0 else None,
+                     "expert_stage_vs_bound": bound_s / exp_s if exp_s > 0 else None,
+                     "note": "activations run as 2 E4M3 terms at the FP8 MMA rate: the issued "
+                             "MMA work is 2x the useful FLOP"},
+        "e2e": {"value": PF_T * args.steps / dte, "unit": UNIT, "h2d_bytes_per_step": PF_T * H * 2,
+                "d2h_bytes_per_step": PF_T * H * 4},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -388,9 +503,13 @@ def main():
     ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
                     help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
     ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: config[1] (the headline line); prefill: config[2]")
     args = ap.parse_args()
     ws, rank, local = dist_setup(args)
-    if args.impl == "reference":
+    if args.workload == "prefill" and args.impl != "reference":
+        run_prefill(args, ws, rank, local)
+    elif args.impl == "reference":
         run_reference(args, ws, rank)
     else:
         run_ours(args, ws, rank, local)

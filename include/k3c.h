@@ -230,6 +230,18 @@ int k3c_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok,
                       const k3c_moe_pool_layer *L, int *idx, float *wt, int *drops,
                       void *scratch, size_t scratch_bytes, k3c_stream_t stream);
 
+/* MoE prefill over ntok tokens: the reference's k3_moe_prefill / moe_prefill_chunk
+ * (src/core/k3_ops.c:689-808) for the non-latent shape -- route, group the (token, expert)
+ * pairs by expert, run each expert's FFN over its group as tcgen05 block-scaled MMAs, combine
+ * in each token's top-k order (k3_ops.c:641-642) plus the shared expert. Activations enter
+ * the MMAs as two E4M3 terms per element (the layer's `terms` field is not used). Same
+ * outputs, drop counting and error behaviour as k3c_moe_decode_tc; hidden must be a multiple
+ * of 256, inter of 128, x 16-byte aligned, ntok <= 65535. */
+size_t k3c_moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int ntok);
+int k3c_moe_prefill_tc(float *out, const void *x, int x_dtype, int ntok,
+                       const k3c_moe_pool_layer *L, int *idx, float *wt, int *drops,
+                       void *scratch, size_t scratch_bytes, k3c_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

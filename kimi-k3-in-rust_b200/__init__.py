@@ -87,6 +87,8 @@ def lib():
         "k3c_pool_pack_expert": ([vp, C.POINTER(K3ExpertQ), i, i, vp], i),
         "k3c_moe_decode_tc_scratch": ([C.POINTER(MoePoolLayerC), i], sz),
         "k3c_moe_decode_tc": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
+        "k3c_moe_prefill_tc_scratch": ([C.POINTER(MoePoolLayerC), i], sz),
+        "k3c_moe_prefill_tc": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
         "k3_mxfp4_dequant": ([vp, vp, vp, i, i, i], None),
         "k3_matmul_mxfp4": ([vp, vp, vp, vp, i, i, i], None),
         "k3_matmul_q8": ([vp, vp, vp, i, i], None),
@@ -431,4 +433,28 @@ class PoolMoeLayer:
                                        C.byref(self.c), _ptr(idx), _ptr(wt), _ptr(drops),
                                        _ptr(self._scratch), self._scratch.numel(), _stream()),
                "k3c_moe_decode_tc")
+        return out, idx, wt
+
+    def prefill(self, x, out=None, idx=None, wt=None, drops=None):
+        """Prefill over ntok tokens (k3c_moe_prefill_tc): expert-sorted tokens through the
+        tcgen05 grouped expert kernels, combined in each token's top-k order."""
+        import torch
+        if x.dtype == torch.int16:
+            x = x.view(torch.bfloat16)
+        x = x.contiguous()
+        ntok = x.shape[0]
+        need = lib().k3c_moe_prefill_tc_scratch(C.byref(self.c), ntok)
+        if self._scratch.numel() < need:
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        H, K = self.c.hidden, self.c.topk
+        if out is None:
+            out = torch.empty((ntok, H), dtype=torch.float32, device=x.device)
+        if idx is None:
+            idx = torch.empty((ntok, K), dtype=torch.int32, device=x.device)
+        if wt is None:
+            wt = torch.empty((ntok, K), dtype=torch.float32, device=x.device)
+        _check(lib().k3c_moe_prefill_tc(_ptr(out), _ptr(x), _dtype_code(x), ntok,
+                                        C.byref(self.c), _ptr(idx), _ptr(wt), _ptr(drops),
+                                        _ptr(self._scratch), self._scratch.numel(), _stream()),
+               "k3c_moe_prefill_tc")
         return out, idx, wt

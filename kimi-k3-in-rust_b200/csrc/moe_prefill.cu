@@ -1,0 +1,656 @@
+// moe_prefill.cu -- MoE prefill on the tcgen05 tensor cores: the reference's
+// k3_moe_prefill / moe_prefill_chunk (src/core/k3_ops.c:689-808) for the non-latent BASELINE
+// shape: route every token, group the (token, expert) pairs by expert, run each expert's
+// SwiGLU FFN over its group, and combine the outputs in each token's top-k order.
+//
+// Layout of the work:
+//   pairs   T*topk (token, k) pairs are counting-sorted by expert (stable: pair index order
+//           within an expert). Rows: expert e's pairs occupy compact rows [eoff_e, eoff_e+n_e),
+//           the shared expert's T rows follow; slots of up to 128 consecutive rows, one
+//           expert owning ceil(n_e/128) of them.
+//   x       each row's token is quantised into J = 2 E4M3 terms per element with one UE8M0
+//           scale per 32 elements (the decode path's term split), in row order, so a slot's
+//           A tile is one TMA box of 128 rows starting at its first row. Rows past the slot's
+//           pairs belong to the next slot: they only feed accumulator rows that are never read.
+//   GU      per work item (slot, 256 gate/up rows): the slot's 128 pair rows are the MMA's M
+//           side, 256 pool-format gate/up weight rows are N. Both terms accumulate into one
+//           TMEM accumulator (each MMA applies its own block scales). The epilogue (one thread
+//           per pair row) forms SwiGLU for 128 intermediate columns and requantises each
+//           32-column block, which lies inside one thread, into the down stage's operand
+//           (same compact rows).
+//   D       per work item (slot, 256 hidden rows): the same MMA over the requantised
+//           activations; the epilogue writes each pair's unweighted expert output.
+//   combine the decode path's fixed-order weighted sum (k3_ops.c:641-642) plus the shared
+//           expert.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdlib.h>
+
+#include "common.cuh"
+#include "pool_common.cuh"
+#include "tc_common.cuh"
+#include "tc_host.cuh"
+
+namespace k3c {
+
+int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
+                  const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
+                  int ntok, double *part, cudaStream_t s);
+size_t router_scratch_bytes(int hidden, int n_experts, int ntok);
+int launch_moe_combine(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
+                       int ntok, int topk, int hidden, int has_shared, cudaStream_t s);
+
+namespace {
+constexpr int PF_J = 2;                       // E4M3 terms per activation
+constexpr int PF_M = 128;                     // pair rows per slot (MMA M)
+constexpr int PF_N = 256;                     // weight rows per work item (MMA N)
+constexpr int PF_CHUNK = 1024;                // pairs per planning block
+constexpr int PF_A = PF_M * 128;              // one term's A tile: 16 KB
+constexpr int PF_B = PF_N * 128;              // padded E2M1 B tile: 32 KB
+constexpr int PF_SF = (PF_J + 2) * 512;       // SFA per term + two SFB atoms
+constexpr int PF_STAGE = PF_J * PF_A + PF_B + PF_SF;
+constexpr int PF_STAGES = 3;
+constexpr int PF_THREADS = 192;
+constexpr int PF_BYTES = 1024 + PF_STAGES * PF_STAGE + PF_M * 4 + 256;
+constexpr uint32_t PF_TMEM = 512;             // accumulator 256 columns + scale factors
+constexpr uint32_t PF_SF_COL = 256;
+constexpr uint32_t PF_TX = PF_J * PF_A + PF_N * 64 + PF_SF;   // E2M1 moves 4 bits per element
+static_assert(PF_STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
+}  // namespace
+
+struct SlotPf {
+    int run, ntok, row0;   // pool run, pairs in the slot, first compact row
+};
+
+// ------------------------------------------------------------------ planning
+// Per chunk of 1024 pairs: the pair's expert (-1 when the expert is not resident, counted as
+// a drop), the chunk's per-expert counts, and each pair's rank among the chunk's earlier
+// pairs of the same expert.
+__global__ void __launch_bounds__(1024) k_pf_count(int *__restrict__ pe_out, int *__restrict__ rank_out,
+                                                   int *__restrict__ cnt, uint8_t *__restrict__ dropped,
+                                                   int *__restrict__ drops, const int *__restrict__ idx, int P,
+                                                   const int *__restrict__ run_of, int n_experts, int n_runs) {
+    extern __shared__ int pfs[];
+    int *hist = pfs, *pe = pfs + n_experts;
+    const int i0 = blockIdx.x * PF_CHUNK, n = min(PF_CHUNK, P - i0);
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+    const int i = threadIdx.x;
+    int e = -1;
+    if (i < n) {
+        e = idx[i0 + i];
+        // a run index outside the arena is treated as not resident: the kernels form raw
+        // addresses from it
+        const bool ok = e >= 0 && e < n_experts && run_of[e] >= 0 && run_of[e] < n_runs;
+        dropped[i0 + i] = ok ? 0 : 1;
+        if (ok) atomicAdd(&hist[e], 1);
+        else {
+            if (drops) atomicAdd(drops, 1);
+            e = -1;
+        }
+        pe_out[i0 + i] = e;
+    }
+    pe[i] = e;
+    __syncthreads();
+    if (i < n && e >= 0) {
+        int r = 0;
+        for (int k = 0; k < i; k++) r += pe[k] == e;
+        rank_out[i0 + i] = r;
+    }
+    for (int x = threadIdx.x; x < n_experts; x += blockDim.x) cnt[(size_t)blockIdx.x * n_experts + x] = hist[x];
+}
+
+// Block-wide exclusive prefix sums of (a, b) over the threads' values; *ta, *tb get the totals.
+__device__ __forceinline__ void block_scan2(int a, int b, int &xa, int &xb, int &ta, int &tb, int2 *warp_sum) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+    int ia = a, ib = b;   // inclusive warp scans
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int va = __shfl_up_sync(0xffffffffu, ia, o), vb = __shfl_up_sync(0xffffffffu, ib, o);
+        if (lane >= o) {
+            ia += va;
+            ib += vb;
+        }
+    }
+    if (lane == 31) warp_sum[warp] = make_int2(ia, ib);
+    __syncthreads();
+    int pa = 0, pb = 0;
+    ta = tb = 0;
+    for (int w = 0; w < nwarp; w++) {
+        const int2 v = warp_sum[w];
+        if (w < warp) {
+            pa += v.x;
+            pb += v.y;
+        }
+        ta += v.x;
+        tb += v.y;
+    }
+    xa = pa + ia - a;
+    xb = pb + ib - b;
+    __syncthreads();   // warp_sum may be rewritten by the caller's next scan
+}
+
+// One block: each expert's per-chunk bases, its first compact row (eoff) and first slot
+// (slot_base) by block-wide prefix sums of n_e and ceil(n_e/128), the slot table, and the
+// shared expert's rows and slots after all routed pairs.
+__global__ void __launch_bounds__(1024) k_pf_slots(int *__restrict__ n_slots, SlotPf *__restrict__ slots,
+                                                   int *__restrict__ pair_tok, int *__restrict__ pair_k,
+                                                   int *__restrict__ row_tok, int *__restrict__ n_rows,
+                                                   int *__restrict__ chunk_base, int *__restrict__ slot_base,
+                                                   int *__restrict__ eoff, const int *__restrict__ cnt,
+                                                   int nchunk, const int *__restrict__ run_of, int n_experts,
+                                                   int T, int topk, int shared_run) {
+    __shared__ int2 warp_sum[32];
+    int sbase = 0, rbase = 0;
+    for (int e0 = 0; e0 < n_experts; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        int ne = 0;
+        if (e < n_experts)
+            for (int c = 0; c < nchunk; c++) {
+                chunk_base[(size_t)c * n_experts + e] = ne;
+                ne += cnt[(size_t)c * n_experts + e];
+            }
+        const int nsl = (ne + PF_M - 1) / PF_M;
+        int xs, xr, ts, tr;
+        block_scan2(nsl, ne, xs, xr, ts, tr, warp_sum);
+        if (e < n_experts) {
+            slot_base[e] = sbase + xs;
+            eoff[e] = rbase + xr;
+            for (int q = 0; q < nsl; q++) {
+                SlotPf &sl = slots[sbase + xs + q];
+                sl.run = run_of[e];
+                sl.ntok = min(PF_M, ne - PF_M * q);
+                sl.row0 = rbase + xr + PF_M * q;
+            }
+        }
+        sbase += ts;
+        rbase += tr;
+    }
+    if (shared_run >= 0) {
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            const size_t pos = (size_t)(sbase + t / PF_M) * PF_M + t % PF_M;
+            pair_tok[pos] = t;
+            pair_k[pos] = topk;
+            row_tok[rbase + t] = t;
+        }
+        const int nsh = (T + PF_M - 1) / PF_M;
+        for (int q = threadIdx.x; q < nsh; q += blockDim.x) {
+            slots[sbase + q].run = shared_run;
+            slots[sbase + q].ntok = min(PF_M, T - PF_M * q);
+            slots[sbase + q].row0 = rbase + PF_M * q;
+        }
+        sbase += nsh;
+        rbase += T;
+    }
+    if (threadIdx.x == 0) {
+        *n_slots = sbase;
+        *n_rows = rbase;
+    }
+}
+
+// Pair i of expert e goes to row r % 128 of slot slot_base[e] + r / 128, r its rank among all
+// pairs of e (chunk base + rank within the chunk).
+__global__ void __launch_bounds__(1024) k_pf_scatter(int *__restrict__ pair_tok, int *__restrict__ pair_k,
+                                                     int *__restrict__ row_tok, const int *__restrict__ pe,
+                                                     const int *__restrict__ rank, const int *__restrict__ chunk_base,
+                                                     const int *__restrict__ slot_base, const int *__restrict__ eoff,
+                                                     int P, int n_experts, int topk) {
+    const int i = blockIdx.x * PF_CHUNK + threadIdx.x;
+    if (i >= P) return;
+    const int e = pe[i];
+    if (e < 0) return;
+    const int r = chunk_base[(size_t)blockIdx.x * n_experts + e] + rank[i];
+    const size_t pos = (size_t)(slot_base[e] + r / PF_M) * PF_M + r % PF_M;
+    pair_tok[pos] = i / topk;
+    pair_k[pos] = i % topk;
+    row_tok[eoff[e] + r] = i / topk;
+}
+
+// Row r of the A operand: the J terms of token row_tok[r], xq [J][rows][H], and their block
+// scales xsf [J][rows][H/32]. One thread per 32-element block.
+
+// Scale atoms of the A operand per slot: sfa [slot][J][H/128][512] from the row-major scales
+// (rows past the last row repeat the slot's first row; their products are never read).
+__global__ void __launch_bounds__(256) k_pf_slot_sf(uint8_t *__restrict__ sfa, const uint8_t *__restrict__ xsf,
+                                                    const int *__restrict__ n_slots, const SlotPf *__restrict__ slots,
+                                                    const int *__restrict__ n_rows, int rows_cap, int H) {
+    const int s = blockIdx.x, j = blockIdx.y;
+    if (s >= *n_slots) return;
+    const int KT = H / 128, row0 = slots[s].row0, nr = *n_rows;
+    for (int i = threadIdx.x; i < PF_M * KT; i += blockDim.x) {
+        const int m = i % PF_M, kt = i / PF_M;
+        const int r = row0 + m < nr ? row0 + m : row0;
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(xsf + ((size_t)j * rows_cap + r) * (H / 32) + 4 * kt);
+        *reinterpret_cast<uint32_t *>(sfa + (((size_t)s * PF_J + j) * KT + kt) * 512 + 16 * (m % 32) + 4 * (m / 32)) = w;
+    }
+}
+
+// ------------------------------------------------------------------ persistent tcgen05 kernel
+struct PfArgs {
+    const int *n_slots;
+    const SlotPf *slots;
+    const int *pair_tok, *pair_k;
+    const uint8_t *arena;
+    size_t run_stride;
+    const uint8_t *sfa;       // A scale atoms [slot][J][KT][512]
+    uint8_t *act_q;           // GU out: [J][rows_cap][I] E4M3, compact rows
+    uint8_t *act_sf;          // GU out: [slot][J][I/128][512]
+    float *contrib;           // D out: [T][topk+1][H]
+    int kstride, T, H, I, act, rows_cap;
+    int *err;
+};
+
+// 32 values of one thread -> J E4M3 terms (32 bytes each) and J UE8M0 scales, the split of
+// quantize_block with the block held by one thread.
+__device__ __forceinline__ void quant_row32(float (&a)[32], uint4 (&q)[PF_J][2], uint32_t (&sf)[PF_J]) {
+#pragma unroll
+    for (int j = 0; j < PF_J; j++) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(a[i]));
+        const int e = block_exp(amax);
+        sf[j] = (uint32_t)(e + 127);
+        const float inv = exp2i(-e);
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) w[i] = 0u;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const uint32_t b = tc::f32_to_e4m3(a[i] * inv);
+            w[i >> 2] |= b << (8 * (i & 3));
+            const float back = tc::e4m3_to_f32(b);
+            a[i] = a[i] - (e >= -126 ? back * exp2i(e) : (back * exp2i(-126)) * 0.5f);
+        }
+        q[j][0] = make_uint4(w[0], w[1], w[2], w[3]);
+        q[j][1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
+// Row r of the A operand: the J terms of token row_tok[r], xq [J][rows_cap][H], and their
+// block scales xsf [J][rows_cap][H/32]. One thread per 32-element block.
+template <typename XT>
+__global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq, uint8_t *__restrict__ xsf,
+                                                       const XT *__restrict__ x, const int *__restrict__ row_tok,
+                                                       const int *__restrict__ n_rows, int rows_cap, int H) {
+    const int nb = H / 32;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = (int)(i / nb), blk = (int)(i % nb);
+    if (r >= *n_rows) return;
+    const XT *src = x + (size_t)row_tok[r] * H + blk * 32;
+    float a[32];
+    if constexpr (sizeof(XT) == 2) {
+#pragma unroll
+        for (int v = 0; v < 4; v++) {
+            const uint4 u = reinterpret_cast<const uint4 *>(src)[v];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                a[8 * v + 2 * h] = __uint_as_float(w[h] << 16);
+                a[8 * v + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int v = 0; v < 8; v++) {
+            const float4 f = reinterpret_cast<const float4 *>(src)[v];
+            a[4 * v] = f.x;
+            a[4 * v + 1] = f.y;
+            a[4 * v + 2] = f.z;
+            a[4 * v + 3] = f.w;
+        }
+    }
+    uint4 q[PF_J][2];
+    uint32_t sf[PF_J];
+    quant_row32(a, q, sf);
+#pragma unroll
+    for (int j = 0; j < PF_J; j++) {
+        uint4 *d = reinterpret_cast<uint4 *>(xq + ((size_t)j * rows_cap + r) * H + blk * 32);
+        d[0] = q[j][0];
+        d[1] = q[j][1];
+        xsf[((size_t)j * rows_cap + r) * nb + blk] = (uint8_t)sf[j];
+    }
+}
+
+template <bool GU>
+__global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ CUtensorMap tmA,
+                                                       const __grid_constant__ CUtensorMap tmW, PfArgs p) {
+    extern __shared__ uint8_t pf_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pf_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PF_STAGES * PF_STAGE);
+    uint64_t *full = bars, *empty = bars + PF_STAGES, *tfull = bars + 2 * PF_STAGES, *tempty = tfull + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PF_STAGES; i++) {
+            tc::mbar_init(&full[i], 1);
+            tc::mbar_init(&empty[i], 1);
+        }
+        tc::mbar_init(tfull, 1);
+        tc::mbar_init(tempty, 4);
+        tc::fence_mbar_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, PF_TMEM);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int n_slots = *p.n_slots;
+    const int KT = GU ? p.H / 128 : p.I / 128;           // K tiles per item
+    const int NTL = GU ? (2 * p.I) / PF_N : p.H / PF_N;  // N tiles per slot
+    const int n_items = n_slots * NTL;
+    const PoolGeom g = pool_geom(p.H, p.I);
+    const size_t sf_off = GU ? g.gu_s : g.d_s;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            bool ok = tc::tc_check((tc::smem_u32(smem) & 1023) == 0, p.err, 40);
+            tc::prefetch_tmap(&tmA);
+            tc::prefetch_tmap(&tmW);
+            uint32_t kiter = 0;
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+                const int s = it / NTL, nt = it % NTL;
+                const SlotPf sl = p.slots[s];
+                const uint8_t *wsf = p.arena + (size_t)sl.run * p.run_stride + sf_off;
+                for (int kt = 0; kt < KT; kt++, kiter++) {
+                    const int st = kiter % PF_STAGES;
+                    const uint32_t ph = (kiter / PF_STAGES) & 1u;
+                    if (kiter >= PF_STAGES && !tc::mbar_wait(&empty[st], ph ^ 1u, p.err, 41)) { ok = false; break; }
+                    uint8_t *sa = smem + st * PF_STAGE;
+                    uint8_t *sb = sa + PF_J * PF_A;
+                    uint8_t *ssf = sb + PF_B;
+                    tc::mbar_expect_tx(&full[st], PF_TX);
+#pragma unroll
+                    for (int j = 0; j < PF_J; j++) {
+                        tc::tma_load_3d(sa + j * PF_A, &tmA, &full[st], kt * 128, sl.row0, j);
+                        tc::bulk_load(ssf + j * 512, p.sfa + (((size_t)s * PF_J + j) * KT + kt) * 512, 512, &full[st]);
+                    }
+                    tc::tma_load_3d(sb, &tmW, &full[st], kt * 128, nt * PF_N, sl.run);
+                    tc::bulk_load(ssf + PF_J * 512, wsf + ((size_t)(2 * nt) * KT + kt) * 512, 512, &full[st]);
+                    tc::bulk_load(ssf + (PF_J + 1) * 512, wsf + ((size_t)(2 * nt + 1) * KT + kt) * 512, 512, &full[st]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            uint32_t kiter = 0, li = 0;
+            bool ok = true;
+            const uint32_t idesc0 = tc::idesc_mxf8f6f4(tc::FMT_E4M3, tc::FMT_E2M1, PF_N, 0, 0);
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, li++) {
+                if (li >= 1 && !tc::mbar_wait(tempty, (li - 1) & 1u, p.err, 44)) { ok = false; break; }
+                tc::tc_fence_after();
+                for (int kt = 0; kt < KT; kt++, kiter++) {
+                    const int st = kiter % PF_STAGES;
+                    const uint32_t ph = (kiter / PF_STAGES) & 1u;
+                    if (!tc::mbar_wait(&full[st], ph, p.err, 42)) { ok = false; break; }
+                    tc::tc_fence_after();
+                    uint8_t *sa = smem + st * PF_STAGE;
+                    uint8_t *sb = sa + PF_J * PF_A;
+                    uint8_t *ssf = sb + PF_B;
+                    const uint32_t sfc = tmem + PF_SF_COL + 16u * (kiter & 1u);
+#pragma unroll
+                    for (int j = 0; j < PF_J; j++) tc::tc_cp_sf(sfc + 4 * j, tc::desc_sf_atom(tc::smem_u32(ssf + j * 512)));
+                    tc::tc_cp_sf(sfc + 8, tc::desc_sf_atom(tc::smem_u32(ssf + PF_J * 512)));
+                    tc::tc_cp_sf(sfc + 12, tc::desc_sf_atom(tc::smem_u32(ssf + (PF_J + 1) * 512)));
+#pragma unroll
+                    for (int kb = 0; kb < 4; kb++) {
+                        const uint64_t db = tc::desc_kmajor_sw128(tc::smem_u32(sb) + 32 * kb);
+                        const uint32_t id = idesc0 | ((uint32_t)kb << 4) | ((uint32_t)kb << 29);
+#pragma unroll
+                        for (int j = 0; j < PF_J; j++) {
+                            const uint64_t da = tc::desc_kmajor_sw128(tc::smem_u32(sa + j * PF_A) + 32 * kb);
+                            tc::tc_mma_mx(tmem, da, db, id, (sfc + 4 * j) | ((uint32_t)kb << 30),
+                                          (sfc + 8) | ((uint32_t)kb << 30), (kt | kb | j) != 0);
+                        }
+                    }
+                    tc::tc_commit(&empty[st]);
+                }
+                if (ok) tc::tc_commit(tfull);
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int q = warp & 3;                 // TMEM lane quadrant
+        const int m = 32 * q + lane;            // pair row of the slot
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        uint32_t li = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, li++) {
+            const int s = it / NTL, nt = it % NTL;
+            const bool ok = *(volatile int *)p.err == 0 && tc::mbar_wait(tfull, li & 1u, p.err, 43);
+            __syncwarp();
+            tc::tc_fence_after();
+            const SlotPf sl = p.slots[s];
+            if (GU) {
+                const int KTd = p.I / 128;
+#pragma unroll 1
+                for (int c = 0; c < 4; c++) {
+                    // gate columns of intermediate block c and the matching up columns
+                    const uint32_t gcol = 128u * (c >> 1) + 32u * (c & 1);
+                    uint32_t vg[32], vu[32];
+                    tc::tmem_ld32(tmem + lane_base + gcol, vg);
+                    tc::tmem_ld32(tmem + lane_base + gcol + 64, vu);
+                    tc::tmem_ld_wait();
+                    if (!ok) continue;
+                    float a[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) a[i] = act_apply(__uint_as_float(vg[i]), __uint_as_float(vu[i]), p.act);
+                    uint4 qv[PF_J][2];
+                    uint32_t sf[PF_J];
+                    quant_row32(a, qv, sf);
+                    if (m >= sl.ntok) continue;   // that row belongs to the next slot
+                    const int col = 128 * nt + 64 * (c >> 1) + 32 * (c & 1);   // intermediate index
+#pragma unroll
+                    for (int j = 0; j < PF_J; j++) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(p.act_q + ((size_t)j * p.rows_cap + sl.row0 + m) * p.I + col);
+                        dst[0] = qv[j][0];
+                        dst[1] = qv[j][1];
+                        p.act_sf[(((size_t)s * PF_J + j) * KTd + col / 128) * 512 + atom_byte(m, (col % 128) / 32)] =
+                            (uint8_t)sf[j];
+                    }
+                }
+            } else {
+                float *dst = nullptr;
+                if (ok && m < sl.ntok) {
+                    const size_t pr = (size_t)s * PF_M + m;
+                    dst = p.contrib + ((size_t)p.pair_tok[pr] * p.kstride + p.pair_k[pr]) * p.H + (size_t)nt * PF_N;
+                }
+#pragma unroll 1
+                for (int c = 0; c < PF_N / 32; c++) {
+                    uint32_t v[32];
+                    tc::tmem_ld32(tmem + lane_base + 32u * c, v);
+                    tc::tmem_ld_wait();
+                    if (dst) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst + 32 * c);
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                                __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(tempty);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) tc::tmem_dealloc(tmem, PF_TMEM);
+}
+
+// ------------------------------------------------------------------ host side
+struct PfBufs {
+    int *idx, *pe, *rank, *cnt, *chunk_base, *slot_base, *eoff, *n_slots, *n_rows, *err, *pair_tok, *pair_k,
+        *row_tok;
+    float *wt, *contrib;
+    double *rpart;
+    uint8_t *dropped, *xq, *xsf, *sfa_x, *actq, *actsf;
+    SlotPf *slots;
+    int max_slots, nchunk, rows_cap;
+};
+
+static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
+    const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->topk;
+    const size_t P = (size_t)T * K;
+    b.nchunk = (int)((P + PF_CHUNK - 1) / PF_CHUNK);
+    b.max_slots = (int)((P + PF_M - 1) / PF_M) + E + (T + PF_M - 1) / PF_M + 1;
+    b.rows_cap = (int)P + T;
+    b.idx = cv.take<int>(P);
+    b.wt = cv.take<float>(P);
+    b.rpart = cv.take<double>(router_scratch_bytes(H, E, T) / sizeof(double));
+    b.pe = cv.take<int>(P);
+    b.rank = cv.take<int>(P);
+    b.dropped = cv.take<uint8_t>(P);
+    b.cnt = cv.take<int>((size_t)b.nchunk * E);
+    b.chunk_base = cv.take<int>((size_t)b.nchunk * E);
+    b.slot_base = cv.take<int>(E);
+    b.eoff = cv.take<int>(E);
+    b.n_slots = cv.take<int>(1);
+    b.n_rows = cv.take<int>(1);
+    b.err = cv.take<int>(1);
+    b.slots = cv.take<SlotPf>(b.max_slots);
+    b.pair_tok = cv.take<int>((size_t)b.max_slots * PF_M);
+    b.pair_k = cv.take<int>((size_t)b.max_slots * PF_M);
+    b.row_tok = cv.take<int>(b.rows_cap);
+    b.xq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * H, 1024);
+    b.xsf = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * (H / 32));
+    b.sfa_x = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (H / 128) * 512);
+    b.actq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * I, 1024);
+    b.actsf = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (I / 128) * 512);
+    b.contrib = cv.take<float>((size_t)T * (K + 1) * H);
+    return b.idx && b.wt && b.rpart && b.pe && b.rank && b.dropped && b.cnt && b.chunk_base && b.slot_base &&
+           b.eoff && b.n_slots && b.n_rows && b.err && b.slots && b.pair_tok && b.pair_k && b.row_tok && b.xq &&
+           b.xsf && b.sfa_x && b.actq && b.actsf && b.contrib;
+}
+
+static char *const kPfSizing = reinterpret_cast<char *>(4096);
+
+size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T) {
+    if (!L || T <= 0) return 0;
+    Carve cv{kPfSizing, (size_t)-1 / 2, 0};
+    PfBufs b;
+    carve_pf(cv, b, L, T);
+    return cv.used + 1024;
+}
+
+int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k3c_moe_pool_layer *L,
+                          int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
+                          cudaStream_t s) {
+    if (!L) return set_error(K3C_EINVAL, "moe_prefill_tc: null layer");
+    const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->topk;
+    if (H <= 0 || I <= 0 || H % PF_N || I % 128)
+        return set_error(K3C_EINVAL, "moe_prefill_tc: hidden=%d must be a multiple of 256, inter=%d of 128", H, I);
+    if (T <= 0) return K3C_OK;
+    if (K <= 0 || K > K3_MAX_TOPK || K > E) return set_error(K3C_EINVAL, "moe_prefill_tc: topk=%d", K);
+    if (T > 65535 || ((long long)T * K + T) * H > (1LL << 40) || (long long)T * K + T > (1LL << 30))
+        return set_error(K3C_EINVAL, "moe_prefill_tc: ntok=%d too large", T);
+    if (x_dtype != K3C_BF16 && x_dtype != K3C_F32) return set_error(K3C_EINVAL, "moe_prefill_tc: x_dtype=%d", x_dtype);
+    if (((uintptr_t)x & 15) != 0) return set_error(K3C_EINVAL, "moe_prefill_tc: x must be 16-byte aligned");
+    if (!L->arena || !L->run_of || L->n_runs <= 0 || L->run_stride % 256 ||
+        L->run_stride < pool_geom(H, I).run || ((uintptr_t)L->arena & 255) || L->shared_run >= L->n_runs)
+        return set_error(K3C_EINVAL, "moe_prefill_tc: bad arena");
+    Carve cv{(char *)scratch, scratch_bytes, 0};
+    PfBufs b;
+    if (!carve_pf(cv, b, L, T)) return set_error(K3C_EINVAL, "moe_prefill_tc: scratch too small (%zu)", scratch_bytes);
+    int *idx = idx_out ? idx_out : b.idx;
+    float *wt = wt_out ? wt_out : b.wt;
+    const int P = T * K;
+    K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), s));
+    // scale atoms of rows past a slot's pairs stay 2^0 (never NaN)
+    K3C_TRY_CUDA(cudaMemsetAsync(b.actsf, 127, (size_t)b.max_slots * PF_J * (I / 128) * 512, s));
+    stage_begin(STAGE_ROUTER, s);
+    K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, H, E, K,
+                          L->renorm, L->routed_scale, T, b.rpart, s));
+    stage_end(STAGE_ROUTER, s);
+    // plan: counting sort of the pairs by expert
+    const size_t csmem = ((size_t)E + PF_CHUNK) * sizeof(int);
+    if (csmem > 48 * 1024) K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem));
+    k_pf_count<<<b.nchunk, PF_CHUNK, csmem, s>>>(b.pe, b.rank, b.cnt, b.dropped, drops, idx, P, L->run_of, E, L->n_runs);
+    K3C_CHECK_LAUNCH();
+    k_pf_slots<<<1, 1024, 0, s>>>(b.n_slots, b.slots, b.pair_tok, b.pair_k, b.row_tok, b.n_rows, b.chunk_base,
+                                  b.slot_base, b.eoff, b.cnt, b.nchunk, L->run_of, E, T, K, L->shared_run);
+    K3C_CHECK_LAUNCH();
+    k_pf_scatter<<<b.nchunk, PF_CHUNK, 0, s>>>(b.pair_tok, b.pair_k, b.row_tok, b.pe, b.rank, b.chunk_base,
+                                               b.slot_base, b.eoff, P, E, K);
+    K3C_CHECK_LAUNCH();
+    // activations of every compact row, then each slot's scale atoms
+    const size_t nthr = (size_t)b.rows_cap * (H / 32);
+    const unsigned qblocks = (unsigned)((nthr + 255) / 256);
+    if (x_dtype == K3C_BF16)
+        k_pf_quant_rows<uint16_t><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, (const uint16_t *)x, b.row_tok, b.n_rows, b.rows_cap, H);
+    else
+        k_pf_quant_rows<float><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, (const float *)x, b.row_tok, b.n_rows, b.rows_cap, H);
+    K3C_CHECK_LAUNCH();
+    k_pf_slot_sf<<<dim3(b.max_slots, PF_J), 256, 0, s>>>(b.sfa_x, b.xsf, b.n_slots, b.slots, b.n_rows, b.rows_cap, H);
+    K3C_CHECK_LAUNCH();
+    // experts
+    const PoolGeom g = pool_geom(H, I);
+    CUtensorMap tmX, tmGU, tmAct, tmD;
+    K3C_TRY(make_map3(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.xq, H, b.rows_cap, PF_J, H, (uint64_t)b.rows_cap * H, 128,
+                      PF_M));
+    K3C_TRY(make_map3(&tmGU, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->arena + g.gu_p, H, 2 * I, L->n_runs, H / 2,
+                      L->run_stride, 128, PF_N));
+    K3C_TRY(make_map3(&tmAct, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.actq, I, b.rows_cap, PF_J, I, (uint64_t)b.rows_cap * I,
+                      128, PF_M));
+    K3C_TRY(make_map3(&tmD, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->arena + g.d_p, I, H, L->n_runs, I / 2,
+                      L->run_stride, 128, PF_N));
+    PfArgs a;
+    a.n_slots = b.n_slots;
+    a.slots = b.slots;
+    a.pair_tok = b.pair_tok;
+    a.pair_k = b.pair_k;
+    a.arena = L->arena;
+    a.run_stride = L->run_stride;
+    a.act_q = b.actq;
+    a.act_sf = b.actsf;
+    a.contrib = b.contrib;
+    a.kstride = K + 1;
+    a.T = T;
+    a.H = H;
+    a.I = I;
+    a.act = L->act;
+    a.rows_cap = b.rows_cap;
+    a.err = b.err;
+    K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_moe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_BYTES));
+    K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_moe<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_BYTES));
+    const int grid = sm_count();
+    stage_begin(STAGE_EXPERTS, s);
+    a.sfa = b.sfa_x;
+    k_pf_moe<true><<<grid, PF_THREADS, PF_BYTES, s>>>(tmX, tmGU, a);
+    K3C_CHECK_LAUNCH();
+    a.sfa = b.actsf;
+    k_pf_moe<false><<<grid, PF_THREADS, PF_BYTES, s>>>(tmAct, tmD, a);
+    K3C_CHECK_LAUNCH();
+    stage_end(STAGE_EXPERTS, s);
+    stage_begin(STAGE_COMBINE, s);
+    K3C_TRY(launch_moe_combine(out, b.contrib, wt, b.dropped, T, K, H, L->shared_run >= 0 ? 1 : 0, s));
+    stage_end(STAGE_COMBINE, s);
+    // K3C_SYNC_CHECK=1: synchronise and report the kernels' own error code (a bounded wait
+    // that gave up, or a failed alignment self-check). Off by default: it costs a host sync.
+    static const int sync_check = getenv("K3C_SYNC_CHECK") ? 1 : 0;
+    if (sync_check) {
+        int code = 0;
+        K3C_TRY_CUDA(cudaMemcpyAsync(&code, b.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+        K3C_TRY_CUDA(cudaStreamSynchronize(s));
+        if (code) return set_error(K3C_ETIMEOUT, "moe_prefill_tc: device check code %d", code);
+    }
+    return K3C_OK;
+}
+
+}  // namespace k3c
+
+extern "C" size_t k3c_moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int ntok) {
+    return k3c::moe_prefill_tc_scratch(L, ntok);
+}
+
+extern "C" int k3c_moe_prefill_tc(float *out, const void *x, int x_dtype, int ntok, const k3c_moe_pool_layer *L,
+                                  int *idx, float *wt, int *drops, void *scratch, size_t scratch_bytes,
+                                  k3c_stream_t stream) {
+    k3c::clear_error();
+    return k3c::launch_moe_prefill_tc(out, x, x_dtype, ntok, L, idx, wt, drops, scratch, scratch_bytes,
+                                      (cudaStream_t)stream);
+}

@@ -127,15 +127,24 @@ struct WSlice {
 template <typename WT, typename XT, int NT>
 __global__ void __launch_bounds__(256) k_router_partial(double *__restrict__ part, const XT *__restrict__ x,
                                                         const WT *__restrict__ W, int hidden, int n_experts,
-                                                        int ntok, int vec_w, int vec_x) {
+                                                        int ntok, int vec_w, int vec_x, int cpb) {
     extern __shared__ __align__(16) double rsm[];   // xs [RT_KC][NT], then red [8][NT][32]
     double *xs = rsm;
     double *red = rsm + RT_KC * NT;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     grid_dep_launch();   // the select kernel may be scheduled; it waits for this grid's end
     grid_dep_wait();     // x may come from the previous kernel
-    const int k0 = blockIdx.y * RT_KC, kn = min(RT_KC, hidden - k0);
     const int t0 = blockIdx.z * NT, nt = min(NT, ntok - t0);
+    const int e = blockIdx.x * 32 + lane;
+    double acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; t++) acc[t] = 0.0;
+    // this block adds chunks [cpb*y, cpb*y + cpb) in order
+    const int nchunk = (hidden + RT_KC - 1) / RT_KC;
+    const int c_end = min(nchunk, (int)(blockIdx.y + 1) * cpb);
+    for (int c = blockIdx.y * cpb; c < c_end; c++) {
+    const int k0 = c * RT_KC, kn = min(RT_KC, hidden - k0);
+    if (c > blockIdx.y * cpb) __syncthreads();   // every warp is done with the previous chunk
     // consecutive threads take consecutive tokens, so stores of one k row are contiguous
 #pragma unroll 4
     for (int i = threadIdx.x; i < NT * (RT_KC / 8); i += 256) {
@@ -149,12 +158,8 @@ __global__ void __launch_bounds__(256) k_router_partial(double *__restrict__ par
         for (int q = 0; q < 8; q++) xs[(kk + q) * NT + t] = (double)v[q];
     }
     __syncthreads();
-    const int e = blockIdx.x * 32 + lane;
     const int kw = warp * RT_KW, kwn = min(RT_KW, kn - kw);   // this warp's slice
     const WT *row = W + (size_t)(e < n_experts ? e : 0) * hidden + k0 + kw;
-    double acc[NT];
-#pragma unroll
-    for (int t = 0; t < NT; t++) acc[t] = 0.0;
     // acc[t] += w[0..8) . x[kw+k .. kw+k+8)[t]
     auto step = [&](const double (&w)[8], int k) {
 #pragma unroll
@@ -188,6 +193,7 @@ __global__ void __launch_bounds__(256) k_router_partial(double *__restrict__ par
             load_w8<WT>(row, k, kwn, vec_w != 0, w);
             step(w, k);
         }
+    }
     }
 #pragma unroll
     for (int t = 0; t < NT; t++) red[(warp * NT + t) * 32 + lane] = acc[t];
@@ -337,8 +343,34 @@ int launch_router_select(int *idx, float *w, const float *scores, const float *b
                          routed_scale, ntok, s);
 }
 
+static int sm_count_rt() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+static int router_nparts(int hidden, int n_experts, int ntok);
+
 size_t router_scratch_bytes(int hidden, int n_experts, int ntok) {
-    return (size_t)((hidden + RT_KC - 1) / RT_KC) * ntok * n_experts * sizeof(double);
+    return (size_t)router_nparts(hidden, n_experts, ntok) * ntok * n_experts * sizeof(double);
+}
+
+// K chunks per block: 1 (most parallel) unless the grid would exceed about three waves,
+// in which case blocks take several chunks and the partial array shrinks accordingly.
+static int router_cpb(int hidden, int n_experts, int ntok) {
+    const int nchunk = (hidden + RT_KC - 1) / RT_KC;
+    const long long blocks = (long long)((n_experts + 31) / 32) * nchunk * ((ntok + 15) / 16);
+    const long long cap = 3LL * 3 * sm_count_rt();
+    int cpb = (int)((blocks + cap - 1) / cap);
+    return cpb < 1 ? 1 : (cpb > nchunk ? nchunk : cpb);
+}
+static int router_nparts(int hidden, int n_experts, int ntok) {
+    const int nchunk = (hidden + RT_KC - 1) / RT_KC, cpb = router_cpb(hidden, n_experts, ntok);
+    return (nchunk + cpb - 1) / cpb;
 }
 
 template <typename WT, typename XT, int NT>
@@ -347,10 +379,11 @@ static int launch_partial_nt(double *part, const void *x, const void *W, int hid
     const int smem = (RT_KC * NT + 8 * NT * 32) * (int)sizeof(double);
     if (smem > 48 * 1024)
         K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_partial<WT, XT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const dim3 grid((n_experts + 31) / 32, (hidden + RT_KC - 1) / RT_KC, (ntok + NT - 1) / NT);
+    const int cpb = router_cpb(hidden, n_experts, ntok);
+    const dim3 grid((n_experts + 31) / 32, router_nparts(hidden, n_experts, ntok), (ntok + NT - 1) / NT);
     count_launch();
     K3C_TRY_CUDA(launch_pdl(k_router_partial<WT, XT, NT>, grid, dim3(256), smem, s, part, (const XT *)x,
-                            (const WT *)W, hidden, n_experts, ntok, vec_w, vec_x));
+                            (const WT *)W, hidden, n_experts, ntok, vec_w, vec_x, cpb));
     return K3C_OK;
 }
 
@@ -378,7 +411,7 @@ int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
     else if (w_dtype == K3C_F32 && x_dtype == K3C_F32) rc = launch_partial_t<float, float>(part, x, W, hidden, n_experts, ntok, s);
     else return set_error(K3C_EINVAL, "router: dtypes x=%d W=%d", x_dtype, w_dtype);
     if (rc) return rc;
-    return launch_select(idx, w, scores, part, (hidden + RT_KC - 1) / RT_KC, bias, n_experts, topk, renorm,
+    return launch_select(idx, w, scores, part, router_nparts(hidden, n_experts, ntok), bias, n_experts, topk, renorm,
                          routed_scale, ntok, s);
 }
 

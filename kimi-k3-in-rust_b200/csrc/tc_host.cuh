@@ -40,6 +40,20 @@ inline int make_map3(CUtensorMap *m, CUtensorMapDataType dt, const void *base, u
     return K3C_OK;
 }
 
+// 2-D tiled map (d0 innermost, row stride s1 bytes), box b0 x b1, 128-byte swizzle.
+inline int make_map2(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t d0, uint64_t d1,
+                     uint64_t s1, uint32_t b0, uint32_t b1) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(K3C_ECUDA, "tc: cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {d0, d1}, strides[1] = {s1};
+    cuuint32_t box[2] = {b0, b1}, es[2] = {1, 1};
+    CUresult r = fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(K3C_ECUDA, "tc: tensor map encode failed (%d)", (int)r);
+    return K3C_OK;
+}
+
 inline int sm_count() {
     static int n = 0;
     if (!n) {

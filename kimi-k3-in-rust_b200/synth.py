@@ -102,3 +102,40 @@ def zipf_bias(n_experts: int, s: float = 1.1, alpha: float = 0.0,
     ids = np.arange(n_experts) if perm is None else perm
     out[ids] = b.astype(np.float32)
     return out
+
+
+def zipf_topk_marginal(n_experts: int, s: float = 1.1, topk: int = 8, samples: int = 65536,
+                       seed: int = 1, device="cpu"):
+    """Expert popularity when every token draws topk distinct experts with Zipf(s) weights
+    (rank r = expert id r-1), estimated by Gumbel-top-k sampling. Under top-k routing no
+    expert can take more than 1/topk of the pairs, so this -- not the Zipf law itself -- is
+    the reachable target."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    logw = -s * torch.log(torch.arange(1, n_experts + 1, dtype=torch.float64, device=device))
+    u = torch.rand((samples, n_experts), generator=g, device=device, dtype=torch.float64)
+    top = torch.topk(logw[None, :] - torch.log(-torch.log(u)), topk, dim=1).indices
+    cnt = torch.bincount(top.reshape(-1), minlength=n_experts).to(torch.float64)
+    return cnt / cnt.sum()
+
+
+def zipf_fit_bias(scores, s: float = 1.1, topk: int = 8, iters: int = 1500, step: float = 0.05,
+                  seed: int = 1):
+    """Router selection bias (fp32, max 0) fitted so that top-k(score + bias) over the sample
+    `scores` [tokens][experts] (a torch tensor of sigmoid router scores) reproduces
+    zipf_topk_marginal: a Zipf(s) popularity over expert ids. The fixed form
+    alpha*log(rank^-s) cannot reach it -- the bounded sigmoid scores cut its tail off -- so
+    the bias is found by damped proportional updates in log space."""
+    import torch
+    T, E = scores.shape
+    target = zipf_topk_marginal(E, s, topk, seed=seed, device=scores.device)
+    sc = scores.to(torch.float64)
+    b = torch.zeros(E, dtype=torch.float64, device=scores.device)
+    eps = 1.0 / (T * topk)
+    for it in range(iters):
+        top = torch.topk(sc + b[None, :], topk, dim=1).indices
+        p = torch.bincount(top.reshape(-1), minlength=E).to(torch.float64) / (T * topk)
+        b += step * torch.clamp(torch.log((target + eps) / (p + eps)), -1.0, 1.0) / (1 + it / 300)
+        b -= b.max()
+    return b.to(torch.float32)

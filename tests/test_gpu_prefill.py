@@ -1,0 +1,124 @@
+"""GPU parity of the tcgen05 MoE prefill (k3c_moe_prefill_tc) against the CPU oracle.
+
+Activations enter the tensor cores as two E4M3 terms per element (about 8 bits relative to
+each 32-element block maximum); the bar is the BASELINE bf16 tolerance, 2e-2 relative
+(max|got-want| / max|want|), with router indices exact.
+"""
+import numpy as np
+import pytest
+
+from conftest import maxrel
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 2e-2
+
+
+@pytest.fixture(scope="module")
+def dev():
+    import torch
+    return torch.device("cuda:0")
+
+
+def T(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _layer(k3, dev, H, I, E, K, seed, shared=True, bias=None, distinct=None, expert_map=None):
+    import torch
+    g = k3.synth.rng(seed)
+    D = distinct or E
+    experts = [k3.synth.expert(g, H, I) for _ in range(D)]
+    sh = k3.synth.expert(g, H, I) if shared else None
+    wf, wb = k3.synth.router_weights(g, E, H)
+    if H < 1024:
+        wf = (wf * 20).astype(np.float32)      # decisive routing at small hidden sizes
+        wb = k3.synth.bf16_bits(wf)
+        wf = k3.synth.bf16_to_f32(wb)
+    devs = [k3.DeviceExpert.from_host(e, dev) for e in experts]
+    W = T(wb.view(np.int16), dev).view(torch.bfloat16)
+    emap = expert_map if expert_map is not None else [i % D for i in range(E)]
+    layer = k3.PoolMoeLayer.pack(devs, k3.DeviceExpert.from_host(sh, dev) if shared else None, W,
+                                 None if bias is None else T(bias, dev), H, I, K, dev, expert_map=emap)
+    routed = [experts[i % D] for i in range(E)]
+    return layer, routed, sh, wf, g
+
+
+@pytest.mark.parametrize("Tn,shared", [(1, True), (300, True), (129, False)])
+def test_prefill_small_vs_oracle(k3, ora, dev, Tn, shared):
+    H, I, E, K = 256, 128, 8, 2
+    layer, experts, sh, wf, g = _layer(k3, dev, H, I, E, K, seed=40 + Tn, shared=shared)
+    xf, xb = k3.synth.activations(g, Tn, H)
+    out, idx, wt = layer.prefill(T(xb.view(np.int16), dev))
+    ro, ri, rw = ora.moe_layer(xf, wf, None, experts, sh, H, I, K)
+    assert np.array_equal(idx.cpu().numpy(), ri)
+    err = maxrel(out.cpu().numpy(), ro)
+    print(f"prefill small T={Tn}: maxrel {err:.3e}")
+    assert err < TOL_BF16
+
+
+def test_prefill_hot_expert_spans_many_slots(k3, ora, dev):
+    """A bias that sends every token to expert 3: its 1500 pairs fill 12 slots, the other
+    experts share the second choice; 6 planning chunks."""
+    H, I, E, K, Tn = 256, 256, 16, 4, 1500
+    bias = np.zeros(E, np.float32)
+    bias[3] = 10.0
+    layer, experts, sh, wf, g = _layer(k3, dev, H, I, E, K, seed=77, bias=bias)
+    xf, xb = k3.synth.activations(g, Tn, H)
+    out, idx, wt = layer.prefill(T(xb.view(np.int16), dev))
+    ro, ri, rw = ora.moe_layer(xf, wf, bias, experts, sh, H, I, K)
+    idx = idx.cpu().numpy()
+    assert np.all(idx[:, 0] == 3)
+    assert np.array_equal(idx, ri)
+    err = maxrel(out.cpu().numpy(), ro)
+    print(f"prefill hot expert: maxrel {err:.3e}")
+    assert err < TOL_BF16
+
+
+def test_prefill_matches_decode_path(k3, dev):
+    """Prefill and the decode kernels on the same tokens: same routing, outputs within the
+    activation-term error of each other."""
+    H, I, E, K, Tn = 512, 256, 8, 2, 16
+    layer, experts, sh, wf, g = _layer(k3, dev, H, I, E, K, seed=5)
+    xf, xb = k3.synth.activations(g, Tn, H)
+    xd = T(xb.view(np.int16), dev)
+    po, pi, pw = layer.prefill(xd)
+    do, di, dw = layer.decode(xd)
+    assert np.array_equal(pi.cpu().numpy(), di.cpu().numpy())
+    assert np.array_equal(pw.cpu().numpy().view(np.uint32), dw.cpu().numpy().view(np.uint32))
+    assert maxrel(po.cpu().numpy(), do.cpu().numpy()) < 1e-2
+
+
+def test_prefill_drops_non_resident(k3, dev):
+    """Experts mapped to no run are dropped and counted, like the decode path."""
+    import torch
+    H, I, E, K, Tn = 256, 128, 8, 2, 200
+    emap = [i if i % 4 else -1 for i in range(E)]        # experts 0 and 4 not resident
+    layer, experts, sh, wf, g = _layer(k3, dev, H, I, E, K, seed=9, expert_map=emap)
+    xf, xb = k3.synth.activations(g, Tn, H)
+    drops = torch.zeros(1, dtype=torch.int32, device=dev)
+    out, idx, wt = layer.prefill(T(xb.view(np.int16), dev), drops=drops)
+    idx = idx.cpu().numpy()
+    assert drops.item() == int(np.isin(idx, [0, 4]).sum()) > 0
+    assert np.all(np.isfinite(out.cpu().numpy()))
+
+
+def test_prefill_config2_shape(k3, ora, dev):
+    """BASELINE config[2] shapes (hidden 7168, inter 2048, 384 experts as 24 distinct runs,
+    top-8, shared expert, Zipf-biased routing) at 384 tokens; the first 24 tokens against
+    the oracle."""
+    import torch
+    H, I, E, K, Tn, D = 7168, 2048, 384, 8, 384, 24
+    bias = k3.synth.zipf_bias(E, 1.1, alpha=0.05)
+    layer, experts, sh, wf, g = _layer(k3, dev, H, I, E, K, seed=202, bias=bias, distinct=D)
+    xf, xb = k3.synth.activations(g, Tn, H)
+    drops = torch.zeros(1, dtype=torch.int32, device=dev)
+    out, idx, wt = layer.prefill(T(xb.view(np.int16), dev), drops=drops)
+    assert drops.item() == 0
+    n = 24
+    ro, ri, rw = ora.moe_layer(xf[:n], wf, bias, experts, sh, H, I, K)
+    assert np.array_equal(idx.cpu().numpy()[:n], ri)
+    err = maxrel(out.cpu().numpy()[:n], ro)
+    print(f"prefill config2 shape: maxrel {err:.3e}")
+    assert err < TOL_BF16
