@@ -50,7 +50,8 @@ constexpr int PF_B = PF_N * 128;              // padded E2M1 B tile: 32 KB
 constexpr int PF_SF = (PF_J + 2) * 512;       // SFA per term + two SFB atoms
 constexpr int PF_STAGE = PF_J * PF_A + PF_B + PF_SF;
 constexpr int PF_STAGES = 3;
-constexpr int PF_THREADS = 192;
+constexpr int PF_EPI_WARPS = 8;               // two per TMEM lane quadrant, each half the columns
+constexpr int PF_THREADS = 64 + 32 * PF_EPI_WARPS;
 constexpr int PF_BYTES = 1024 + PF_STAGES * PF_STAGE + PF_M * 4 + 256;
 constexpr uint32_t PF_TMEM = 512;             // accumulator 256 columns + scale factors
 constexpr uint32_t PF_SF_COL = 256;
@@ -311,6 +312,13 @@ __global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq,
     }
 }
 
+// The activation with the hardware exponential and divide: its result is requantised to two
+// E4M3 terms right away, so the last-bit differences from act_apply do not survive.
+__device__ __forceinline__ float act_fast(float g, float u, int act) {
+    if (act == K3C_ACT_SWIGLU) return __fdividef(g, 1.0f + __expf(-g)) * u;
+    return act_apply(g, u, act);
+}
+
 template <bool GU>
 __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ CUtensorMap tmA,
                                                        const __grid_constant__ CUtensorMap tmW, PfArgs p) {
@@ -327,7 +335,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
             tc::mbar_init(&empty[i], 1);
         }
         tc::mbar_init(tfull, 1);
-        tc::mbar_init(tempty, 4);
+        tc::mbar_init(tempty, PF_EPI_WARPS);
         tc::fence_mbar_init();
     }
     if (warp == 1) tc::tmem_alloc(tmem_slot, PF_TMEM);
@@ -414,6 +422,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
     } else {
         // ---------------------------------------------------------------- epilogue
         const int q = warp & 3;                 // TMEM lane quadrant
+        const int half = (warp - 2) >> 2;       // which half of the item's columns
         const int m = 32 * q + lane;            // pair row of the slot
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         uint32_t li = 0;
@@ -426,7 +435,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
             if (GU) {
                 const int KTd = p.I / 128;
 #pragma unroll 1
-                for (int c = 0; c < 4; c++) {
+                for (int c = 2 * half; c < 2 * half + 2; c++) {
                     // gate columns of intermediate block c and the matching up columns
                     const uint32_t gcol = 128u * (c >> 1) + 32u * (c & 1);
                     uint32_t vg[32], vu[32];
@@ -436,7 +445,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
                     if (!ok) continue;
                     float a[32];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) a[i] = act_apply(__uint_as_float(vg[i]), __uint_as_float(vu[i]), p.act);
+                    for (int i = 0; i < 32; i++) a[i] = act_fast(__uint_as_float(vg[i]), __uint_as_float(vu[i]), p.act);
                     uint4 qv[PF_J][2];
                     uint32_t sf[PF_J];
                     quant_row32(a, qv, sf);
@@ -458,7 +467,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
                     dst = p.contrib + ((size_t)p.pair_tok[pr] * p.kstride + p.pair_k[pr]) * p.H + (size_t)nt * PF_N;
                 }
 #pragma unroll 1
-                for (int c = 0; c < PF_N / 32; c++) {
+                for (int c = half * (PF_N / 64); c < (half + 1) * (PF_N / 64); c++) {
                     uint32_t v[32];
                     tc::tmem_ld32(tmem + lane_base + 32u * c, v);
                     tc::tmem_ld_wait();

@@ -125,7 +125,7 @@ struct WSlice {
 };
 
 template <typename WT, typename XT, int NT>
-__global__ void __launch_bounds__(256) k_router_partial(double *__restrict__ part, const XT *__restrict__ x,
+__global__ void __launch_bounds__(256, 2) k_router_partial(double *__restrict__ part, const XT *__restrict__ x,
                                                         const WT *__restrict__ W, int hidden, int n_experts,
                                                         int ntok, int vec_w, int vec_x, int cpb) {
     extern __shared__ __align__(16) double rsm[];   // xs [RT_KC][NT], then red [8][NT][32]
@@ -139,61 +139,86 @@ __global__ void __launch_bounds__(256) k_router_partial(double *__restrict__ par
     double acc[NT];
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t] = 0.0;
-    // this block adds chunks [cpb*y, cpb*y + cpb) in order
+    // this block adds chunks [cpb*y, cpb*y + cpb) in order; chunk c+1's activations and W
+    // slices are loaded into registers while chunk c is multiplied
     const int nchunk = (hidden + RT_KC - 1) / RT_KC;
-    const int c_end = min(nchunk, (int)(blockIdx.y + 1) * cpb);
-    for (int c = blockIdx.y * cpb; c < c_end; c++) {
-    const int k0 = c * RT_KC, kn = min(RT_KC, hidden - k0);
-    if (c > blockIdx.y * cpb) __syncthreads();   // every warp is done with the previous chunk
-    // consecutive threads take consecutive tokens, so stores of one k row are contiguous
-#pragma unroll 4
-    for (int i = threadIdx.x; i < NT * (RT_KC / 8); i += 256) {
-        const int t = i % NT, kk = (i / NT) * 8;
-        float v[8];
-        if (t < nt) load_x8<XT>(x + (size_t)(t0 + t) * hidden + k0 + kk, kn - kk, vec_x != 0, v);
-        else
+    const int c_begin = blockIdx.y * cpb, c_end = min(nchunk, c_begin + cpb);
+    constexpr int NG = NT * (RT_KC / 8);                 // 8-element groups per chunk
+    constexpr int XR = NG >= 256 ? NG / 256 : 1;         // groups per thread
+    float xv[XR][8];
+    auto load_chunk = [&](int c) {
+        const int k0 = c * RT_KC, kn = min(RT_KC, hidden - k0);
 #pragma unroll
-            for (int q = 0; q < 8; q++) v[q] = 0.0f;
+        for (int r = 0; r < XR; r++) {
+            const int i = threadIdx.x + 256 * r;
+            // consecutive threads take consecutive tokens, so stores of one k row are contiguous
+            const int t = i % NT, kk = (i / NT) * 8;
+            if (i < NG && t < nt) load_x8<XT>(x + (size_t)(t0 + t) * hidden + k0 + kk, kn - kk, vec_x != 0, xv[r]);
+            else
 #pragma unroll
-        for (int q = 0; q < 8; q++) xs[(kk + q) * NT + t] = (double)v[q];
-    }
-    __syncthreads();
-    const int kw = warp * RT_KW, kwn = min(RT_KW, kn - kw);   // this warp's slice
-    const WT *row = W + (size_t)(e < n_experts ? e : 0) * hidden + k0 + kw;
-    // acc[t] += w[0..8) . x[kw+k .. kw+k+8)[t]
-    auto step = [&](const double (&w)[8], int k) {
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-            const double *xp = xs + (kw + k + q) * NT;   // same address in every lane: broadcast
-            if constexpr (NT % 2 == 0) {
-#pragma unroll
-                for (int t2 = 0; t2 < NT / 2; t2++) {
-                    const double2 xv = reinterpret_cast<const double2 *>(xp)[t2];
-                    acc[2 * t2] = fma(w[q], xv.x, acc[2 * t2]);
-                    acc[2 * t2 + 1] = fma(w[q], xv.y, acc[2 * t2 + 1]);
-                }
-            } else {
-#pragma unroll
-                for (int t = 0; t < NT; t++) acc[t] = fma(w[q], xp[t], acc[t]);
-            }
+                for (int q = 0; q < 8; q++) xv[r][q] = 0.0f;
         }
     };
-    if (kwn == RT_KW && vec_w) {
-        WSlice<WT> ws;
-        ws.load(row);                    // one round trip for the whole slice
+    auto store_chunk = [&]() {
 #pragma unroll
-        for (int g = 0; g < RT_KW / 8; g++) {
-            double w[8];
-            ws.get(g, w);
-            step(w, 8 * g);
+        for (int r = 0; r < XR; r++) {
+            const int i = threadIdx.x + 256 * r;
+            if (i >= NG) continue;
+            const int t = i % NT, kk = (i / NT) * 8;
+#pragma unroll
+            for (int q = 0; q < 8; q++) xs[(kk + q) * NT + t] = (double)xv[r][q];
         }
-    } else {
-        for (int k = 0; k < kwn; k += 8) {
-            double w[8];
-            load_w8<WT>(row, k, kwn, vec_w != 0, w);
-            step(w, k);
+    };
+    // every chunk full and rows 16-byte aligned: whole W slices, one round trip each
+    const bool wfast = vec_w && hidden % RT_KC == 0;
+    const WT *wbase = W + (size_t)(e < n_experts ? e : 0) * hidden + warp * RT_KW;
+    WSlice<WT> wnext;
+    load_chunk(c_begin);
+    if (wfast) wnext.load(wbase + (size_t)c_begin * RT_KC);
+    for (int c = c_begin; c < c_end; c++) {
+        const int k0 = c * RT_KC, kn = min(RT_KC, hidden - k0);
+        if (c > c_begin) __syncthreads();   // every warp is done with the previous chunk
+        store_chunk();
+        __syncthreads();
+        const WSlice<WT> wcur = wnext;
+        if (c + 1 < c_end) {
+            load_chunk(c + 1);
+            if (wfast) wnext.load(wbase + (size_t)(c + 1) * RT_KC);
         }
-    }
+        const int kw = warp * RT_KW, kwn = min(RT_KW, kn - kw);   // this warp's slice
+        // acc[t] += w[0..8) . x[kw+k .. kw+k+8)[t]
+        auto step = [&](const double (&w)[8], int k) {
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const double *xp = xs + (kw + k + q) * NT;   // same address in every lane: broadcast
+                if constexpr (NT % 2 == 0) {
+#pragma unroll
+                    for (int t2 = 0; t2 < NT / 2; t2++) {
+                        const double2 xq = reinterpret_cast<const double2 *>(xp)[t2];
+                        acc[2 * t2] = fma(w[q], xq.x, acc[2 * t2]);
+                        acc[2 * t2 + 1] = fma(w[q], xq.y, acc[2 * t2 + 1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int t = 0; t < NT; t++) acc[t] = fma(w[q], xp[t], acc[t]);
+                }
+            }
+        };
+        if (wfast) {
+#pragma unroll
+            for (int g = 0; g < RT_KW / 8; g++) {
+                double w[8];
+                wcur.get(g, w);
+                step(w, 8 * g);
+            }
+        } else {
+            const WT *row = W + (size_t)(e < n_experts ? e : 0) * hidden + k0 + kw;
+            for (int k = 0; k < kwn; k += 8) {
+                double w[8];
+                load_w8<WT>(row, k, kwn, vec_w != 0, w);
+                step(w, k);
+            }
+        }
     }
 #pragma unroll
     for (int t = 0; t < NT; t++) red[(warp * NT + t) * 32 + lane] = acc[t];
