@@ -11,6 +11,7 @@ touches ~110 different experts (~2.6 GB): inputs larger than L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload prefill [--steps K] [--warmup W]   (config[2], one line)
+  python bench.py --workload streamed [--steps K] [--warmup W]  (config[4], one line)
 
 N > 1 (torchrun) runs N independent replicas (decode does not shard; scaling "weak").
 --impl reference times the reference's own CPU kernels (oracle/_ref, built from its
@@ -490,6 +491,154 @@ def run_prefill(args, ws, rank, local):
     }))
 
 
+# ------------------------------------------------------------------ streamed (config[4])
+ST_LAYERS = 16
+ST_WORKLOAD = "config[4] streamed-expert decode: 16-layer stack of config[1] MoE layers, 1 token per " \
+              "step, seeded top-8 routing reusing 4 of the previous step's experts per layer, HBM " \
+              "expert pool = 25% of the 143.7 GB of expert bytes, the rest in pinned host memory"
+
+
+def streamed_routing(seed, steps, layers=ST_LAYERS, n_experts=E, topk=K, reuse=4):
+    """Per (step, layer): topk distinct experts, `reuse` of them drawn from the previous
+    step's set of that layer, the rest new; weights positive and normalised."""
+    g = np.random.default_rng(seed)
+    prev = [g.choice(n_experts, topk, replace=False) for _ in range(layers)]
+    idx = np.empty((steps, layers, topk), np.int32)
+    wt = np.empty((steps, layers, topk), np.float32)
+    for s in range(steps):
+        for l in range(layers):
+            keep = g.choice(prev[l], reuse, replace=False)
+            pool_ids = np.setdiff1d(np.arange(n_experts), keep)
+            new = g.choice(pool_ids, topk - reuse, replace=False)
+            ids = np.concatenate([keep, new])
+            g.shuffle(ids)
+            idx[s, l] = ids
+            w = g.random(topk).astype(np.float32) + 0.05
+            wt[s, l] = w / w.sum()
+            prev[l] = ids
+    return idx, wt
+
+
+def run_streamed(args, ws, rank, local):
+    """One step = one token through 16 MoE layers whose experts come from an HBM pool of
+    25% of the stack's expert bytes; misses are copied from pinned host memory on the pool's
+    copy stream (k3c_pool_*), then the layer runs on the tensor-core decode path."""
+    import ctypes as C
+    import torch
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    run_bytes = k3.pool_run_bytes(H, I)
+    n_keys = ST_LAYERS * (E + 1)                            # expert E of a layer: its shared expert
+    total_bytes = ST_LAYERS * E * run_bytes
+    n_slots = int(0.25 * total_bytes // run_bytes) + ST_LAYERS
+    # pinned host images: 32 distinct pool-format runs tiled over the keys (every miss still
+    # moves a whole run over PCIe)
+    D = 32
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    lay, _ = k3.pool_layout(H, I)
+    images = []
+    tmp = torch.empty(run_bytes, dtype=torch.uint8, device=dev)
+    for d in range(D):
+        for name, (off, nb) in lay.items():
+            seg = tmp[off:off + nb]
+            if name.endswith("_p"):
+                seg.copy_(torch.randint(0, 256, (nb,), generator=g, device=dev, dtype=torch.uint8))
+            else:
+                seg.copy_(torch.randint(118, 125, (nb,), generator=g, device=dev, dtype=torch.uint8))
+        images.append(tmp.cpu().pin_memory())
+
+    def src(layer, expert):
+        return images[(layer * (E + 1) + expert) % D]
+
+    pool = k3.ExpertPool(H, I, ST_LAYERS, E + 1, n_slots, src)
+    W = (torch.randn((E, H), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    shared_slots = [pool.pin(l, E) for l in range(ST_LAYERS)]
+    tables = [pool.run_table() for _ in range(ST_LAYERS)]
+    layers = [pool.layer(W, H, I, K, E, tables[l], shared_slot=shared_slots[l], terms=3)
+              for l in range(ST_LAYERS)]
+    total_steps = args.warmup + args.steps
+    idx_h, wt_h = streamed_routing(2024 + rank, total_steps)
+    idx_d = torch.from_numpy(idx_h).to(dev)
+    wt_d = torch.from_numpy(wt_h).to(dev)
+    x0 = torch.randn((1, H), generator=g, device=dev).to(torch.bfloat16)
+    torch.cuda.synchronize()
+
+    def step(s):
+        x = x0
+        for l in range(ST_LAYERS):
+            ids = idx_h[s, l]
+            pool.acquire(l, ids, run_of=tables[l])
+            out = layers[l].decode_routed(x, idx_d[s, l:l + 1], wt_d[s, l:l + 1])
+            pool.release(l, ids)
+            x = out.to(torch.bfloat16)
+        return out
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    st0 = pool.stats()
+    clk = Clocks(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = L.k3c_launch_count()
+    t0 = time.perf_counter()
+    e0.record()
+    for s in range(args.warmup, total_steps):
+        out = step(s)
+    h_out = out.cpu()                                      # the step's result read back
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clocks = clk.stop()
+    dt = e0.elapsed_time(e1) / 1e3
+    launches = L.k3c_launch_count() - launches0
+    st1 = pool.stats()
+    req = (st1["hits"] - st0["hits"]) + (st1["misses"] - st0["misses"])
+    hits = st1["hits"] - st0["hits"]
+    h2d = st1["bytes_h2d"] - st0["bytes_h2d"]
+    hbm_bytes = args.steps * ST_LAYERS * (K + 1) * run_bytes
+    hbm, _, kind = peaks()
+    pool.close()
+    # the link's own ceiling: one large pinned host -> device copy
+    big = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dbig = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    dbig.copy_(big, non_blocking=True)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(4):
+        dbig.copy_(big, non_blocking=True)
+    c1.record()
+    torch.cuda.synchronize()
+    pcie_peak = 4 * (1 << 30) / (c0.elapsed_time(c1) / 1e3) / 1e9
+    del big, dbig
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": METRIC, "value": args.steps / dt, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 x e4m3 (activations as 3 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
+        "data": "synthetic",
+        "config": {"workload": ST_WORKLOAD, "layers": ST_LAYERS, "hidden": H, "inter": I, "experts": E,
+                   "topk": K, "pool_slots": n_slots, "pool_gb": n_slots * run_bytes / 1e9,
+                   "expert_bytes_gb": total_bytes / 1e9, "host_images": D},
+        "cache": {"requests": req, "hit_rate": hits / req if req else None,
+                  "misses_per_step": (req - hits) / args.steps,
+                  "evictions": st1["evictions"] - st0["evictions"]},
+        "pcie_h2d_gbs": h2d / dt / 1e9, "h2d_bytes_per_step": h2d / args.steps,
+        "roofline": {"bound": "pcie", "achieved": h2d / dt / 1e9, "peak": pcie_peak, "unit": "GB/s",
+                     "frac": h2d / dt / 1e9 / pcie_peak, "peak_kind": "measured in this run: 1 GiB pinned copies"},
+        "hbm_expert_gbs": hbm_bytes / dt / 1e9, "hbm_peak_gbs": hbm, "peak_kind": kind,
+        "e2e": {"value": args.steps / wall, "unit": UNIT, "h2d_bytes_per_step": h2d / args.steps,
+                "d2h_bytes_per_step": H * 4 / args.steps},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -503,12 +652,14 @@ def main():
     ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
                     help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
     ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: config[1] (the headline line); prefill: config[2]")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed"],
+                    help="decode: config[1] (the headline line); prefill: config[2]; streamed: config[4]")
     args = ap.parse_args()
     ws, rank, local = dist_setup(args)
     if args.workload == "prefill" and args.impl != "reference":
         run_prefill(args, ws, rank, local)
+    elif args.workload == "streamed" and args.impl != "reference":
+        run_streamed(args, ws, rank, local)
     elif args.impl == "reference":
         run_reference(args, ws, rank)
     else:

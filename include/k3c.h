@@ -230,6 +230,13 @@ int k3c_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok,
                       const k3c_moe_pool_layer *L, int *idx, float *wt, int *drops,
                       void *scratch, size_t scratch_bytes, k3c_stream_t stream);
 
+/* Same as k3c_moe_decode_tc with the routing given: idx/wt [ntok][topk] on the device (top-k
+ * expert ids and their weights, as k3c_router writes them); the router is not run. Used when
+ * routing comes from elsewhere (the streamed-expert stack, replays of recorded routing). */
+int k3c_moe_decode_tc_routed(float *out, const void *x, int x_dtype, int ntok,
+                             const k3c_moe_pool_layer *L, const int *idx, const float *wt,
+                             int *drops, void *scratch, size_t scratch_bytes, k3c_stream_t stream);
+
 /* MoE prefill over ntok tokens: the reference's k3_moe_prefill / moe_prefill_chunk
  * (src/core/k3_ops.c:689-808) for the non-latent shape -- route, group the (token, expert)
  * pairs by expert, run each expert's FFN over its group as tcgen05 block-scaled MMAs, combine
@@ -241,6 +248,48 @@ size_t k3c_moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int ntok);
 int k3c_moe_prefill_tc(float *out, const void *x, int x_dtype, int ntok,
                        const k3c_moe_pool_layer *L, int *idx, float *wt, int *drops,
                        void *scratch, size_t scratch_bytes, k3c_stream_t stream);
+
+/* ---- HBM expert pool: the reference's expert cache (src/cache/k3_cache.c:24-261) with
+ * experts streamed from pinned host memory. A slot holds one pool-format run
+ * (k3c_pool_run_bytes). Keys are layer*n_experts + expert; victim choice, hit/miss/eviction
+ * and batch-prefetch accounting follow the reference (pick_victim k3_cache.c:46-57, getmany
+ * :131-234, report :416-425). Not thread-safe across pools' shared streams (one pool per
+ * caller, as the reference). ---- */
+enum { K3C_SLOT_EMPTY = -1, K3C_SLOT_INFLIGHT = -2 };
+/* Where the host bytes of (layer, expert) live: a pool-format run in pinned host memory, or
+ * NULL if there are none (the request then fails with K3C_ENOTFOUND). */
+typedef const void *(*k3c_pool_src_fn)(void *ctx, int layer, int expert);
+typedef struct {
+    long long hits, misses, evictions, prefetch_reads, bytes_h2d;
+} k3c_pool_stats_t;
+typedef struct k3c_expert_pool k3c_expert_pool;
+
+/* Allocates n_slots slots in HBM and the pool's copy stream; NULL on failure
+ * (k3c_last_error says why). */
+k3c_expert_pool *k3c_pool_create(int hidden, int inter, int n_layers, int n_experts, int n_slots,
+                                 k3c_pool_src_fn src, void *ctx);
+void k3c_pool_destroy(k3c_expert_pool *pool);
+uint8_t *k3c_pool_arena(k3c_expert_pool *pool);            /* slot s at arena + s*stride */
+size_t k3c_pool_slot_stride(const k3c_expert_pool *pool);
+int k3c_pool_slots(const k3c_expert_pool *pool);
+/* Slot holding (layer, expert) -- possibly still filling -- or -1 (reference: resident). */
+int k3c_pool_resident(k3c_expert_pool *pool, int layer, int expert);
+/* Batch hint (reference: getmany): start the copies of the ids not resident; returns how
+ * many were started. Counted as prefetch reads, not as hits or misses. */
+int k3c_pool_getmany(k3c_expert_pool *pool, int layer, const int *ids, int n);
+/* get() for each id (hits and misses counted per request): copies the misses, pins every
+ * slot until k3c_pool_release, and makes `stream` wait for any copy still in flight.
+ * slots (host, may be NULL) receives the slot of each id; dev_run_of (device, may be NULL,
+ * n_experts ints) receives -1 everywhere except run_of[ids[i]] = slot, ordered on `stream`:
+ * the run table of k3c_moe_pool_layer. */
+int k3c_pool_acquire(k3c_expert_pool *pool, int layer, const int *ids, int n, int *slots,
+                     int *dev_run_of, k3c_stream_t stream);
+/* Unpins; the slots may be overwritten once the work enqueued on `stream` so far is done. */
+int k3c_pool_release(k3c_expert_pool *pool, int layer, const int *ids, int n, k3c_stream_t stream);
+/* Acquire that is never released (shared experts); returns the slot or a negative status. */
+int k3c_pool_pin(k3c_expert_pool *pool, int layer, int expert, k3c_stream_t stream);
+int k3c_pool_stats(k3c_expert_pool *pool, k3c_pool_stats_t *out);
+int k3c_pool_sync(k3c_expert_pool *pool);                  /* waits for the copy stream */
 
 #ifdef __cplusplus
 }

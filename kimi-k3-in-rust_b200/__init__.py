@@ -57,6 +57,15 @@ class K3CError(RuntimeError):
 _lib = None
 
 
+# host bytes of (layer, expert): a pointer to its pool-format run in pinned memory, or NULL
+POOL_SRC_FN = C.CFUNCTYPE(C.c_void_p, C.c_void_p, C.c_int, C.c_int)
+
+
+class PoolStatsC(C.Structure):
+    _fields_ = [("hits", C.c_longlong), ("misses", C.c_longlong), ("evictions", C.c_longlong),
+                ("prefetch_reads", C.c_longlong), ("bytes_h2d", C.c_longlong)]
+
+
 def lib():
     """Load libk3cuda.so (building it with make if this checkout has not been built)."""
     global _lib
@@ -87,6 +96,19 @@ def lib():
         "k3c_pool_pack_expert": ([vp, C.POINTER(K3ExpertQ), i, i, vp], i),
         "k3c_moe_decode_tc_scratch": ([C.POINTER(MoePoolLayerC), i], sz),
         "k3c_moe_decode_tc": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
+        "k3c_moe_decode_tc_routed": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
+        "k3c_pool_create": ([i, i, i, i, i, POOL_SRC_FN, vp], vp),
+        "k3c_pool_destroy": ([vp], None),
+        "k3c_pool_arena": ([vp], vp),
+        "k3c_pool_slot_stride": ([vp], sz),
+        "k3c_pool_slots": ([vp], i),
+        "k3c_pool_resident": ([vp, i, i], i),
+        "k3c_pool_getmany": ([vp, i, vp, i], i),
+        "k3c_pool_acquire": ([vp, i, vp, i, vp, vp, vp], i),
+        "k3c_pool_release": ([vp, i, vp, i, vp], i),
+        "k3c_pool_pin": ([vp, i, i, vp], i),
+        "k3c_pool_stats": ([vp, C.POINTER(PoolStatsC)], i),
+        "k3c_pool_sync": ([vp], i),
         "k3c_moe_prefill_tc_scratch": ([C.POINTER(MoePoolLayerC), i], sz),
         "k3c_moe_prefill_tc": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
         "k3_mxfp4_dequant": ([vp, vp, vp, i, i, i], None),
@@ -435,6 +457,25 @@ class PoolMoeLayer:
                "k3c_moe_decode_tc")
         return out, idx, wt
 
+    def decode_routed(self, x, idx, wt, out=None, drops=None):
+        """decode with the routing given (idx/wt [ntok][topk] on the device); the router is
+        not run (k3c_moe_decode_tc_routed)."""
+        import torch
+        if x.dtype == torch.int16:
+            x = x.view(torch.bfloat16)
+        x = x.contiguous()
+        ntok = x.shape[0]
+        need = self.scratch_bytes(ntok)
+        if self._scratch.numel() < need:
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        if out is None:
+            out = torch.empty((ntok, self.c.hidden), dtype=torch.float32, device=x.device)
+        _check(lib().k3c_moe_decode_tc_routed(_ptr(out), _ptr(x), _dtype_code(x), ntok,
+                                              C.byref(self.c), _ptr(idx), _ptr(wt), _ptr(drops),
+                                              _ptr(self._scratch), self._scratch.numel(), _stream()),
+               "k3c_moe_decode_tc_routed")
+        return out
+
     def prefill(self, x, out=None, idx=None, wt=None, drops=None):
         """Prefill over ntok tokens (k3c_moe_prefill_tc): expert-sorted tokens through the
         tcgen05 grouped expert kernels, combined in each token's top-k order."""
@@ -458,3 +499,114 @@ class PoolMoeLayer:
                                         _ptr(self._scratch), self._scratch.numel(), _stream()),
                "k3c_moe_prefill_tc")
         return out, idx, wt
+
+
+class ExpertPool:
+    """HBM expert pool (k3c_pool_*): the reference's expert cache with experts copied from
+    pinned host memory. host_src(layer, expert) returns the pinned host uint8 tensor holding
+    that expert's pool-format run (pool_run_bytes bytes), or None."""
+
+    def __init__(self, hidden, inter, n_layers, n_experts, n_slots, host_src):
+        self.hidden, self.inter, self.n_layers, self.n_experts = hidden, inter, n_layers, n_experts
+        self._host_src = host_src
+
+        def cb(ctx, layer, expert):
+            t = self._host_src(layer, expert)
+            return None if t is None else t.data_ptr()
+
+        self._cb = POOL_SRC_FN(cb)          # kept alive as long as the pool
+        self.p = lib().k3c_pool_create(hidden, inter, n_layers, n_experts, n_slots, self._cb, None)
+        if not self.p:
+            raise RuntimeError(f"k3c_pool_create: {lib().k3c_last_error().decode()}")
+        self.n_slots = n_slots
+        self.stride = lib().k3c_pool_slot_stride(self.p)
+        self.arena_ptr = lib().k3c_pool_arena(self.p)
+
+    def close(self):
+        if self.p:
+            lib().k3c_pool_destroy(self.p)
+            self.p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def _ids(ids):
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        return a, a.ctypes.data
+
+    def getmany(self, layer, ids):
+        a, p = self._ids(ids)
+        rc = lib().k3c_pool_getmany(self.p, layer, p, len(a))
+        if rc < 0:
+            _check(rc, "k3c_pool_getmany")
+        return rc
+
+    def acquire(self, layer, ids, run_of=None):
+        """Returns the slots (numpy); fills the device run table run_of if given."""
+        a, p = self._ids(ids)
+        slots = np.empty(len(a), np.int32)
+        _check(lib().k3c_pool_acquire(self.p, layer, p, len(a), slots.ctypes.data, _ptr(run_of),
+                                      _stream()), "k3c_pool_acquire")
+        return slots
+
+    def release(self, layer, ids):
+        a, p = self._ids(ids)
+        _check(lib().k3c_pool_release(self.p, layer, p, len(a), _stream()), "k3c_pool_release")
+
+    def pin(self, layer, expert):
+        rc = lib().k3c_pool_pin(self.p, layer, expert, _stream())
+        if rc < 0:
+            _check(rc, "k3c_pool_pin")
+        return rc
+
+    def resident(self, layer, expert):
+        return lib().k3c_pool_resident(self.p, layer, expert)
+
+    def stats(self):
+        st = PoolStatsC()
+        _check(lib().k3c_pool_stats(self.p, C.byref(st)), "k3c_pool_stats")
+        d = {k: getattr(st, k) for k, _ in PoolStatsC._fields_}
+        n = d["hits"] + d["misses"]
+        d["hit_rate"] = d["hits"] / n if n else None
+        d["true_hit_rate"] = max(d["hits"] - d["prefetch_reads"], 0) / n if n else None
+        return d
+
+    def sync(self):
+        _check(lib().k3c_pool_sync(self.p), "k3c_pool_sync")
+
+    def run_table(self):
+        """A device run table for k3c_pool_acquire: int32 [n_experts of the pool], -1."""
+        import torch
+        return torch.full((self.n_experts,), -1, dtype=torch.int32, device="cuda")
+
+    def slot_tensor(self, slot):
+        """uint8 device view of one slot's bytes (no copy)."""
+        import torch
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (self.stride,), "typestr": "|u1",
+                                        "data": (self.arena_ptr + int(slot) * self.stride, False),
+                                        "version": 3}
+        return torch.as_tensor(_View(), device="cuda")
+
+    def layer(self, router_w, hidden, inter, topk, routed_experts, run_table, shared_slot=-1, **kw):
+        """A PoolMoeLayer over this pool's slots for a layer routed over the first
+        routed_experts ids of run_table (the table k3c_pool_acquire fills)."""
+        return PoolMoeLayer(_PoolArena(self), self.n_slots, run_table[:routed_experts], shared_slot,
+                            router_w, None, hidden, inter, topk, **kw)
+
+
+class _PoolArena:
+    """Adapter giving PoolMoeLayer the pool's arena pointer and device."""
+
+    def __init__(self, pool):
+        import torch
+        self.pool = pool
+        self.device = torch.device("cuda", torch.cuda.current_device())
+
+    def data_ptr(self):
+        return self.pool.arena_ptr

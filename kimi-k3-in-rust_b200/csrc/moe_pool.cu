@@ -516,9 +516,10 @@ static int launch_quant_x(const TcBufs &b, const void *x, int x_dtype, int ntok,
     return K3C_OK;
 }
 
+// routed: idx_out/wt_out hold the routing on entry and the router is skipped.
 int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const k3c_moe_pool_layer *L,
                          int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
-                         cudaStream_t s) {
+                         cudaStream_t s, bool routed = false) {
     if (!L) return set_error(K3C_EINVAL, "moe_decode_tc: null layer");
     const int H = L->hidden, I = L->inter;
     if (H <= 0 || I <= 0 || H % 128 || I % 128)
@@ -536,12 +537,15 @@ int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const
     if (!carve_tc(cv, b, L, ntok)) return set_error(K3C_EINVAL, "moe_decode_tc: scratch too small (%zu)", scratch_bytes);
     int *idx = idx_out ? idx_out : b.idx;
     float *wt = wt_out ? wt_out : b.wt;
+    if (routed && (!idx_out || !wt_out)) return set_error(K3C_EINVAL, "moe_decode_tc_routed: null routing");
     K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), s));
-    stage_begin(STAGE_ROUTER, s);
-    K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, H,
-                          L->n_experts, L->topk, L->renorm, L->routed_scale, ntok,
-                          reinterpret_cast<double *>(b.contrib), s));
-    stage_end(STAGE_ROUTER, s);
+    if (!routed) {
+        stage_begin(STAGE_ROUTER, s);
+        K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, H,
+                              L->n_experts, L->topk, L->renorm, L->routed_scale, ntok,
+                              reinterpret_cast<double *>(b.contrib), s));
+        stage_end(STAGE_ROUTER, s);
+    }
     const size_t psmem = ((size_t)L->n_experts * 2 + (size_t)ntok * L->topk) * sizeof(int);
     if (psmem > 48 * 1024)
         K3C_TRY_CUDA(cudaFuncSetAttribute(k_moe_plan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
@@ -598,6 +602,14 @@ extern "C" int k3c_pool_pack_expert(uint8_t *run, const K3ExpertQ *src, int hidd
 
 extern "C" size_t k3c_moe_decode_tc_scratch(const k3c_moe_pool_layer *L, int ntok) {
     return L ? k3c::moe_decode_tc_scratch(L, ntok) : 0;
+}
+
+extern "C" int k3c_moe_decode_tc_routed(float *out, const void *x, int x_dtype, int ntok,
+                                        const k3c_moe_pool_layer *L, const int *idx, const float *wt, int *drops,
+                                        void *scratch, size_t scratch_bytes, k3c_stream_t stream) {
+    k3c::clear_error();
+    return k3c::launch_moe_decode_tc(out, x, x_dtype, ntok, L, const_cast<int *>(idx), const_cast<float *>(wt),
+                                     drops, scratch, scratch_bytes, (cudaStream_t)stream, true);
 }
 
 extern "C" int k3c_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok,

@@ -1,0 +1,153 @@
+"""HBM expert pool (k3c_pool_*) against the restated cache bookkeeping (oracle/cache_model.py)
+and the resident-expert decode path."""
+import numpy as np
+import pytest
+
+from oracle.cache_model import CacheModel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    import torch
+    return torch.device("cuda:0")
+
+
+def T(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+class HostRuns:
+    """Pinned host pool-format runs, one per (layer, expert) key, packed on the device from
+    random experts and copied back (so the bytes are exactly the pool format)."""
+
+    def __init__(self, k3, dev, H, I, n_layers, n_experts, seed):
+        import torch
+        self.n_experts = n_experts
+        g = k3.synth.rng(seed)
+        self.experts, self.runs = [], []
+        rb = k3.pool_run_bytes(H, I)
+        dev_run = torch.empty(rb, dtype=torch.uint8, device=dev)
+        for _ in range(n_layers * n_experts):
+            e = k3.synth.expert(g, H, I)
+            k3.pool_pack(dev_run, k3.DeviceExpert.from_host(e, dev).q(), H, I)
+            self.experts.append(e)
+            self.runs.append(dev_run.cpu().pin_memory())
+
+    def __call__(self, layer, expert):
+        return self.runs[layer * self.n_experts + expert]
+
+
+def test_pool_bookkeeping_matches_cache_model(k3, dev):
+    """Slot choice, hits, misses, evictions and prefetch accounting, request by request."""
+    import torch
+    H, I, NL, NE, NS = 256, 128, 2, 8, 5
+    host = HostRuns(k3, dev, H, I, NL, NE, seed=1)
+    pool = k3.ExpertPool(H, I, NL, NE, NS, host)
+    model = CacheModel(NL, NE, NS)
+    rng = np.random.default_rng(3)
+    for step in range(60):
+        layer = int(rng.integers(NL))
+        ids = rng.choice(NE, size=int(rng.integers(1, 5)), replace=False).tolist()
+        if step % 7 == 3:
+            assert pool.getmany(layer, ids) == model.getmany(layer, ids)
+        got = pool.acquire(layer, ids).tolist()
+        assert got == model.acquire(layer, ids), step
+        for e, s in zip(ids, got):
+            assert pool.resident(layer, e) == s
+        pool.release(layer, ids)
+        model.release(layer, ids)
+    torch.cuda.synchronize()
+    st, ms = pool.stats(), model.stats()
+    for k in ("hits", "misses", "evictions", "prefetch_reads"):
+        assert st[k] == ms[k], k
+    assert st["bytes_h2d"] == (ms["misses"] + ms["prefetch_reads"]) * k3.pool_run_bytes(H, I)
+    assert st["true_hit_rate"] == pytest.approx(ms["true_hit_rate"])
+    pool.close()
+
+
+def test_pool_slots_hold_the_host_bytes(k3, dev):
+    import torch
+    H, I, NL, NE, NS = 256, 128, 1, 6, 4
+    host = HostRuns(k3, dev, H, I, NL, NE, seed=2)
+    pool = k3.ExpertPool(H, I, NL, NE, NS, host)
+    rb = k3.pool_run_bytes(H, I)
+    for ids in ([0, 1, 2], [3, 4], [5, 0, 1]):
+        slots = pool.acquire(0, ids)
+        for e, s in zip(ids, slots):
+            got = pool.slot_tensor(s)[:rb].cpu().numpy()   # ordered after the copy
+            assert np.array_equal(got, host(0, e).numpy())
+        pool.release(0, ids)
+    pool.close()
+
+
+def test_pool_all_pinned_is_reported(k3, dev):
+    H, I, NL, NE, NS = 256, 128, 1, 6, 2
+    host = HostRuns(k3, dev, H, I, NL, NE, seed=4)
+    pool = k3.ExpertPool(H, I, NL, NE, NS, host)
+    pool.acquire(0, [0, 1])
+    with pytest.raises(k3.K3CError, match="pinned"):
+        pool.acquire(0, [2])
+    pool.release(0, [0, 1])
+    pool.acquire(0, [2])          # now evicts the least recently used
+    pool.release(0, [2])
+    pool.close()
+
+
+def test_streamed_decode_matches_resident_layers(k3, dev):
+    """Several layers through a pool that holds fewer slots than one layer's experts plus
+    the next one's, back to back without host syncs: every layer's output equals the same
+    layer run with all of its experts resident."""
+    import torch
+    H, I, NL, NE, K, NS = 256, 128, 4, 8, 3, 7
+    host = HostRuns(k3, dev, H, I, NL, NE, seed=5)
+    g = k3.synth.rng(6)
+    shared = [k3.synth.expert(g, H, I) for _ in range(NL)]
+    # the shared experts live in the pool too, pinned: they get the keys of extra experts
+    host_sh = []
+    rb = k3.pool_run_bytes(H, I)
+    dev_run = torch.empty(rb, dtype=torch.uint8, device=dev)
+    for e in shared:
+        k3.pool_pack(dev_run, k3.DeviceExpert.from_host(e, dev).q(), H, I)
+        host_sh.append(dev_run.cpu().pin_memory())
+
+    def src(layer, expert):
+        return host_sh[layer] if expert == NE else host(layer, expert)
+
+    pool = k3.ExpertPool(H, I, NL, NE + 1, NS + NL, src)
+    wf, wb = k3.synth.router_weights(g, NE, H)
+    W = T(wb.view(np.int16), dev).view(torch.bfloat16)
+    xf, xb = k3.synth.activations(g, 2, H)
+    x0 = T(xb.view(np.int16), dev).view(torch.bfloat16)
+    # routing for every layer from the resident reference layers
+    refs, routes = [], []
+    x = x0
+    for l in range(NL):
+        lay = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in host.experts[l * NE:(l + 1) * NE]],
+                                   k3.DeviceExpert.from_host(shared[l], dev), W, None, H, I, K, dev)
+        out, idx, wt = lay.decode(x)
+        refs.append(out.clone())
+        routes.append((idx.clone(), wt.clone()))
+        x = out.to(torch.bfloat16)
+    torch.cuda.synchronize()
+    shared_slots = [pool.pin(l, NE) for l in range(NL)]
+    run_ofs = [pool.run_table() for _ in range(NL)]
+    layers = [pool.layer(W, H, I, K, NE, run_ofs[l], shared_slot=shared_slots[l]) for l in range(NL)]
+    outs = []
+    x = x0
+    for l in range(NL):
+        idx, wt = routes[l]
+        ids = sorted(set(idx.cpu().numpy().ravel().tolist()))
+        pool.acquire(l, ids, run_of=run_ofs[l])
+        out = layers[l].decode_routed(x, idx, wt)
+        pool.release(l, ids)
+        outs.append(out)
+        x = out.to(torch.bfloat16)
+    torch.cuda.synchronize()
+    for l in range(NL):
+        assert np.array_equal(outs[l].cpu().numpy().view(np.uint32), refs[l].cpu().numpy().view(np.uint32)), l
+    st = pool.stats()
+    assert st["evictions"] > 0
+    pool.close()
