@@ -12,6 +12,7 @@ touches ~110 different experts (~2.6 GB): inputs larger than L2.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload prefill [--steps K] [--warmup W]   (config[2], one line)
   python bench.py --workload streamed [--steps K] [--warmup W]  (config[4], one line)
+  torchrun ... bench.py --workload ep --gpus N                   (config[3], one line)
 
 N > 1 (torchrun) runs N independent replicas (decode does not shard; scaling "weak").
 --impl reference times the reference's own CPU kernels (oracle/_ref, built from its
@@ -639,6 +640,117 @@ def run_streamed(args, ws, rank, local):
     }))
 
 
+# ------------------------------------------------------------------ expert parallel (config[3])
+EP_T = 16384
+EP_WORKLOAD = "config[3] expert-parallel MoE prefill: 16384 bf16 tokens sharded over the GPUs, 384 " \
+              "MXFP4 experts (7168->2048->7168) as 384/N contiguous ids per GPU + a shared expert on " \
+              "each, top-8 under a Zipf(1.1) selection bias (popularity over a random permutation of " \
+              "the ids), NCCL all-to-all dispatch and combine"
+
+
+def run_ep(args, ws, rank, local):
+    import datetime
+    import ctypes as C
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    else:
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29577", rank=0, world_size=1)
+    assert E % ws == 0
+    per = E // ws
+    lo, hi = rank * per, (rank + 1) * per
+    owner = torch.arange(E, device=dev) // per
+    # this rank's experts (distinct weights per id) + the shared expert, pool format
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    lay, run = k3.pool_layout(H, I)
+    blob = torch.empty((per + 1) * run, dtype=torch.uint8, device=dev)
+    b2 = blob.view(per + 1, run)
+    for name, (off, nb) in lay.items():
+        seg = b2[:, off:off + nb]
+        if name.endswith("_p"):
+            seg.copy_(torch.randint(0, 256, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+        else:
+            seg.copy_(torch.randint(118, 125, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+    gw = torch.Generator(device=dev)
+    gw.manual_seed(77)                                     # router W identical on every rank
+    W = (torch.randn((E, H), generator=gw, device=dev) * 0.02).to(torch.bfloat16)
+    sample = torch.randn((2048, H), generator=gw, device=dev).to(torch.bfloat16)
+    scores = torch.sigmoid(sample.float() @ W.float().T)
+    perm = torch.randperm(E, generator=torch.Generator().manual_seed(5)).to(dev)   # rank -> id
+    bias_rank = k3.synth.zipf_fit_bias(scores[:, perm], s=1.1, topk=K, iters=600)
+    bias = torch.empty_like(bias_rank)
+    bias[perm] = bias_rank
+    if ws > 1:
+        dist.broadcast(bias, 0)
+    run_of = torch.full((E,), -1, dtype=torch.int32, device=dev)
+    run_of[lo:hi] = torch.arange(per, dtype=torch.int32, device=dev)
+    none = torch.full((E,), -1, dtype=torch.int32, device=dev)
+    lr = k3.PoolMoeLayer(blob, per + 1, run_of, -1, W, bias, H, I, K, terms=2)
+    lsh = k3.PoolMoeLayer(blob, per + 1, none, per, W, bias, H, I, K, terms=2)
+    route, routed, shared = k3.ep.gpu_layer_fns(k3, lr, lsh, W, bias, K)
+    epl = k3.ep.ExpertParallel(owner, route, routed, shared)
+    T = EP_T // ws
+    gx = torch.Generator(device=dev)
+    gx.manual_seed(99 + rank)
+    xs = [torch.randn((T, H), generator=gx, device=dev).to(torch.bfloat16) for _ in range(2)]
+    for i in range(args.warmup):
+        epl.forward(xs[i % 2])
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(local)
+    launches0 = L.k3c_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    sent = 0
+    for i in range(args.steps):
+        epl.forward(xs[i % 2])
+        sent += epl.last["sent_tokens"]
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    dt_local = e0.elapsed_time(e1) / 1e3
+    t = torch.tensor([dt_local, float(sent)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        dt, sent_all = float(mx[0]), float(sm[1])
+    else:
+        dt, sent_all = dt_local, sent
+    launches = L.k3c_launch_count() - launches0
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    flop = (EP_T * K + EP_T) * 2 * 3 * I * H
+    print(json.dumps({
+        "metric": METRIC, "value": EP_T * args.steps / dt, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
+        "data": "synthetic",
+        "config": {"workload": EP_WORKLOAD, "tokens": EP_T, "hidden": H, "inter": I, "experts": E, "topk": K,
+                   "parallelism": f"ep{ws}"},
+        "useful_tflops": flop * args.steps / dt / 1e12,
+        "dispatch": {"token_rows_per_step": sent_all / args.steps,
+                     "dispatch_gb_per_step": sent_all / args.steps * H * 2 / 1e9,
+                     "combine_gb_per_step": sent_all / args.steps * H * 4 / 1e9,
+                     "collective": "torch.distributed all_to_all_single (NCCL)" if ws > 1 else "none (1 GPU)"},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -652,14 +764,17 @@ def main():
     ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
                     help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
     ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed"],
-                    help="decode: config[1] (the headline line); prefill: config[2]; streamed: config[4]")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed", "ep"],
+                    help="decode: config[1] (the headline line); prefill: config[2]; streamed: config[4]; "
+                         "ep: config[3] (expert-parallel prefill; torchrun for N > 1)")
     args = ap.parse_args()
     ws, rank, local = dist_setup(args)
     if args.workload == "prefill" and args.impl != "reference":
         run_prefill(args, ws, rank, local)
     elif args.workload == "streamed" and args.impl != "reference":
         run_streamed(args, ws, rank, local)
+    elif args.workload == "ep" and args.impl != "reference":
+        run_ep(args, ws, rank, local)
     elif args.impl == "reference":
         run_reference(args, ws, rank)
     else:

@@ -245,6 +245,13 @@ int k3c_moe_decode_tc_routed(float *out, const void *x, int x_dtype, int ntok,
  * outputs, drop counting and error behaviour as k3c_moe_decode_tc; hidden must be a multiple
  * of 256, inter of 128, x 16-byte aligned, ntok <= 65535. */
 size_t k3c_moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int ntok);
+/* Prefill with the routing given (idx/wt [ntok][topk] on the device); ids that are negative
+ * or not resident are skipped (counted in drops if drops is not NULL). With shared_run < 0
+ * the output is the routed experts' weighted sum only. Expert parallelism runs each GPU's
+ * received tokens through this with the experts of other GPUs marked -1. */
+int k3c_moe_prefill_tc_routed(float *out, const void *x, int x_dtype, int ntok,
+                              const k3c_moe_pool_layer *L, const int *idx, const float *wt,
+                              int *drops, void *scratch, size_t scratch_bytes, k3c_stream_t stream);
 int k3c_moe_prefill_tc(float *out, const void *x, int x_dtype, int ntok,
                        const k3c_moe_pool_layer *L, int *idx, float *wt, int *drops,
                        void *scratch, size_t scratch_bytes, k3c_stream_t stream);

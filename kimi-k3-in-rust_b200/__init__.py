@@ -13,7 +13,7 @@ import os
 
 import numpy as np
 
-from . import synth  # noqa: F401
+from . import ep, synth  # noqa: F401
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libk3cuda.so")
@@ -110,6 +110,7 @@ def lib():
         "k3c_pool_stats": ([vp, C.POINTER(PoolStatsC)], i),
         "k3c_pool_sync": ([vp], i),
         "k3c_moe_prefill_tc_scratch": ([C.POINTER(MoePoolLayerC), i], sz),
+        "k3c_moe_prefill_tc_routed": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
         "k3c_moe_prefill_tc": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
         "k3_mxfp4_dequant": ([vp, vp, vp, i, i, i], None),
         "k3_matmul_mxfp4": ([vp, vp, vp, vp, i, i, i], None),
@@ -474,6 +475,26 @@ class PoolMoeLayer:
                                               C.byref(self.c), _ptr(idx), _ptr(wt), _ptr(drops),
                                               _ptr(self._scratch), self._scratch.numel(), _stream()),
                "k3c_moe_decode_tc_routed")
+        return out
+
+    def prefill_routed(self, x, idx, wt, out=None, drops=None):
+        """prefill with the routing given (k3c_moe_prefill_tc_routed); ids < 0 are skipped."""
+        import torch
+        if x.dtype == torch.int16:
+            x = x.view(torch.bfloat16)
+        x = x.contiguous()
+        ntok = x.shape[0]
+        need = lib().k3c_moe_prefill_tc_scratch(C.byref(self.c), max(ntok, 1))
+        if self._scratch.numel() < need:
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        if out is None:
+            out = torch.empty((ntok, self.c.hidden), dtype=torch.float32, device=x.device)
+        if ntok == 0:
+            return out
+        _check(lib().k3c_moe_prefill_tc_routed(_ptr(out), _ptr(x), _dtype_code(x), ntok,
+                                               C.byref(self.c), _ptr(idx), _ptr(wt), _ptr(drops),
+                                               _ptr(self._scratch), self._scratch.numel(), _stream()),
+               "k3c_moe_prefill_tc_routed")
         return out
 
     def prefill(self, x, out=None, idx=None, wt=None, drops=None):

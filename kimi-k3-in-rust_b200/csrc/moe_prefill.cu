@@ -546,9 +546,11 @@ size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T) {
     return cv.used + 1024;
 }
 
+// routed: idx_out/wt_out hold the routing on entry (ids < 0 or not resident are skipped and
+// counted in drops when it is given) and the router is not run.
 int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k3c_moe_pool_layer *L,
                           int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
-                          cudaStream_t s) {
+                          cudaStream_t s, bool routed = false) {
     if (!L) return set_error(K3C_EINVAL, "moe_prefill_tc: null layer");
     const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->topk;
     if (H <= 0 || I <= 0 || H % PF_N || I % 128)
@@ -568,13 +570,16 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     int *idx = idx_out ? idx_out : b.idx;
     float *wt = wt_out ? wt_out : b.wt;
     const int P = T * K;
+    if (routed && (!idx_out || !wt_out)) return set_error(K3C_EINVAL, "moe_prefill_tc_routed: null routing");
     K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), s));
     // scale atoms of rows past a slot's pairs stay 2^0 (never NaN)
     K3C_TRY_CUDA(cudaMemsetAsync(b.actsf, 127, (size_t)b.max_slots * PF_J * (I / 128) * 512, s));
-    stage_begin(STAGE_ROUTER, s);
-    K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, H, E, K,
-                          L->renorm, L->routed_scale, T, b.rpart, s));
-    stage_end(STAGE_ROUTER, s);
+    if (!routed) {
+        stage_begin(STAGE_ROUTER, s);
+        K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, H, E,
+                              K, L->renorm, L->routed_scale, T, b.rpart, s));
+        stage_end(STAGE_ROUTER, s);
+    }
     // plan: counting sort of the pairs by expert
     const size_t csmem = ((size_t)E + PF_CHUNK) * sizeof(int);
     if (csmem > 48 * 1024) K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem));
@@ -654,6 +659,14 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
 
 extern "C" size_t k3c_moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int ntok) {
     return k3c::moe_prefill_tc_scratch(L, ntok);
+}
+
+extern "C" int k3c_moe_prefill_tc_routed(float *out, const void *x, int x_dtype, int ntok,
+                                         const k3c_moe_pool_layer *L, const int *idx, const float *wt, int *drops,
+                                         void *scratch, size_t scratch_bytes, k3c_stream_t stream) {
+    k3c::clear_error();
+    return k3c::launch_moe_prefill_tc(out, x, x_dtype, ntok, L, const_cast<int *>(idx), const_cast<float *>(wt),
+                                      drops, scratch, scratch_bytes, (cudaStream_t)stream, true);
 }
 
 extern "C" int k3c_moe_prefill_tc(float *out, const void *x, int x_dtype, int ntok, const k3c_moe_pool_layer *L,

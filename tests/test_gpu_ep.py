@@ -1,0 +1,70 @@
+"""Expert parallelism on two GPUs over NCCL: each rank's output equals the single-GPU
+tensor-core prefill of the same layer on its tokens (same activation terms; only the order in
+which the per-rank partial sums are added differs)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, err):
+    sys.path.insert(0, ROOT)
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from __graft_entry__ import load_package
+        k3 = load_package()
+        H, I, E, K, T = 256, 128, 8, 2, 200 + 37 * rank
+        g = k3.synth.rng(31)                               # the same model on every rank
+        experts = [k3.synth.expert(g, H, I) for _ in range(E)]
+        shared = k3.synth.expert(g, H, I)
+        wf, wb = k3.synth.router_weights(g, E, H)
+        wf = (wf * 20).astype(np.float32)
+        wb = k3.synth.bf16_bits(wf)
+        W = torch.from_numpy(wb.view(np.int16)).to(dev).view(torch.bfloat16)
+        full = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in experts],
+                                    k3.DeviceExpert.from_host(shared, dev), W, None, H, I, K, dev, terms=2)
+        per = E // world
+        owner = torch.arange(E, device=dev) // per
+        run_of = torch.full((E,), -1, dtype=torch.int32, device=dev)
+        run_of[rank * per:(rank + 1) * per] = full.run_of[rank * per:(rank + 1) * per]
+        none = torch.full((E,), -1, dtype=torch.int32, device=dev)
+        lr = k3.PoolMoeLayer(full.arena, E + 1, run_of, -1, W, None, H, I, K, terms=2)
+        lsh = k3.PoolMoeLayer(full.arena, E + 1, none, E, W, None, H, I, K, terms=2)
+        route, routed, sh = k3.ep.gpu_layer_fns(k3, lr, lsh, W, None, K)
+        ep = k3.ep.ExpertParallel(owner, route, routed, sh)
+        xb = k3.synth.bf16_bits(k3.synth.rng(500 + rank).standard_normal((T, H)).astype(np.float32))
+        x = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
+        y = ep.forward(x)
+        want, _, _ = full.prefill(x)
+        torch.cuda.synchronize()
+        y, want = y.cpu().numpy(), want.cpu().numpy()
+        rel = np.abs(y - want).max() / np.abs(want).max()
+        assert rel < 1e-5, rel
+    except Exception as e:
+        err.put(f"rank {rank}: {e!r}")
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_two_gpus_matches_single_gpu():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    err = mp.get_context("spawn").SimpleQueue()
+    mp.start_processes(_worker, args=(2, 29650, err), nprocs=2, join=True, start_method="spawn")
+    assert err.empty()
