@@ -13,6 +13,7 @@ touches ~110 different experts (~2.6 GB): inputs larger than L2.
   python bench.py --workload prefill [--steps K] [--warmup W]   (config[2], one line)
   python bench.py --workload streamed [--steps K] [--warmup W]  (config[4], one line)
   torchrun ... bench.py --workload ep --gpus N                   (config[3], one line)
+  python bench.py --workload expert [--steps K] [--warmup W]    (config[0], one line)
 
 N > 1 (torchrun) runs N independent replicas (decode does not shard; scaling "weak").
 --impl reference times the reference's own CPU kernels (oracle/_ref, built from its
@@ -640,6 +641,95 @@ def run_streamed(args, ws, rank, local):
     }))
 
 
+# ------------------------------------------------------------------ single expert (config[0])
+EX_WORKLOAD = "config[0] single MXFP4 expert SwiGLU FFN, 1 fp32 token per step (7168->2048->7168, " \
+              "E2M1 codes uniform, E8M0 uniform in [118,124]), fp32 accumulate"
+
+
+def run_expert(args, ws, rank, local):
+    """One step = one fp32 token through one expert (k3c_expert_ffn, the fp32-activation
+    CUDA-core path the 1e-5 tolerance calls for), rotating over 16 experts (374 MB, more than
+    L2) so every step streams its 23.4 MB from HBM."""
+    import ctypes as C
+    import torch
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    NX = 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242 + rank)
+    lay, run = k3.expert_run_layout(H, I)
+    blob = torch.empty(NX * run, dtype=torch.uint8, device=dev)
+    b2 = blob.view(NX, run)
+    for name, (off, nb) in lay.items():
+        seg = b2[:, off:off + nb]
+        if name.endswith("_p"):
+            seg.copy_(torch.randint(0, 256, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+        else:
+            seg.copy_(torch.randint(118, 125, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+    qs = k3.experts_from_blob(blob, NX, H, I)
+    xs = torch.randn((NX, H), generator=g, device=dev)
+    y = torch.empty((1, H), dtype=torch.float32, device=dev)
+    nbytes = L.k3c_expert_ffn_scratch(1, H, I)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    stream = k3._stream()
+
+    def step(i, x=None):
+        q = qs[i % NX]
+        xx = xs[i % NX:i % NX + 1] if x is None else x
+        rc = L.k3c_expert_ffn(C.c_void_p(y.data_ptr()), C.c_void_p(xx.data_ptr()), 1, C.byref(q), H, I, 0,
+                              C.c_void_p(scratch.data_ptr()), nbytes, stream)
+        assert rc == 0, L.k3c_last_error()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clk = Clocks(local)
+    launches0 = L.k3c_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    launches = L.k3c_launch_count() - launches0
+    dt = e0.elapsed_time(e1) / 1e3
+    # end to end: the token from pinned host memory, the output back, every step
+    hx = xs.cpu().pin_memory()
+    hy = torch.empty((1, H), dtype=torch.float32).pin_memory()
+    xd = torch.empty((1, H), dtype=torch.float32, device=dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(args.steps):
+        xd.copy_(hx[i % NX:i % NX + 1], non_blocking=True)
+        step(i, xd)
+        hy.copy_(y, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    dte = f0.elapsed_time(f1) / 1e3
+    if rank != 0:
+        return
+    hbm, _, kind = peaks()
+    achieved = args.steps * run / dt / 1e9
+    print(json.dumps({
+        "metric": "MXFP4 expert tokens/s", "value": args.steps / dt, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (MXFP4 weights, fp32 activations, fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": EX_WORKLOAD, "hidden": H, "inter": I,
+                   "l2": "16 experts rotated (374 MB) > L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "kernel": "gate/up + down CUDA-core GEMVs (k3c_expert_ffn)",
+                     "bytes_per_token": run, "peak_kind": kind},
+        "e2e": {"value": args.steps / dte, "unit": UNIT, "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }))
+
+
 # ------------------------------------------------------------------ expert parallel (config[3])
 EP_T = 16384
 EP_WORKLOAD = "config[3] expert-parallel MoE prefill: 16384 bf16 tokens sharded over the GPUs, 384 " \
@@ -764,7 +854,7 @@ def main():
     ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
                     help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
     ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed", "ep"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed", "ep", "expert"],
                     help="decode: config[1] (the headline line); prefill: config[2]; streamed: config[4]; "
                          "ep: config[3] (expert-parallel prefill; torchrun for N > 1)")
     args = ap.parse_args()
@@ -775,6 +865,8 @@ def main():
         run_streamed(args, ws, rank, local)
     elif args.workload == "ep" and args.impl != "reference":
         run_ep(args, ws, rank, local)
+    elif args.workload == "expert" and args.impl != "reference":
+        run_expert(args, ws, rank, local)
     elif args.impl == "reference":
         run_reference(args, ws, rank)
     else:
