@@ -13,8 +13,10 @@
 //         a double sum and a float inverse (:469-474); times routed_scale (:475).
 #include <cuda_runtime.h>
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
+#include "rt_tc.cuh"
 
 namespace k3c {
 
@@ -238,6 +240,30 @@ __device__ __forceinline__ float sigmoid_score(double logit_d) {
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
 }
 
+// The tensor-core logit of (token, expert e) completed with the residual terms, or the
+// plain double dot product (the reference's own summation order) when either list overflowed.
+__device__ __noinline__ double rt_finish(const RtFix &fix, double logit, const uint16_t *xrow, int nx, int ex,
+                                         const int *s_xk, const float *s_xr, int e, int n_experts) {
+    const uint16_t *wrow = fix.W + (size_t)e * fix.H;
+    const int nw = fix.wcnt[e];
+    if (nx > fix.cap || nw > fix.cap) {
+        double acc = 0.0;
+        for (int k = 0; k < fix.H; k++)
+            acc += (double)bf16_bits_to_f32(wrow[k]) * (double)bf16_bits_to_f32(xrow[k]);
+        return acc;
+    }
+    double c = 0.0;
+    for (int i = 0; i < nx; i++) c += (double)s_xr[i] * (double)bf16_bits_to_f32(wrow[s_xk[i]]);
+    for (int i = 0; i < nw; i++) {
+        const int k = fix.wk[(size_t)i * n_experts + e];
+        const float xv = bf16_bits_to_f32(xrow[k]);
+        int q0, q1, q2;
+        const float rx = rt_split(xv, ex, q0, q1, q2);
+        c += (double)(xv - rx) * (double)fix.wr[(size_t)i * n_experts + e];
+    }
+    return logit + c;
+}
+
 // One block per token. With `part`, all threads first form the scores from the logit chunks
 // (added in chunk order) and write them to `scores` if that is not null; otherwise `scores`
 // holds them on entry. Warp 0 then takes the top-k by repeated warp argmax over score+bias.
@@ -246,13 +272,27 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
                                                        const double *__restrict__ part, int nchunk,
                                                        const float *__restrict__ bias,
                                                        int n_experts, int topk, int renorm,
-                                                       float routed_scale, int ntok) {
+                                                       float routed_scale, int ntok, RtFix fix) {
     extern __shared__ float ch[];  // [2][n_experts]: choice values, scores
+    __shared__ int s_xk[RT_CAP];
+    __shared__ float s_xr[RT_CAP];
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x;
     grid_dep_wait();   // the logit chunks come from the partial kernel
     float *c = ch;
     float *sc = ch + n_experts;
+    int nx = 0, ex = 0;
+    const uint16_t *xrow = nullptr;
+    if (fix.x) {   // this token's residual list, for the tensor-core logits
+        nx = fix.xcnt[t];
+        ex = fix.xexp[t];
+        xrow = fix.x + (size_t)t * fix.H;
+        for (int i = threadIdx.x; i < nx && i < fix.cap; i += blockDim.x) {
+            s_xk[i] = fix.xk[(size_t)t * fix.cap + i];
+            s_xr[i] = fix.xr[(size_t)t * fix.cap + i];
+        }
+        __syncthreads();
+    }
     for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
         float v;
         if (part) {
@@ -267,6 +307,7 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
                 for (int k = 0; k < 16; k++)
                     if (k0 + k < nchunk) logit += v16[k];
             }
+            if (fix.x) logit = rt_finish(fix, logit, xrow, nx, ex, s_xk, s_xr, e, n_experts);
             v = sigmoid_score(logit);
             if (scores) scores[(size_t)t * n_experts + e] = v;
         } else {
@@ -346,7 +387,7 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
 
 static int launch_select(int *idx, float *w, float *scores, const double *part, int nchunk,
                          const float *bias, int n_experts, int topk, int renorm, float routed_scale,
-                         int ntok, cudaStream_t s) {
+                         int ntok, cudaStream_t s, RtFix fix = RtFix{}) {
     if (n_experts <= 0 || topk <= 0 || topk > K3_MAX_TOPK || ntok < 0)
         return set_error(K3C_EINVAL, "router_select: n_experts=%d topk=%d ntok=%d", n_experts,
                          topk, ntok);
@@ -357,7 +398,7 @@ static int launch_select(int *idx, float *w, float *scores, const double *part, 
         K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     count_launch();
     K3C_TRY_CUDA(launch_pdl(k_router_select, dim3(ntok), dim3(256), smem, s, idx, w, scores, part, nchunk, bias,
-                            n_experts, topk, renorm, routed_scale, ntok));
+                            n_experts, topk, renorm, routed_scale, ntok, fix));
     return K3C_OK;
 }
 
@@ -380,8 +421,14 @@ static int sm_count_rt() {
 }
 static int router_nparts(int hidden, int n_experts, int ntok);
 
+// Enough for either logit path (the operand dtypes are not known here).
 size_t router_scratch_bytes(int hidden, int n_experts, int ntok) {
-    return (size_t)router_nparts(hidden, n_experts, ntok) * ntok * n_experts * sizeof(double);
+    size_t b = (size_t)router_nparts(hidden, n_experts, ntok) * ntok * n_experts * sizeof(double);
+    if (router_tc_applies(K3C_BF16, K3C_BF16, hidden, ntok)) {
+        const size_t t = router_tc_scratch_bytes(hidden, n_experts, ntok);
+        if (t > b) b = t;
+    }
+    return b;
 }
 
 // K chunks per block: 1 (most parallel) unless the grid would exceed about three waves,
@@ -430,6 +477,15 @@ int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
     if (hidden <= 0 || n_experts <= 0) return set_error(K3C_EINVAL, "router: hidden=%d n_experts=%d", hidden, n_experts);
     if (ntok == 0) return K3C_OK;
     int rc;
+    if (router_tc_applies(x_dtype, w_dtype, hidden, ntok) && ((uintptr_t)x % 16) == 0 && ((uintptr_t)W % 16) == 0) {
+        RtFix fix;
+        double *tpart = nullptr;
+        int S = 1;
+        K3C_TRY(launch_router_tc(&fix, &tpart, &S, x, W, hidden, n_experts, ntok, part, s));
+        K3C_TRY(launch_select(idx, w, scores, tpart, S, bias, n_experts, topk, renorm, routed_scale, ntok, s, fix));
+        static const int sync_check = getenv("K3C_SYNC_CHECK") ? 1 : 0;
+        return sync_check ? router_tc_check(s) : K3C_OK;
+    }
     if (w_dtype == K3C_BF16 && x_dtype == K3C_BF16) rc = launch_partial_t<uint16_t, uint16_t>(part, x, W, hidden, n_experts, ntok, s);
     else if (w_dtype == K3C_BF16 && x_dtype == K3C_F32) rc = launch_partial_t<uint16_t, float>(part, x, W, hidden, n_experts, ntok, s);
     else if (w_dtype == K3C_F32 && x_dtype == K3C_BF16) rc = launch_partial_t<float, uint16_t>(part, x, W, hidden, n_experts, ntok, s);
