@@ -118,17 +118,77 @@ __global__ void __launch_bounds__(1024) k_moe_plan(Plan p, const int *__restrict
     }
 }
 
-// Single-expert plan for k3c_expert_ffn: slot 0 = e, pairs t -> (t, 0).
-__global__ void k_ffn_plan(Plan p, K3ExpertQ e, int ntok) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) {
-        *p.n_slots = 1;
-        p.slots[0].q = e;
-        p.slots[0].ntok = ntok;
-        p.slots[0].pair_base = 0;
+// ------------------------------------------------------- single expert (k3c_expert_ffn)
+// gate/up + activation for every token: grid ceil(inter/8), warp w takes gate row and up row
+// r = 8*bx + w with CPL weight chunks per lane requested at once.
+template <int NT, int CPL>
+__global__ void __launch_bounds__(256) k_ffn_gateup(K3ExpertQ q, const float *__restrict__ x, int ntok,
+                                                    int hidden, int inter, int act, float *__restrict__ actbuf) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // the down kernel may start fetching
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    if (r >= inter) return;
+    const size_t pitch = (size_t)hidden / 2, spitch = (size_t)hidden / 32;
+    const uint8_t *prow[2] = {q.p1 + r * pitch, q.p3 + r * pitch};
+    const uint8_t *srow[2] = {q.s1 + r * spitch, q.s3 + r * spitch};
+    for (int t0 = 0; t0 < ntok; t0 += NT) {
+        const int nt = ntok - t0 < NT ? ntok - t0 : NT;
+        const float *xrow[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) xrow[t] = x + (size_t)(t0 + (t < nt ? t : 0)) * hidden;
+        float acc[2][NT];
+        mx_dot_rows<2, NT, CPL>(prow, srow, xrow, nt, hidden / 32, acc);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const float g = warp_sum(acc[0][t]);
+            const float u = warp_sum(acc[1][t]);
+            if (lane == 0 && t < nt) actbuf[(size_t)(t0 + t) * inter + r] = act_fn(g, u, act);
+        }
     }
-    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < ntok; t += gridDim.x * blockDim.x) {
-        p.pair_tok[t] = t;
-        p.pair_k[t] = 0;
+}
+
+// down: grid ceil(hidden/16), warp w takes rows 2*(8*bx+w)+{0,1}. Launched as a programmatic
+// dependent of k_ffn_gateup: the first weight chunks are requested before the wait for the
+// activations.
+template <int NT, int CPL>
+__global__ void __launch_bounds__(256) k_ffn_down(K3ExpertQ q, const float *__restrict__ actbuf, int ntok,
+                                                  int hidden, int inter, float *__restrict__ y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = (blockIdx.x * 8 + warp) * 2;
+    const bool live = r0 < hidden;
+    const int r1 = r0 + 1 < hidden ? r0 + 1 : r0;
+    const size_t pitch = (size_t)inter / 2, spitch = (size_t)inter / 32;
+    const int nchunk = inter / 32;
+    const uint8_t *prow[2] = {q.p2 + (size_t)(live ? r0 : 0) * pitch, q.p2 + (size_t)(live ? r1 : 0) * pitch};
+    const uint8_t *srow[2] = {q.s2 + (size_t)(live ? r0 : 0) * spitch, q.s2 + (size_t)(live ? r1 : 0) * spitch};
+    MxChunks<2, CPL> ch;
+    if (live) ch.load(prow, srow, 0, nchunk);
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // actbuf is complete
+    if (!live) return;
+    for (int t0 = 0; t0 < ntok; t0 += NT) {
+        const int nt = ntok - t0 < NT ? ntok - t0 : NT;
+        const float *xrow[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) xrow[t] = actbuf + (size_t)(t0 + (t < nt ? t : 0)) * inter;
+        float acc[2][NT];
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+#pragma unroll
+            for (int t = 0; t < NT; t++) acc[r][t] = 0.f;
+        for (int c0 = 0; c0 < nchunk; c0 += 32 * CPL) {
+            if (c0 > 0 || t0 > 0) ch.load(prow, srow, c0, nchunk);
+            ch.template fma<NT>(xrow, nt, c0, nchunk, acc);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const float a0 = warp_sum(acc[0][t]);
+            const float a1 = warp_sum(acc[1][t]);
+            if (lane == 0 && t < nt) {
+                float *o = y + (size_t)(t0 + t) * hidden;
+                o[r0] = a0;
+                if (r1 != r0) o[r1] = a1;
+            }
+        }
     }
 }
 
@@ -279,9 +339,7 @@ static char *const kSizingBase = reinterpret_cast<char *>(4096);
 
 size_t ffn_scratch(int ntok, int hidden, int inter) {
     Carve cv{kSizingBase, (size_t)-1 / 2, 0};
-    Plan p;
-    carve_plan(cv, p, 1, ntok, 0);
-    cv.take<float>((size_t)ntok * inter);
+    cv.take<float>((size_t)(ntok > 0 ? ntok : 1) * inter);
     return cv.used + 256;
 }
 
@@ -292,13 +350,22 @@ int launch_expert_ffn(float *y, const float *x, int ntok, const K3ExpertQ *e, in
     if (ntok <= 0) return K3C_OK;
     if (((uintptr_t)x & 15) != 0) return set_error(K3C_EINVAL, "expert_ffn: x not 16-byte aligned");
     Carve cv{(char *)scratch, scratch_bytes, 0};
-    Plan p;
-    if (!carve_plan(cv, p, 1, ntok, 0)) return set_error(K3C_EINVAL, "expert_ffn: scratch too small");
     float *actbuf = cv.take<float>((size_t)ntok * inter);
     if (!actbuf) return set_error(K3C_EINVAL, "expert_ffn: scratch too small (%zu)", scratch_bytes);
-    k_ffn_plan<<<1, 256, 0, s>>>(p, *e, ntok);
-    K3C_CHECK_LAUNCH();
-    return launch_ffn_kernels(p, 1, x, hidden, inter, act, actbuf, 1, y, ntok, s);
+    const dim3 ga((inter + 7) / 8), gd((hidden + 15) / 16);
+    if (ntok <= 1) {
+        k_ffn_gateup<1, 8><<<ga, 256, 0, s>>>(*e, x, ntok, hidden, inter, act, actbuf);
+        K3C_CHECK_LAUNCH();
+        K3C_TRY_CUDA(launch_pdl(k_ffn_down<1, 2>, gd, dim3(256), 0, s, *e, (const float *)actbuf, ntok, hidden,
+                                inter, y));
+    } else {
+        k_ffn_gateup<4, 4><<<ga, 256, 0, s>>>(*e, x, ntok, hidden, inter, act, actbuf);
+        K3C_CHECK_LAUNCH();
+        K3C_TRY_CUDA(launch_pdl(k_ffn_down<4, 2>, gd, dim3(256), 0, s, *e, (const float *)actbuf, ntok, hidden,
+                                inter, y));
+    }
+    count_launch();
+    return K3C_OK;
 }
 
 struct DecodeBufs {

@@ -35,9 +35,18 @@ class ExpertParallel:
         self.rank = dist.get_rank(group)
         self.last = {}
 
+    def _a2a(self, out, inp, out_splits=None, in_splits=None):
+        """all_to_all_single; on a one-rank group the exchange is the identity (a copy), which
+        keeps device tensors off a host-staged backend."""
+        import torch.distributed as dist
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                                   group=self.group)
+
     def forward(self, x):
         import torch
-        import torch.distributed as dist
         T, H = x.shape
         N = self.world
         idx, wt = self.route(x)
@@ -49,26 +58,22 @@ class ExpertParallel:
         send_tok = pairs[:, 1]
         send_counts = member.sum(0).to(torch.int64)                    # tokens to each rank
         recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        self._a2a(recv_counts, send_counts)
         ss = send_counts.cpu().tolist()
         rs = recv_counts.cpu().tolist()
         R = sum(rs)
         recv_x = x.new_empty((R, H))
-        dist.all_to_all_single(recv_x, x[send_tok].contiguous(), output_split_sizes=rs,
-                               input_split_sizes=ss, group=self.group)
+        self._a2a(recv_x, x[send_tok].contiguous(), rs, ss)
         K = idx.shape[1]
         recv_idx = idx.new_empty((R, K))
-        dist.all_to_all_single(recv_idx, idx[send_tok].contiguous(), output_split_sizes=rs,
-                               input_split_sizes=ss, group=self.group)
+        self._a2a(recv_idx, idx[send_tok].contiguous(), rs, ss)
         recv_wt = wt.new_empty((R, K))
-        dist.all_to_all_single(recv_wt, wt[send_tok].contiguous(), output_split_sizes=rs,
-                               input_split_sizes=ss, group=self.group)
+        self._a2a(recv_wt, wt[send_tok].contiguous(), rs, ss)
         # 3. compute over this rank's experts
         part = self.routed(recv_x, recv_idx, recv_wt)                  # [R, H] fp32
         # 4. combine: partials back in the order they were sent
         back = part.new_empty((len(send_tok), H))
-        dist.all_to_all_single(back, part.contiguous(), output_split_sizes=ss,
-                               input_split_sizes=rs, group=self.group)
+        self._a2a(back, part.contiguous(), ss, rs)
         y = self.shared(x)
         off = 0
         for r in range(N):                 # fixed rank order; one row per token per rank
