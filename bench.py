@@ -396,14 +396,15 @@ def run_prefill(args, ws, rank, local):
     L = k3.lib()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    blob, layer0, _, _ = build_device_workload(k3, dev, 1234 + rank, E, "tc", 2)
+    D = args.distinct                                    # < 384 only for small profiling runs
+    blob, layer0, _, _ = build_device_workload(k3, dev, 1234 + rank, D, "tc", 2)
     W = layer0.router_w
     g = torch.Generator(device=dev)
     g.manual_seed(77 + rank)
     sample = torch.randn((2048, H), generator=g, device=dev).to(torch.bfloat16)
     scores = torch.sigmoid(sample.float() @ W.float().T)
     bias = k3.synth.zipf_fit_bias(scores, s=1.1, topk=K, iters=600)
-    layer = k3.PoolMoeLayer(blob, E + 1, layer0.run_of, E, W, bias, H, I, K, terms=2)
+    layer = k3.PoolMoeLayer(blob, D + 1, layer0.run_of, D, W, bias, H, I, K, terms=2)
     NB = 2
     xs = [torch.randn((PF_T, H), generator=g, device=dev).to(torch.bfloat16) for _ in range(NB)]
     host_x = xs[0].cpu().pin_memory()
@@ -469,7 +470,8 @@ def run_prefill(args, ws, rank, local):
         "data": "synthetic",
         "config": {"workload": PF_WORKLOAD, "tokens": PF_T, "hidden": H, "inter": I, "experts": E,
                    "topk": K, "parallelism": "single GPU",
-                   "l2": "inputs larger than L2: ~9 GB of expert weights per step"},
+                   "l2": "inputs larger than L2: ~9 GB of expert weights per step",
+                   "distinct_expert_weights": D},
         "routing": {"unique_experts": float(np.mean(uniq)), "top1_share": float(pop[0]),
                     "top10_share": float(pop[:10].sum()),
                     "zipf_topk_target": {"top1": float(target[0]), "top10": float(target[:10].sum())},

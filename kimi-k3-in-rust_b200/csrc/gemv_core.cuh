@@ -36,6 +36,61 @@ struct MxChunks {
         }
     }
 
+    // fma with the activation rows in shared memory (row t at sx + t * ld, x_swz order)
+    template <int NT>
+    __device__ __forceinline__ void fma_smem(const float *sx, int ld, int ntok, int c0, int nchunk,
+                                             float (&acc)[RW][NT]) const {
+        const int lane = threadIdx.x & 31;
+#pragma unroll
+        for (int i = 0; i < CPL; i++) {
+            const int c = c0 + lane + 32 * i;
+            if (c >= nchunk) break;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                float xv[NT][8];
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    if (t < ntok) {
+                        const float *xr = sx + t * ld + (c << 5);
+                        const float4 a = *reinterpret_cast<const float4 *>(xr + (((2 * q) ^ (c & 7)) << 2));
+                        const float4 b = *reinterpret_cast<const float4 *>(xr + (((2 * q + 1) ^ (c & 7)) << 2));
+                        xv[t][0] = a.x; xv[t][1] = a.y; xv[t][2] = a.z; xv[t][3] = a.w;
+                        xv[t][4] = b.x; xv[t][5] = b.y; xv[t][6] = b.z; xv[t][7] = b.w;
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 8; k++) xv[t][k] = 0.f;
+                    }
+                }
+                mac(i, q, xv, acc);
+            }
+        }
+    }
+
+    // the weight side of one 8-element group: decode, scale, multiply-add into acc
+    template <int NT>
+    __device__ __forceinline__ void mac(int i, int q, const float (&xv)[NT][8], float (&acc)[RW][NT]) const {
+#pragma unroll
+        for (int r = 0; r < RW; r++) {
+            if (sb[i][r] == 255u) continue;
+            const uint32_t w = q == 0 ? wv[i][r].x : q == 1 ? wv[i][r].y : q == 2 ? wv[i][r].z : wv[i][r].w;
+            float f[8];
+            e2m1x8_to_f32(w, f);
+            const float sc = e8m0_to_f32(sb[i][r]);
+            const bool fold = sb[i][r] >= 250u;
+            if (fold) {
+#pragma unroll
+                for (int k = 0; k < 8; k++) f[k] *= sc;
+            }
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                float p = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; k++) p = fmaf(f[k], xv[t][k], p);
+                acc[r][t] = fold ? acc[r][t] + p : fmaf(p, sc, acc[r][t]);
+            }
+        }
+    }
+
     template <int NT>
     __device__ __forceinline__ void fma(const float *const (&xrow)[NT], int ntok, int c0, int nchunk,
                                         float (&acc)[RW][NT]) const {
@@ -59,30 +114,26 @@ struct MxChunks {
                         for (int k = 0; k < 8; k++) xv[t][k] = 0.f;
                     }
                 }
-#pragma unroll
-                for (int r = 0; r < RW; r++) {
-                    if (sb[i][r] == 255u) continue;
-                    const uint32_t w = q == 0 ? wv[i][r].x : q == 1 ? wv[i][r].y : q == 2 ? wv[i][r].z : wv[i][r].w;
-                    float f[8];
-                    e2m1x8_to_f32(w, f);
-                    const float sc = e8m0_to_f32(sb[i][r]);
-                    const bool fold = sb[i][r] >= 250u;
-                    if (fold) {
-#pragma unroll
-                        for (int k = 0; k < 8; k++) f[k] *= sc;
-                    }
-#pragma unroll
-                    for (int t = 0; t < NT; t++) {
-                        float p = 0.f;
-#pragma unroll
-                        for (int k = 0; k < 8; k++) p = fmaf(f[k], xv[t][k], p);
-                        acc[r][t] = fold ? acc[r][t] + p : fmaf(p, sc, acc[r][t]);
-                    }
-                }
+                mac(i, q, xv, acc);
             }
         }
     }
 };
+
+// Activations staged in shared memory for MxChunks::fma_smem: element e = 32c + 4u + w of a
+// row is stored at 32c + 4(u ^ (c & 7)) + w, so the eight lanes reading chunks c..c+7 touch
+// eight different 16-byte units and a warp's float4 reads cost the minimum four wavefronts
+// (unswizzled, the 128-byte chunk stride puts every lane on the same four banks).
+__device__ __forceinline__ int x_swz(int e) {
+    const int c = e >> 5;
+    return (c << 5) | ((((e >> 2) & 7) ^ (c & 7)) << 2) | (e & 3);
+}
+// Copies n floats (n a multiple of 4, src 16-byte aligned) into dst in the swizzled order;
+// every thread of the block takes part.
+__device__ __forceinline__ void stage_x_swz(float *dst, const float *__restrict__ src, int n) {
+    for (int v = threadIdx.x; v < n / 4; v += blockDim.x)
+        *reinterpret_cast<float4 *>(dst + x_swz(4 * v)) = __ldg(reinterpret_cast<const float4 *>(src) + v);
+}
 
 template <int RW, int NT, int CPL = 4>
 __device__ __forceinline__ void mx_dot_rows(const uint8_t *const (&prow)[RW],

@@ -119,40 +119,55 @@ __global__ void __launch_bounds__(1024) k_moe_plan(Plan p, const int *__restrict
 }
 
 // ------------------------------------------------------- single expert (k3c_expert_ffn)
-// gate/up + activation for every token: grid ceil(inter/8), warp w takes gate row and up row
-// r = 8*bx + w with CPL weight chunks per lane requested at once.
+// gate/up + activation: grid ceil(inter/8), warp w takes gate row and up row r = 8*bx + w,
+// CPL weight chunks per lane requested at once (the first ones before the activations are
+// staged); the NT token rows sit in shared memory in the x_swz order. Dynamic shared memory:
+// NT * hidden floats.
 template <int NT, int CPL>
 __global__ void __launch_bounds__(256) k_ffn_gateup(K3ExpertQ q, const float *__restrict__ x, int ntok,
                                                     int hidden, int inter, int act, float *__restrict__ actbuf) {
+    extern __shared__ __align__(16) float ffn_sx[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // the down kernel may start fetching
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 8 + warp;
-    if (r >= inter) return;
+    const bool live = r < inter;
     const size_t pitch = (size_t)hidden / 2, spitch = (size_t)hidden / 32;
-    const uint8_t *prow[2] = {q.p1 + r * pitch, q.p3 + r * pitch};
-    const uint8_t *srow[2] = {q.s1 + r * spitch, q.s3 + r * spitch};
+    const int nchunk = hidden / 32;
+    const uint8_t *prow[2] = {q.p1 + (size_t)(live ? r : 0) * pitch, q.p3 + (size_t)(live ? r : 0) * pitch};
+    const uint8_t *srow[2] = {q.s1 + (size_t)(live ? r : 0) * spitch, q.s3 + (size_t)(live ? r : 0) * spitch};
+    MxChunks<2, CPL> ch;
+    if (live) ch.load(prow, srow, 0, nchunk);
     for (int t0 = 0; t0 < ntok; t0 += NT) {
         const int nt = ntok - t0 < NT ? ntok - t0 : NT;
-        const float *xrow[NT];
-#pragma unroll
-        for (int t = 0; t < NT; t++) xrow[t] = x + (size_t)(t0 + (t < nt ? t : 0)) * hidden;
+        if (t0) __syncthreads();                  // every warp is done with the previous rows
+        for (int t = 0; t < nt; t++) stage_x_swz(ffn_sx + t * hidden, x + (size_t)(t0 + t) * hidden, hidden);
+        __syncthreads();
         float acc[2][NT];
-        mx_dot_rows<2, NT, CPL>(prow, srow, xrow, nt, hidden / 32, acc);
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int t = 0; t < NT; t++) acc[i][t] = 0.f;
+        for (int c0 = 0; c0 < nchunk; c0 += 32 * CPL) {
+            if (!live) break;
+            if (c0 > 0 || t0 > 0) ch.load(prow, srow, c0, nchunk);
+            ch.template fma_smem<NT>(ffn_sx, hidden, nt, c0, nchunk, acc);
+        }
 #pragma unroll
         for (int t = 0; t < NT; t++) {
             const float g = warp_sum(acc[0][t]);
             const float u = warp_sum(acc[1][t]);
-            if (lane == 0 && t < nt) actbuf[(size_t)(t0 + t) * inter + r] = act_fn(g, u, act);
+            if (live && lane == 0 && t < nt) actbuf[(size_t)(t0 + t) * inter + r] = act_fn(g, u, act);
         }
     }
 }
 
 // down: grid ceil(hidden/16), warp w takes rows 2*(8*bx+w)+{0,1}. Launched as a programmatic
 // dependent of k_ffn_gateup: the first weight chunks are requested before the wait for the
-// activations.
+// activations, which are then staged like k_ffn_gateup's (NT * inter floats).
 template <int NT, int CPL>
 __global__ void __launch_bounds__(256) k_ffn_down(K3ExpertQ q, const float *__restrict__ actbuf, int ntok,
                                                   int hidden, int inter, float *__restrict__ y) {
+    extern __shared__ __align__(16) float ffn_sa[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = (blockIdx.x * 8 + warp) * 2;
     const bool live = r0 < hidden;
@@ -164,32 +179,51 @@ __global__ void __launch_bounds__(256) k_ffn_down(K3ExpertQ q, const float *__re
     MxChunks<2, CPL> ch;
     if (live) ch.load(prow, srow, 0, nchunk);
     asm volatile("griddepcontrol.wait;" ::: "memory");   // actbuf is complete
-    if (!live) return;
     for (int t0 = 0; t0 < ntok; t0 += NT) {
         const int nt = ntok - t0 < NT ? ntok - t0 : NT;
-        const float *xrow[NT];
-#pragma unroll
-        for (int t = 0; t < NT; t++) xrow[t] = actbuf + (size_t)(t0 + (t < nt ? t : 0)) * inter;
+        if (t0) __syncthreads();
+        for (int t = 0; t < nt; t++) stage_x_swz(ffn_sa + t * inter, actbuf + (size_t)(t0 + t) * inter, inter);
+        __syncthreads();
         float acc[2][NT];
 #pragma unroll
-        for (int r = 0; r < 2; r++)
+        for (int i = 0; i < 2; i++)
 #pragma unroll
-            for (int t = 0; t < NT; t++) acc[r][t] = 0.f;
+            for (int t = 0; t < NT; t++) acc[i][t] = 0.f;
         for (int c0 = 0; c0 < nchunk; c0 += 32 * CPL) {
+            if (!live) break;
             if (c0 > 0 || t0 > 0) ch.load(prow, srow, c0, nchunk);
-            ch.template fma<NT>(xrow, nt, c0, nchunk, acc);
+            ch.template fma_smem<NT>(ffn_sa, inter, nt, c0, nchunk, acc);
         }
 #pragma unroll
         for (int t = 0; t < NT; t++) {
             const float a0 = warp_sum(acc[0][t]);
             const float a1 = warp_sum(acc[1][t]);
-            if (lane == 0 && t < nt) {
+            if (live && lane == 0 && t < nt) {
                 float *o = y + (size_t)(t0 + t) * hidden;
                 o[r0] = a0;
                 if (r1 != r0) o[r1] = a1;
             }
         }
     }
+}
+
+template <int NT>
+static int launch_ffn_pair(const K3ExpertQ &e, const float *x, int ntok, int hidden, int inter, int act,
+                           float *actbuf, float *y, cudaStream_t s) {
+    constexpr int CG = NT == 1 ? 8 : 4;
+    const size_t sg = (size_t)NT * hidden * sizeof(float), sd = (size_t)NT * inter * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k_ffn_gateup<NT, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k_ffn_down<NT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr = true;
+    }
+    k_ffn_gateup<NT, CG><<<(inter + 7) / 8, 256, sg, s>>>(e, x, ntok, hidden, inter, act, actbuf);
+    K3C_CHECK_LAUNCH();
+    K3C_TRY_CUDA(launch_pdl(k_ffn_down<NT, 2>, dim3((hidden + 15) / 16), dim3(256), sd, s, e, (const float *)actbuf,
+                            ntok, hidden, inter, y));
+    count_launch();
+    return K3C_OK;
 }
 
 // ---------------------------------------------------------------- gate/up + act
@@ -352,20 +386,10 @@ int launch_expert_ffn(float *y, const float *x, int ntok, const K3ExpertQ *e, in
     Carve cv{(char *)scratch, scratch_bytes, 0};
     float *actbuf = cv.take<float>((size_t)ntok * inter);
     if (!actbuf) return set_error(K3C_EINVAL, "expert_ffn: scratch too small (%zu)", scratch_bytes);
-    const dim3 ga((inter + 7) / 8), gd((hidden + 15) / 16);
-    if (ntok <= 1) {
-        k_ffn_gateup<1, 8><<<ga, 256, 0, s>>>(*e, x, ntok, hidden, inter, act, actbuf);
-        K3C_CHECK_LAUNCH();
-        K3C_TRY_CUDA(launch_pdl(k_ffn_down<1, 2>, gd, dim3(256), 0, s, *e, (const float *)actbuf, ntok, hidden,
-                                inter, y));
-    } else {
-        k_ffn_gateup<4, 4><<<ga, 256, 0, s>>>(*e, x, ntok, hidden, inter, act, actbuf);
-        K3C_CHECK_LAUNCH();
-        K3C_TRY_CUDA(launch_pdl(k_ffn_down<4, 2>, gd, dim3(256), 0, s, *e, (const float *)actbuf, ntok, hidden,
-                                inter, y));
-    }
-    count_launch();
-    return K3C_OK;
+    if ((size_t)(hidden > inter ? hidden : inter) * 4 * 4 > 200 * 1024)
+        return set_error(K3C_EINVAL, "expert_ffn: hidden=%d inter=%d too large (12800 at most)", hidden, inter);
+    return ntok <= 1 ? launch_ffn_pair<1>(*e, x, ntok, hidden, inter, act, actbuf, y, s)
+                     : launch_ffn_pair<4>(*e, x, ntok, hidden, inter, act, actbuf, y, s);
 }
 
 struct DecodeBufs {

@@ -228,8 +228,10 @@ __global__ void __launch_bounds__(256) k_pf_slot_sf(uint8_t *__restrict__ sfa, c
 
 // ------------------------------------------------------------------ persistent tcgen05 kernel
 struct PfArgs {
-    const int *n_slots;
+    const int *n_list;        // slots this launch runs: list[0 .. *n_list)
+    const int *list;
     const SlotPf *slots;
+    const uint8_t *sfb;       // tail kernel: token scale atoms [slot][J][KT][512]
     const int *pair_tok, *pair_k;
     const uint8_t *arena;
     size_t run_stride;
@@ -344,7 +346,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    const int n_slots = *p.n_slots;
+    const int n_slots = *p.n_list;
     const int KT = GU ? p.H / 128 : p.I / 128;           // K tiles per item
     const int NTL = GU ? (2 * p.I) / PF_N : p.H / PF_N;  // N tiles per slot
     const int n_items = n_slots * NTL;
@@ -359,7 +361,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
             tc::prefetch_tmap(&tmW);
             uint32_t kiter = 0;
             for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
-                const int s = it / NTL, nt = it % NTL;
+                const int s = p.list[it / NTL], nt = it % NTL;
                 const SlotPf sl = p.slots[s];
                 const uint8_t *wsf = p.arena + (size_t)sl.run * p.run_stride + sf_off;
                 for (int kt = 0; kt < KT; kt++, kiter++) {
@@ -427,7 +429,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         uint32_t li = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, li++) {
-            const int s = it / NTL, nt = it % NTL;
+            const int s = p.list[it / NTL], nt = it % NTL;
             const bool ok = *(volatile int *)p.err == 0 && tc::mbar_wait(tfull, li & 1u, p.err, 43);
             __syncwarp();
             tc::tc_fence_after();
@@ -491,10 +493,243 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
     if (warp == 1) tc::tmem_dealloc(tmem, PF_TMEM);
 }
 
+constexpr int PT_NMAX = 64;                     // pairs per tail slot at most (MMA N <= 64)
+
+// ------------------------------------------------------------------ slot lists
+// One block: slots of at most PT_NMAX pairs (an expert's last, partial slot) go to `tail`
+// (k_pf_tail), the others to `full` (the kernel above), both in slot order. all_full: every
+// slot to full.
+__global__ void __launch_bounds__(1024) k_pf_split(int *__restrict__ full, int *__restrict__ n_full,
+                                                   int *__restrict__ tail, int *__restrict__ n_tail,
+                                                   const int *__restrict__ n_slots, const SlotPf *__restrict__ slots,
+                                                   int all_full) {
+    __shared__ int2 warp_sum[32];
+    const int ns = *n_slots;
+    int bf = 0, bt = 0;
+    for (int s0 = 0; s0 < ns; s0 += blockDim.x) {
+        const int s = s0 + threadIdx.x;
+        const int f = s < ns && (all_full || slots[s].ntok > PT_NMAX);
+        const int t = s < ns && !f;
+        int xf, xt, tf, tt;
+        block_scan2(f, t, xf, xt, tf, tt, warp_sum);
+        if (f) full[bf + xf] = s;
+        if (t) tail[bt + xt] = s;
+        bf += tf;
+        bt += tt;
+    }
+    if (threadIdx.x == 0) {
+        *n_full = bf;
+        *n_tail = bt;
+    }
+}
+
+// ------------------------------------------------------------------ tail slots (swap A/B)
+// A slot with n < 128 pairs wastes 128 - n rows of the kernel above. For n <= 64 the roles swap:
+// the MMA's M side is 128 pool-format weight rows (GU: 64 gate + 64 up rows of one
+// intermediate block of 64; D: 128 hidden rows) and N is the slot's pairs rounded up to 16,
+// both E4M3 terms accumulating into one accumulator (two MMAs per K step, each with its own
+// token scales). Work item = (tail slot, weight row tile). GU epilogue: the up rows' values
+// go through shared memory to the gate rows' threads, which form SwiGLU and requantise each
+// 32-column block across the warp (lane = intermediate column) into the same compact rows
+// and slot scale atoms the D stages read. D epilogue: lane = hidden row, one coalesced store
+// per pair.
+// The kernel streams every tail expert's weights once with little math per byte, so the
+// stages are small (8 KB of packed weights each) and many (six) to keep ~48 KB per SM in
+// flight.
+constexpr int PT_STAGES = 6;
+constexpr int PT_A = 128 * 128;                 // padded E2M1 weight tile
+constexpr int PT_BJ = PT_NMAX * 128;            // one term's token rows
+constexpr int PT_STAGE = PT_A + PF_J * PT_BJ + 2048;   // + SFA and J SFB atoms (1024-aligned)
+constexpr int PT_TILE = 64 * (PT_NMAX + 1) * 4; // up rows [64][PT_NMAX + 1] fp32
+constexpr int PT_THREADS = 192;                 // producer, MMA, four epilogue warps
+constexpr int PT_BYTES = 1024 + PT_STAGES * PT_STAGE + PT_TILE + 256;
+constexpr uint32_t PT_TMEM = 256;               // two accumulators of PT_NMAX columns + scale factors
+constexpr uint32_t PT_SF_COL = 2 * PT_NMAX;
+static_assert(PT_BYTES <= 227 * 1024, "fits one CTA per SM");
+static_assert(PT_STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
+
+template <bool GU>
+__global__ void __launch_bounds__(PT_THREADS) k_pf_tail(const __grid_constant__ CUtensorMap tmW,
+                                                        const __grid_constant__ CUtensorMap tmB, PfArgs p) {
+    extern __shared__ uint8_t pt_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pt_raw + 1023) & ~(uintptr_t)1023);
+    float *tile = reinterpret_cast<float *>(smem + PT_STAGES * PT_STAGE);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PT_STAGES * PT_STAGE + PT_TILE);
+    uint64_t *full = bars, *empty = bars + PT_STAGES, *tfull = bars + 2 * PT_STAGES, *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2 * PT_STAGES; i++) tc::mbar_init(&bars[i], 1);
+        tc::mbar_init(&tfull[0], 1);
+        tc::mbar_init(&tfull[1], 1);
+        tc::mbar_init(&tempty[0], 4);
+        tc::mbar_init(&tempty[1], 4);
+        tc::fence_mbar_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, PT_TMEM);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int n_list = *p.n_list;
+    const int KT = GU ? p.H / 128 : p.I / 128;         // K tiles per item
+    const int RT = GU ? (2 * p.I) / 128 : p.H / 128;   // weight row tiles per slot
+    const int n_items = n_list * RT;
+    const PoolGeom g = pool_geom(p.H, p.I);
+    const size_t sf_off = GU ? g.gu_s : g.d_s;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ producer
+        bool ok = tc::tc_check((tc::smem_u32(smem) & 1023) == 0, p.err, 50);
+        tc::prefetch_tmap(&tmW);
+        tc::prefetch_tmap(&tmB);
+        uint32_t kiter = 0;
+        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+            const int s = p.list[it / RT], rt = it % RT;
+            const SlotPf sl = p.slots[s];
+            const int nb = (sl.ntok + 15) / 16;           // 16-row token boxes
+            const uint8_t *wsf = p.arena + (size_t)sl.run * p.run_stride + sf_off + (size_t)rt * KT * 512;
+            for (int kt = 0; kt < KT; kt++, kiter++) {
+                const int st = kiter % PT_STAGES;
+                const uint32_t ph = (kiter / PT_STAGES) & 1u;
+                if (kiter >= PT_STAGES && !tc::mbar_wait(&empty[st], ph ^ 1u, p.err, 51)) { ok = false; break; }
+                uint8_t *sa = smem + st * PT_STAGE;
+                uint8_t *sb = sa + PT_A;
+                uint8_t *ssf = sb + PF_J * PT_BJ;
+                tc::mbar_expect_tx(&full[st], PT_A / 2 + PF_J * nb * 16 * 128 + (1 + PF_J) * 512);
+                tc::tma_load_3d(sa, &tmW, &full[st], kt * 128, rt * 128, sl.run);
+#pragma unroll
+                for (int j = 0; j < PF_J; j++) {
+                    for (int b = 0; b < nb; b++)
+                        tc::tma_load_3d(sb + j * PT_BJ + b * 2048, &tmB, &full[st], kt * 128, sl.row0 + 16 * b, j);
+                    tc::bulk_load(ssf + 512 * (1 + j), p.sfb + (((size_t)s * PF_J + j) * KT + kt) * 512, 512, &full[st]);
+                }
+                tc::bulk_load(ssf, wsf + (size_t)kt * 512, 512, &full[st]);
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------ MMA issuer
+        uint32_t kiter = 0, li = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, li++) {
+            const int s = p.list[it / RT];
+            const uint32_t npad = (uint32_t)((p.slots[s].ntok + 15) & ~15);
+            const uint32_t idesc0 = tc::idesc_mxf8f6f4(tc::FMT_E2M1, tc::FMT_E4M3, npad, 0, 0);
+            const uint32_t a = li & 1u, use = li >> 1;
+            if (use >= 1 && !tc::mbar_wait(&tempty[a], (use - 1) & 1u, p.err, 54)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint32_t d = tmem + a * PT_NMAX;
+            for (int kt = 0; kt < KT; kt++, kiter++) {
+                const int st = kiter % PT_STAGES;
+                const uint32_t ph = (kiter / PT_STAGES) & 1u;
+                if (!tc::mbar_wait(&full[st], ph, p.err, 52)) { ok = false; break; }
+                tc::tc_fence_after();
+                uint8_t *sa = smem + st * PT_STAGE;
+                uint8_t *sb = sa + PT_A;
+                uint8_t *ssf = sb + PF_J * PT_BJ;
+                const uint32_t sfc = tmem + PT_SF_COL + 16u * (kiter & 1u);
+                tc::tc_cp_sf(sfc, tc::desc_sf_atom(tc::smem_u32(ssf)));
+#pragma unroll
+                for (int j = 0; j < PF_J; j++)
+                    tc::tc_cp_sf(sfc + 4 + 4 * j, tc::desc_sf_atom(tc::smem_u32(ssf + 512 * (1 + j))));
+#pragma unroll
+                for (int kb = 0; kb < 4; kb++) {
+                    const uint64_t da = tc::desc_kmajor_sw128(tc::smem_u32(sa) + 32 * kb);
+                    const uint32_t id = idesc0 | ((uint32_t)kb << 4) | ((uint32_t)kb << 29);
+#pragma unroll
+                    for (int j = 0; j < PF_J; j++) {
+                        const uint64_t db = tc::desc_kmajor_sw128(tc::smem_u32(sb + j * PT_BJ) + 32 * kb);
+                        tc::tc_mma_mx(d, da, db, id, sfc | ((uint32_t)kb << 30),
+                                      (sfc + 4 + 4 * j) | ((uint32_t)kb << 30), (kt | kb | j) != 0);
+                    }
+                }
+                tc::tc_commit(&empty[st]);
+            }
+            if (ok) tc::tc_commit(&tfull[a]);
+        }
+    } else if (warp >= 2) {
+        // ------------------------------------------------------------ epilogue
+        // Every epilogue warp runs every item and every named barrier even after a failed
+        // wait (it then skips the TMEM reads and the stores), so no barrier strands a warp.
+        const int q = warp & 3;                 // TMEM lane quadrant
+        const int row = 32 * q + lane;          // weight row within the tile
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        uint32_t li = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, li++) {
+            const int s = p.list[it / RT], rt = it % RT;
+            const uint32_t a = li & 1u;
+            const SlotPf sl = p.slots[s];
+            const int n = sl.ntok;
+            const bool ok = *(volatile int *)p.err == 0 && tc::mbar_wait(&tfull[a], (li >> 1) & 1u, p.err, 53);
+            __syncwarp();
+            tc::tc_fence_after();
+            if constexpr (GU) {
+                const int col = 64 * rt + (row & 63);       // intermediate index of this row
+                const int KTd = p.I / 128;
+#pragma unroll 1
+                for (int c0 = 0; c0 < n; c0 += 32) {
+                    uint32_t v[32];
+                    if (ok) {
+                        tc::tmem_ld32(tmem + lane_base + a * PT_NMAX + c0, v);
+                        tc::tmem_ld_wait();
+                    }
+                    if (ok && q >= 2) {
+#pragma unroll
+                        for (int i = 0; i < 32; i++) tile[(row - 64) * (PT_NMAX + 1) + c0 + i] = __uint_as_float(v[i]);
+                    }
+                    tc::named_bar_sync(1, 128);
+                    if (ok && q < 2) {
+                        const int cn = min(32, n - c0);
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            if (i >= cn) break;
+                            const int pl = c0 + i;
+                            const float av = act_fast(__uint_as_float(v[i]), tile[row * (PT_NMAX + 1) + pl], p.act);
+                            quantize_block<PF_J>(
+                                av,
+                                [&](int j, uint32_t qv) {
+                                    p.act_q[((size_t)j * p.rows_cap + sl.row0 + pl) * p.I + col] = (uint8_t)qv;
+                                },
+                                [&](int j, uint32_t sf) {
+                                    p.act_sf[(((size_t)s * PF_J + j) * KTd + col / 128) * 512 +
+                                             atom_byte(pl, (col % 128) / 32)] = (uint8_t)sf;
+                                });
+                        }
+                    }
+                    tc::named_bar_sync(1, 128);           // the tile is rewritten by the next chunk
+                }
+            } else if (ok) {
+                const int h = 128 * rt + row;
+#pragma unroll 1
+                for (int c0 = 0; c0 < n; c0 += 32) {
+                    uint32_t v[32];
+                    tc::tmem_ld32(tmem + lane_base + a * PT_NMAX + c0, v);
+                    tc::tmem_ld_wait();
+                    const int cn = min(32, n - c0);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        if (i >= cn) break;
+                        const size_t pr = (size_t)s * PF_M + c0 + i;
+                        p.contrib[((size_t)p.pair_tok[pr] * p.kstride + p.pair_k[pr]) * p.H + h] = __uint_as_float(v[i]);
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&tempty[a]);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) tc::tmem_dealloc(tmem, PT_TMEM);
+}
+
 // ------------------------------------------------------------------ host side
 struct PfBufs {
     int *idx, *pe, *rank, *cnt, *chunk_base, *slot_base, *eoff, *n_slots, *n_rows, *err, *pair_tok, *pair_k,
-        *row_tok;
+        *row_tok, *full_ids, *tail_ids, *n_full, *n_tail;
     float *wt, *contrib;
     double *rpart;
     uint8_t *dropped, *xq, *xsf, *sfa_x, *actq, *actsf;
@@ -522,6 +757,10 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
     b.n_rows = cv.take<int>(1);
     b.err = cv.take<int>(1);
     b.slots = cv.take<SlotPf>(b.max_slots);
+    b.full_ids = cv.take<int>(b.max_slots);
+    b.tail_ids = cv.take<int>(b.max_slots);
+    b.n_full = cv.take<int>(1);
+    b.n_tail = cv.take<int>(1);
     b.pair_tok = cv.take<int>((size_t)b.max_slots * PF_M);
     b.pair_k = cv.take<int>((size_t)b.max_slots * PF_M);
     b.row_tok = cv.take<int>(b.rows_cap);
@@ -532,7 +771,8 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
     b.actsf = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (I / 128) * 512);
     b.contrib = cv.take<float>((size_t)T * (K + 1) * H);
     return b.idx && b.wt && b.rpart && b.pe && b.rank && b.dropped && b.cnt && b.chunk_base && b.slot_base &&
-           b.eoff && b.n_slots && b.n_rows && b.err && b.slots && b.pair_tok && b.pair_k && b.row_tok && b.xq &&
+           b.eoff && b.n_slots && b.n_rows && b.err && b.slots && b.full_ids && b.tail_ids && b.n_full && b.n_tail &&
+           b.pair_tok && b.pair_k && b.row_tok && b.xq &&
            b.xsf && b.sfa_x && b.actq && b.actsf && b.contrib;
 }
 
@@ -601,6 +841,13 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     K3C_CHECK_LAUNCH();
     k_pf_slot_sf<<<dim3(b.max_slots, PF_J), 256, 0, s>>>(b.sfa_x, b.xsf, b.n_slots, b.slots, b.n_rows, b.rows_cap, H);
     K3C_CHECK_LAUNCH();
+    // K3C_PF_TAIL=1: slots of at most PT_NMAX pairs on the weight-major kernel, the rest on the
+    // token-major one. Off by default: at config[2] the weight-major kernels stream their
+    // weights at ~2.5 TB/s (latency-bound, 16 KB per K tile per SM) and the split measured
+    // 5.58 ms for the expert stage against 4.90 ms with every slot on the token-major kernel.
+    const int use_tail = getenv("K3C_PF_TAIL") ? atoi(getenv("K3C_PF_TAIL")) : 0;
+    k_pf_split<<<1, 1024, 0, s>>>(b.full_ids, b.n_full, b.tail_ids, b.n_tail, b.n_slots, b.slots, use_tail ? 0 : 1);
+    K3C_CHECK_LAUNCH();
     // experts
     const PoolGeom g = pool_geom(H, I);
     CUtensorMap tmX, tmGU, tmAct, tmD;
@@ -612,8 +859,16 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
                       128, PF_M));
     K3C_TRY(make_map3(&tmD, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->arena + g.d_p, I, H, L->n_runs, I / 2,
                       L->run_stride, 128, PF_N));
+    CUtensorMap tmX16, tmGU128, tmAct16, tmD128;   // the tail kernel's boxes
+    K3C_TRY(make_map3(&tmX16, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.xq, H, b.rows_cap, PF_J, H, (uint64_t)b.rows_cap * H,
+                      128, 16));
+    K3C_TRY(make_map3(&tmGU128, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->arena + g.gu_p, H, 2 * I, L->n_runs, H / 2,
+                      L->run_stride, 128, 128));
+    K3C_TRY(make_map3(&tmAct16, CU_TENSOR_MAP_DATA_TYPE_UINT8, b.actq, I, b.rows_cap, PF_J, I,
+                      (uint64_t)b.rows_cap * I, 128, 16));
+    K3C_TRY(make_map3(&tmD128, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->arena + g.d_p, I, H, L->n_runs, I / 2,
+                      L->run_stride, 128, 128));
     PfArgs a;
-    a.n_slots = b.n_slots;
     a.slots = b.slots;
     a.pair_tok = b.pair_tok;
     a.pair_k = b.pair_k;
@@ -631,13 +886,29 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     a.err = b.err;
     K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_moe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_BYTES));
     K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_moe<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_BYTES));
+    K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_tail<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PT_BYTES));
+    K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_tail<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PT_BYTES));
     const int grid = sm_count();
     stage_begin(STAGE_EXPERTS, s);
     a.sfa = b.sfa_x;
+    a.sfb = b.sfa_x;
+    a.n_list = b.n_full;
+    a.list = b.full_ids;
     k_pf_moe<true><<<grid, PF_THREADS, PF_BYTES, s>>>(tmX, tmGU, a);
     K3C_CHECK_LAUNCH();
+    a.n_list = b.n_tail;
+    a.list = b.tail_ids;
+    k_pf_tail<true><<<grid, PT_THREADS, PT_BYTES, s>>>(tmGU128, tmX16, a);
+    K3C_CHECK_LAUNCH();
     a.sfa = b.actsf;
+    a.sfb = b.actsf;
+    a.n_list = b.n_full;
+    a.list = b.full_ids;
     k_pf_moe<false><<<grid, PF_THREADS, PF_BYTES, s>>>(tmAct, tmD, a);
+    K3C_CHECK_LAUNCH();
+    a.n_list = b.n_tail;
+    a.list = b.tail_ids;
+    k_pf_tail<false><<<grid, PT_THREADS, PT_BYTES, s>>>(tmD128, tmAct16, a);
     K3C_CHECK_LAUNCH();
     stage_end(STAGE_EXPERTS, s);
     stage_begin(STAGE_COMBINE, s);
