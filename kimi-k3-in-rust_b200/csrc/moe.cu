@@ -161,22 +161,28 @@ __global__ void __launch_bounds__(256) k_ffn_gateup(K3ExpertQ q, const float *__
     }
 }
 
-// down: grid ceil(hidden/16), warp w takes rows 2*(8*bx+w)+{0,1}. Launched as a programmatic
-// dependent of k_ffn_gateup: the first weight chunks are requested before the wait for the
-// activations, which are then staged like k_ffn_gateup's (NT * inter floats).
+// down: grid ceil(hidden/32), warp w takes rows 4*(8*bx+w)+{0..3} (one wave of blocks on
+// 148 SMs at hidden 7168). Launched as a programmatic dependent of k_ffn_gateup: the first
+// weight chunks are requested before the wait for the activations, which are then staged
+// like k_ffn_gateup's (NT * inter floats).
 template <int NT, int CPL>
 __global__ void __launch_bounds__(256) k_ffn_down(K3ExpertQ q, const float *__restrict__ actbuf, int ntok,
                                                   int hidden, int inter, float *__restrict__ y) {
     extern __shared__ __align__(16) float ffn_sa[];
+    constexpr int RD = 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r0 = (blockIdx.x * 8 + warp) * 2;
-    const bool live = r0 < hidden;
-    const int r1 = r0 + 1 < hidden ? r0 + 1 : r0;
+    const int rb = (blockIdx.x * 8 + warp) * RD;
+    const bool live = rb < hidden;
     const size_t pitch = (size_t)inter / 2, spitch = (size_t)inter / 32;
     const int nchunk = inter / 32;
-    const uint8_t *prow[2] = {q.p2 + (size_t)(live ? r0 : 0) * pitch, q.p2 + (size_t)(live ? r1 : 0) * pitch};
-    const uint8_t *srow[2] = {q.s2 + (size_t)(live ? r0 : 0) * spitch, q.s2 + (size_t)(live ? r1 : 0) * spitch};
-    MxChunks<2, CPL> ch;
+    const uint8_t *prow[RD], *srow[RD];
+#pragma unroll
+    for (int i = 0; i < RD; i++) {
+        const int r = live && rb + i < hidden ? rb + i : 0;
+        prow[i] = q.p2 + (size_t)r * pitch;
+        srow[i] = q.s2 + (size_t)r * spitch;
+    }
+    MxChunks<RD, CPL> ch;
     if (live) ch.load(prow, srow, 0, nchunk);
     asm volatile("griddepcontrol.wait;" ::: "memory");   // actbuf is complete
     for (int t0 = 0; t0 < ntok; t0 += NT) {
@@ -184,9 +190,9 @@ __global__ void __launch_bounds__(256) k_ffn_down(K3ExpertQ q, const float *__re
         if (t0) __syncthreads();
         for (int t = 0; t < nt; t++) stage_x_swz(ffn_sa + t * inter, actbuf + (size_t)(t0 + t) * inter, inter);
         __syncthreads();
-        float acc[2][NT];
+        float acc[RD][NT];
 #pragma unroll
-        for (int i = 0; i < 2; i++)
+        for (int i = 0; i < RD; i++)
 #pragma unroll
             for (int t = 0; t < NT; t++) acc[i][t] = 0.f;
         for (int c0 = 0; c0 < nchunk; c0 += 32 * CPL) {
@@ -196,12 +202,10 @@ __global__ void __launch_bounds__(256) k_ffn_down(K3ExpertQ q, const float *__re
         }
 #pragma unroll
         for (int t = 0; t < NT; t++) {
-            const float a0 = warp_sum(acc[0][t]);
-            const float a1 = warp_sum(acc[1][t]);
-            if (live && lane == 0 && t < nt) {
-                float *o = y + (size_t)(t0 + t) * hidden;
-                o[r0] = a0;
-                if (r1 != r0) o[r1] = a1;
+#pragma unroll
+            for (int i = 0; i < RD; i++) {
+                const float v = warp_sum(acc[i][t]);
+                if (live && lane == 0 && t < nt && rb + i < hidden) y[(size_t)(t0 + t) * hidden + rb + i] = v;
             }
         }
     }
@@ -220,7 +224,7 @@ static int launch_ffn_pair(const K3ExpertQ &e, const float *x, int ntok, int hid
     }
     k_ffn_gateup<NT, CG><<<(inter + 7) / 8, 256, sg, s>>>(e, x, ntok, hidden, inter, act, actbuf);
     K3C_CHECK_LAUNCH();
-    K3C_TRY_CUDA(launch_pdl(k_ffn_down<NT, 2>, dim3((hidden + 15) / 16), dim3(256), sd, s, e, (const float *)actbuf,
+    K3C_TRY_CUDA(launch_pdl(k_ffn_down<NT, 2>, dim3((hidden + 31) / 32), dim3(256), sd, s, e, (const float *)actbuf,
                             ntok, hidden, inter, y));
     count_launch();
     return K3C_OK;
