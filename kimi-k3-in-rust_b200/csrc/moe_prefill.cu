@@ -842,9 +842,10 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     k_pf_slot_sf<<<dim3(b.max_slots, PF_J), 256, 0, s>>>(b.sfa_x, b.xsf, b.n_slots, b.slots, b.n_rows, b.rows_cap, H);
     K3C_CHECK_LAUNCH();
     // K3C_PF_TAIL=1: slots of at most PT_NMAX pairs on the weight-major kernel, the rest on the
-    // token-major one. Off by default: at config[2] the weight-major kernels stream their
-    // weights at ~2.5 TB/s (latency-bound, 16 KB per K tile per SM) and the split measured
-    // 5.58 ms for the expert stage against 4.90 ms with every slot on the token-major kernel.
+    // token-major one. Off by default: with N of 16..64 a block-scaled MMA costs the tensor
+    // pipe nearly as much as one with N = 256 (its pipe was 61% busy at 13% math), and the
+    // split measured 5.58 ms for the config[2] expert stage against 4.90 ms with every slot
+    // on the token-major kernel.
     const int use_tail = getenv("K3C_PF_TAIL") ? atoi(getenv("K3C_PF_TAIL")) : 0;
     k_pf_split<<<1, 1024, 0, s>>>(b.full_ids, b.n_full, b.tail_ids, b.n_tail, b.n_slots, b.slots, use_tail ? 0 : 1);
     K3C_CHECK_LAUNCH();
@@ -896,20 +897,24 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     a.list = b.full_ids;
     k_pf_moe<true><<<grid, PF_THREADS, PF_BYTES, s>>>(tmX, tmGU, a);
     K3C_CHECK_LAUNCH();
-    a.n_list = b.n_tail;
-    a.list = b.tail_ids;
-    k_pf_tail<true><<<grid, PT_THREADS, PT_BYTES, s>>>(tmGU128, tmX16, a);
-    K3C_CHECK_LAUNCH();
+    if (use_tail) {
+        a.n_list = b.n_tail;
+        a.list = b.tail_ids;
+        k_pf_tail<true><<<grid, PT_THREADS, PT_BYTES, s>>>(tmGU128, tmX16, a);
+        K3C_CHECK_LAUNCH();
+    }
     a.sfa = b.actsf;
     a.sfb = b.actsf;
     a.n_list = b.n_full;
     a.list = b.full_ids;
     k_pf_moe<false><<<grid, PF_THREADS, PF_BYTES, s>>>(tmAct, tmD, a);
     K3C_CHECK_LAUNCH();
-    a.n_list = b.n_tail;
-    a.list = b.tail_ids;
-    k_pf_tail<false><<<grid, PT_THREADS, PT_BYTES, s>>>(tmD128, tmAct16, a);
-    K3C_CHECK_LAUNCH();
+    if (use_tail) {
+        a.n_list = b.n_tail;
+        a.list = b.tail_ids;
+        k_pf_tail<false><<<grid, PT_THREADS, PT_BYTES, s>>>(tmD128, tmAct16, a);
+        K3C_CHECK_LAUNCH();
+    }
     stage_end(STAGE_EXPERTS, s);
     stage_begin(STAGE_COMBINE, s);
     K3C_TRY(launch_moe_combine(out, b.contrib, wt, b.dropped, T, K, H, L->shared_run >= 0 ? 1 : 0, s));
