@@ -319,10 +319,56 @@ __global__ void k_moe_combine(float *__restrict__ out, const float *__restrict__
     }
 }
 
+// Four consecutive outputs per thread (hidden % 4 == 0, 16-byte aligned rows): the same
+// per-element operations in the same order, with every one of a thread's topk+1 16-byte
+// loads in flight at once.
+__global__ void k_moe_combine4(float4 *__restrict__ out, const float4 *__restrict__ contrib,
+                               const float *__restrict__ wt, const uint8_t *__restrict__ dropped,
+                               int ntok, int topk, int h4, int has_shared) {
+    const int t = blockIdx.y;
+    const int ks = topk + 1;
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h >= h4) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr int JM = 8;                       // rows loaded ahead of their use
+    for (int j0 = 0; j0 < topk; j0 += JM) {
+        float4 cj[JM];
+#pragma unroll
+        for (int i = 0; i < JM; i++)
+            if (j0 + i < topk) cj[i] = contrib[((size_t)t * ks + j0 + i) * h4 + h];
+#pragma unroll
+        for (int i = 0; i < JM; i++) {
+            const int j = j0 + i;
+            if (j >= topk || dropped[t * topk + j]) continue;
+            const float w = wt[t * topk + j];
+            const float4 c = cj[i];
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, c.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, c.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, c.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, c.w));
+        }
+    }
+    if (has_shared) {
+        const float4 c = contrib[((size_t)t * ks + topk) * h4 + h];
+        acc.x = __fadd_rn(acc.x, c.x);
+        acc.y = __fadd_rn(acc.y, c.y);
+        acc.z = __fadd_rn(acc.z, c.z);
+        acc.w = __fadd_rn(acc.w, c.w);
+    }
+    out[(size_t)t * h4 + h] = acc;
+}
+
 int launch_moe_combine(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
                        int ntok, int topk, int hidden, int has_shared, cudaStream_t s) {
-    k_moe_combine<<<dim3((hidden + 255) / 256, ntok), 256, 0, s>>>(out, contrib, wt, dropped, ntok,
-                                                                  topk, hidden, has_shared);
+    if (hidden % 4 == 0 && ((uintptr_t)out & 15) == 0 && ((uintptr_t)contrib & 15) == 0) {
+        const int h4 = hidden / 4;
+        k_moe_combine4<<<dim3((h4 + 127) / 128, ntok), 128, 0, s>>>(
+            reinterpret_cast<float4 *>(out), reinterpret_cast<const float4 *>(contrib), wt, dropped, ntok, topk, h4,
+            has_shared);
+    } else {
+        k_moe_combine<<<dim3((hidden + 255) / 256, ntok), 256, 0, s>>>(out, contrib, wt, dropped, ntok,
+                                                                      topk, hidden, has_shared);
+    }
     K3C_CHECK_LAUNCH();
     return K3C_OK;
 }

@@ -207,21 +207,21 @@ __global__ void __launch_bounds__(1024) k_pf_scatter(int *__restrict__ pair_tok,
     row_tok[eoff[e] + r] = i / topk;
 }
 
-// Row r of the A operand: the J terms of token row_tok[r], xq [J][rows][H], and their block
-// scales xsf [J][rows][H/32]. One thread per 32-element block.
-
-// Scale atoms of the A operand per slot: sfa [slot][J][H/128][512] from the row-major scales
-// (rows past the last row repeat the slot's first row; their products are never read).
-__global__ void __launch_bounds__(256) k_pf_slot_sf(uint8_t *__restrict__ sfa, const uint8_t *__restrict__ xsf,
+// Scale atoms of the A operand per slot: sfa [slot][J][H/128][512] from the per-token scales
+// tsf [J][T][H/32] of each row's token (rows past the last row repeat the slot's first row;
+// their products are never read).
+__global__ void __launch_bounds__(256) k_pf_slot_sf(uint8_t *__restrict__ sfa, const uint8_t *__restrict__ tsf,
+                                                    const int *__restrict__ row_tok,
                                                     const int *__restrict__ n_slots, const SlotPf *__restrict__ slots,
-                                                    const int *__restrict__ n_rows, int rows_cap, int H) {
+                                                    const int *__restrict__ n_rows, int T, int H) {
     const int s = blockIdx.x, j = blockIdx.y;
     if (s >= *n_slots) return;
     const int KT = H / 128, row0 = slots[s].row0, nr = *n_rows;
     for (int i = threadIdx.x; i < PF_M * KT; i += blockDim.x) {
         const int m = i % PF_M, kt = i / PF_M;
         const int r = row0 + m < nr ? row0 + m : row0;
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(xsf + ((size_t)j * rows_cap + r) * (H / 32) + 4 * kt);
+        const int tok = row_tok[r];
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(tsf + ((size_t)j * T + tok) * (H / 32) + 4 * kt);
         *reinterpret_cast<uint32_t *>(sfa + (((size_t)s * PF_J + j) * KT + kt) * 512 + 16 * (m % 32) + 4 * (m / 32)) = w;
     }
 }
@@ -269,17 +269,17 @@ __device__ __forceinline__ void quant_row32(float (&a)[32], uint4 (&q)[PF_J][2],
     }
 }
 
-// Row r of the A operand: the J terms of token row_tok[r], xq [J][rows_cap][H], and their
-// block scales xsf [J][rows_cap][H/32]. One thread per 32-element block.
+// Token t's J terms, xq [J][T][H], and their block scales xsf [J][T][H/32]: every token once.
+// One thread per 32-element block.
 template <typename XT>
 __global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq, uint8_t *__restrict__ xsf,
-                                                       const XT *__restrict__ x, const int *__restrict__ row_tok,
-                                                       const int *__restrict__ n_rows, int rows_cap, int H) {
+                                                       const XT *__restrict__ x, int T, int H) {
     const int nb = H / 32;
+    const int rows_cap = T;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int r = (int)(i / nb), blk = (int)(i % nb);
-    if (r >= *n_rows) return;
-    const XT *src = x + (size_t)row_tok[r] * H + blk * 32;
+    if (r >= T) return;
+    const XT *src = x + (size_t)r * H + blk * 32;
     float a[32];
     if constexpr (sizeof(XT) == 2) {
 #pragma unroll
@@ -311,6 +311,20 @@ __global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq,
         d[0] = q[j][0];
         d[1] = q[j][1];
         xsf[((size_t)j * rows_cap + r) * nb + blk] = (uint8_t)sf[j];
+    }
+}
+
+// Compact row r of the A operand = token row_tok[r]'s terms: xq [J][rows_cap][H] copied from
+// tq [J][T][H] in 16-byte pieces (the token rows stay in L2; each is read topk+1 times).
+__global__ void __launch_bounds__(256) k_pf_gather_rows(uint8_t *__restrict__ xq, const uint8_t *__restrict__ tq,
+                                                        const int *__restrict__ row_tok,
+                                                        const int *__restrict__ n_rows, int rows_cap, int T, int H) {
+    const int j = blockIdx.y, h16 = H / 16;
+    const size_t n = (size_t)(*n_rows) * h16;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / h16), c = (int)(i % h16);
+        const uint4 v = *reinterpret_cast<const uint4 *>(tq + ((size_t)j * T + row_tok[r]) * H + 16 * c);
+        *reinterpret_cast<uint4 *>(xq + ((size_t)j * rows_cap + r) * H + 16 * c) = v;
     }
 }
 
@@ -732,7 +746,7 @@ struct PfBufs {
         *row_tok, *full_ids, *tail_ids, *n_full, *n_tail;
     float *wt, *contrib;
     double *rpart;
-    uint8_t *dropped, *xq, *xsf, *sfa_x, *actq, *actsf;
+    uint8_t *dropped, *xq, *tq, *xsf, *sfa_x, *actq, *actsf;
     SlotPf *slots;
     int max_slots, nchunk, rows_cap;
 };
@@ -765,7 +779,8 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
     b.pair_k = cv.take<int>((size_t)b.max_slots * PF_M);
     b.row_tok = cv.take<int>(b.rows_cap);
     b.xq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * H, 1024);
-    b.xsf = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * (H / 32));
+    b.tq = cv.take<uint8_t>((size_t)PF_J * T * H, 256);
+    b.xsf = cv.take<uint8_t>((size_t)PF_J * T * (H / 32));
     b.sfa_x = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (H / 128) * 512);
     b.actq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * I, 1024);
     b.actsf = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (I / 128) * 512);
@@ -773,7 +788,7 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
     return b.idx && b.wt && b.rpart && b.pe && b.rank && b.dropped && b.cnt && b.chunk_base && b.slot_base &&
            b.eoff && b.n_slots && b.n_rows && b.err && b.slots && b.full_ids && b.tail_ids && b.n_full && b.n_tail &&
            b.pair_tok && b.pair_k && b.row_tok && b.xq &&
-           b.xsf && b.sfa_x && b.actq && b.actsf && b.contrib;
+           b.tq && b.xsf && b.sfa_x && b.actq && b.actsf && b.contrib;
 }
 
 static char *const kPfSizing = reinterpret_cast<char *>(4096);
@@ -831,15 +846,17 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     k_pf_scatter<<<b.nchunk, PF_CHUNK, 0, s>>>(b.pair_tok, b.pair_k, b.row_tok, b.pe, b.rank, b.chunk_base,
                                                b.slot_base, b.eoff, P, E, K);
     K3C_CHECK_LAUNCH();
-    // activations of every compact row, then each slot's scale atoms
-    const size_t nthr = (size_t)b.rows_cap * (H / 32);
+    // every token's terms once, the compact rows copied from them, each slot's scale atoms
+    const size_t nthr = (size_t)T * (H / 32);
     const unsigned qblocks = (unsigned)((nthr + 255) / 256);
     if (x_dtype == K3C_BF16)
-        k_pf_quant_rows<uint16_t><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, (const uint16_t *)x, b.row_tok, b.n_rows, b.rows_cap, H);
+        k_pf_quant_rows<uint16_t><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, (const uint16_t *)x, T, H);
     else
-        k_pf_quant_rows<float><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, (const float *)x, b.row_tok, b.n_rows, b.rows_cap, H);
+        k_pf_quant_rows<float><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, (const float *)x, T, H);
     K3C_CHECK_LAUNCH();
-    k_pf_slot_sf<<<dim3(b.max_slots, PF_J), 256, 0, s>>>(b.sfa_x, b.xsf, b.n_slots, b.slots, b.n_rows, b.rows_cap, H);
+    k_pf_gather_rows<<<dim3(sm_count() * 16, PF_J), 256, 0, s>>>(b.xq, b.tq, b.row_tok, b.n_rows, b.rows_cap, T, H);
+    K3C_CHECK_LAUNCH();
+    k_pf_slot_sf<<<dim3(b.max_slots, PF_J), 256, 0, s>>>(b.sfa_x, b.xsf, b.row_tok, b.n_slots, b.slots, b.n_rows, T, H);
     K3C_CHECK_LAUNCH();
     // K3C_PF_TAIL=1: slots of at most PT_NMAX pairs on the weight-major kernel, the rest on the
     // token-major one. Off by default: with N of 16..64 a block-scaled MMA costs the tensor
