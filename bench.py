@@ -755,7 +755,7 @@ EP_T = 16384
 EP_WORKLOAD = "config[3] expert-parallel MoE prefill: 16384 bf16 tokens sharded over the GPUs, 384 " \
               "MXFP4 experts (7168->2048->7168) as 384/N contiguous ids per GPU + a shared expert on " \
               "each, top-8 under a Zipf(1.1) selection bias (popularity over a random permutation of " \
-              "the ids), NCCL all-to-all dispatch and combine"
+              "the ids); dispatch and combine over NVLink peer memory inside the expert kernels (--ep-impl a2a: NCCL all-to-all)"
 
 
 def run_ep(args, ws, rank, local):
@@ -802,11 +802,15 @@ def run_ep(args, ws, rank, local):
     run_of = torch.full((E,), -1, dtype=torch.int32, device=dev)
     run_of[lo:hi] = torch.arange(per, dtype=torch.int32, device=dev)
     none = torch.full((E,), -1, dtype=torch.int32, device=dev)
-    lr = k3.PoolMoeLayer(blob, per + 1, run_of, -1, W, bias, H, I, K, terms=2)
-    lsh = k3.PoolMoeLayer(blob, per + 1, none, per, W, bias, H, I, K, terms=2)
-    route, routed, shared = k3.ep.gpu_layer_fns(k3, lr, lsh, W, bias, K)
-    epl = k3.ep.ExpertParallel(owner, route, routed, shared)
     T = EP_T // ws
+    if args.ep_impl == "fused":
+        layer = k3.PoolMoeLayer(blob, per + 1, run_of, per, W, bias, H, I, K, terms=2)
+        epl = k3.ep.FusedExpertParallel(k3, layer, t_max=T)
+    else:
+        lr = k3.PoolMoeLayer(blob, per + 1, run_of, -1, W, bias, H, I, K, terms=2)
+        lsh = k3.PoolMoeLayer(blob, per + 1, none, per, W, bias, H, I, K, terms=2)
+        route, routed, shared = k3.ep.gpu_layer_fns(k3, lr, lsh, W, bias, K)
+        epl = k3.ep.ExpertParallel(owner, route, routed, shared)
     gx = torch.Generator(device=dev)
     gx.manual_seed(99 + rank)
     xs = [torch.randn((T, H), generator=gx, device=dev).to(torch.bfloat16) for _ in range(2)]
@@ -822,7 +826,7 @@ def run_ep(args, ws, rank, local):
     sent = 0
     for i in range(args.steps):
         epl.forward(xs[i % 2])
-        sent += epl.last["sent_tokens"]
+        sent += epl.last.get("sent_tokens", epl.last.get("remote_rows_read", 0))
     e1.record()
     torch.cuda.synchronize()
     dist.barrier()
@@ -839,6 +843,8 @@ def run_ep(args, ws, rank, local):
     else:
         dt, sent_all = dt_local, sent
     launches = L.k3c_launch_count() - launches0
+    if args.ep_impl == "fused":
+        epl.close()
     dist.destroy_process_group()
     if rank != 0:
         return
@@ -852,10 +858,13 @@ def run_ep(args, ws, rank, local):
         "config": {"workload": EP_WORKLOAD, "tokens": EP_T, "hidden": H, "inter": I, "experts": E, "topk": K,
                    "parallelism": f"ep{ws}"},
         "useful_tflops": flop * args.steps / dt / 1e12,
-        "dispatch": {"token_rows_per_step": sent_all / args.steps,
-                     "dispatch_gb_per_step": sent_all / args.steps * H * 2 / 1e9,
-                     "combine_gb_per_step": sent_all / args.steps * H * 4 / 1e9,
-                     "collective": "torch.distributed all_to_all_single (NCCL)" if ws > 1 else "none (1 GPU)"},
+        "dispatch": ({"impl": "fused: expert kernels read peers' token rows and store pair outputs over NVLink",
+                      "remote_token_rows_read_per_step": sent_all / args.steps,
+                      "sync": "two one-element NCCL all-reduces per layer"} if args.ep_impl == "fused" else
+                     {"impl": "torch.distributed all_to_all_single (NCCL)" if ws > 1 else "none (1 GPU)",
+                      "token_rows_per_step": sent_all / args.steps,
+                      "dispatch_gb_per_step": sent_all / args.steps * H * 2 / 1e9,
+                      "combine_gb_per_step": sent_all / args.steps * H * 4 / 1e9}),
         "gpu_launches": int(launches),
         "clocks": clocks,
     }))
@@ -874,6 +883,8 @@ def main():
     ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
                     help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
     ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
+    ap.add_argument("--ep-impl", default="fused", choices=["fused", "a2a"],
+                    help="ep workload: fused peer-memory exchange in the expert kernels, or NCCL all-to-all")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed", "ep", "expert"],
                     help="decode: config[1] (the headline line); prefill: config[2]; streamed: config[4]; "
                          "ep: config[3] (expert-parallel prefill; torchrun for N > 1)")

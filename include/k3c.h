@@ -140,6 +140,13 @@ int k3c_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok
 int k3c_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
                const void *W, int w_dtype, const float *bias, int hidden, int n_experts,
                int topk, int renorm, float routed_scale, int ntok, k3c_stream_t stream);
+/* k3c_router with caller-owned device scratch (k3c_router_scratch bytes) instead of a
+ * stream-ordered allocation per call. */
+size_t k3c_router_scratch(int hidden, int n_experts, int ntok);
+int k3c_router_ws(int *idx, float *w, float *scores, const void *x, int x_dtype,
+                  const void *W, int w_dtype, const float *bias, int hidden, int n_experts,
+                  int topk, int renorm, float routed_scale, int ntok, void *scratch,
+                  size_t scratch_bytes, k3c_stream_t stream);
 /* Selection stage alone, on given fp32 scores [ntok][n_experts]: the parity boundary at
  * which indices must match the reference bit-exactly. */
 int k3c_router_select(int *idx, float *w, const float *scores, const float *bias,
@@ -255,6 +262,49 @@ int k3c_moe_prefill_tc_routed(float *out, const void *x, int x_dtype, int ntok,
 int k3c_moe_prefill_tc(float *out, const void *x, int x_dtype, int ntok,
                        const k3c_moe_pool_layer *L, int *idx, float *wt, int *drops,
                        void *scratch, size_t scratch_bytes, k3c_stream_t stream);
+
+/* The combine alone (k3_ops.c:641-642): out[t] = sum_j wt[t][j] * contrib[t][j] in top-k order,
+ * plus contrib[t][topk] when has_shared; contrib [ntok][topk+1][hidden] fp32. Pairs whose id
+ * (idx, may be NULL) lies outside [0, n_experts) are skipped. */
+int k3c_moe_combine(float *out, const float *contrib, const float *wt, const int *idx, int n_experts,
+                    int ntok, int topk, int hidden, int has_shared, k3c_stream_t stream);
+
+/* ---- Expert-parallel prefill over peer memory (no reference counterpart: the reference is
+ * a single-process CPU engine). The ranks of one node each own a set of routed experts (the
+ * layer's run table marks the others -1; every id must be owned by exactly one rank) and
+ * their own tokens. Per layer, with a cross-rank barrier (a one-element NCCL all-reduce on
+ * the stream) between the steps:
+ *   1. each rank writes its tokens' bf16 or fp32 activations into its x buffer and their
+ *      top-k ids into its idx buffer (k3c_router);                       -- barrier
+ *   2. k3c_moe_prefill_ep_experts on every rank: plans over all ranks' pairs (reading the
+ *      peers' idx), quantises the tokens straight out of the peers' x buffers (loads over
+ *      NVLink), runs its own experts and its own tokens' shared expert, and writes every
+ *      pair's output row into the contrib buffer of the rank that owns the token (stores
+ *      over NVLink);                                                      -- barrier
+ *   3. k3c_moe_combine on every rank over its own tokens and contrib buffer.
+ * The buffers of step 1-3 are exchanged once per process: k3c_ep_alloc returns device memory
+ * and its IPC handle, k3c_ep_open maps a peer's handle (same node). ---- */
+#define K3C_EP_MAX 8
+typedef struct {
+    unsigned char bytes[64];
+} k3c_ipc_handle;
+int k3c_ep_alloc(void **ptr, size_t bytes, k3c_ipc_handle *handle);
+int k3c_ep_free(void *ptr);
+int k3c_ep_open(void **ptr, const k3c_ipc_handle *handle);
+int k3c_ep_close(void *peer_ptr);
+
+typedef struct {
+    int world, rank;              /* ranks sharing the layer, this process's rank */
+    int t_max;                    /* rows of every rank's buffers */
+    int x_dtype;                  /* K3C_BF16 or K3C_F32 */
+    int ntok[K3C_EP_MAX];         /* each rank's token count (<= t_max) */
+    const void *x[K3C_EP_MAX];    /* each rank's activations [t_max][hidden] */
+    const int *idx[K3C_EP_MAX];   /* each rank's top-k ids [t_max][topk] */
+    float *contrib[K3C_EP_MAX];   /* each rank's pair outputs [t_max][topk+1][hidden] fp32 */
+} k3c_ep_peers;
+size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers);
+int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers,
+                               void *scratch, size_t scratch_bytes, k3c_stream_t stream);
 
 /* ---- HBM expert pool: the reference's expert cache (src/cache/k3_cache.c:24-261) with
  * experts streamed from pinned host memory. A slot holds one pool-format run

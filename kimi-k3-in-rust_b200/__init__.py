@@ -50,6 +50,23 @@ class MoePoolLayerC(C.Structure):
                 ("run_of", C.c_void_p), ("shared_run", C.c_int), ("terms", C.c_int)]
 
 
+EP_MAX = 8
+
+
+class IpcHandleC(C.Structure):
+    """Mirror of k3c_ipc_handle (include/k3c.h)."""
+
+    _fields_ = [("bytes", C.c_ubyte * 64)]
+
+
+class EpPeersC(C.Structure):
+    """Mirror of k3c_ep_peers (include/k3c.h)."""
+
+    _fields_ = [("world", C.c_int), ("rank", C.c_int), ("t_max", C.c_int), ("x_dtype", C.c_int),
+                ("ntok", C.c_int * EP_MAX), ("x", C.c_void_p * EP_MAX), ("idx", C.c_void_p * EP_MAX),
+                ("contrib", C.c_void_p * EP_MAX)]
+
+
 class K3CError(RuntimeError):
     pass
 
@@ -112,6 +129,15 @@ def lib():
         "k3c_moe_prefill_tc_scratch": ([C.POINTER(MoePoolLayerC), i], sz),
         "k3c_moe_prefill_tc_routed": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
         "k3c_moe_prefill_tc": ([vp, vp, i, i, C.POINTER(MoePoolLayerC), vp, vp, vp, vp, sz, vp], i),
+        "k3c_moe_combine": ([vp, vp, vp, vp, i, i, i, i, i, vp], i),
+        "k3c_router_scratch": ([i, i, i], sz),
+        "k3c_router_ws": ([vp, vp, vp, vp, i, vp, i, vp, i, i, i, i, f, i, vp, sz, vp], i),
+        "k3c_ep_alloc": ([C.POINTER(vp), sz, C.POINTER(IpcHandleC)], i),
+        "k3c_ep_free": ([vp], i),
+        "k3c_ep_open": ([C.POINTER(vp), C.POINTER(IpcHandleC)], i),
+        "k3c_ep_close": ([vp], i),
+        "k3c_moe_prefill_ep_scratch": ([C.POINTER(MoePoolLayerC), C.POINTER(EpPeersC)], sz),
+        "k3c_moe_prefill_ep_experts": ([C.POINTER(MoePoolLayerC), C.POINTER(EpPeersC), vp, sz, vp], i),
         "k3_mxfp4_dequant": ([vp, vp, vp, i, i, i], None),
         "k3_matmul_mxfp4": ([vp, vp, vp, vp, i, i, i], None),
         "k3_matmul_q8": ([vp, vp, vp, i, i], None),
@@ -393,6 +419,19 @@ def pool_pack(run, q: K3ExpertQ, hidden, inter):
     device uint8 tensor view of pool_run_bytes bytes, 256-byte aligned)."""
     _check(lib().k3c_pool_pack_expert(_ptr(run), C.byref(q), hidden, inter, _stream()),
            "k3c_pool_pack_expert")
+
+
+def device_view(ptr, shape, dtype):
+    """A torch tensor over device memory this process did not allocate through torch (no
+    copy; the memory must outlive the tensor). Only for local memory: a peer's memory is
+    handed to this library's kernels by address, never to torch operations."""
+    import torch
+    nbytes = int(np.prod(shape)) * torch.empty(0, dtype=dtype).element_size()
+
+    class _View:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (int(ptr), False),
+                                    "version": 3}
+    return torch.as_tensor(_View(), device="cuda").view(dtype).view(tuple(shape))
 
 
 class PoolMoeLayer:

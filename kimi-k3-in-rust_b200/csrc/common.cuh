@@ -43,6 +43,23 @@ void stage_end(int stage, cudaStream_t s);
 
 static inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Entry points that allocate their scratch per call (k3c_router, k3c_q8_gemv) use the
+// device's default stream-ordered pool. Its default release threshold of 0 hands freed memory
+// back to the driver at every synchronisation, so the next call maps it again (hundreds of
+// ms for a few hundred MB); keeping it in the pool for the life of the process makes a
+// repeated call an O(1) suballocation. This is a per-process attribute of the pool.
+inline void keep_async_pool() {
+    static bool done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || done[dev]) return;
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+        uint64_t keep = ~0ull;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    done[dev] = true;
+}
+
 // Launch as a programmatic dependent of the previous work in the stream: the kernel may be
 // scheduled before its predecessor ends, and must execute griddepcontrol.wait before it
 // reads anything the predecessor writes.

@@ -303,15 +303,22 @@ __global__ void __launch_bounds__(256) k_moe_down(Plan p, const float *__restric
 }
 
 // ----------------------------------------------------------------------- combine
+// A pair is skipped when dropped[t*topk+j] is set (if given) or its id is outside
+// [0, n_experts) (if ids is given).
+__device__ __forceinline__ bool pair_skipped(const uint8_t *dropped, const int *ids, int n_experts, int i) {
+    return (dropped && dropped[i]) || (ids && (unsigned)ids[i] >= (unsigned)n_experts);
+}
+
 __global__ void k_moe_combine(float *__restrict__ out, const float *__restrict__ contrib,
                               const float *__restrict__ wt, const uint8_t *__restrict__ dropped,
+                              const int *__restrict__ ids, int n_experts,
                               int ntok, int topk, int hidden, int has_shared) {
     const int t = blockIdx.y;
     const int ks = topk + 1;
     for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < hidden; h += gridDim.x * blockDim.x) {
         float acc = 0.0f;
         for (int j = 0; j < topk; j++) {
-            if (dropped[t * topk + j]) continue;
+            if (pair_skipped(dropped, ids, n_experts, t * topk + j)) continue;
             acc = __fadd_rn(acc, __fmul_rn(wt[t * topk + j], contrib[((size_t)t * ks + j) * hidden + h]));
         }
         if (has_shared) acc = __fadd_rn(acc, contrib[((size_t)t * ks + topk) * hidden + h]);
@@ -324,6 +331,7 @@ __global__ void k_moe_combine(float *__restrict__ out, const float *__restrict__
 // loads in flight at once.
 __global__ void k_moe_combine4(float4 *__restrict__ out, const float4 *__restrict__ contrib,
                                const float *__restrict__ wt, const uint8_t *__restrict__ dropped,
+                               const int *__restrict__ ids, int n_experts,
                                int ntok, int topk, int h4, int has_shared) {
     const int t = blockIdx.y;
     const int ks = topk + 1;
@@ -339,7 +347,7 @@ __global__ void k_moe_combine4(float4 *__restrict__ out, const float4 *__restric
 #pragma unroll
         for (int i = 0; i < JM; i++) {
             const int j = j0 + i;
-            if (j >= topk || dropped[t * topk + j]) continue;
+            if (j >= topk || pair_skipped(dropped, ids, n_experts, t * topk + j)) continue;
             const float w = wt[t * topk + j];
             const float4 c = cj[i];
             acc.x = __fadd_rn(acc.x, __fmul_rn(w, c.x));
@@ -358,19 +366,26 @@ __global__ void k_moe_combine4(float4 *__restrict__ out, const float4 *__restric
     out[(size_t)t * h4 + h] = acc;
 }
 
-int launch_moe_combine(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
-                       int ntok, int topk, int hidden, int has_shared, cudaStream_t s) {
+int launch_moe_combine_ids(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
+                           const int *ids, int n_experts, int ntok, int topk, int hidden, int has_shared,
+                           cudaStream_t s) {
+    if (ntok <= 0) return K3C_OK;
     if (hidden % 4 == 0 && ((uintptr_t)out & 15) == 0 && ((uintptr_t)contrib & 15) == 0) {
         const int h4 = hidden / 4;
         k_moe_combine4<<<dim3((h4 + 127) / 128, ntok), 128, 0, s>>>(
-            reinterpret_cast<float4 *>(out), reinterpret_cast<const float4 *>(contrib), wt, dropped, ntok, topk, h4,
-            has_shared);
+            reinterpret_cast<float4 *>(out), reinterpret_cast<const float4 *>(contrib), wt, dropped, ids, n_experts,
+            ntok, topk, h4, has_shared);
     } else {
-        k_moe_combine<<<dim3((hidden + 255) / 256, ntok), 256, 0, s>>>(out, contrib, wt, dropped, ntok,
-                                                                      topk, hidden, has_shared);
+        k_moe_combine<<<dim3((hidden + 255) / 256, ntok), 256, 0, s>>>(out, contrib, wt, dropped, ids, n_experts,
+                                                                      ntok, topk, hidden, has_shared);
     }
     K3C_CHECK_LAUNCH();
     return K3C_OK;
+}
+
+int launch_moe_combine(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
+                       int ntok, int topk, int hidden, int has_shared, cudaStream_t s) {
+    return launch_moe_combine_ids(out, contrib, wt, dropped, nullptr, 0, ntok, topk, hidden, has_shared, s);
 }
 
 template <typename XT>
@@ -508,7 +523,8 @@ int launch_moe_decode(float *out, const void *x, int x_dtype, int ntok, const k3
     K3C_TRY(launch_ffn_kernels(b.p, max_slots, b.xf, L->hidden, L->inter, L->act, b.actbuf,
                                L->topk + 1, b.contrib, ntok, s));
     stage_end(STAGE_EXPERTS, s);
-    k_moe_combine<<<dim3((L->hidden + 255) / 256, ntok), 256, 0, s>>>(out, b.contrib, wt, b.p.dropped, ntok, L->topk, L->hidden, L->shared ? 1 : 0);
+    k_moe_combine<<<dim3((L->hidden + 255) / 256, ntok), 256, 0, s>>>(out, b.contrib, wt, b.p.dropped, nullptr, 0,
+                                                                       ntok, L->topk, L->hidden, L->shared ? 1 : 0);
     K3C_CHECK_LAUNCH();
     return K3C_OK;
 }

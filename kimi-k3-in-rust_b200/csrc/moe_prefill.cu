@@ -39,6 +39,9 @@ int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
 size_t router_scratch_bytes(int hidden, int n_experts, int ntok);
 int launch_moe_combine(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
                        int ntok, int topk, int hidden, int has_shared, cudaStream_t s);
+int launch_moe_combine_ids(float *out, const float *contrib, const float *wt, const uint8_t *dropped,
+                           const int *ids, int n_experts, int ntok, int topk, int hidden, int has_shared,
+                           cudaStream_t s);
 
 namespace {
 constexpr int PF_J = 2;                       // E4M3 terms per activation
@@ -133,14 +136,14 @@ __device__ __forceinline__ void block_scan2(int a, int b, int &xa, int &xb, int 
 
 // One block: each expert's per-chunk bases, its first compact row (eoff) and first slot
 // (slot_base) by block-wide prefix sums of n_e and ceil(n_e/128), the slot table, and the
-// shared expert's rows and slots after all routed pairs.
+// shared expert's rows and slots after all routed pairs (tokens sh_base .. sh_base+sh_n-1).
 __global__ void __launch_bounds__(1024) k_pf_slots(int *__restrict__ n_slots, SlotPf *__restrict__ slots,
                                                    int *__restrict__ pair_tok, int *__restrict__ pair_k,
                                                    int *__restrict__ row_tok, int *__restrict__ n_rows,
                                                    int *__restrict__ chunk_base, int *__restrict__ slot_base,
                                                    int *__restrict__ eoff, const int *__restrict__ cnt,
                                                    int nchunk, const int *__restrict__ run_of, int n_experts,
-                                                   int T, int topk, int shared_run) {
+                                                   int sh_base, int sh_n, int topk, int shared_run) {
     __shared__ int2 warp_sum[32];
     int sbase = 0, rbase = 0;
     for (int e0 = 0; e0 < n_experts; e0 += blockDim.x) {
@@ -168,20 +171,20 @@ __global__ void __launch_bounds__(1024) k_pf_slots(int *__restrict__ n_slots, Sl
         rbase += tr;
     }
     if (shared_run >= 0) {
-        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        for (int t = threadIdx.x; t < sh_n; t += blockDim.x) {
             const size_t pos = (size_t)(sbase + t / PF_M) * PF_M + t % PF_M;
-            pair_tok[pos] = t;
+            pair_tok[pos] = sh_base + t;
             pair_k[pos] = topk;
-            row_tok[rbase + t] = t;
+            row_tok[rbase + t] = sh_base + t;
         }
-        const int nsh = (T + PF_M - 1) / PF_M;
+        const int nsh = (sh_n + PF_M - 1) / PF_M;
         for (int q = threadIdx.x; q < nsh; q += blockDim.x) {
             slots[sbase + q].run = shared_run;
-            slots[sbase + q].ntok = min(PF_M, T - PF_M * q);
+            slots[sbase + q].ntok = min(PF_M, sh_n - PF_M * q);
             slots[sbase + q].row0 = rbase + PF_M * q;
         }
         sbase += nsh;
-        rbase += T;
+        rbase += sh_n;
     }
     if (threadIdx.x == 0) {
         *n_slots = sbase;
@@ -238,7 +241,8 @@ struct PfArgs {
     const uint8_t *sfa;       // A scale atoms [slot][J][KT][512]
     uint8_t *act_q;           // GU out: [J][rows_cap][I] E4M3, compact rows
     uint8_t *act_sf;          // GU out: [slot][J][I/128][512]
-    float *contrib;           // D out: [T][topk+1][H]
+    float *contrib[K3C_EP_MAX];   // D out: rank q's [tmax][topk+1][H] (one rank: [0] = [T][..])
+    int tmax;                     // pair token g lives on rank g / tmax, row g % tmax
     int kstride, T, H, I, act, rows_cap;
     int *err;
 };
@@ -269,17 +273,28 @@ __device__ __forceinline__ void quant_row32(float (&a)[32], uint4 (&q)[PF_J][2],
     }
 }
 
-// Token t's J terms, xq [J][T][H], and their block scales xsf [J][T][H/32]: every token once.
+// Where token g's activations are: rank g / tmax's buffer x[rank], row g % tmax (a peer's
+// memory under expert parallelism, read with plain loads over NVLink); rows at or past that
+// rank's ntok are quantised as zeros.
+struct XSrc {
+    const void *x[K3C_EP_MAX];
+    int ntok[K3C_EP_MAX];
+    int tmax;
+};
+
+// Token g's J terms, xq [J][T][H], and their block scales xsf [J][T][H/32]: every token once.
 // One thread per 32-element block.
 template <typename XT>
 __global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq, uint8_t *__restrict__ xsf,
-                                                       const XT *__restrict__ x, int T, int H) {
+                                                       const XSrc src_x, int T, int H) {
     const int nb = H / 32;
     const int rows_cap = T;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int r = (int)(i / nb), blk = (int)(i % nb);
     if (r >= T) return;
-    const XT *src = x + (size_t)r * H + blk * 32;
+    const int rq = r / src_x.tmax, tr = r % src_x.tmax;
+    const bool live = tr < src_x.ntok[rq];
+    const XT *src = reinterpret_cast<const XT *>(src_x.x[rq]) + (size_t)(live ? tr : 0) * H + blk * 32;
     float a[32];
     if constexpr (sizeof(XT) == 2) {
 #pragma unroll
@@ -302,6 +317,9 @@ __global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq,
             a[4 * v + 3] = f.w;
         }
     }
+    if (!live)
+#pragma unroll
+        for (int v = 0; v < 32; v++) a[v] = 0.0f;
     uint4 q[PF_J][2];
     uint32_t sf[PF_J];
     quant_row32(a, q, sf);
@@ -480,7 +498,9 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
                 float *dst = nullptr;
                 if (ok && m < sl.ntok) {
                     const size_t pr = (size_t)s * PF_M + m;
-                    dst = p.contrib + ((size_t)p.pair_tok[pr] * p.kstride + p.pair_k[pr]) * p.H + (size_t)nt * PF_N;
+                    const int g = p.pair_tok[pr];
+                    dst = p.contrib[g / p.tmax] + ((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H +
+                          (size_t)nt * PF_N;
                 }
 #pragma unroll 1
                 for (int c = half * (PF_N / 64); c < (half + 1) * (PF_N / 64); c++) {
@@ -501,6 +521,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
             if (lane == 0) tc::mbar_arrive(tempty);
         }
     }
+    if constexpr (!GU) __threadfence_system();   // pair outputs may live in a peer's memory
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -725,7 +746,9 @@ __global__ void __launch_bounds__(PT_THREADS) k_pf_tail(const __grid_constant__ 
                     for (int i = 0; i < 32; i++) {
                         if (i >= cn) break;
                         const size_t pr = (size_t)s * PF_M + c0 + i;
-                        p.contrib[((size_t)p.pair_tok[pr] * p.kstride + p.pair_k[pr]) * p.H + h] = __uint_as_float(v[i]);
+                        const int g = p.pair_tok[pr];
+                        p.contrib[g / p.tmax][((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H + h] =
+                            __uint_as_float(v[i]);
                     }
                 }
             }
@@ -734,6 +757,7 @@ __global__ void __launch_bounds__(PT_THREADS) k_pf_tail(const __grid_constant__ 
             if (lane == 0) tc::mbar_arrive(&tempty[a]);
         }
     }
+    if constexpr (!GU) __threadfence_system();
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -751,7 +775,7 @@ struct PfBufs {
     int max_slots, nchunk, rows_cap;
 };
 
-static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
+static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T, bool own_contrib = true) {
     const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->topk;
     const size_t P = (size_t)T * K;
     b.nchunk = (int)((P + PF_CHUNK - 1) / PF_CHUNK);
@@ -784,7 +808,7 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
     b.sfa_x = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (H / 128) * 512);
     b.actq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * I, 1024);
     b.actsf = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (I / 128) * 512);
-    b.contrib = cv.take<float>((size_t)T * (K + 1) * H);
+    b.contrib = own_contrib ? cv.take<float>((size_t)T * (K + 1) * H) : reinterpret_cast<float *>(16);
     return b.idx && b.wt && b.rpart && b.pe && b.rank && b.dropped && b.cnt && b.chunk_base && b.slot_base &&
            b.eoff && b.n_slots && b.n_rows && b.err && b.slots && b.full_ids && b.tail_ids && b.n_full && b.n_tail &&
            b.pair_tok && b.pair_k && b.row_tok && b.xq &&
@@ -793,19 +817,33 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T) {
 
 static char *const kPfSizing = reinterpret_cast<char *>(4096);
 
-size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T) {
+size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contrib = true) {
     if (!L || T <= 0) return 0;
     Carve cv{kPfSizing, (size_t)-1 / 2, 0};
     PfBufs b;
-    carve_pf(cv, b, L, T);
+    carve_pf(cv, b, L, T, own_contrib);
     return cv.used + 1024;
+}
+
+// Every rank's top-k ids, ranks after one another ([world*t_max][topk]); rows at or past a
+// rank's token count get -1 (no pair).
+__global__ void k_ep_gather_idx(int *__restrict__ all, k3c_ep_peers ep, int topk) {
+    const size_t n = (size_t)ep.world * ep.t_max * topk;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int g = (int)(i / topk), k = (int)(i % topk);
+        const int q = g / ep.t_max, t = g % ep.t_max;
+        all[i] = t < ep.ntok[q] ? ep.idx[q][(size_t)t * topk + k] : -1;
+    }
 }
 
 // routed: idx_out/wt_out hold the routing on entry (ids < 0 or not resident are skipped and
 // counted in drops when it is given) and the router is not run.
+// ep: expert-parallel step 2 (k3c_moe_prefill_ep_experts): T is world * t_max virtual tokens,
+// x/idx come from the ranks' buffers, pair outputs go to the owning rank's contrib, no router,
+// no drop counting and no combine.
 int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k3c_moe_pool_layer *L,
                           int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
-                          cudaStream_t s, bool routed = false) {
+                          cudaStream_t s, bool routed = false, const k3c_ep_peers *ep = nullptr) {
     if (!L) return set_error(K3C_EINVAL, "moe_prefill_tc: null layer");
     const int H = L->hidden, I = L->inter, E = L->n_experts, K = L->topk;
     if (H <= 0 || I <= 0 || H % PF_N || I % 128)
@@ -815,17 +853,25 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     if (T > 65535 || ((long long)T * K + T) * H > (1LL << 40) || (long long)T * K + T > (1LL << 30))
         return set_error(K3C_EINVAL, "moe_prefill_tc: ntok=%d too large", T);
     if (x_dtype != K3C_BF16 && x_dtype != K3C_F32) return set_error(K3C_EINVAL, "moe_prefill_tc: x_dtype=%d", x_dtype);
-    if (((uintptr_t)x & 15) != 0) return set_error(K3C_EINVAL, "moe_prefill_tc: x must be 16-byte aligned");
+    if (!ep && ((uintptr_t)x & 15) != 0) return set_error(K3C_EINVAL, "moe_prefill_tc: x must be 16-byte aligned");
     if (!L->arena || !L->run_of || L->n_runs <= 0 || L->run_stride % 256 ||
         L->run_stride < pool_geom(H, I).run || ((uintptr_t)L->arena & 255) || L->shared_run >= L->n_runs)
         return set_error(K3C_EINVAL, "moe_prefill_tc: bad arena");
     Carve cv{(char *)scratch, scratch_bytes, 0};
     PfBufs b;
-    if (!carve_pf(cv, b, L, T)) return set_error(K3C_EINVAL, "moe_prefill_tc: scratch too small (%zu)", scratch_bytes);
+    if (!carve_pf(cv, b, L, T, ep == nullptr))
+        return set_error(K3C_EINVAL, "moe_prefill_tc: scratch too small (%zu)", scratch_bytes);
     int *idx = idx_out ? idx_out : b.idx;
     float *wt = wt_out ? wt_out : b.wt;
     const int P = T * K;
-    if (routed && (!idx_out || !wt_out)) return set_error(K3C_EINVAL, "moe_prefill_tc_routed: null routing");
+    if (routed && !ep && (!idx_out || !wt_out)) return set_error(K3C_EINVAL, "moe_prefill_tc_routed: null routing");
+    if (ep) {
+        routed = true;
+        drops = nullptr;
+        idx = b.idx;
+        k_ep_gather_idx<<<sm_count() * 4, 256, 0, s>>>(idx, *ep, K);
+        K3C_CHECK_LAUNCH();
+    }
     K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), s));
     // scale atoms of rows past a slot's pairs stay 2^0 (never NaN)
     K3C_TRY_CUDA(cudaMemsetAsync(b.actsf, 127, (size_t)b.max_slots * PF_J * (I / 128) * 512, s));
@@ -840,8 +886,10 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     if (csmem > 48 * 1024) K3C_TRY_CUDA(cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem));
     k_pf_count<<<b.nchunk, PF_CHUNK, csmem, s>>>(b.pe, b.rank, b.cnt, b.dropped, drops, idx, P, L->run_of, E, L->n_runs);
     K3C_CHECK_LAUNCH();
+    const int sh_base = ep ? ep->rank * ep->t_max : 0, sh_n = ep ? ep->ntok[ep->rank] : T;
     k_pf_slots<<<1, 1024, 0, s>>>(b.n_slots, b.slots, b.pair_tok, b.pair_k, b.row_tok, b.n_rows, b.chunk_base,
-                                  b.slot_base, b.eoff, b.cnt, b.nchunk, L->run_of, E, T, K, L->shared_run);
+                                  b.slot_base, b.eoff, b.cnt, b.nchunk, L->run_of, E, sh_base, sh_n, K,
+                                  L->shared_run);
     K3C_CHECK_LAUNCH();
     k_pf_scatter<<<b.nchunk, PF_CHUNK, 0, s>>>(b.pair_tok, b.pair_k, b.row_tok, b.pe, b.rank, b.chunk_base,
                                                b.slot_base, b.eoff, P, E, K);
@@ -849,10 +897,22 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     // every token's terms once, the compact rows copied from them, each slot's scale atoms
     const size_t nthr = (size_t)T * (H / 32);
     const unsigned qblocks = (unsigned)((nthr + 255) / 256);
+    XSrc xs{};
+    if (ep) {
+        for (int q = 0; q < ep->world; q++) {
+            xs.x[q] = ep->x[q];
+            xs.ntok[q] = ep->ntok[q];
+        }
+        xs.tmax = ep->t_max;
+    } else {
+        xs.x[0] = x;
+        xs.ntok[0] = T;
+        xs.tmax = T;
+    }
     if (x_dtype == K3C_BF16)
-        k_pf_quant_rows<uint16_t><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, (const uint16_t *)x, T, H);
+        k_pf_quant_rows<uint16_t><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, xs, T, H);
     else
-        k_pf_quant_rows<float><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, (const float *)x, T, H);
+        k_pf_quant_rows<float><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, xs, T, H);
     K3C_CHECK_LAUNCH();
     k_pf_gather_rows<<<dim3(sm_count() * 16, PF_J), 256, 0, s>>>(b.xq, b.tq, b.row_tok, b.n_rows, b.rows_cap, T, H);
     K3C_CHECK_LAUNCH();
@@ -894,7 +954,13 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     a.run_stride = L->run_stride;
     a.act_q = b.actq;
     a.act_sf = b.actsf;
-    a.contrib = b.contrib;
+    if (ep) {
+        for (int q = 0; q < ep->world; q++) a.contrib[q] = ep->contrib[q];
+        a.tmax = ep->t_max;
+    } else {
+        a.contrib[0] = b.contrib;
+        a.tmax = T;
+    }
     a.kstride = K + 1;
     a.T = T;
     a.H = H;
@@ -933,9 +999,11 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         K3C_CHECK_LAUNCH();
     }
     stage_end(STAGE_EXPERTS, s);
-    stage_begin(STAGE_COMBINE, s);
-    K3C_TRY(launch_moe_combine(out, b.contrib, wt, b.dropped, T, K, H, L->shared_run >= 0 ? 1 : 0, s));
-    stage_end(STAGE_COMBINE, s);
+    if (!ep) {
+        stage_begin(STAGE_COMBINE, s);
+        K3C_TRY(launch_moe_combine(out, b.contrib, wt, b.dropped, T, K, H, L->shared_run >= 0 ? 1 : 0, s));
+        stage_end(STAGE_COMBINE, s);
+    }
     // K3C_SYNC_CHECK=1: synchronise and report the kernels' own error code (a bounded wait
     // that gave up, or a failed alignment self-check). Off by default: it costs a host sync.
     static const int sync_check = getenv("K3C_SYNC_CHECK") ? 1 : 0;
@@ -968,4 +1036,39 @@ extern "C" int k3c_moe_prefill_tc(float *out, const void *x, int x_dtype, int nt
     k3c::clear_error();
     return k3c::launch_moe_prefill_tc(out, x, x_dtype, ntok, L, idx, wt, drops, scratch, scratch_bytes,
                                       (cudaStream_t)stream);
+}
+
+static int check_ep(const k3c_moe_pool_layer *L, const k3c_ep_peers *ep) {
+    if (!L || !ep || ep->world < 1 || ep->world > K3C_EP_MAX || ep->rank < 0 || ep->rank >= ep->world ||
+        ep->t_max <= 0 || (long long)ep->world * ep->t_max > 65535)
+        return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: bad peers (world, rank or t_max)");
+    if (ep->x_dtype != K3C_BF16 && ep->x_dtype != K3C_F32)
+        return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: x_dtype=%d", ep->x_dtype);
+    for (int q = 0; q < ep->world; q++)
+        if (ep->ntok[q] < 0 || ep->ntok[q] > ep->t_max || !ep->x[q] || !ep->idx[q] || !ep->contrib[q] ||
+            ((uintptr_t)ep->x[q] & 15) || ((uintptr_t)ep->contrib[q] & 15))
+            return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: rank %d's buffers (ntok %d)", q, ep->ntok[q]);
+    return K3C_OK;
+}
+
+extern "C" size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers) {
+    if (check_ep(L, peers)) return 0;
+    return k3c::moe_prefill_tc_scratch(L, peers->world * peers->t_max, false);
+}
+
+extern "C" int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers, void *scratch,
+                                          size_t scratch_bytes, k3c_stream_t stream) {
+    k3c::clear_error();
+    K3C_TRY(check_ep(L, peers));
+    return k3c::launch_moe_prefill_tc(nullptr, nullptr, peers->x_dtype, peers->world * peers->t_max, L, nullptr,
+                                      nullptr, nullptr, scratch, scratch_bytes, (cudaStream_t)stream, true, peers);
+}
+
+extern "C" int k3c_moe_combine(float *out, const float *contrib, const float *wt, const int *idx, int n_experts,
+                               int ntok, int topk, int hidden, int has_shared, k3c_stream_t stream) {
+    k3c::clear_error();
+    if (ntok < 0 || topk <= 0 || topk > K3_MAX_TOPK || hidden <= 0 || (ntok > 0 && (!out || !contrib || !wt)))
+        return k3c::set_error(K3C_EINVAL, "moe_combine: ntok=%d topk=%d hidden=%d", ntok, topk, hidden);
+    return k3c::launch_moe_combine_ids(out, contrib, wt, nullptr, idx, n_experts, ntok, topk, hidden, has_shared,
+                                       (cudaStream_t)stream);
 }

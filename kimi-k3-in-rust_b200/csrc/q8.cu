@@ -423,6 +423,7 @@ static int launch_q8_tc(float *y, int ldy, const void *x, int ldx, int ntok, con
     const size_t part_bytes = S > 1 ? (size_t)TB * MT * S * Q8_NT * 128 * sizeof(double) : 0;
     const size_t texp_bytes = align_up((size_t)S * TB * Q8_NT * sizeof(int), 256);
     char *buf = nullptr;
+    k3c::keep_async_pool();
     K3C_TRY_CUDA(cudaMallocAsync((void **)&buf, part_bytes + term_bytes + texp_bytes + (size_t)TB * MT * sizeof(int), s));
     double *part = reinterpret_cast<double *>(buf);
     int8_t *terms = reinterpret_cast<int8_t *>(buf + part_bytes);

@@ -516,9 +516,32 @@ extern "C" int k3c_router(int *idx, float *w, float *scores, const void *x, int 
         return k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk, renorm,
                                   routed_scale, ntok, nullptr, s);
     double *part = nullptr;
+    k3c::keep_async_pool();
     K3C_TRY_CUDA(cudaMallocAsync((void **)&part, k3c::router_scratch_bytes(hidden, n_experts, ntok), s));
     const int rc = k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk,
                                       renorm, routed_scale, ntok, part, s);
     cudaFreeAsync(part, s);
     return rc;
+}
+
+extern "C" size_t k3c_router_scratch(int hidden, int n_experts, int ntok) {
+    if (hidden <= 0 || n_experts <= 0 || ntok <= 0) return 0;
+    return k3c::router_scratch_bytes(hidden, n_experts, ntok) + 256;
+}
+
+extern "C" int k3c_router_ws(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W,
+                             int w_dtype, const float *bias, int hidden, int n_experts, int topk, int renorm,
+                             float routed_scale, int ntok, void *scratch, size_t scratch_bytes,
+                             k3c_stream_t stream) {
+    k3c::clear_error();
+    cudaStream_t s = (cudaStream_t)stream;
+    if (ntok <= 0 || hidden <= 0 || n_experts <= 0)
+        return k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk, renorm,
+                                  routed_scale, ntok, nullptr, s);
+    const size_t need = k3c::router_scratch_bytes(hidden, n_experts, ntok);
+    char *base = reinterpret_cast<char *>(((uintptr_t)scratch + 255) & ~(uintptr_t)255);
+    if (!scratch || (size_t)(base - (char *)scratch) + need > scratch_bytes)
+        return k3c::set_error(K3C_EINVAL, "router: scratch of %zu bytes, %zu needed", scratch_bytes, need + 256);
+    return k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk, renorm,
+                              routed_scale, ntok, reinterpret_cast<double *>(base), s);
 }

@@ -1,6 +1,11 @@
-"""Expert parallelism on two GPUs over NCCL: each rank's output equals the single-GPU
-tensor-core prefill of the same layer on its tokens (same activation terms; only the order in
-which the per-rank partial sums are added differs)."""
+"""Expert parallelism on two GPUs: each rank's output against the single-GPU tensor-core
+prefill of the same layer on its tokens.
+- NCCL all-to-all path (ep.ExpertParallel): same activation terms, only the order in which
+  the per-rank partial sums are added differs (1e-5).
+- Peer-memory path (ep.FusedExpertParallel: tokens read and pair outputs stored over
+  NVLink by the expert kernels): every pair output and the combine are the single-GPU ones,
+  so the outputs are equal bit for bit, for two layer calls in a row with different token
+  counts per rank."""
 import os
 import sys
 
@@ -58,6 +63,63 @@ def _worker(rank, world, port, err):
         raise
     finally:
         dist.destroy_process_group()
+
+
+def _fused_worker(rank, world, port, err):
+    sys.path.insert(0, ROOT)
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    ep = None
+    try:
+        from __graft_entry__ import load_package
+        k3 = load_package()
+        H, I, E, K = 256, 128, 8, 2
+        g = k3.synth.rng(31)                               # the same model on every rank
+        experts = [k3.synth.expert(g, H, I) for _ in range(E)]
+        shared = k3.synth.expert(g, H, I)
+        wf, wb = k3.synth.router_weights(g, E, H)
+        wb = k3.synth.bf16_bits((wf * 20).astype(np.float32))
+        W = torch.from_numpy(wb.view(np.int16)).to(dev).view(torch.bfloat16)
+        full = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in experts],
+                                    k3.DeviceExpert.from_host(shared, dev), W, None, H, I, K, dev, terms=2)
+        per = E // world
+        run_of = torch.full((E,), -1, dtype=torch.int32, device=dev)
+        run_of[rank * per:(rank + 1) * per] = full.run_of[rank * per:(rank + 1) * per]
+        layer = k3.PoolMoeLayer(full.arena, E + 1, run_of, E, W, None, H, I, K, terms=2)
+        ep = k3.ep.FusedExpertParallel(k3, layer, t_max=300)
+        for call, T in enumerate((200 + 37 * rank, 131 - 50 * rank)):
+            xb = k3.synth.bf16_bits(k3.synth.rng(700 + 10 * call + rank).standard_normal((T, H)).astype(np.float32))
+            x = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
+            y = ep.forward(x)
+            want, _, _ = full.prefill(x)
+            torch.cuda.synchronize()
+            y, want = y.cpu().numpy(), want.cpu().numpy()
+            assert np.array_equal(y.view(np.uint32), want.view(np.uint32)), (call, np.abs(y - want).max())
+    except Exception as e:
+        err.put(f"rank {rank}: {e!r}")
+        raise
+    finally:
+        if ep is not None:
+            ep.close()
+        dist.destroy_process_group()
+
+
+def test_ep_fused_two_gpus_equals_single_gpu():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    err = mp.get_context("spawn").SimpleQueue()
+    mp.start_processes(_fused_worker, args=(2, 29652, err), nprocs=2, join=True, start_method="spawn")
+    assert err.empty()
 
 
 def test_ep_two_gpus_matches_single_gpu():
