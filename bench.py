@@ -869,7 +869,7 @@ def run_ep(args, ws, rank, local):
         "config": {"workload": EP_WORKLOAD, "tokens": EP_T, "hidden": H, "inter": I, "experts": E, "topk": K,
                    "parallelism": f"ep{ws}"},
         "useful_tflops": flop * args.steps / dt / 1e12,
-        "dispatch": ({"impl": "fused: expert kernels read peers' token rows and store pair outputs over NVLink",
+        "dispatch": ({"impl": "fused: peers' token rows read by the quantisation kernel, per-rank partial rows stored at the token owner, over NVLink",
                       "remote_token_rows_read_per_step": sent_all / args.steps,
                       "sync": "two one-element NCCL all-reduces per layer"} if args.ep_impl == "fused" else
                      {"impl": "torch.distributed all_to_all_single (NCCL)" if ws > 1 else "none (1 GPU)",

@@ -275,15 +275,19 @@ int k3c_moe_combine(float *out, const float *contrib, const float *wt, const int
  * their own tokens. Per layer, with a cross-rank barrier (a one-element NCCL all-reduce on
  * the stream) between the steps:
  *   1. each rank writes its tokens' bf16 or fp32 activations into its x buffer and their
- *      top-k ids into its idx buffer (k3c_router);                       -- barrier
+ *      top-k ids and weights into its idx and wt buffers (k3c_router_ws);  -- barrier
  *   2. k3c_moe_prefill_ep_experts on every rank: plans over all ranks' pairs (reading the
- *      peers' idx), quantises the tokens straight out of the peers' x buffers (loads over
- *      NVLink), runs its own experts and its own tokens' shared expert, and writes every
- *      pair's output row into the contrib buffer of the rank that owns the token (stores
- *      over NVLink);                                                      -- barrier
- *   3. k3c_moe_combine on every rank over its own tokens and contrib buffer.
- * The buffers of step 1-3 are exchanged once per process: k3c_ep_alloc returns device memory
- * and its IPC handle, k3c_ep_open maps a peer's handle (same node). ---- */
+ *      peers' idx), quantises the tokens it needs straight out of the peers' x buffers
+ *      (loads over NVLink), runs its own experts and its own tokens' shared expert, adds each
+ *      token's pairs on this rank in top-k order (weights read from the token owner's wt)
+ *      and stores that partial row into the owner's partial buffer, setting the owner's flag
+ *      for (this rank, token) (stores over NVLink);                          -- barrier
+ *   3. k3c_moe_ep_combine on every rank: its tokens' flagged partials added in rank order;
+ *      the flags are cleared for the next layer.
+ * Buffers are exchanged once per process: k3c_ep_alloc gives device memory and its IPC
+ * handle, k3c_ep_open maps a peer's handle (same node). The partial buffer holds
+ * [world][t_max][hidden] fp32, the flag buffer [world][t_max] ints (zero before the first
+ * layer). ---- */
 #define K3C_EP_MAX 8
 typedef struct {
     unsigned char bytes[64];
@@ -295,16 +299,20 @@ int k3c_ep_close(void *peer_ptr);
 
 typedef struct {
     int world, rank;              /* ranks sharing the layer, this process's rank */
-    int t_max;                    /* rows of every rank's buffers */
+    int t_max;                    /* token rows of every rank's buffers */
     int x_dtype;                  /* K3C_BF16 or K3C_F32 */
     int ntok[K3C_EP_MAX];         /* each rank's token count (<= t_max) */
     const void *x[K3C_EP_MAX];    /* each rank's activations [t_max][hidden] */
     const int *idx[K3C_EP_MAX];   /* each rank's top-k ids [t_max][topk] */
-    float *contrib[K3C_EP_MAX];   /* each rank's pair outputs [t_max][topk+1][hidden] fp32 */
+    const float *wt[K3C_EP_MAX];  /* each rank's top-k weights [t_max][topk] */
+    float *partial[K3C_EP_MAX];   /* each rank's received partial rows [world][t_max][hidden] */
+    int *flag[K3C_EP_MAX];        /* each rank's received-row flags [world][t_max] */
 } k3c_ep_peers;
 size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers);
 int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers,
                                void *scratch, size_t scratch_bytes, k3c_stream_t stream);
+/* Step 3: out [ntok of this rank][hidden] fp32. */
+int k3c_moe_ep_combine(float *out, const k3c_ep_peers *peers, int hidden, k3c_stream_t stream);
 
 /* ---- HBM expert pool: the reference's expert cache (src/cache/k3_cache.c:24-261) with
  * experts streamed from pinned host memory. A slot holds one pool-format run

@@ -817,6 +817,74 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T, b
 
 static char *const kPfSizing = reinterpret_cast<char *>(4096);
 
+// Expert-parallel step 2, last kernel: one block per virtual token g (rank g / t_max, row
+// g % t_max). The token's pairs that ran on this rank (dropped = not resident here) are added
+// in top-k order with the owner's weights, the shared expert's row after them for this
+// rank's own tokens (the single-GPU combine's operations, k3_ops.c:641-642), and the partial
+// row is stored into the owner's partial buffer at [this rank][row] with its flag set. A
+// token with nothing on this rank sends nothing.
+__global__ void __launch_bounds__(128) k_ep_partial(k3c_ep_peers ep, const float *__restrict__ contrib,
+                                                    const uint8_t *__restrict__ dropped, int topk, int H,
+                                                    int has_shared) {
+    const int g = blockIdx.x, q = g / ep.t_max, t = g % ep.t_max;
+    if (t >= ep.ntok[q]) return;
+    const bool own_sh = has_shared && q == ep.rank;
+    bool any = own_sh;
+    for (int k = 0; k < topk; k++) any |= !dropped[(size_t)g * topk + k];
+    if (!any) return;
+    const float *wq = ep.wt[q] + (size_t)t * topk;
+    const int ks = topk + 1, h4 = H / 4;
+    const float4 *c4 = reinterpret_cast<const float4 *>(contrib) + (size_t)g * ks * h4;
+    float4 *dst = reinterpret_cast<float4 *>(ep.partial[q] + ((size_t)ep.rank * ep.t_max + t) * H);
+    for (int h = threadIdx.x; h < h4; h += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < topk; k++) {
+            if (dropped[(size_t)g * topk + k]) continue;
+            const float w = wq[k];
+            const float4 c = c4[(size_t)k * h4 + h];
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, c.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, c.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, c.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, c.w));
+        }
+        if (own_sh) {
+            const float4 c = c4[(size_t)topk * h4 + h];
+            acc.x = __fadd_rn(acc.x, c.x);
+            acc.y = __fadd_rn(acc.y, c.y);
+            acc.z = __fadd_rn(acc.z, c.z);
+            acc.w = __fadd_rn(acc.w, c.w);
+        }
+        dst[h] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        ep.flag[q][(size_t)ep.rank * ep.t_max + t] = 1;
+    }
+}
+
+// Expert-parallel step 3: this rank's tokens, the flagged partial rows added in rank order;
+// the flags are cleared for the next layer.
+__global__ void __launch_bounds__(128) k_ep_combine(float *__restrict__ out, k3c_ep_peers ep, int H) {
+    const int t = blockIdx.x, h4 = H / 4;
+    const float *part = ep.partial[ep.rank];
+    int *flag = ep.flag[ep.rank];
+    for (int h = threadIdx.x; h < h4; h += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < ep.world; q++) {
+            if (!flag[(size_t)q * ep.t_max + t]) continue;
+            const float4 c = reinterpret_cast<const float4 *>(part + ((size_t)q * ep.t_max + t) * H)[h];
+            acc.x = __fadd_rn(acc.x, c.x);
+            acc.y = __fadd_rn(acc.y, c.y);
+            acc.z = __fadd_rn(acc.z, c.z);
+            acc.w = __fadd_rn(acc.w, c.w);
+        }
+        reinterpret_cast<float4 *>(out + (size_t)t * H)[h] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x < ep.world) flag[(size_t)threadIdx.x * ep.t_max + t] = 0;
+}
+
 size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contrib = true) {
     if (!L || T <= 0) return 0;
     Carve cv{kPfSizing, (size_t)-1 / 2, 0};
@@ -859,7 +927,7 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         return set_error(K3C_EINVAL, "moe_prefill_tc: bad arena");
     Carve cv{(char *)scratch, scratch_bytes, 0};
     PfBufs b;
-    if (!carve_pf(cv, b, L, T, ep == nullptr))
+    if (!carve_pf(cv, b, L, T))
         return set_error(K3C_EINVAL, "moe_prefill_tc: scratch too small (%zu)", scratch_bytes);
     int *idx = idx_out ? idx_out : b.idx;
     float *wt = wt_out ? wt_out : b.wt;
@@ -954,13 +1022,8 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     a.run_stride = L->run_stride;
     a.act_q = b.actq;
     a.act_sf = b.actsf;
-    if (ep) {
-        for (int q = 0; q < ep->world; q++) a.contrib[q] = ep->contrib[q];
-        a.tmax = ep->t_max;
-    } else {
-        a.contrib[0] = b.contrib;
-        a.tmax = T;
-    }
+    a.contrib[0] = b.contrib;   // pair outputs stay on this rank ([T][topk+1][H])
+    a.tmax = T;
     a.kstride = K + 1;
     a.T = T;
     a.H = H;
@@ -1003,6 +1066,10 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         stage_begin(STAGE_COMBINE, s);
         K3C_TRY(launch_moe_combine(out, b.contrib, wt, b.dropped, T, K, H, L->shared_run >= 0 ? 1 : 0, s));
         stage_end(STAGE_COMBINE, s);
+    } else {
+        // this rank's pairs of every token, summed per token and stored at the token's owner
+        k_ep_partial<<<T, 128, 0, s>>>(*ep, b.contrib, b.dropped, K, H, L->shared_run >= 0 ? 1 : 0);
+        K3C_CHECK_LAUNCH();
     }
     // K3C_SYNC_CHECK=1: synchronise and report the kernels' own error code (a bounded wait
     // that gave up, or a failed alignment self-check). Off by default: it costs a host sync.
@@ -1045,15 +1112,28 @@ static int check_ep(const k3c_moe_pool_layer *L, const k3c_ep_peers *ep) {
     if (ep->x_dtype != K3C_BF16 && ep->x_dtype != K3C_F32)
         return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: x_dtype=%d", ep->x_dtype);
     for (int q = 0; q < ep->world; q++)
-        if (ep->ntok[q] < 0 || ep->ntok[q] > ep->t_max || !ep->x[q] || !ep->idx[q] || !ep->contrib[q] ||
-            ((uintptr_t)ep->x[q] & 15) || ((uintptr_t)ep->contrib[q] & 15))
+        if (ep->ntok[q] < 0 || ep->ntok[q] > ep->t_max || !ep->x[q] || !ep->idx[q] || !ep->wt[q] ||
+            !ep->partial[q] || !ep->flag[q] || ((uintptr_t)ep->x[q] & 15) || ((uintptr_t)ep->partial[q] & 15))
             return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: rank %d's buffers (ntok %d)", q, ep->ntok[q]);
+    if (L->hidden % 4) return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: hidden=%d", L->hidden);
     return K3C_OK;
 }
 
 extern "C" size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers) {
     if (check_ep(L, peers)) return 0;
-    return k3c::moe_prefill_tc_scratch(L, peers->world * peers->t_max, false);
+    return k3c::moe_prefill_tc_scratch(L, peers->world * peers->t_max);
+}
+
+extern "C" int k3c_moe_ep_combine(float *out, const k3c_ep_peers *peers, int hidden, k3c_stream_t stream) {
+    k3c::clear_error();
+    if (!peers || peers->world < 1 || peers->world > K3C_EP_MAX || peers->rank < 0 || peers->rank >= peers->world ||
+        hidden <= 0 || hidden % 4 || ((uintptr_t)out & 15) || !peers->partial[peers->rank] || !peers->flag[peers->rank])
+        return k3c::set_error(K3C_EINVAL, "moe_ep_combine: bad arguments");
+    const int n = peers->ntok[peers->rank];
+    if (n <= 0) return K3C_OK;
+    k3c::k_ep_combine<<<n, 128, 0, (cudaStream_t)stream>>>(out, *peers, hidden);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
 }
 
 extern "C" int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers, void *scratch,

@@ -114,20 +114,21 @@ def gpu_layer_fns(k3, layer_routed, layer_shared, router_w, router_bias, topk, r
 
 
 class FusedExpertParallel:
-    """Expert-parallel MoE prefill with the exchange done by the expert kernels themselves
-    (k3c_moe_prefill_ep_experts): no all-to-all of activations or partial sums.
+    """Expert-parallel MoE prefill with the exchange done by this library's kernels over peer
+    memory (k3c_moe_prefill_ep_experts, k3c_moe_ep_combine): no all-to-all.
 
     Per layer: (1) this rank copies its tokens into its shared x buffer and routes them into
-    its shared idx buffer; (2) after a barrier, every rank runs its own experts over the pairs
-    of ALL ranks, its quantisation kernel reading the peers' token rows over NVLink and its
-    down kernel storing each pair's output row into the token owner's contrib buffer; (3)
-    after a second barrier, each rank combines its own tokens in top-k order. Every pair's
-    output is computed exactly as on one GPU and the combine is the single-GPU one, so the
-    result equals the single-GPU layer on this rank's tokens.
+    its shared idx / wt buffers; (2) after a barrier, every rank runs its own experts over the
+    pairs of ALL ranks (its quantisation kernel reads the peers' token rows over NVLink), adds
+    each token's pairs that ran here in top-k order and stores that one partial row into the
+    token owner's partial buffer (stores over NVLink); (3) after a second barrier, each rank
+    adds its tokens' partial rows in rank order. The result equals the single-GPU layer up to
+    the grouping of the fp32 additions (per rank, then across ranks); on one rank it is the
+    single-GPU combine.
 
     The barriers are one-element NCCL all-reduces on the current stream: a rank's step-2
     kernels start only after every rank's step-1 writes are complete, and its combine only
-    after every rank's down kernel has finished storing into its buffer.
+    after every rank has stored its partial rows.
 
     layer: a PoolMoeLayer whose run table marks the other ranks' experts -1 and whose shared
     run is the shared expert (each rank computes its own tokens' shared expert).
@@ -147,22 +148,29 @@ class FusedExpertParallel:
         self.x_dtype = x_dtype or torch.bfloat16
         L = k3.lib()
         esize = torch.empty(0, dtype=self.x_dtype).element_size()
-        sizes = {"x": self.t_max * self.H * esize, "idx": self.t_max * self.K * 4,
-                 "contrib": self.t_max * (self.K + 1) * self.H * 4}
+        W_, T_ = self.world, self.t_max
+        sizes = {"x": T_ * self.H * esize, "idx": T_ * self.K * 4, "wt": T_ * self.K * 4,
+                 "partial": W_ * T_ * self.H * 4, "flag": W_ * T_ * 4}
         self._own, handles = {}, {}
         for name, nb in sizes.items():
             ptr, h = C.c_void_p(), k3.IpcHandleC()
             k3._check(L.k3c_ep_alloc(C.byref(ptr), nb, C.byref(h)), "k3c_ep_alloc")
             self._own[name] = ptr.value
             handles[name] = bytes(h.bytes)
-        everyone = [None] * self.world
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.x_buf = k3.device_view(self._own["x"], (T_, self.H), self.x_dtype)
+        self.idx_buf = k3.device_view(self._own["idx"], (T_, self.K), torch.int32)
+        self.wt_buf = k3.device_view(self._own["wt"], (T_, self.K), torch.float32)
+        k3.device_view(self._own["flag"], (W_, T_), torch.int32).zero_()
+        torch.cuda.synchronize()
+        everyone = [None] * W_
         dist.all_gather_object(everyone, handles, group=group)
         self._opened = []
         self.peers = k3.EpPeersC()
-        self.peers.world, self.peers.rank, self.peers.t_max = self.world, self.rank, self.t_max
+        self.peers.world, self.peers.rank, self.peers.t_max = W_, self.rank, T_
         self.peers.x_dtype = k3._dtype_code(torch.empty(0, dtype=self.x_dtype))
-        for q in range(self.world):
-            for name in ("x", "idx", "contrib"):
+        for q in range(W_):
+            for name in sizes:
                 if q == self.rank:
                     p = self._own[name]
                 else:
@@ -173,14 +181,11 @@ class FusedExpertParallel:
                     p = ptr.value
                     self._opened.append(p)
                 getattr(self.peers, name)[q] = p
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.x_buf = k3.device_view(self._own["x"], (self.t_max, self.H), self.x_dtype)
-        self.idx_buf = k3.device_view(self._own["idx"], (self.t_max, self.K), torch.int32)
-        self.contrib_buf = k3.device_view(self._own["contrib"], (self.t_max, self.K + 1, self.H), torch.float32)
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
-        self._ntok = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self._ntok = torch.zeros(W_, dtype=torch.int32, device=dev)
         self._scratch = torch.empty(0, dtype=torch.uint8, device=dev)
         self._rscratch = torch.empty(0, dtype=torch.uint8, device=dev)
+        self._counts = None
         self.last = {}
 
     def _barrier(self):
@@ -196,8 +201,8 @@ class FusedExpertParallel:
         if T > self.t_max:
             raise ValueError(f"{T} tokens > t_max {self.t_max}")
         # every rank's token count (a host read: the plan is sized on the host)
-        mine = torch.tensor([T], dtype=torch.int32, device=x.device)
         if self.world > 1:
+            mine = torch.full((1,), T, dtype=torch.int32, device=x.device)
             dist.all_gather_into_tensor(self._ntok, mine, group=self.group)
             counts = self._ntok.cpu().tolist()
         else:
@@ -206,18 +211,17 @@ class FusedExpertParallel:
             self.peers.ntok[q] = int(counts[q])
         # 1. this rank's tokens and their routing into the shared buffers
         self.x_buf[:T].copy_(x)
-        wt = torch.empty((T, self.K), dtype=torch.float32, device=x.device)
         if T:
             rneed = L.k3c_router_scratch(self.H, self.E, T)
             if self._rscratch.numel() < rneed:
                 self._rscratch = torch.empty(rneed, dtype=torch.uint8, device=x.device)
-            k3._check(L.k3c_router_ws(k3._ptr(self.idx_buf), k3._ptr(wt), None, k3._ptr(self.x_buf),
+            k3._check(L.k3c_router_ws(k3._ptr(self.idx_buf), k3._ptr(self.wt_buf), None, k3._ptr(self.x_buf),
                                       k3._dtype_code(self.x_buf), C.c_void_p(c.router_w), c.router_dtype,
                                       C.c_void_p(c.router_bias), self.H, self.E, self.K, c.renorm,
                                       c.routed_scale, T, k3._ptr(self._rscratch), self._rscratch.numel(),
                                       k3._stream()), "k3c_router_ws")
         self._barrier()
-        # 2. every rank's pairs through this rank's experts, outputs to the tokens' owners
+        # 2. every rank's pairs through this rank's experts; partial rows to the tokens' owners
         need = L.k3c_moe_prefill_ep_scratch(C.byref(c), C.byref(self.peers))
         if need == 0:
             raise k3.K3CError(f"k3c_moe_prefill_ep_scratch: {L.k3c_last_error().decode()}")
@@ -227,17 +231,15 @@ class FusedExpertParallel:
                                                self._scratch.numel(), k3._stream()),
                   "k3c_moe_prefill_ep_experts")
         self._barrier()
-        # 3. this rank's tokens, in top-k order
+        # 3. this rank's tokens: the partial rows in rank order
         out = torch.empty((T, self.H), dtype=torch.float32, device=x.device)
-        if T:
-            k3._check(L.k3c_moe_combine(k3._ptr(out), k3._ptr(self.contrib_buf), k3._ptr(wt),
-                                        k3._ptr(self.idx_buf), self.E, T, self.K, self.H,
-                                        1 if c.shared_run >= 0 else 0, k3._stream()), "k3c_moe_combine")
+        k3._check(L.k3c_moe_ep_combine(k3._ptr(out), C.byref(self.peers), self.H, k3._stream()),
+                  "k3c_moe_ep_combine")
         self.last = {"tokens": counts, "remote_rows_read": sum(counts) - T}
         return out
 
     def close(self):
-        """Unmaps the peers' buffers and frees this rank's (after a barrier, so no peer is
+        """Unmaps the peers' buffers and frees this rank's (between barriers, so no peer is
         still using them)."""
         import torch
         if not self._own:

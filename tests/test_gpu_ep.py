@@ -2,10 +2,10 @@
 prefill of the same layer on its tokens.
 - NCCL all-to-all path (ep.ExpertParallel): same activation terms, only the order in which
   the per-rank partial sums are added differs (1e-5).
-- Peer-memory path (ep.FusedExpertParallel: tokens read and pair outputs stored over
-  NVLink by the expert kernels): every pair output and the combine are the single-GPU ones,
-  so the outputs are equal bit for bit, for two layer calls in a row with different token
-  counts per rank."""
+- Peer-memory path (ep.FusedExpertParallel: token rows read and per-rank partial rows
+  stored over NVLink by this library's kernels): every pair output is the single-GPU one and
+  the combine adds the same products, grouped per rank (1e-5), for two layer calls in a row
+  with different token counts per rank."""
 import os
 import sys
 
@@ -102,7 +102,8 @@ def _fused_worker(rank, world, port, err):
             want, _, _ = full.prefill(x)
             torch.cuda.synchronize()
             y, want = y.cpu().numpy(), want.cpu().numpy()
-            assert np.array_equal(y.view(np.uint32), want.view(np.uint32)), (call, np.abs(y - want).max())
+            rel = np.abs(y - want).max() / np.abs(want).max()
+            assert rel < 1e-5, (call, rel)
     except Exception as e:
         err.put(f"rank {rank}: {e!r}")
         raise
