@@ -280,6 +280,7 @@ struct XSrc {
     const void *x[K3C_EP_MAX];
     int ntok[K3C_EP_MAX];
     int tmax;
+    const uint8_t *need;   // tokens to quantise (NULL: all)
 };
 
 // Token g's J terms, xq [J][T][H], and their block scales xsf [J][T][H/32]: every token once.
@@ -292,6 +293,7 @@ __global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq,
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int r = (int)(i / nb), blk = (int)(i % nb);
     if (r >= T) return;
+    if (src_x.need && !src_x.need[r]) return;   // no pair of this token runs here
     const int rq = r / src_x.tmax, tr = r % src_x.tmax;
     const bool live = tr < src_x.ntok[rq];
     const XT *src = reinterpret_cast<const XT *>(src_x.x[rq]) + (size_t)(live ? tr : 0) * H + blk * 32;
@@ -786,7 +788,7 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T, b
     b.rpart = cv.take<double>(router_scratch_bytes(H, E, T) / sizeof(double));
     b.pe = cv.take<int>(P);
     b.rank = cv.take<int>(P);
-    b.dropped = cv.take<uint8_t>(P);
+    b.dropped = cv.take<uint8_t>(P + T);   // + per-token need flags (expert parallelism)
     b.cnt = cv.take<int>((size_t)b.nchunk * E);
     b.chunk_base = cv.take<int>((size_t)b.nchunk * E);
     b.slot_base = cv.take<int>(E);
@@ -894,13 +896,22 @@ size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contr
 }
 
 // Every rank's top-k ids, ranks after one another ([world*t_max][topk]); rows at or past a
-// rank's token count get -1 (no pair).
-__global__ void k_ep_gather_idx(int *__restrict__ all, k3c_ep_peers ep, int topk) {
-    const size_t n = (size_t)ep.world * ep.t_max * topk;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int g = (int)(i / topk), k = (int)(i % topk);
+// rank's token count get -1 (no pair). need[g] = 1 when token g has a pair on this rank
+// (its expert resident here) or is this rank's own token with a shared expert: only those
+// tokens are quantised (read from their owner).
+__global__ void k_ep_gather_idx(int *__restrict__ all, uint8_t *__restrict__ need, k3c_ep_peers ep, int topk,
+                                const int *__restrict__ run_of, int n_experts, int has_shared) {
+    const int n = ep.world * ep.t_max;
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < n; g += gridDim.x * blockDim.x) {
         const int q = g / ep.t_max, t = g % ep.t_max;
-        all[i] = t < ep.ntok[q] ? ep.idx[q][(size_t)t * topk + k] : -1;
+        const bool live = t < ep.ntok[q];
+        bool here = live && has_shared && q == ep.rank;
+        for (int k = 0; k < topk; k++) {
+            const int e = live ? ep.idx[q][(size_t)t * topk + k] : -1;
+            all[(size_t)g * topk + k] = e;
+            here |= e >= 0 && e < n_experts && run_of[e] >= 0;
+        }
+        need[g] = here;
     }
 }
 
@@ -937,7 +948,8 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         routed = true;
         drops = nullptr;
         idx = b.idx;
-        k_ep_gather_idx<<<sm_count() * 4, 256, 0, s>>>(idx, *ep, K);
+        k_ep_gather_idx<<<sm_count() * 4, 256, 0, s>>>(idx, b.dropped + P, *ep, K, L->run_of, E,
+                                                       L->shared_run >= 0 ? 1 : 0);
         K3C_CHECK_LAUNCH();
     }
     K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), s));
@@ -972,6 +984,7 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
             xs.ntok[q] = ep->ntok[q];
         }
         xs.tmax = ep->t_max;
+        xs.need = b.dropped + P;
     } else {
         xs.x[0] = x;
         xs.ntok[0] = T;
