@@ -764,7 +764,7 @@ def run_expert(args, ws, rank, local):
 # ------------------------------------------------------------------ expert parallel (config[3])
 EP_T = 16384
 EP_WORKLOAD = "config[3] expert-parallel MoE prefill: 16384 bf16 tokens sharded over the GPUs, 384 " \
-              "MXFP4 experts (7168->2048->7168) as 384/N contiguous ids per GPU + a shared expert on " \
+              "MXFP4 experts (7168->2048->7168), 384/N per GPU (placement balanced on a routing sample) + a shared expert on " \
               "each, top-8 under a Zipf(1.1) selection bias (popularity over a random permutation of " \
               "the ids); dispatch and combine over NVLink peer memory inside the expert kernels (--ep-impl a2a: NCCL all-to-all)"
 
@@ -811,7 +811,18 @@ def run_ep(args, ws, rank, local):
     if ws > 1:
         dist.broadcast(bias, 0)
     run_of = torch.full((E,), -1, dtype=torch.int32, device=dev)
-    run_of[lo:hi] = torch.arange(per, dtype=torch.int32, device=dev)
+    if args.ep_place == "balanced" and ws > 1:
+        # expert placement from the pair counts of a routing sample (the sample the bias was
+        # fitted on, routed with it): greedy, heaviest expert to the least-loaded rank
+        sidx, _, _ = k3.router(sample, W, bias, K)
+        load = torch.bincount(sidx.reshape(-1).long(), minlength=E).double()
+        dist.broadcast(load, 0)
+        owner_l, lists = k3.ep.balanced_placement(load.cpu().tolist(), ws)
+        owner = torch.tensor(owner_l, dtype=torch.int64, device=dev)
+        mine = torch.tensor(lists[rank], dtype=torch.int64, device=dev)
+        run_of[mine] = torch.arange(per, dtype=torch.int32, device=dev)
+    else:
+        run_of[lo:hi] = torch.arange(per, dtype=torch.int32, device=dev)
     none = torch.full((E,), -1, dtype=torch.int32, device=dev)
     T = EP_T // ws
     if args.ep_impl == "fused":
@@ -867,7 +878,7 @@ def run_ep(args, ws, rank, local):
         "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
         "data": "synthetic",
         "config": {"workload": EP_WORKLOAD, "tokens": EP_T, "hidden": H, "inter": I, "experts": E, "topk": K,
-                   "parallelism": f"ep{ws}"},
+                   "parallelism": f"ep{ws}", "placement": args.ep_place if ws > 1 else "all experts"},
         "useful_tflops": flop * args.steps / dt / 1e12,
         "dispatch": ({"impl": "fused: peers' token rows read by the quantisation kernel, per-rank partial rows stored at the token owner, over NVLink",
                       "remote_token_rows_read_per_step": sent_all / args.steps,
@@ -894,6 +905,9 @@ def main():
     ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
                     help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
     ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
+    ap.add_argument("--ep-place", default="balanced", choices=["balanced", "contiguous"],
+                    help="ep workload: expert placement balanced on a routing sample's pair counts, or "
+                         "contiguous id ranges")
     ap.add_argument("--ep-impl", default="fused", choices=["fused", "a2a"],
                     help="ep workload: fused peer-memory exchange in the expert kernels, or NCCL all-to-all")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed", "ep", "expert"],

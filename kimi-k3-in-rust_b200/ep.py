@@ -256,3 +256,25 @@ class FusedExpertParallel:
         for p in self._own.values():
             L.k3c_ep_free(C.c_void_p(p))
         self._own = {}
+
+
+def balanced_placement(load, world):
+    """Expert -> rank placement with every rank holding len(load) / world experts and the
+    ranks' summed loads as even as a greedy pass makes them: experts in decreasing load, each
+    to the least-loaded rank that still has room (longest-processing-time first). `load` is a
+    per-expert pair count from a routing sample. Returns (owner [E] list, per-rank id lists,
+    each ascending)."""
+    E = len(load)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    cap = E // world
+    order = sorted(range(E), key=lambda e: (-float(load[e]), e))
+    sums = [0.0] * world
+    lists = [[] for _ in range(world)]
+    owner = [0] * E
+    for e in order:
+        r = min((q for q in range(world) if len(lists[q]) < cap), key=lambda q: (sums[q], q))
+        lists[r].append(e)
+        sums[r] += float(load[e])
+        owner[e] = r
+    return owner, [sorted(v) for v in lists]

@@ -74,3 +74,23 @@ def test_ep_dispatch_combine_two_ranks(skew):
     port = 29600 + (7 if skew else 3)
     mp.start_processes(_worker, args=(2, port, 11, skew, err), nprocs=2, join=True, start_method="spawn")
     assert err.empty()
+
+
+def test_balanced_placement():
+    """Equal expert counts per rank; Zipf loads spread much more evenly than contiguous ranges."""
+    import sys
+    sys.path.insert(0, ROOT)
+    from __graft_entry__ import load_package
+    k3 = load_package()
+    E, W = 384, 8
+    rng = np.random.default_rng(2)
+    marg = k3.synth.zipf_topk_marginal(E, 1.1, 8, samples=8192).numpy()   # reachable top-8 loads
+    load = marg[rng.permutation(E)]
+    owner, lists = k3.ep.balanced_placement(load, W)
+    assert sorted(sum(lists, [])) == list(range(E))
+    assert all(len(v) == E // W for v in lists)
+    assert all(owner[e] == r for r, v in enumerate(lists) for e in v)
+    sums = np.array([load[v].sum() for v in lists])
+    contiguous = load.reshape(W, -1).sum(1)
+    assert sums.max() / sums.mean() < contiguous.max() / contiguous.mean()
+    assert sums.max() / sums.mean() < 1.3
