@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+    if constexpr (GU) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // D may be scheduled
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2 * STAGES; i++) tc::mbar_init(&bars[i], 1);
         tc::mbar_init(&tfull[0], 1);
@@ -283,13 +284,42 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
         tc::prefetch_tmap(&tmB);
         const uint64_t pol = l2_evict_first_policy();
         uint32_t kiter = 0;
+        int kt_first = 0;   // K tiles of this CTA's first item already issued
+        if constexpr (!GU) {
+            // D runs as a programmatic dependent of GU: its first weight tiles and their scale
+            // atoms need nothing from GU and stream while GU finishes; the activation terms and
+            // their atoms are read only after the wait.
+            const int it = blockIdx.x;
+            if (ok && it < n_items) {
+                const int s = it / RT, rt = it % RT;
+                const SlotTc sl = p.slots[s];
+                const uint8_t *sfa = p.arena + (size_t)sl.run * p.run_stride + sf_off + (size_t)rt * KT * 512;
+                kt_first = KT < STAGES ? KT : STAGES;
+                for (int kt = 0; kt < kt_first; kt++) {
+                    uint8_t *sa = smem + kt * Cfg::STAGE;
+                    tc::mbar_expect_tx(&full[kt], Cfg::TX);
+                    tma_load_3d_hint(sa, &tmW, &full[kt], kt * 128, rt * 128, sl.run, pol);
+                    tc::bulk_load(sa + TC_A_BYTES + Cfg::B_BYTES, sfa + (size_t)kt * 512, 512, &full[kt]);
+                }
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                const uint8_t *sfb = p.act_sf + (size_t)s * KT * 512;
+                for (int kt = 0; kt < kt_first; kt++) {
+                    uint8_t *sb = smem + kt * Cfg::STAGE + TC_A_BYTES;
+                    tc::tma_load_3d(sb, &tmB, &full[kt], kt * 128, NCOL * s, 0);
+                    tc::bulk_load(sb + Cfg::B_BYTES + 512, sfb + (size_t)kt * 512, 512, &full[kt]);
+                }
+                kiter = kt_first;
+            } else {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+            }
+        }
         for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
             const int s = it / RT, rt = it % RT;
             const SlotTc sl = p.slots[s];
             const uint8_t *sfa = p.arena + (size_t)sl.run * p.run_stride + sf_off + (size_t)rt * KT * 512;
             const uint8_t *sfb = GU ? p.x_sf : p.act_sf + (size_t)s * KT * 512;
             const int b_row = GU ? 0 : NCOL * s;
-            for (int kt = 0; kt < KT; kt++, kiter++) {
+            for (int kt = it == (int)blockIdx.x ? kt_first : 0; kt < KT; kt++, kiter++) {
                 const int st = kiter % STAGES;
                 const uint32_t ph = (kiter / STAGES) & 1u;
                 if (kiter >= STAGES && !tc::mbar_wait(&empty[st], ph ^ 1u, p.err, 1)) { ok = false; break; }
@@ -500,7 +530,7 @@ static int launch_tc_stages(const TcBufs &b, const k3c_moe_pool_layer *L, cudaSt
     stage_begin(STAGE_EXPERTS, s);
     kgu<<<grid, TC_THREADS, Cfg::BYTES, s>>>(tmGU, tmX, a);
     K3C_CHECK_LAUNCH();
-    kd<<<grid, TC_THREADS, Cfg::BYTES, s>>>(tmD, tmAct, a);
+    K3C_TRY_CUDA(launch_pdl(kd, dim3(grid), dim3(TC_THREADS), Cfg::BYTES, s, tmD, tmAct, a));
     K3C_CHECK_LAUNCH();
     stage_end(STAGE_EXPERTS, s);
     return K3C_OK;
