@@ -468,20 +468,32 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
             __syncwarp();
             tc::tc_fence_after();
             const SlotPf sl = p.slots[s];
+            // The whole accumulator slice of this thread goes to registers first and the
+            // accumulator is released, so the next item's MMAs overlap the arithmetic and the
+            // stores below.
             if (GU) {
-                const int KTd = p.I / 128;
-#pragma unroll 1
-                for (int c = 2 * half; c < 2 * half + 2; c++) {
+                uint32_t vg[2][32], vu[2][32];
+#pragma unroll
+                for (int cc = 0; cc < 2; cc++) {
+                    const int c = 2 * half + cc;
                     // gate columns of intermediate block c and the matching up columns
                     const uint32_t gcol = 128u * (c >> 1) + 32u * (c & 1);
-                    uint32_t vg[32], vu[32];
-                    tc::tmem_ld32(tmem + lane_base + gcol, vg);
-                    tc::tmem_ld32(tmem + lane_base + gcol + 64, vu);
-                    tc::tmem_ld_wait();
+                    tc::tmem_ld32(tmem + lane_base + gcol, vg[cc]);
+                    tc::tmem_ld32(tmem + lane_base + gcol + 64, vu[cc]);
+                }
+                tc::tmem_ld_wait();
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tempty);
+                const int KTd = p.I / 128;
+#pragma unroll
+                for (int cc = 0; cc < 2; cc++) {
+                    const int c = 2 * half + cc;
                     if (!ok) continue;
                     float a[32];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) a[i] = act_fast(__uint_as_float(vg[i]), __uint_as_float(vu[i]), p.act);
+                    for (int i = 0; i < 32; i++)
+                        a[i] = act_fast(__uint_as_float(vg[cc][i]), __uint_as_float(vu[cc][i]), p.act);
                     uint4 qv[PF_J][2];
                     uint32_t sf[PF_J];
                     quant_row32(a, qv, sf);
@@ -497,30 +509,29 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
                     }
                 }
             } else {
-                float *dst = nullptr;
+                constexpr int NC = PF_N / 64;   // 32-column chunks per half
+                uint32_t v[NC][32];
+#pragma unroll
+                for (int cc = 0; cc < NC; cc++) tc::tmem_ld32(tmem + lane_base + 32u * (half * NC + cc), v[cc]);
+                tc::tmem_ld_wait();
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tempty);
                 if (ok && m < sl.ntok) {
                     const size_t pr = (size_t)s * PF_M + m;
                     const int g = p.pair_tok[pr];
-                    dst = p.contrib[g / p.tmax] + ((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H +
-                          (size_t)nt * PF_N;
-                }
-#pragma unroll 1
-                for (int c = half * (PF_N / 64); c < (half + 1) * (PF_N / 64); c++) {
-                    uint32_t v[32];
-                    tc::tmem_ld32(tmem + lane_base + 32u * c, v);
-                    tc::tmem_ld_wait();
-                    if (dst) {
-                        float4 *d4 = reinterpret_cast<float4 *>(dst + 32 * c);
+                    float *dst = p.contrib[g / p.tmax] + ((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H +
+                                 (size_t)nt * PF_N;
+#pragma unroll
+                    for (int cc = 0; cc < NC; cc++) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst + 32 * (half * NC + cc));
 #pragma unroll
                         for (int i = 0; i < 8; i++)
-                            d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                                __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                            d4[i] = make_float4(__uint_as_float(v[cc][4 * i]), __uint_as_float(v[cc][4 * i + 1]),
+                                                __uint_as_float(v[cc][4 * i + 2]), __uint_as_float(v[cc][4 * i + 3]));
                     }
                 }
             }
-            tc::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tempty);
         }
     }
     if constexpr (!GU) __threadfence_system();   // pair outputs may live in a peer's memory
