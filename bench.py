@@ -843,8 +843,9 @@ def run_ep(args, ws, rank, local):
     gx = torch.Generator(device=dev)
     gx.manual_seed(99 + rank)
     xs = [torch.randn((T, H), generator=gx, device=dev).to(torch.bfloat16) for _ in range(2)]
+    fwd_kw = {"counts": [T] * ws} if args.ep_impl == "fused" else {}   # equal splits: no count exchange
     for i in range(args.warmup):
-        epl.forward(xs[i % 2])
+        epl.forward(xs[i % 2], **fwd_kw)
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
@@ -854,7 +855,7 @@ def run_ep(args, ws, rank, local):
     e0.record()
     sent = 0
     for i in range(args.steps):
-        epl.forward(xs[i % 2])
+        epl.forward(xs[i % 2], **fwd_kw)
         sent += epl.last.get("sent_tokens", epl.last.get("remote_rows_read", 0))
     e1.record()
     torch.cuda.synchronize()

@@ -304,9 +304,12 @@ int rt_slices(int H, int E, int T) {
 }  // namespace
 
 bool router_tc_applies(int x_dtype, int w_dtype, int hidden, int ntok) {
-    if (const char *v = getenv("K3C_ROUTER_TC"))
+    int min_tok = RT_TC_MIN_TOKENS;
+    if (const char *v = getenv("K3C_ROUTER_TC")) {
         if (v[0] == '0') return false;
-    return x_dtype == K3C_BF16 && w_dtype == K3C_BF16 && hidden % 16 == 0 && ntok >= RT_TC_MIN_TOKENS;
+        if (atoi(v) > 1) min_tok = atoi(v);   // K3C_ROUTER_TC=<n>: tensor cores from n tokens
+    }
+    return x_dtype == K3C_BF16 && w_dtype == K3C_BF16 && hidden % 16 == 0 && ntok >= min_tok;
 }
 
 size_t router_tc_scratch_bytes(int hidden, int n_experts, int ntok) {

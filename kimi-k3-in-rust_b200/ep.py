@@ -193,15 +193,21 @@ class FusedExpertParallel:
         if self.world > 1:
             dist.all_reduce(self._flag, group=self.group)
 
-    def forward(self, x):
+    def forward(self, x, counts=None):
+        """counts: every rank's token count when the caller knows it (e.g. equal splits);
+        otherwise it is gathered, which costs a host synchronisation per layer."""
         import torch
         import torch.distributed as dist
         k3, L, c = self.k3, self.k3.lib(), self.layer.c
         T = x.shape[0]
         if T > self.t_max:
             raise ValueError(f"{T} tokens > t_max {self.t_max}")
-        # every rank's token count (a host read: the plan is sized on the host)
-        if self.world > 1:
+        # every rank's token count (the plan is sized on the host)
+        if counts is not None:
+            counts = [int(v) for v in counts]
+            if len(counts) != self.world or counts[self.rank] != T:
+                raise ValueError(f"counts {counts} do not match this rank's {T} tokens")
+        elif self.world > 1:
             mine = torch.full((1,), T, dtype=torch.int32, device=x.device)
             dist.all_gather_into_tensor(self._ntok, mine, group=self.group)
             counts = self._ntok.cpu().tolist()
