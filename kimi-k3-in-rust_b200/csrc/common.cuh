@@ -43,6 +43,15 @@ void stage_end(int stage, cudaStream_t s);
 
 static inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// The current device (0..63) for per-device caches of symbol addresses and function
+// attributes: a process may drive several GPUs, and a __device__ symbol's address and a
+// kernel's shared-memory opt-in are per device.
+inline int cur_dev() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    return dev;
+}
+
 // Entry points that allocate their scratch per call (k3c_router, k3c_q8_gemv) use the
 // device's default stream-ordered pool. Its default release threshold of 0 hands freed memory
 // back to the driver at every synchronisation, so the next call maps it again (hundreds of

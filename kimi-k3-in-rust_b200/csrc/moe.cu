@@ -216,7 +216,8 @@ static int launch_ffn_pair(const K3ExpertQ &e, const float *x, int ntok, int hid
                            float *actbuf, float *y, cudaStream_t s) {
     constexpr int CG = NT == 1 ? 8 : 4;
     const size_t sg = (size_t)NT * hidden * sizeof(float), sd = (size_t)NT * inter * sizeof(float);
-    static bool attr = false;
+    static bool attr_of[64] = {};
+    bool &attr = attr_of[cur_dev()];
     if (!attr) {
         K3C_TRY_CUDA(cudaFuncSetAttribute(k_ffn_gateup<NT, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         K3C_TRY_CUDA(cudaFuncSetAttribute(k_ffn_down<NT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));

@@ -413,7 +413,8 @@ static int q8_split(int tiles, int KT, int per_sm) {
 template <typename XT>
 static int launch_q8_tc(float *y, int ldy, const void *x, int ldx, int ntok, const int8_t *wq,
                         const float *wscale, int ldw, int in, int out, cudaStream_t s) {
-    static int *err = nullptr;
+    static int *err_of[64] = {};
+    int *&err = err_of[cur_dev()];
     if (!err) K3C_TRY_CUDA(cudaGetSymbolAddress((void **)&err, g_q8_err));
     const int KT = (in + 127) / 128, kpad = KT * 128;
     const int MT = (out + 127) / 128, TB = (ntok + Q8_NT - 1) / Q8_NT;

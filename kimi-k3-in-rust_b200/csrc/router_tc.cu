@@ -339,7 +339,8 @@ int launch_router_tc(RtFix *fix, double **part, int *nslices, const void *x, con
     const int H = hidden, E = n_experts, T = ntok, S = rt_slices(H, E, T);
     if ((uintptr_t)x % 16 || (uintptr_t)W % 16 || H % 16)
         return set_error(K3C_EINVAL, "router_tc: x and W must be 16-byte aligned, hidden a multiple of 16");
-    static int *err = nullptr;
+    static int *err_of[64] = {};
+    int *&err = err_of[cur_dev()];
     if (!err) K3C_TRY_CUDA(cudaGetSymbolAddress((void **)&err, g_rt_err));
     RtBufs b = carve_rt(scratch, H, E, T, S);
     k_rt_digits<<<T, 256, 0, s>>>((const uint16_t *)x, H, T, H, b.xd, b.xexp, b.xcnt, b.xk, b.xr, RT_CAP, 1, RT_CAP);
@@ -350,7 +351,8 @@ int launch_router_tc(RtFix *fix, double **part, int *nslices, const void *x, con
     K3C_TRY(make_digit_map(&mx, b.xd, H, T, 128));
     K3C_TRY(make_digit_map(&mw, b.wd, H, E, RT_N));
     using C = RtCfg<RT_N>;
-    static bool attr = false;
+    static bool attr_of[64] = {};
+    bool &attr = attr_of[cur_dev()];
     if (!attr) {
         K3C_TRY_CUDA(cudaFuncSetAttribute(k_rt_tc<RT_N>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr = true;
