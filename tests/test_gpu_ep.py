@@ -131,3 +131,42 @@ def test_ep_two_gpus_matches_single_gpu():
     err = mp.get_context("spawn").SimpleQueue()
     mp.start_processes(_worker, args=(2, 29650, err), nprocs=2, join=True, start_method="spawn")
     assert err.empty()
+
+
+def test_ep_fused_one_rank_equals_single_gpu():
+    """The peer-memory path's kernels (id gather, token quantisation from the x buffer,
+    per-rank partial rows, owner combine) on a one-rank group: one partial row per token, so
+    the output equals the single-GPU layer bit for bit (up to the sign of zeros)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    from __graft_entry__ import load_package
+    k3 = load_package()
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(0)
+    dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29661", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=60))
+    ep = None
+    try:
+        H, I, E, K = 512, 256, 16, 4
+        g = k3.synth.rng(77)
+        experts = [k3.synth.expert(g, H, I) for _ in range(E)]
+        shared = k3.synth.expert(g, H, I)
+        wf, wb = k3.synth.router_weights(g, E, H)
+        W = torch.from_numpy(wb.view(np.int16)).to(dev).view(torch.bfloat16)
+        full = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in experts],
+                                    k3.DeviceExpert.from_host(shared, dev), W, None, H, I, K, dev, terms=2)
+        ep = k3.ep.FusedExpertParallel(k3, full, t_max=400)
+        for call, T in enumerate((333, 97)):
+            xb = k3.synth.bf16_bits(k3.synth.rng(800 + call).standard_normal((T, H)).astype(np.float32))
+            x = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
+            y = ep.forward(x)
+            want, _, _ = full.prefill(x)
+            torch.cuda.synchronize()
+            y, want = y.cpu().numpy(), want.cpu().numpy()
+            assert np.array_equal(y, want), (call, np.abs(y - want).max())
+    finally:
+        if ep is not None:
+            ep.close()
+        dist.destroy_process_group()
