@@ -264,36 +264,44 @@ __device__ __noinline__ double rt_finish(const RtFix &fix, double logit, const u
     return logit + c;
 }
 
-// One block per token. With `part`, all threads first form the scores from the logit chunks
-// (added in chunk order) and write them to `scores` if that is not null; otherwise `scores`
-// holds them on entry. Warp 0 then takes the top-k by repeated warp argmax over score+bias.
+// TPB tokens per block (1 for small batches, 8 for large ones). With `part`, all threads
+// first form the scores from the logit chunks (added in chunk order) and write them to
+// `scores` if that is not null; otherwise `scores` holds them on entry. Warp tt then takes
+// token tt's top-k by repeated warp argmax over score+bias.
+template <int TPB>
 __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, float *__restrict__ w,
                                                        float *__restrict__ scores,
                                                        const double *__restrict__ part, int nchunk,
                                                        const float *__restrict__ bias,
                                                        int n_experts, int topk, int renorm,
                                                        float routed_scale, int ntok, RtFix fix) {
-    extern __shared__ float ch[];  // [2][n_experts]: choice values, scores
-    __shared__ int s_xk[RT_CAP];
-    __shared__ float s_xr[RT_CAP];
-    const int lane = threadIdx.x & 31;
-    const int t = blockIdx.x;
+    extern __shared__ float ch[];  // [TPB][2][n_experts]: choice values, scores
+    __shared__ int s_xk[TPB][RT_CAP];
+    __shared__ float s_xr[TPB][RT_CAP];
+    __shared__ int s_nx[TPB], s_ex[TPB];
+    __shared__ int s_idx[TPB][K3_MAX_TOPK];
+    __shared__ float s_w[TPB][K3_MAX_TOPK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * TPB;
+    const int nt = ntok - t0 < TPB ? ntok - t0 : TPB;
     grid_dep_wait();   // the logit chunks come from the partial kernel
-    float *c = ch;
-    float *sc = ch + n_experts;
-    int nx = 0, ex = 0;
-    const uint16_t *xrow = nullptr;
-    if (fix.x) {   // this token's residual list, for the tensor-core logits
-        nx = fix.xcnt[t];
-        ex = fix.xexp[t];
-        xrow = fix.x + (size_t)t * fix.H;
-        for (int i = threadIdx.x; i < nx && i < fix.cap; i += blockDim.x) {
-            s_xk[i] = fix.xk[(size_t)t * fix.cap + i];
-            s_xr[i] = fix.xr[(size_t)t * fix.cap + i];
+    if (fix.x) {   // the tokens' residual lists, for the tensor-core logits
+        for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+            s_nx[i] = fix.xcnt[t0 + i];
+            s_ex[i] = fix.xexp[t0 + i];
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < nt * RT_CAP; i += blockDim.x) {
+            const int tt = i / RT_CAP, k = i % RT_CAP;
+            if (k < s_nx[tt] && k < fix.cap) {
+                s_xk[tt][k] = fix.xk[(size_t)(t0 + tt) * fix.cap + k];
+                s_xr[tt][k] = fix.xr[(size_t)(t0 + tt) * fix.cap + k];
+            }
         }
         __syncthreads();
     }
-    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+    for (int i = threadIdx.x; i < nt * n_experts; i += blockDim.x) {
+        const int tt = i / n_experts, e = i % n_experts, t = t0 + tt;
         float v;
         if (part) {
             // chunks in order; up to 16 loads in flight per pass
@@ -307,19 +315,24 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
                 for (int k = 0; k < 16; k++)
                     if (k0 + k < nchunk) logit += v16[k];
             }
-            if (fix.x) logit = rt_finish(fix, logit, xrow, nx, ex, s_xk, s_xr, e, n_experts);
+            if (fix.x)
+                logit = rt_finish(fix, logit, fix.x + (size_t)t * fix.H, s_nx[tt], s_ex[tt], s_xk[tt], s_xr[tt], e,
+                                  n_experts);
             v = sigmoid_score(logit);
             if (scores) scores[(size_t)t * n_experts + e] = v;
         } else {
             v = scores[(size_t)t * n_experts + e];
         }
-        sc[e] = v;
-        c[e] = __fadd_rn(v, bias ? bias[e] : 0.0f);
+        ch[(size_t)(2 * tt + 1) * n_experts + e] = v;
+        ch[(size_t)(2 * tt) * n_experts + e] = __fadd_rn(v, bias ? bias[e] : 0.0f);
     }
     __syncthreads();
-    if (threadIdx.x >= 32) return;
-    __shared__ int s_idx[K3_MAX_TOPK];
-    __shared__ float s_w[K3_MAX_TOPK];
+    if (warp >= nt) return;
+    const int t = t0 + warp;
+    float *c = ch + (size_t)(2 * warp) * n_experts;
+    const float *sc = c + n_experts;
+    int *sidx = s_idx[warp];
+    float *sw = s_w[warp];
     // warp argmax of (value, index) pairs: largest value, lowest index on ties, -1 if none
     auto warp_best = [&](float bv, int bi) {
 #pragma unroll
@@ -348,8 +361,8 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
                     if (q == (bi >> 5)) v[q] = -INFINITY;
             }
             if (lane == 0) {
-                s_idx[j] = bi < 0 ? 0 : bi;
-                s_w[j] = bi < 0 ? 0.0f : sc[bi];
+                sidx[j] = bi < 0 ? 0 : bi;
+                sw[j] = bi < 0 ? 0.0f : sc[bi];
             }
         }
     } else {
@@ -362,8 +375,8 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
             }
             bi = warp_best(bv, bi);
             if (lane == 0) {
-                if (bi < 0) { s_idx[j] = 0; s_w[j] = 0.0f; }
-                else { s_idx[j] = bi; s_w[j] = sc[bi]; c[bi] = -INFINITY; }
+                if (bi < 0) { sidx[j] = 0; sw[j] = 0.0f; }
+                else { sidx[j] = bi; sw[j] = sc[bi]; c[bi] = -INFINITY; }
             }
             __syncwarp();
         }
@@ -372,16 +385,16 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
     if (lane == 0) {
         if (renorm && topk > 1) {
             double sum = 0.0;
-            for (int j = 0; j < topk; j++) sum += (double)s_w[j];
+            for (int j = 0; j < topk; j++) sum += (double)sw[j];
             const float inv = (float)(1.0 / (sum + 1e-20));
-            for (int j = 0; j < topk; j++) s_w[j] = __fmul_rn(s_w[j], inv);
+            for (int j = 0; j < topk; j++) sw[j] = __fmul_rn(sw[j], inv);
         }
-        for (int j = 0; j < topk; j++) s_w[j] = __fmul_rn(s_w[j], routed_scale);
+        for (int j = 0; j < topk; j++) sw[j] = __fmul_rn(sw[j], routed_scale);
     }
     __syncwarp();
     for (int j = lane; j < topk; j += 32) {
-        idx[(size_t)t * topk + j] = s_idx[j];
-        w[(size_t)t * topk + j] = s_w[j];
+        idx[(size_t)t * topk + j] = sidx[j];
+        w[(size_t)t * topk + j] = sw[j];
     }
 }
 
@@ -392,12 +405,22 @@ static int launch_select(int *idx, float *w, float *scores, const double *part, 
         return set_error(K3C_EINVAL, "router_select: n_experts=%d topk=%d ntok=%d", n_experts,
                          topk, ntok);
     if (ntok == 0) return K3C_OK;
-    const size_t smem = (size_t)2 * n_experts * sizeof(float);
-    if (smem > 200 * 1024) return set_error(K3C_EINVAL, "router_select: n_experts=%d too large", n_experts);
-    if (smem > 48 * 1024)
-        K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const size_t smem1 = (size_t)2 * n_experts * sizeof(float);
+    if (smem1 > 200 * 1024) return set_error(K3C_EINVAL, "router_select: n_experts=%d too large", n_experts);
+    // eight tokens per block for large batches (the top-k of each runs in its own warp)
+    if (ntok >= 256 && 8 * smem1 <= 200 * 1024) {
+        const size_t smem = 8 * smem1;
+        if (smem > 48 * 1024)
+            K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        count_launch();
+        K3C_TRY_CUDA(launch_pdl(k_router_select<8>, dim3((ntok + 7) / 8), dim3(256), smem, s, idx, w, scores, part,
+                                nchunk, bias, n_experts, topk, renorm, routed_scale, ntok, fix));
+        return K3C_OK;
+    }
+    if (smem1 > 48 * 1024)
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
     count_launch();
-    K3C_TRY_CUDA(launch_pdl(k_router_select, dim3(ntok), dim3(256), smem, s, idx, w, scores, part, nchunk, bias,
+    K3C_TRY_CUDA(launch_pdl(k_router_select<1>, dim3(ntok), dim3(256), smem1, s, idx, w, scores, part, nchunk, bias,
                             n_experts, topk, renorm, routed_scale, ntok, fix));
     return K3C_OK;
 }
