@@ -88,7 +88,9 @@ __global__ void __launch_bounds__(256) k_rt_digits(const uint16_t *__restrict__ 
             for (int j = 0; j < 3; j++)
                 *reinterpret_cast<uint2 *>(d0 + j * dstride + k) = make_uint2(q[j][0], q[j][1]);
         }
-        // list entries in k order: block-wide exclusive scan of the per-thread counts
+        // list entries in k order: block-wide exclusive scan of the per-thread counts (most
+        // chunks of an ordinary row have none)
+        if (__syncthreads_count(nres) == 0) continue;
         int incl = nres;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
