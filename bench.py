@@ -907,6 +907,10 @@ def run_ep(args, ws, rank, local):
     dist.barrier()
     torch.cuda.synchronize()
     clk = Clocks(local)
+    L.k3c_timing_enable(1)
+    ms_buf = (C.c_double * 4)()
+    n_buf = (C.c_longlong * 4)()
+    L.k3c_timing_read(ms_buf, n_buf, 4)          # discard warm-up records
     launches0 = L.k3c_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -916,6 +920,10 @@ def run_ep(args, ws, rank, local):
         sent += epl.last.get("sent_tokens", epl.last.get("remote_rows_read", 0))
     e1.record()
     torch.cuda.synchronize()
+    L.k3c_timing_enable(0)
+    L.k3c_timing_read(ms_buf, n_buf, 4)
+    stages = {name: ms_buf[j] / args.steps for j, name in enumerate(("experts", "router", "partial_rows", "q8"))
+              if j != 3}
     dist.barrier()
     torch.cuda.synchronize()
     clocks = clk.stop()
@@ -945,6 +953,7 @@ def run_ep(args, ws, rank, local):
         "config": {"workload": EP_WORKLOAD, "tokens": EP_T, "hidden": H, "inter": I, "experts": E, "topk": K,
                    "parallelism": f"ep{ws}", "placement": args.ep_place if ws > 1 else "all experts"},
         "useful_tflops": flop * args.steps / dt / 1e12,
+        "stages_ms_per_step_rank0": stages if args.ep_impl == "fused" else None,
         "dispatch": ({"impl": "fused: peers' token rows read by the quantisation kernel, per-rank partial rows stored at the token owner, over NVLink",
                       "remote_token_rows_read_per_step": sent_all / args.steps,
                       "sync": "two one-element NCCL all-reduces per layer"} if args.ep_impl == "fused" else

@@ -1092,8 +1092,10 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         stage_end(STAGE_COMBINE, s);
     } else {
         // this rank's pairs of every token, summed per token and stored at the token's owner
+        stage_begin(STAGE_COMBINE, s);
         k_ep_partial<<<T, 128, 0, s>>>(*ep, b.contrib, b.dropped, K, H, L->shared_run >= 0 ? 1 : 0);
         K3C_CHECK_LAUNCH();
+        stage_end(STAGE_COMBINE, s);
     }
     // K3C_SYNC_CHECK=1: synchronise and report the kernels' own error code (a bounded wait
     // that gave up, or a failed alignment self-check). Off by default: it costs a host sync.

@@ -565,6 +565,9 @@ extern "C" int k3c_router_ws(int *idx, float *w, float *scores, const void *x, i
     char *base = reinterpret_cast<char *>(((uintptr_t)scratch + 255) & ~(uintptr_t)255);
     if (!scratch || (size_t)(base - (char *)scratch) + need > scratch_bytes)
         return k3c::set_error(K3C_EINVAL, "router: scratch of %zu bytes, %zu needed", scratch_bytes, need + 256);
-    return k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk, renorm,
-                              routed_scale, ntok, reinterpret_cast<double *>(base), s);
+    k3c::stage_begin(k3c::STAGE_ROUTER, s);
+    const int rc = k3c::launch_router(idx, w, scores, x, x_dtype, W, w_dtype, bias, hidden, n_experts, topk, renorm,
+                                      routed_scale, ntok, reinterpret_cast<double *>(base), s);
+    k3c::stage_end(k3c::STAGE_ROUTER, s);
+    return rc;
 }
