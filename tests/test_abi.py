@@ -73,3 +73,49 @@ def test_errors_are_reported_without_a_gpu(k3):
     assert rc == -1 and b"odd" in L.k3c_last_error()
     rc = L.k3c_mxfp4_gemv(None, 4, None, 64, 1, None, None, 64, 4, 65, None)  # group > 64
     assert rc == -1 and b"group" in L.k3c_last_error()
+
+
+def test_pool_and_ep_struct_layouts_match_header(k3):
+    """The ctypes mirrors of the tensor-core layer, the expert-parallel peer table and the IPC
+    handle have the C layout (offsets of every pointer array)."""
+    prog = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "k3c.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n",
+         sizeof(k3c_moe_pool_layer), offsetof(k3c_moe_pool_layer, run_of),
+         offsetof(k3c_moe_pool_layer, shared_run), offsetof(k3c_moe_pool_layer, terms),
+         sizeof(k3c_ep_peers), offsetof(k3c_ep_peers, ntok), offsetof(k3c_ep_peers, x),
+         offsetof(k3c_ep_peers, idx), offsetof(k3c_ep_peers, wt), offsetof(k3c_ep_peers, partial),
+         offsetof(k3c_ep_peers, flag), sizeof(k3c_ipc_handle));
+  return 0; }
+"""
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(prog)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        got = [int(v) for v in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
+    P, E = k3.MoePoolLayerC, k3.EpPeersC
+    want = [C.sizeof(P), P.run_of.offset, P.shared_run.offset, P.terms.offset,
+            C.sizeof(E), E.ntok.offset, E.x.offset, E.idx.offset, E.wt.offset, E.partial.offset,
+            E.flag.offset, C.sizeof(k3.IpcHandleC)]
+    assert got == want
+
+
+def test_ep_arguments_are_checked_without_a_gpu(k3):
+    """The expert-parallel entry points validate the peer table before any CUDA call."""
+    L = k3.lib()
+    peers = k3.EpPeersC()
+    peers.world, peers.rank, peers.t_max = 9, 0, 16                 # more ranks than supported
+    layer = k3.MoePoolLayerC()
+    layer.hidden, layer.inter, layer.n_experts, layer.topk = 512, 256, 8, 2
+    assert L.k3c_moe_prefill_ep_scratch(C.byref(layer), C.byref(peers)) == 0
+    rc = L.k3c_moe_prefill_ep_experts(C.byref(layer), C.byref(peers), None, 0, None)
+    assert rc == -1 and b"peers" in L.k3c_last_error()
+    peers.world = 2                                                   # buffers missing
+    rc = L.k3c_moe_prefill_ep_experts(C.byref(layer), C.byref(peers), None, 0, None)
+    assert rc == -1 and b"buffers" in L.k3c_last_error()
+    rc = L.k3c_moe_ep_combine(None, C.byref(peers), 512, None)
+    assert rc == -1
