@@ -200,9 +200,16 @@ __global__ void __launch_bounds__(1024) k_moe_plan_tc(int *__restrict__ n_slots,
 // GU items: 64 gate + 64 up rows for output columns [64*rt, 64*rt+64); the epilogue applies
 // the activation and requantises it into the D stage's operand. D items: 128 down rows x
 // the slot's pairs; the epilogue writes each pair's unweighted expert output to contrib.
+// GU hands items out round robin (they are all the same size). D runs as a programmatic
+// dependent of GU and starts on the SMs that GU's CTAs leave: its producer takes items from
+// a queue shared by all CTAs (slot-major, so the slots GU finished first come first), passes
+// them to the MMA and epilogue warps through a small ring in shared memory, and waits only
+// for the GU row tiles of the item's own slot (a per-slot counter GU releases), so the down
+// projections fill the SMs while the last GU items finish.
 constexpr int TC_A_BYTES = 128 * 128;   // shared-memory footprint of a padded E2M1 tile
 constexpr int TC_A_TX = 128 * 128 / 2;  // its TMA transaction bytes: 4 bits per element
 constexpr int TC_THREADS = 192;
+constexpr int TC_IRING = 4;             // D: items in flight between the producer and the consumers
 
 __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
     return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
@@ -215,6 +222,9 @@ struct TcCfg {
     static constexpr int STAGE = TC_A_BYTES + B_BYTES + 1024;   // + SFA and SFB atoms
     static constexpr int TILE = 128 * (NT + 1) * 4;       // epilogue staging [128][NT+1] fp32
     static constexpr int BYTES = STAGES * STAGE + TILE + 256 + 1024;
+    // mbarriers (full/empty per stage, two accumulator pairs, the item ring's pair), the TMEM
+    // address and the item ring share the 256 bytes after the staging tile
+    static_assert(8 * (2 * STAGES + 4 + 2 * TC_IRING) + 4 + 4 * TC_IRING <= 256, "barrier area");
     static constexpr uint32_t SF_COL = 2 * NCOL;          // after the two accumulators
     static constexpr uint32_t TMEM_COLS = pow2_cols(2 * NCOL + 16);
     static constexpr uint32_t TX = TC_A_TX + B_BYTES + 1024;
@@ -233,6 +243,8 @@ struct TcArgs {
     int kstride;             // topk + 1
     int H, I, act;
     int *err;
+    int *d_next;             // D: next item of the queue (zero at launch)
+    int *gu_done;            // [S] GU row tiles of each slot written (zero at launch)
 };
 
 using tc::l2_evict_first_policy;
@@ -252,7 +264,9 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
     float *tile = reinterpret_cast<float *>(smem + STAGES * Cfg::STAGE);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::STAGE + Cfg::TILE);
     uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = tfull + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *ifull = tempty + 2, *iempty = ifull + TC_IRING;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(iempty + TC_IRING);
+    int *iring = reinterpret_cast<int *>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if constexpr (GU) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // D may be scheduled
@@ -262,6 +276,10 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
         tc::mbar_init(&tfull[1], 1);
         tc::mbar_init(&tempty[0], 4);
         tc::mbar_init(&tempty[1], 4);
+        for (int i = 0; i < TC_IRING; i++) {
+            tc::mbar_init(&ifull[i], 1);
+            tc::mbar_init(&iempty[i], 5);   // the MMA thread and one lane of each epilogue warp
+        }
         tc::fence_mbar_init();
     }
     if (warp == 1) tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -284,42 +302,41 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
         tc::prefetch_tmap(&tmB);
         const uint64_t pol = l2_evict_first_policy();
         uint32_t kiter = 0;
-        int kt_first = 0;   // K tiles of this CTA's first item already issued
-        if constexpr (!GU) {
-            // D runs as a programmatic dependent of GU: its first weight tiles and their scale
-            // atoms need nothing from GU and stream while GU finishes; the activation terms and
-            // their atoms are read only after the wait.
-            const int it = blockIdx.x;
-            if (ok && it < n_items) {
-                const int s = it / RT, rt = it % RT;
-                const SlotTc sl = p.slots[s];
-                const uint8_t *sfa = p.arena + (size_t)sl.run * p.run_stride + sf_off + (size_t)rt * KT * 512;
-                kt_first = KT < STAGES ? KT : STAGES;
-                for (int kt = 0; kt < kt_first; kt++) {
-                    uint8_t *sa = smem + kt * Cfg::STAGE;
-                    tc::mbar_expect_tx(&full[kt], Cfg::TX);
-                    tma_load_3d_hint(sa, &tmW, &full[kt], kt * 128, rt * 128, sl.run, pol);
-                    tc::bulk_load(sa + TC_A_BYTES + Cfg::B_BYTES, sfa + (size_t)kt * 512, 512, &full[kt]);
-                }
-                asm volatile("griddepcontrol.wait;" ::: "memory");
-                const uint8_t *sfb = p.act_sf + (size_t)s * KT * 512;
-                for (int kt = 0; kt < kt_first; kt++) {
-                    uint8_t *sb = smem + kt * Cfg::STAGE + TC_A_BYTES;
-                    tc::tma_load_3d(sb, &tmB, &full[kt], kt * 128, NCOL * s, 0);
-                    tc::bulk_load(sb + Cfg::B_BYTES + 512, sfb + (size_t)kt * 512, 512, &full[kt]);
-                }
-                kiter = kt_first;
+        int ready_s = -1;   // D: the last slot whose activation terms were seen complete
+        for (uint32_t li = 0; ok; li++) {
+            int it;
+            if constexpr (GU) {
+                it = (int)(blockIdx.x + li * gridDim.x);
+                if (it >= n_items) break;
             } else {
-                asm volatile("griddepcontrol.wait;" ::: "memory");
+                // take the next item of the queue and hand it to the MMA and epilogue warps
+                const uint32_t r = li % TC_IRING;
+                if (li >= TC_IRING && !tc::mbar_wait(&iempty[r], (li / TC_IRING - 1) & 1u, p.err, 11)) {
+                    ok = false;
+                    break;
+                }
+                it = atomicAdd(p.d_next, 1);
+                iring[r] = it < n_items ? it : -1;
+                tc::mbar_arrive(&ifull[r]);
+                if (it >= n_items) break;
             }
-        }
-        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
             const int s = it / RT, rt = it % RT;
             const SlotTc sl = p.slots[s];
             const uint8_t *sfa = p.arena + (size_t)sl.run * p.run_stride + sf_off + (size_t)rt * KT * 512;
             const uint8_t *sfb = GU ? p.x_sf : p.act_sf + (size_t)s * KT * 512;
             const int b_row = GU ? 0 : NCOL * s;
-            for (int kt = it == (int)blockIdx.x ? kt_first : 0; kt < KT; kt++, kiter++) {
+            if constexpr (!GU) {
+                // the slot's activation terms are complete once all of its GU row tiles are
+                if (s != ready_s) {
+                    if (!tc::wait_count(p.gu_done + s, (2 * p.I) / 128, p.err, 12)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_proxy_async_global();
+                    ready_s = s;
+                }
+            }
+            for (int kt = 0; kt < KT; kt++, kiter++) {
                 const int st = kiter % STAGES;
                 const uint32_t ph = (kiter / STAGES) & 1u;
                 if (kiter >= STAGES && !tc::mbar_wait(&empty[st], ph ^ 1u, p.err, 1)) { ok = false; break; }
@@ -335,10 +352,19 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
         }
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
-        uint32_t kiter = 0, li = 0;
+        uint32_t kiter = 0;
         bool ok = true;
         const uint32_t idesc0 = tc::idesc_mxf8f6f4(tc::FMT_E2M1, tc::FMT_E4M3, NCOL, 0, 0);
-        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, li++) {
+        for (uint32_t li = 0; ok; li++) {
+            if constexpr (GU) {
+                if ((int)(blockIdx.x + li * gridDim.x) >= n_items) break;
+            } else {
+                const uint32_t r = li % TC_IRING;
+                if (!tc::mbar_wait(&ifull[r], (li / TC_IRING) & 1u, p.err, 13)) break;
+                const int it = iring[r];
+                tc::mbar_arrive(&iempty[r]);
+                if (it < 0) break;
+            }
             const uint32_t a = li & 1u, use = li >> 1;
             if (use >= 1 && !tc::mbar_wait(&tempty[a], (use - 1) & 1u, p.err, 4)) { ok = false; break; }
             tc::tc_fence_after();
@@ -368,13 +394,25 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
         }
     } else if (warp >= 2) {
         // ------------------------------------------------------------ epilogue
-        // Every epilogue warp runs every item and every named barrier even after a failed
+        // GU: every epilogue warp runs every item and every named barrier even after a failed
         // wait (it then skips the TMEM read and the work), so the barriers cannot strand a
-        // warp; once an error is recorded the remaining waits return at once.
+        // warp; once an error is recorded the remaining waits return at once. D has no named
+        // barriers: a warp leaves the queue at the first failed wait.
         const int q = warp & 3;                 // TMEM lane quadrant
         const int row = 32 * q + lane;          // row within the 128-row tile
-        uint32_t li = 0;
-        for (int it = blockIdx.x; it < n_items; it += gridDim.x, li++) {
+        for (uint32_t li = 0;; li++) {
+            int it;
+            if constexpr (GU) {
+                it = (int)(blockIdx.x + li * gridDim.x);
+                if (it >= n_items) break;
+            } else {
+                const uint32_t r = li % TC_IRING;
+                if (*(volatile int *)p.err != 0 || !tc::mbar_wait(&ifull[r], (li / TC_IRING) & 1u, p.err, 14)) break;
+                it = iring[r];
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&iempty[r]);
+                if (it < 0) break;
+            }
             const int s = it / RT, rt = it % RT;
             const uint32_t a = li & 1u;
             const bool ok = *(volatile int *)p.err == 0 && tc::mbar_wait(&tfull[a], (li >> 1) & 1u, p.err, 3);
@@ -419,8 +457,14 @@ __global__ void __launch_bounds__(TC_THREADS) k_tc_moe(const __grid_constant__ C
                                     (uint8_t)sf;
                             });
                     }
+                    // the down kernel reads these bytes with TMA in other CTAs
+                    tc::fence_proxy_async_global();
+                    __threadfence();
                 }
                 named_bar_sync(1, 128);          // the tile is reused by the next item
+                // this row tile of slot s is written (also after a failed wait: the error code
+                // is set, and the down kernel should not wait out its timeout as well)
+                if (q == 2 && lane == 0) tc::red_release_add1(p.gu_done + s);
             } else if (ok) {
                 const int h = 128 * rt + row;
 #pragma unroll
@@ -456,7 +500,8 @@ static bool carve_tc(Carve &cv, TcBufs &b, const k3c_moe_pool_layer *L, int ntok
     const int H = L->hidden, I = L->inter, J = L->terms;
     b.max_slots = (P < L->n_experts ? P : L->n_experts) + 1;
     b.n_slots = cv.take<int>(1);
-    b.err = cv.take<int>(1);
+    // error code, the down kernel's queue head, then the per-slot GU counters: zeroed together
+    b.err = cv.take<int>(2 + (size_t)b.max_slots);
     b.slots = cv.take<SlotTc>(b.max_slots);
     b.pair_tok = cv.take<int>((size_t)b.max_slots * 32);
     b.pair_k = cv.take<int>((size_t)b.max_slots * 32);
@@ -516,6 +561,8 @@ static int launch_tc_stages(const TcBufs &b, const k3c_moe_pool_layer *L, cudaSt
     a.I = I;
     a.act = L->act;
     a.err = b.err;
+    a.d_next = b.err + 1;
+    a.gu_done = b.err + 2;
     auto kgu = k_tc_moe<J, NT, STAGES, true>;
     auto kd = k_tc_moe<J, NT, STAGES, false>;
     K3C_TRY_CUDA(cudaFuncSetAttribute(kgu, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
@@ -568,7 +615,7 @@ int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const
     int *idx = idx_out ? idx_out : b.idx;
     float *wt = wt_out ? wt_out : b.wt;
     if (routed && (!idx_out || !wt_out)) return set_error(K3C_EINVAL, "moe_decode_tc_routed: null routing");
-    K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, sizeof(int), s));
+    K3C_TRY_CUDA(cudaMemsetAsync(b.err, 0, (2 + (size_t)b.max_slots) * sizeof(int), s));
     if (!routed) {
         stage_begin(STAGE_ROUTER, s);
         K3C_TRY(launch_router(idx, wt, nullptr, x, x_dtype, L->router_w, L->router_dtype, L->router_bias, H,

@@ -221,6 +221,34 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders generic-proxy global-memory accesses against async-proxy ones (TMA and bulk copies)
+// of the same bytes: a producer CTA runs it after its plain stores, a consumer CTA after it
+// has observed the producer's release and before its TMA reads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Release-add of 1 to a device-scope counter in global memory.
+__device__ __forceinline__ void red_release_add1(int *ctr) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+// Bounded wait until a device-scope counter reaches `target` (acquire), for a dependency
+// between CTAs of different kernels that run at the same time. Gives up after ~2 s of device
+// time, or as soon as another thread has recorded an error, and returns false (recording
+// `code` on a timeout).
+__device__ __forceinline__ bool wait_count(const int *ctr, int target, int *err, int code) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        if (*(volatile int *)err) return false;
+        if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+            atomicExch(err, code);
+            return false;
+        }
+        __nanosleep(128);
+    }
+}
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
