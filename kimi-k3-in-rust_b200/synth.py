@@ -139,3 +139,33 @@ def zipf_fit_bias(scores, s: float = 1.1, topk: int = 8, iters: int = 1500, step
         b += step * torch.clamp(torch.log((target + eps) / (p + eps)), -1.0, 1.0) / (1 + it / 300)
         b -= b.max()
     return b.to(torch.float32)
+
+
+def latent_layer(g: np.random.Generator, hidden: int, latent: int, inter: int,
+                 n_experts: int, topk: int, n_shared: int = 2, wdt: int = 1,
+                 scale_lo: int = SCALE_LO, scale_hi: int = SCALE_HI) -> dict:
+    """One K3 latent MoE layer with the fields of the oracle's ora_latent: an fp32 router
+    [n_experts][hidden] (spread so routing is decisive), routed MXFP4 experts at the latent
+    width (``experts``), trunk matrices down [latent][hidden], up [hidden][latent],
+    sh1/sh3 [inter*n_shared][hidden], sh2 [hidden][inter*n_shared] as bf16 bit patterns
+    (wdt=1) or fp32 (wdt=0), each ~N(0, 1/in), and latent-norm weights near 1."""
+    SI = inter * n_shared
+
+    def trunk(out_, in_):
+        w = g.standard_normal((out_, in_), dtype=np.float32) * np.float32(1.0 / np.sqrt(in_))
+        return bf16_bits(w) if wdt == 1 else w
+
+    router = g.standard_normal((n_experts, hidden), dtype=np.float32) * np.float32(0.4)
+    if wdt == 1:
+        router = bf16_to_f32(bf16_bits(router))
+    return dict(
+        router_w=router.astype(np.float32),
+        router_bias=(g.standard_normal(n_experts, dtype=np.float32) * 0.05).astype(np.float32),
+        experts=[expert(g, latent, inter, scale_lo=scale_lo, scale_hi=scale_hi)
+                 for _ in range(n_experts)],
+        latent_norm=(1.0 + 0.1 * g.standard_normal(latent, dtype=np.float32)).astype(np.float32),
+        down=trunk(latent, hidden), up=trunk(hidden, latent),
+        sh1=trunk(SI, hidden), sh3=trunk(SI, hidden), sh2=trunk(hidden, SI),
+        wdt=wdt, hidden=hidden, latent=latent, inter=inter, n_shared=n_shared,
+        n_experts=n_experts, topk=topk, renorm=1, latent_norm_on=1,
+        routed_scale=1.0, rms_eps=1e-5, situ_b1=4.0, situ_b2=25.0)

@@ -22,6 +22,14 @@ static void ora_fatal(const char *msg, long v)
     abort();
 }
 
+/* bf16 bit pattern -> fp32: the pattern is the top half of the float (include/k3/k3.h:274-279). */
+static float ora_bf16f(uint16_t h)
+{
+    union { uint32_t u; float f; } v;
+    v.u = (uint32_t)h << 16;
+    return v.f;
+}
+
 /* E2M1 code -> value. Bit 3 is the sign, bits 0-2 index the eight magnitudes
  * {0, .5, 1, 1.5, 2, 3, 4, 6}; code 8 is -0.0. Restates K3_E2M1, src/core/k3_ops.c:1049-1052. */
 float ora_e2m1(unsigned code)
@@ -99,19 +107,54 @@ void ora_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
     }
 }
 
-/* y[o] = sum_i W[o][i] x[i], fp32 weights, double accumulator, one rounding at the end.
- * The reference's k3_matmul (src/core/k3_ops.c:265-291) splits the sum over 16 lanes;
- * this sums in element order. Used only to build dequantise-then-matmul comparisons,
- * the check the reference itself makes at tests/unit/test_expert.c:192-238. */
+/* One output of the trunk matmuls in the reference's fixed summation order: element i of
+ * the first in - in%16 feeds double accumulator i%16 by a fused multiply-add in element
+ * order; the sixteen are combined as b_l = (a_l + a_{l+4}) + (a_{l+8} + a_{l+12}) for
+ * l = 0..3 and then (b0 + b1) + (b2 + b3); the in%16 tail is fused onto that total in
+ * element order; the result is rounded once to float. Restates k3_matmul,
+ * src/core/k3_ops.c:265-291. k3_matmul_bf16 (:1091-1196) keeps the same partition and
+ * tree in each of its paths (the bf16 value is its bit pattern shifted into an fp32), so
+ * both are bit-exact against this. bf16 != 0 selects uint16 weights. */
+static float ora_dot_tree(const void *row, int bf16, const float *x, int in)
+{
+    const float *rf = (const float *)row;
+    const uint16_t *rh = (const uint16_t *)row;
+#define ORA_W(i) (bf16 ? ora_bf16f(rh[(i)]) : rf[(i)])
+    double a[16] = { 0 };
+    int i = 0;
+    for (; i + 15 < in; i += 16)
+        for (int l = 0; l < 16; l++) a[l] = fma((double)ORA_W(i + l), (double)x[i + l], a[l]);
+    const double b0 = (a[0] + a[4]) + (a[8] + a[12]);
+    const double b1 = (a[1] + a[5]) + (a[9] + a[13]);
+    const double b2 = (a[2] + a[6]) + (a[10] + a[14]);
+    const double b3 = (a[3] + a[7]) + (a[11] + a[15]);
+    double acc = (b0 + b1) + (b2 + b3);
+    for (; i < in; i++) acc = fma((double)ORA_W(i), (double)x[i], acc);
+#undef ORA_W
+    return (float)acc;
+}
+
+/* y[o] = sum_i W[o][i] x[i], fp32 weights [out][in], k3_matmul's order (above). */
 void ora_matmul_f32(float *y, const float *x, const float *W, int in, int out)
 {
 #pragma omp parallel for schedule(static) if (out > 64)
-    for (int o = 0; o < out; o++) {
-        const float *row = W + (size_t)o * in;
-        double acc = 0.0;
-        for (int i = 0; i < in; i++) acc += (double)row[i] * (double)x[i];
-        y[o] = (float)acc;
-    }
+    for (int o = 0; o < out; o++) y[o] = ora_dot_tree(W + (size_t)o * in, 0, x, in);
+}
+
+/* The same with bf16 weights (uint16 bit patterns [out][in]): k3_matmul_bf16,
+ * src/core/k3_ops.c:1091-1196. */
+void ora_matmul_bf16(float *y, const float *x, const uint16_t *W, int in, int out)
+{
+#pragma omp parallel for schedule(static) if (out > 64)
+    for (int o = 0; o < out; o++) y[o] = ora_dot_tree(W + (size_t)o * in, 1, x, in);
+}
+
+/* The trunk matmul dispatch on the weight type, include/k3/k3.h:289-296. */
+void ora_mmw(float *y, const float *x, const void *W, int wdt, int in, int out)
+{
+    if (wdt == ORA_WBF16) ora_matmul_bf16(y, x, (const uint16_t *)W, in, out);
+    else if (wdt == ORA_WI8) ora_matmul_q8(y, x, W, in, out);
+    else ora_matmul_f32(y, x, (const float *)W, in, out);
 }
 
 /* Per-row int8 matmul over the reference's inline row layout [f32 scale][int8 * in],
@@ -283,4 +326,70 @@ void ora_moe_layer(float *out, const float *x, int ntok, const float *router_w,
         if (wt) memcpy(wt + (size_t)t * topk, lw, (size_t)topk * sizeof(float));
     }
     free(li); free(lw); free(edn); free(sdn);
+}
+
+/* The latent MoE layer of the K3 model, src/core/k3_ops.c:556-656, per token:
+ *   1. route on the full-width input (:576);
+ *   2. z = down x, the trunk matmul into the latent width (:596);
+ *   3. accL = sum over the top-k of w_j * expert_j(z), in float, in top-k order, from zero,
+ *      each expert gate/up -> SiTU-GLU -> down at the latent width (:599-642); the experts
+ *      come from the fp32 bank w1/w3/w2 through k3_matmul (:635-638) or, when w1 is NULL,
+ *      from MXFP4 experts through k3_matmul_mxfp4 (:628-631);
+ *   4. RMSNorm of the aggregate when latent_norm_on (:646);
+ *   5. out = up accL (:647);
+ *   6. the shared expert at full width (sh1/sh3 -> SiTU-GLU -> sh2, intermediate
+ *      inter*n_shared) on the original input, added with no weight (:650-654).
+ * idx/wt ([ntok][topk]) receive the routing when non-NULL. The draft-only cache_only mode
+ * (:580-593) is not part of this path. */
+void ora_moe_latent(float *out, const float *x, int ntok, const ora_latent *L, int *idx,
+                    float *wt)
+{
+    const int E = L->hidden, Lw = L->latent, I = L->inter, SI = L->inter * L->n_shared;
+    const int K = L->topk;
+    int *li = (int *)malloc((size_t)K * sizeof(int));
+    float *lw = (float *)malloc((size_t)K * sizeof(float));
+    float *z = (float *)malloc((size_t)Lw * sizeof(float));
+    float *acc = (float *)malloc((size_t)Lw * sizeof(float));
+    float *gu = (float *)malloc((size_t)3 * I * sizeof(float));
+    float *edn = (float *)malloc((size_t)Lw * sizeof(float));
+    float *sgu = (float *)malloc((size_t)3 * SI * sizeof(float));
+    float *sdn = (float *)malloc((size_t)E * sizeof(float));
+    if (!li || !lw || !z || !acc || !gu || !edn || !sgu || !sdn)
+        ora_fatal("ora_moe_latent: out of memory", E);
+    float *act = gu + 2 * I, *sact = sgu + 2 * SI;
+    for (int t = 0; t < ntok; t++) {
+        const float *xt = x + (size_t)t * E;
+        float *ot = out + (size_t)t * E;
+        ora_router(li, lw, xt, L->router_w, L->router_bias, E, L->n_experts, K, L->renorm,
+                   L->routed_scale);
+        ora_mmw(z, xt, L->down, L->wdt, E, Lw);
+        for (int i = 0; i < Lw; i++) acc[i] = 0.0f;
+        for (int j = 0; j < K; j++) {
+            const int e = li[j];
+            if (L->w1) {
+                ora_matmul_f32(gu, z, L->w1 + (size_t)e * I * Lw, Lw, I);
+                ora_matmul_f32(gu + I, z, L->w3 + (size_t)e * I * Lw, Lw, I);
+                ora_situ_glu(act, gu, I, L->situ_b1, L->situ_b2);
+                ora_matmul_f32(edn, act, L->w2 + (size_t)e * Lw * I, I, Lw);
+            } else {
+                const ora_expert *q = &L->experts[e];
+                ora_matmul_mxfp4(gu, z, q->p1, q->s1, Lw, I, 32);
+                ora_matmul_mxfp4(gu + I, z, q->p3, q->s3, Lw, I, 32);
+                ora_situ_glu(act, gu, I, L->situ_b1, L->situ_b2);
+                ora_matmul_mxfp4(edn, act, q->p2, q->s2, I, Lw, 32);
+            }
+            const float wj = lw[j];
+            for (int i = 0; i < Lw; i++) acc[i] += wj * edn[i];
+        }
+        if (L->latent_norm_on) ora_rmsnorm(acc, acc, L->latent_norm, Lw, L->rms_eps);
+        ora_mmw(ot, acc, L->up, L->wdt, Lw, E);
+        ora_mmw(sgu, xt, L->sh1, L->wdt, E, SI);
+        ora_mmw(sgu + SI, xt, L->sh3, L->wdt, E, SI);
+        ora_situ_glu(sact, sgu, SI, L->situ_b1, L->situ_b2);
+        ora_mmw(sdn, sact, L->sh2, L->wdt, SI, E);
+        for (int i = 0; i < E; i++) ot[i] += sdn[i];
+        if (idx) memcpy(idx + (size_t)t * K, li, (size_t)K * sizeof(int));
+        if (wt) memcpy(wt + (size_t)t * K, lw, (size_t)K * sizeof(float));
+    }
+    free(li); free(lw); free(z); free(acc); free(gu); free(edn); free(sgu); free(sdn);
 }

@@ -31,6 +31,8 @@ typedef struct {
 } ora_expert;
 
 enum { ORA_ACT_SWIGLU = 0, ORA_ACT_SITU = 1 };
+/* Trunk weight types, the reference's K3_WF32 / K3_WBF16 / K3_WI8 (include/k3/k3.h:270). */
+enum { ORA_WF32 = 0, ORA_WBF16 = 1, ORA_WI8 = 2 };
 
 float ora_e2m1(unsigned code);
 float ora_e8m0(unsigned char b);
@@ -40,6 +42,8 @@ void ora_mxfp4_dequant(float *out, const unsigned char *packed, const unsigned c
 void ora_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
                       const unsigned char *scales, int in, int rows, int group);
 void ora_matmul_f32(float *y, const float *x, const float *W, int in, int out);
+void ora_matmul_bf16(float *y, const float *x, const uint16_t *W, int in, int out);
+void ora_mmw(float *y, const float *x, const void *W, int wdt, int in, int out);
 void ora_matmul_q8(float *y, const float *x, const void *W, int in, int out);
 void ora_router(int *idx, float *w, const float *x, const float *W, const float *bias,
                 int hidden, int n_experts, int topk, int renorm, float routed_scale);
@@ -63,6 +67,26 @@ void ora_moe_layer(float *out, const float *x, int ntok, const float *router_w,
                    const ora_expert *shared, int hidden, int inter, int n_experts,
                    int topk, int renorm, float routed_scale, int act,
                    int *idx, float *wt);
+
+/* A latent MoE layer of the K3 model (the K3MoeW fields of include/k3/k3.h:357-380 and
+ * the K3Cfg fields the layer reads, :94-113). Routed experts live at the latent width:
+ * either the fp32 bank w1/w3 [n_experts][inter][latent], w2 [n_experts][latent][inter]
+ * (the reference's fixtures), or, when w1 is NULL, experts[] in MXFP4. The trunk matrices
+ * down [latent][hidden], up [hidden][latent], sh1/sh3 [inter*n_shared][hidden],
+ * sh2 [hidden][inter*n_shared] have type wdt. */
+typedef struct {
+    const float *router_w, *router_bias;
+    const float *w1, *w3, *w2;
+    const ora_expert *experts;
+    const float *latent_norm;
+    const void *down, *up, *sh1, *sh3, *sh2;
+    int wdt;
+    int hidden, latent, inter, n_shared, n_experts, topk, renorm, latent_norm_on;
+    float routed_scale, rms_eps, situ_b1, situ_b2;
+} ora_latent;
+
+void ora_moe_latent(float *out, const float *x, int ntok, const ora_latent *L, int *idx,
+                    float *wt);
 
 #ifdef __cplusplus
 }

@@ -26,6 +26,7 @@ REF_SO = os.path.join(HERE, "_ref", "libk3ref.so")
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 
 
 class Expert6(C.Structure):
@@ -33,6 +34,17 @@ class Expert6(C.Structure):
     (include/k3/k3.h:323-327 of the reference)."""
 
     _fields_ = [(n, C.c_void_p) for n in ("p1", "s1", "p3", "s3", "p2", "s2")]
+
+
+class OraLatent(C.Structure):
+    """ora_latent (oracle/k3_oracle.h): one K3 latent MoE layer."""
+
+    _fields_ = ([(n, C.c_void_p) for n in ("router_w", "router_bias", "w1", "w3", "w2",
+                                           "experts", "latent_norm", "down", "up", "sh1",
+                                           "sh3", "sh2")]
+                + [(n, C.c_int) for n in ("wdt", "hidden", "latent", "inter", "n_shared",
+                                          "n_experts", "topk", "renorm", "latent_norm_on")]
+                + [(n, C.c_float) for n in ("routed_scale", "rms_eps", "situ_b1", "situ_b2")])
 
 
 def expert6(e: dict) -> Expert6:
@@ -59,6 +71,8 @@ def lib():
         L.ora_mxfp4_dequant.argtypes = [_f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
         L.ora_matmul_mxfp4.argtypes = [_f32p, _f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
         L.ora_matmul_f32.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
+        L.ora_matmul_bf16.argtypes = [_f32p, _f32p, _u16p, C.c_int, C.c_int]
+        L.ora_moe_latent.argtypes = [_f32p, _f32p, C.c_int, C.POINTER(OraLatent), _i32p, _f32p]
         L.ora_matmul_q8.argtypes = [_f32p, _f32p, _u8p, C.c_int, C.c_int]
         L.ora_router.argtypes = [_i32p, _f32p, _f32p, _f32p, C.c_void_p, C.c_int, C.c_int,
                                  C.c_int, C.c_int, C.c_float]
@@ -95,6 +109,10 @@ def ref():
         L.k3_matmul_mxfp4.argtypes = [_f32p, _f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
         L.k3_matmul_q8.argtypes = [_f32p, _f32p, _u8p, C.c_int, C.c_int]
         L.k3_matmul.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
+        L.k3_matmul_bf16.argtypes = [_f32p, _f32p, _u16p, C.c_int, C.c_int]
+        L.refh_moe_latent.argtypes = ([_f32p, _f32p, C.c_int] + [C.c_void_p] * 12
+                                      + [C.c_int] * 7 + [C.c_int, C.c_float, C.c_int]
+                                      + [C.c_float] * 3 + [_i32p, _f32p])
         L.k3_router.argtypes = [_i32p, _f32p, _f32p, _f32p, C.c_void_p, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.c_float]
         L.refh_expert_ffn.argtypes = [_f32p, _f32p, C.c_int, C.POINTER(Expert6), C.c_int,
@@ -204,4 +222,76 @@ def moe_layer(x, router_w, router_bias, experts: list, shared, hidden, inter, to
         assert ref().refh_moe_layer(*args) == 0
     else:
         lib().ora_moe_layer(*args)
+    return out, idx, wt
+
+
+def matmul_f32(x, W, use_ref=False):
+    """y = W x with fp32 W [out][in] in the reference's k3_matmul order."""
+    out_, in_ = W.shape
+    y = np.empty(out_, np.float32)
+    fn = ref().k3_matmul if use_ref else lib().ora_matmul_f32
+    fn(y, np.ascontiguousarray(x, np.float32), np.ascontiguousarray(W, np.float32), in_, out_)
+    return y
+
+
+def matmul_bf16(x, W, use_ref=False):
+    """y = W x with bf16 W (uint16 bit patterns [out][in]) in the reference's order."""
+    out_, in_ = W.shape
+    y = np.empty(out_, np.float32)
+    fn = ref().k3_matmul_bf16 if use_ref else lib().ora_matmul_bf16
+    fn(y, np.ascontiguousarray(x, np.float32), np.ascontiguousarray(W, np.uint16), in_, out_)
+    return y
+
+
+_LATENT_INTS = ("wdt", "hidden", "latent", "inter", "n_shared", "n_experts", "topk", "renorm",
+                "latent_norm_on")
+_LATENT_FLOATS = ("routed_scale", "rms_eps", "situ_b1", "situ_b2")
+
+
+def moe_latent(x, layer: dict, use_ref=False):
+    """The K3 latent MoE layer on x [T][hidden]. layer holds numpy arrays (router_w,
+    router_bias or None, latent_norm, down, up, sh1, sh3, sh2 -- fp32 or uint16 bf16 per
+    layer["wdt"] -- and either the fp32 bank w1/w3/w2 or a list ``experts`` of MXFP4 expert
+    dicts at the latent width) plus the integer and float fields of ora_latent. Returns
+    (out, idx, wt). use_ref runs the reference's own k3_moe."""
+    H, K = layer["hidden"], layer["topk"]
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, H)
+    T = x.shape[0]
+    keep = []
+
+    def ptr(name, dtype=None):
+        a = layer.get(name)
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, dtype) if dtype is not None else np.ascontiguousarray(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    wdtype = np.uint16 if layer["wdt"] == 1 else (np.uint8 if layer["wdt"] == 2 else np.float32)
+    experts = layer.get("experts")
+    arr = None
+    if experts is not None:
+        arr = (Expert6 * len(experts))(*[expert6(e) for e in experts])
+    out = np.empty_like(x)
+    idx = np.empty((T, K), np.int32)
+    wt = np.empty((T, K), np.float32)
+    ptrs = dict(router_w=ptr("router_w", np.float32), router_bias=ptr("router_bias", np.float32),
+                w1=ptr("w1", np.float32), w3=ptr("w3", np.float32), w2=ptr("w2", np.float32),
+                experts=None if arr is None else C.addressof(arr),
+                latent_norm=ptr("latent_norm", np.float32),
+                down=ptr("down", wdtype), up=ptr("up", wdtype), sh1=ptr("sh1", wdtype),
+                sh3=ptr("sh3", wdtype), sh2=ptr("sh2", wdtype))
+    if use_ref:
+        rc = ref().refh_moe_latent(
+            out, x, T, ptrs["router_w"], ptrs["router_bias"], ptrs["experts"], ptrs["w1"],
+            ptrs["w3"], ptrs["w2"], ptrs["latent_norm"], ptrs["down"], ptrs["up"],
+            ptrs["sh1"], ptrs["sh3"], ptrs["sh2"], layer["wdt"], H, layer["latent"],
+            layer["inter"], layer["n_shared"], layer["n_experts"], K, layer["renorm"],
+            layer["routed_scale"], layer["latent_norm_on"], layer["rms_eps"],
+            layer["situ_b1"], layer["situ_b2"], idx, wt)
+        assert rc == 0
+    else:
+        c = OraLatent(**ptrs, **{k: int(layer[k]) for k in _LATENT_INTS},
+                      **{k: float(layer[k]) for k in _LATENT_FLOATS})
+        lib().ora_moe_latent(out, x, T, C.byref(c), idx, wt)
     return out, idx, wt

@@ -9,7 +9,9 @@
  *   - SwiGLU, which the reference does not have (the BASELINE configs use it), written as
  *     (g*sigmoid(g))*u with the reference's sigmoid (src/core/k3_ops.c:105);
  *   - the non-latent layer composition of the BASELINE configs, i.e. k3_moe
- *     (src/core/k3_ops.c:556-656) without the latent down/up/norm steps.
+ *     (src/core/k3_ops.c:556-656) without the latent down/up/norm steps;
+ *   - for the latent layer, only the K3Cfg/K3MoeW set-up and an in-memory expert source
+ *     around the reference's own k3_moe.
  *
  * bench.py times refh_moe_layer as the reference arm (cpu_baseline kind "reference").
  */
@@ -86,6 +88,74 @@ int refh_moe_layer(float *out, const float *x, int ntok, const float *router_w,
         if (wt_out) memcpy(wt_out + (size_t)t * topk, wt, (size_t)topk * sizeof(float));
     }
     free(idx); free(wt); free(edn); free(s);
+    return 0;
+}
+
+/* An in-memory expert source for k3_moe: get() hands out experts[expert] (MXFP4). */
+static int refh_src_get(struct K3ExpertSrc *self, int layer, int expert, K3ExpertQ *out)
+{
+    (void)layer;
+    *out = ((const K3ExpertQ *)self->ctx)[expert];
+    return 0;
+}
+
+/* The K3 latent MoE layer run by the reference's OWN k3_moe (src/core/k3_ops.c:556-656):
+ * this function only fills a K3Cfg and a K3MoeW (zeroed first, as include/k3/k3.h:305-313
+ * requires) and, for MXFP4 experts, an in-memory K3ExpertSrc. experts != NULL streams
+ * MXFP4 experts through the source; otherwise the fp32 bank w1/w3/w2 is used. k3_moe runs
+ * one token per call so that each token's routing can be returned. */
+int refh_moe_latent(float *out, const float *x, int ntok, const float *router_w,
+                    const float *router_bias, const K3ExpertQ *experts, const float *w1,
+                    const float *w3, const float *w2, const float *latent_norm,
+                    const void *down, const void *up, const void *sh1, const void *sh3,
+                    const void *sh2, int wdt, int hidden, int latent, int inter, int n_shared,
+                    int n_experts, int topk, int renorm, float routed_scale,
+                    int latent_norm_on, float rms_eps, float situ_b1, float situ_b2,
+                    int *idx_out, float *wt_out)
+{
+    K3Cfg c;
+    memset(&c, 0, sizeof(c));
+    c.hidden = hidden;
+    c.rms_eps = rms_eps;
+    c.n_experts = n_experts;
+    c.topk = topk;
+    c.n_shared = n_shared;
+    c.latent = latent;
+    c.moe_inter = inter;
+    c.routed_scale = routed_scale;
+    c.moe_renorm = renorm;
+    c.latent_norm = latent_norm_on;
+    c.situ_b1 = situ_b1;
+    c.situ_b2 = situ_b2;
+    K3ExpertSrc src;
+    memset(&src, 0, sizeof(src));
+    src.get = refh_src_get;
+    src.ctx = (void *)experts;
+    K3MoeW w;
+    memset(&w, 0, sizeof(w));
+    w.gate = router_w;
+    w.bias = router_bias;
+    w.w1 = w1;
+    w.w3 = w3;
+    w.w2 = w2;
+    w.latent_norm = latent_norm;
+    w.down = down;
+    w.up = up;
+    w.sh1 = sh1;
+    w.sh3 = sh3;
+    w.sh2 = sh2;
+    w.wdt = wdt;
+    w.src = experts ? &src : NULL;
+    int *idx = (int *)malloc((size_t)topk * sizeof(int));
+    float *wt = (float *)malloc((size_t)topk * sizeof(float));
+    float *scratch = (float *)malloc(k3_moe_scratch(&c) * sizeof(float));
+    if (!idx || !wt || !scratch) { free(idx); free(wt); free(scratch); return -1; }
+    for (int t = 0; t < ntok; t++) {
+        k3_moe(out + (size_t)t * hidden, x + (size_t)t * hidden, &w, &c, 1, idx, wt, scratch);
+        if (idx_out) memcpy(idx_out + (size_t)t * topk, idx, (size_t)topk * sizeof(int));
+        if (wt_out) memcpy(wt_out + (size_t)t * topk, wt, (size_t)topk * sizeof(float));
+    }
+    free(idx); free(wt); free(scratch);
     return 0;
 }
 

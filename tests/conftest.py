@@ -54,3 +54,20 @@ def maxrel(got, want):
     want = np.asarray(want, np.float64)
     den = np.abs(want).max()
     return float(np.abs(got - want).max() / den) if den > 0 else float(np.abs(got).max())
+
+
+@pytest.fixture(scope="session")
+def golden_gen():
+    """tests/golden/make_golden.py as a module: the seeded cases its fixtures were made from
+    (it reads the reference tree only when run as a script)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(GOLDEN, "make_golden.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def latent_layer_from_npz(f):
+    """A latent layer dict (oracle.moe_latent form) from moe_latent_fixture.npz."""
+    skip = ("x", "want", "ref_out", "ref_idx", "ref_wt")
+    return {k: (f[k] if f[k].ndim else f[k].item()) for k in f.files if k not in skip}

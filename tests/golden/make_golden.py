@@ -17,6 +17,15 @@ Writes:
   ref_router_full.npz the reference's k3_router at the BASELINE shape (384 x 7168, top-8)
                    on 16 seeded bf16 tokens; inputs are regenerated from the seed, a
                    checksum of them is stored to catch generator drift.
+  moe_latent_fixture.npz from tests/fixtures/ops/moe.json: the K3 latent MoE layer
+                   (hidden 128, latent 64, inter 48, 8 experts, top-2, 2 shared, fp32 expert
+                   bank and trunk) with its published output, plus the reference's own
+                   k3_moe output on the same inputs.
+  ref_latent.npz   the reference's own k3_moe on a seeded latent layer with MXFP4 experts
+                   (through an in-memory expert source) and a bf16 trunk (hidden 256,
+                   latent 128, inter 128, 8 experts, top-2, 2 shared), 3 tokens; the layer
+                   is regenerated from the seed by synth.latent_layer and a checksum of its
+                   bytes is stored to catch generator drift.
 """
 from __future__ import annotations
 
@@ -148,12 +157,73 @@ def ref_router_full():
                         seed=np.int32(51), input_checksum=chk)
 
 
+def fixture_moe_latent(ref_root):
+    r = json.load(open(os.path.join(ref_root, "tests/fixtures/ops/moe.json")))
+    H, Lw, I, E = r["hidden"], r["latent"], r["moe_inter"], r["n_experts"]
+    f = lambda k: _arr(r[k]).astype(np.float32)   # noqa: E731
+    layer = dict(router_w=f("gate_weight").reshape(E, H),
+                 router_bias=f("e_score_correction_bias"),
+                 w1=np.stack([f(f"experts_{e}_w1_weight").reshape(I, Lw) for e in range(E)]),
+                 w3=np.stack([f(f"experts_{e}_w3_weight").reshape(I, Lw) for e in range(E)]),
+                 w2=np.stack([f(f"experts_{e}_w2_weight").reshape(Lw, I) for e in range(E)]),
+                 latent_norm=f("norm_weight"), down=f("down_weight").reshape(Lw, H),
+                 up=f("up_weight").reshape(H, Lw),
+                 sh1=f("shared_w1_weight").reshape(-1, H), sh3=f("shared_w3_weight").reshape(-1, H),
+                 sh2=f("shared_w2_weight").reshape(H, -1), wdt=0, hidden=H, latent=Lw, inter=I,
+                 n_shared=r["n_shared"], n_experts=E, topk=r["top_k"], renorm=int(r["renorm"]),
+                 latent_norm_on=int(r["latent_norm"]), routed_scale=float(r["routed_scale"]),
+                 rms_eps=float(r["rms_eps"]), situ_b1=float(r["situ_b1"]),
+                 situ_b2=float(r["situ_b2"]))
+    x = f("in").reshape(-1, H)
+    want = f("out").reshape(-1, H)
+    ref_out, ref_idx, ref_wt = ora.moe_latent(x, layer, use_ref=True)
+    arrays = {k: v for k, v in layer.items() if isinstance(v, np.ndarray)}
+    scalars = {k: np.asarray(v) for k, v in layer.items() if not isinstance(v, np.ndarray)}
+    np.savez_compressed(os.path.join(HERE, "moe_latent_fixture.npz"), x=x, want=want,
+                        ref_out=ref_out, ref_idx=ref_idx, ref_wt=ref_wt, **arrays, **scalars)
+
+
+LATENT_CASE = dict(seed=61, hidden=256, latent=128, inter=128, n_experts=8, topk=2, n_shared=2,
+                   ntok=3)
+
+
+def latent_case():
+    """The seeded latent layer and tokens of ref_latent.npz (shared with the tests)."""
+    c = LATENT_CASE
+    g = synth.rng(c["seed"])
+    layer = synth.latent_layer(g, c["hidden"], c["latent"], c["inter"], c["n_experts"],
+                               c["topk"], c["n_shared"], wdt=1)
+    x, _ = synth.activations(g, c["ntok"], c["hidden"], bf16=False)
+    return layer, x
+
+
+def layer_checksum(layer):
+    h = np.uint64(1469598103934665603)
+    parts = [layer[k] for k in ("router_w", "router_bias", "latent_norm", "down", "up", "sh1",
+                                "sh3", "sh2")]
+    parts += [e[k] for e in layer["experts"] for k in sorted(e)]
+    total = 0
+    for a in parts:
+        total = (total * 1000003 + int(np.frombuffer(np.ascontiguousarray(a).tobytes(),
+                                                     np.uint8).astype(np.uint64).sum())) % (1 << 61)
+    return np.int64(total + int(h % 7))
+
+
+def ref_latent():
+    layer, x = latent_case()
+    out, idx, wt = ora.moe_latent(x, layer, use_ref=True)
+    np.savez_compressed(os.path.join(HERE, "ref_latent.npz"), x=x, out=out, idx=idx, wt=wt,
+                        checksum=layer_checksum(layer))
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     fixture_mxfp4(ref_root)
     fixture_router(ref_root)
     ref_kernels()
     ref_router_full()
+    fixture_moe_latent(ref_root)
+    ref_latent()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f"{f}: {os.path.getsize(os.path.join(HERE, f))} bytes")
