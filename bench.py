@@ -14,6 +14,7 @@ touches ~110 different experts (~2.6 GB): inputs larger than L2.
   python bench.py --workload streamed [--steps K] [--warmup W]  (config[4], one line)
   torchrun ... bench.py --workload ep --gpus N                   (config[3], one line)
   python bench.py --workload expert [--steps K] [--warmup W]    (config[0], one line)
+  python bench.py --workload latent [--steps K] [--warmup W]    (K3 latent MoE layer, one line)
 
 N > 1 (torchrun) runs N independent replicas (decode does not shard; scaling "weak").
 --impl reference times the reference's own CPU kernels (oracle/_ref, built from its
@@ -825,6 +826,175 @@ def run_expert(args, ws, rank, local):
     }))
 
 
+# ------------------------------------------------------------------ K3 latent MoE layer
+LH, LL, LI, LE, LK, LS = 7168, 3584, 3072, 896, 16, 2
+LAT_WORKLOAD = ("K3 latent MoE layer decode: B=16 fp32 tokens, full-width fp32 sigmoid top-16 router over "
+                "896 HBM-resident MXFP4 experts at the latent width (3584->3072->3584, SiTU), bf16 trunk "
+                "down 7168->3584 / up 3584->7168, aggregate RMSNorm, full-width shared expert "
+                "(7168->6144->7168, bf16), the K3 model's shapes")
+
+
+def host_latent_workload(seed, ndistinct=8):
+    """Host copy of the latent workload for the CPU runs: ndistinct random experts tiled over
+    the 896 ids, bf16 trunk, fp32 router."""
+    import __graft_entry__ as ge
+    synth = ge.load_package().synth
+    g = synth.rng(seed)
+    distinct = [synth.expert(g, LL, LI) for _ in range(ndistinct)]
+    SI = LI * LS
+
+    def trunk(o, i):
+        return synth.bf16_bits(g.standard_normal((o, i), dtype=np.float32) * np.float32(1 / np.sqrt(i)))
+
+    layer = dict(router_w=synth.bf16_to_f32(synth.bf16_bits(
+                     g.standard_normal((LE, LH), dtype=np.float32) * np.float32(0.02))),
+                 router_bias=None, experts=[distinct[i % ndistinct] for i in range(LE)],
+                 latent_norm=np.ones(LL, np.float32), down=trunk(LL, LH), up=trunk(LH, LL),
+                 sh1=trunk(SI, LH), sh3=trunk(SI, LH), sh2=trunk(LH, SI), wdt=1, hidden=LH, latent=LL,
+                 inter=LI, n_shared=LS, n_experts=LE, topk=LK, renorm=1, latent_norm_on=1,
+                 routed_scale=1.0, rms_eps=1e-5, situ_b1=4.0, situ_b2=25.0)
+    xs = [g.standard_normal((16, LH), dtype=np.float32) for _ in range(2)]
+    return layer, xs
+
+
+def cpu_latent_tokens_per_s(budget_s, steps=None, warmup=0, seed=8):
+    """The reference's own k3_moe (oracle/_ref) on the latent workload, one token at a time as
+    it runs; returns (tokens/s, threads, tokens run, seconds)."""
+    from oracle import oracle as ora
+    layer, xs = host_latent_workload(seed)
+    for w in range(warmup):
+        ora.moe_latent(xs[0][w % 16:w % 16 + 1], layer, use_ref=True)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        ora.moe_latent(xs[(n // 16) % 2][n % 16:n % 16 + 1], layer, use_ref=True)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= budget_s):
+            break
+    return n / el, ora.ref().refh_threads(), n, el
+
+
+def run_latent(args, ws, rank, local):
+    """One step = 16 fp32 tokens through k3c_moe_latent_decode (router, trunk down, routed
+    experts at the latent width on the tensor-core path, aggregate RMSNorm, trunk up, shared
+    expert), rotating over 32 token batches: each step reads ~230 distinct experts (~4 GB)."""
+    import ctypes as C
+    import torch
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5151 + rank)
+    lay, run = k3.pool_layout(LL, LI)
+    arena = torch.empty(LE * run, dtype=torch.uint8, device=dev)
+    a2 = arena.view(LE, run)
+    for name, (off, nb) in lay.items():
+        seg = a2[:, off:off + nb]
+        if name.endswith("_p"):
+            seg.copy_(torch.randint(0, 256, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+        else:
+            seg.copy_(torch.randint(118, 125, seg.shape, generator=g, device=dev, dtype=torch.uint8))
+    SI = LI * LS
+
+    def trunk(o, i):
+        return (torch.randn((o, i), generator=g, device=dev) / float(np.sqrt(i))).to(torch.bfloat16)
+
+    router = (torch.randn((LE, LH), generator=g, device=dev) * 0.02).to(torch.bfloat16).float()
+    down, up, sh1, sh3, sh2 = trunk(LL, LH), trunk(LH, LL), trunk(SI, LH), trunk(SI, LH), trunk(LH, SI)
+    norm = torch.ones(LL, dtype=torch.float32, device=dev)
+    run_of = torch.arange(LE, dtype=torch.int32, device=dev)
+    lat = k3.LatentMoeLayer(arena, LE, run_of, router, None, down, up, sh1, sh3, sh2, norm, k3.WBF16,
+                            LH, LL, LI, LS, LK, terms=args.terms)
+    B, NB = 16, 32
+    xs = [torch.randn((B, LH), generator=g, device=dev) for _ in range(NB)]
+    out = torch.empty((B, LH), dtype=torch.float32, device=dev)
+    idx_log = [torch.empty((B, LK), dtype=torch.int32, device=dev) for _ in range(args.steps)]
+    wt = torch.empty((B, LK), dtype=torch.float32, device=dev)
+    for i in range(args.warmup):
+        lat.decode(xs[i % NB], out=out, idx=idx_log[0], wt=wt)
+    torch.cuda.synchronize()
+    clk = Clocks(local)
+    L.k3c_timing_enable(1)
+    ms_buf, n_buf = (C.c_double * 4)(), (C.c_longlong * 4)()
+    L.k3c_timing_read(ms_buf, n_buf, 4)
+    l0 = L.k3c_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        lat.decode(xs[(args.warmup + i) % NB], out=out, idx=idx_log[i], wt=wt)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = L.k3c_launch_count() - l0
+    L.k3c_timing_enable(0)
+    L.k3c_timing_read(ms_buf, n_buf, 4)
+    clocks = clk.stop()
+    dt = e0.elapsed_time(e1) / 1e3
+    # end to end: pinned host tokens in, outputs back, every step (copies on their own streams)
+    hx = [x.cpu().pin_memory() for x in xs]
+    pipe = CopyPipe(lambda i: [hx[i % NB]],
+                    [[torch.empty((B, LH), dtype=torch.float32, device=dev)] for _ in range(2)],
+                    [[torch.empty((B, LH), dtype=torch.float32, device=dev)] for _ in range(2)],
+                    [[torch.empty((B, LH), dtype=torch.float32).pin_memory()] for _ in range(2)])
+
+    def e2e_compute(i, din, dout):
+        lat.decode(din[0], out=dout[0], idx=idx_log[0], wt=wt)
+
+    for i in range(3):
+        pipe.step(i, e2e_compute)
+    pipe.finish()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(args.steps):
+        pipe.step(args.warmup + i, e2e_compute)
+    pipe.finish()
+    f1.record()
+    torch.cuda.synchronize()
+    dte = f0.elapsed_time(f1) / 1e3
+    if rank != 0:
+        return
+    uniq = [int(torch.unique(t).numel()) for t in idx_log]
+    run_bytes = k3.expert_run_layout(LL, LI)[1]
+    expert_bytes = sum(u * run_bytes for u in uniq)
+    trunk_bytes = 2 * (2 * LL * LH + 3 * SI * LH)
+    hbm, _, kind = peaks()
+    exp_ms, trunk_ms = ms_buf[0], ms_buf[3]
+    achieved = expert_bytes / (exp_ms / 1e3) / 1e9 if exp_ms > 0 else None
+    cpu = None
+    if not args.no_cpu:
+        from oracle import oracle as ora
+        if ora.ref_available():
+            tps, threads, n, el = cpu_latent_tokens_per_s(args.cpu_seconds)
+            cpu = {"value": tps, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": f"{n} tokens through the reference's k3_moe ({el:.1f} s), 8 distinct experts tiled over 896 ids"}
+    print(json.dumps({
+        "metric": "K3 latent MoE-layer tokens/s", "value": B * args.steps / dt, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": (f"experts mxfp4 x e4m3 ({args.terms} terms, tcgen05 kind::mxf8f6f4); trunk bf16 weights x fp32 "
+                  "activations, fp64 accumulate in the reference's order (bit-exact)"),
+        "data": "synthetic",
+        "config": {"workload": LAT_WORKLOAD, "batch": B, "hidden": LH, "latent": LL, "inter": LI, "experts": LE,
+                   "topk": LK, "n_shared": LS, "l2": "inputs larger than L2: ~230 distinct experts (~4 GB) per step"},
+        "unique_experts_per_step": float(np.mean(uniq)),
+        "stages_ms_per_step": {"experts": exp_ms / args.steps, "router": ms_buf[1] / args.steps,
+                               "trunk": trunk_ms / args.steps},
+        "trunk_gbs": trunk_bytes * args.steps / (trunk_ms / 1e3) / 1e9 if trunk_ms > 0 else None,
+        "layer_hbm_gbs": (expert_bytes + args.steps * (trunk_bytes + LE * LH * 4)) / dt / 1e9,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm if achieved else None,
+                     "kernel": "expert stage (tcgen05 gate/up+SiTU and down kernels at the latent width)",
+                     "algorithmic_bytes_per_step": expert_bytes / args.steps, "peak_kind": kind},
+        "cpu_baseline": cpu,
+        "e2e": {"value": B * args.steps / dte, "unit": UNIT, "h2d_bytes_per_step": B * LH * 4,
+                "d2h_bytes_per_step": B * LH * 4},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }))
+
+
 # ------------------------------------------------------------------ expert parallel (config[3])
 EP_T = 16384
 EP_WORKLOAD = "config[3] expert-parallel MoE prefill: 16384 bf16 tokens sharded over the GPUs, 384 " \
@@ -984,7 +1154,8 @@ def main():
                          "contiguous id ranges")
     ap.add_argument("--ep-impl", default="fused", choices=["fused", "a2a"],
                     help="ep workload: fused peer-memory exchange in the expert kernels, or NCCL all-to-all")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "streamed", "ep", "expert"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "streamed", "ep", "expert", "latent"],
                     help="decode: config[1] (the headline line); prefill: config[2]; streamed: config[4]; "
                          "ep: config[3] (expert-parallel prefill; torchrun for N > 1)")
     args = ap.parse_args()
@@ -997,6 +1168,8 @@ def main():
         run_ep(args, ws, rank, local)
     elif args.workload == "expert" and args.impl != "reference":
         run_expert(args, ws, rank, local)
+    elif args.workload == "latent" and args.impl != "reference":
+        run_latent(args, ws, rank, local)
     elif args.impl == "reference":
         run_reference(args, ws, rank)
     else:

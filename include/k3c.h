@@ -80,6 +80,8 @@ int k3c_timing_read(double *ms, long long *count, int nstage);
 enum { K3C_F32 = 0, K3C_BF16 = 1 };
 /* Expert activation functions. */
 enum { K3C_ACT_SWIGLU = 0, K3C_ACT_SITU = 1 };
+/* Trunk weight types, the reference's K3_WF32 / K3_WBF16 (include/k3/k3.h:270). */
+enum { K3C_WF32 = 0, K3C_WBF16 = 1 };
 
 /* ====================================================================================
  * 1. DROP-IN ENTRY POINTS (host pointers)
@@ -98,6 +100,13 @@ void k3_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
 
 /* include/k3/k3.h:285. W is `out` rows of [f32 scale][int8 * in] (row stride 4+in). */
 void k3_matmul_q8(float *y, const float *x, const void *W, int in, int out);
+
+/* src/core/k3_ops.c:265 and include/k3/k3.h:281. y[out] = W[out][in] . x[in], fp32 or bf16
+ * weights, bit-exact with the reference: its fixed order (16 double accumulators over
+ * i%16 by fused multiply-adds, a fixed combining tree, the in%16 tail fused in order, one
+ * rounding to float). */
+void k3_matmul(float *y, const float *x, const float *W, int in, int out);
+void k3_matmul_bf16(float *y, const float *x, const uint16_t *W, int in, int out);
 
 /* include/k3/k3.h:241-243. Sigmoid scores, selection on score+bias, weights from the
  * unbiased score, optional renorm, times routed_scale; idx/w in descending order. */
@@ -243,6 +252,54 @@ int k3c_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok,
 int k3c_moe_decode_tc_routed(float *out, const void *x, int x_dtype, int ntok,
                              const k3c_moe_pool_layer *L, const int *idx, const float *wt,
                              int *drops, void *scratch, size_t scratch_bytes, k3c_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * The K3 latent MoE layer (src/core/k3_ops.c:556-656) and its trunk operations.
+ * ------------------------------------------------------------------------------------ */
+
+/* Device form of k3_mmw (include/k3/k3.h:289-296) for ntok <= 32 tokens:
+ * y[t*ldy + o] = sum_i W[o][i] x[t*ldx + i] (accumulate != 0: y += that, one float add),
+ * W [out][in] of type wdt (K3C_WF32 or K3C_WBF16), fp32 x. Bit-exact with k3_matmul /
+ * k3_matmul_bf16 token by token. Int8 trunk rows run through k3c_q8_pack / k3c_q8_gemv. */
+int k3c_mmw(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int wdt,
+            int in, int out, int accumulate, k3c_stream_t stream);
+/* k3_situ_glu (src/core/k3_ops.c:110-122) on ntok rows: gu [ntok][2n] (gate | up),
+ * y [ntok][n]. */
+int k3c_situ_glu(float *y, const float *gu, int n, int ntok, float b1, float b2,
+                 k3c_stream_t stream);
+/* k3_rmsnorm (src/core/k3_ops.c:94-102) on ntok rows of n: y may alias x. */
+int k3c_rmsnorm(float *y, const float *x, const float *w, int n, int ntok, float eps,
+                k3c_stream_t stream);
+
+/* One latent MoE layer (the K3MoeW / K3Cfg fields of include/k3/k3.h:94-113, 357-380).
+ * Routing runs on the full-width input with router_w; the routed experts are pool-format
+ * runs at the latent width, described by `experts` (experts.hidden = latent,
+ * experts.inter = moe_inter; its n_experts, topk, renorm, routed_scale, act and terms apply;
+ * its router fields are not used; shared_run must be -1). The trunk matrices have type
+ * wdt: down [latent][hidden], up [hidden][latent], sh1/sh3 [inter*n_shared][hidden],
+ * sh2 [hidden][inter*n_shared]. All pointers are device addresses. */
+typedef struct {
+    int hidden;
+    k3c_moe_pool_layer experts;
+    const float *router_w;        /* [experts.n_experts][hidden] fp32 */
+    const float *router_bias;     /* [experts.n_experts] or NULL */
+    const void *down, *up;
+    const void *sh1, *sh3, *sh2;
+    const float *latent_norm;     /* [latent] (used when latent_norm_on) */
+    int wdt, n_shared, latent_norm_on;
+    float rms_eps, situ_b1, situ_b2;
+} k3c_moe_latent_layer;
+
+/* k3_moe (src/core/k3_ops.c:556-656) for ntok <= 32 tokens: out [ntok][hidden] fp32 from x
+ * [ntok][hidden] fp32. Per token: route on x; z = down x; the top-k experts on z at the
+ * latent width, summed with their weights in top-k order (tensor-core decode kernels, the
+ * activation as experts.terms E4M3 terms); RMSNorm of the sum; out = up sum; plus the
+ * shared expert sh2(SiTU(sh1 x, sh3 x)) unweighted. idx/wt (device, may be NULL) receive
+ * the routing [ntok][topk]; drops counts selected experts without a resident run. */
+size_t k3c_moe_latent_scratch(const k3c_moe_latent_layer *L, int ntok);
+int k3c_moe_latent_decode(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L,
+                          int *idx, float *wt, int *drops, void *scratch, size_t scratch_bytes,
+                          k3c_stream_t stream);
 
 /* MoE prefill over ntok tokens: the reference's k3_moe_prefill / moe_prefill_chunk
  * (src/core/k3_ops.c:689-808) for the non-latent shape -- route, group the (token, expert)

@@ -50,6 +50,16 @@ class MoePoolLayerC(C.Structure):
                 ("run_of", C.c_void_p), ("shared_run", C.c_int), ("terms", C.c_int)]
 
 
+class MoeLatentLayerC(C.Structure):
+    """Mirror of k3c_moe_latent_layer (include/k3c.h)."""
+
+    _fields_ = ([("hidden", C.c_int), ("experts", MoePoolLayerC)]
+                + [(n, C.c_void_p) for n in ("router_w", "router_bias", "down", "up", "sh1", "sh3",
+                                             "sh2", "latent_norm")]
+                + [(n, C.c_int) for n in ("wdt", "n_shared", "latent_norm_on")]
+                + [(n, C.c_float) for n in ("rms_eps", "situ_b1", "situ_b2")])
+
+
 EP_MAX = 8
 
 
@@ -143,6 +153,13 @@ def lib():
         "k3_matmul_mxfp4": ([vp, vp, vp, vp, i, i, i], None),
         "k3_matmul_q8": ([vp, vp, vp, i, i], None),
         "k3_router": ([vp, vp, vp, vp, vp, i, i, i, i, f], None),
+        "k3_matmul": ([vp, vp, vp, i, i], None),
+        "k3_matmul_bf16": ([vp, vp, vp, i, i], None),
+        "k3c_mmw": ([vp, i, vp, i, i, vp, i, i, i, i, vp], i),
+        "k3c_situ_glu": ([vp, vp, i, i, f, f, vp], i),
+        "k3c_rmsnorm": ([vp, vp, vp, i, i, f, vp], i),
+        "k3c_moe_latent_scratch": ([C.POINTER(MoeLatentLayerC), i], sz),
+        "k3c_moe_latent_decode": ([vp, vp, i, C.POINTER(MoeLatentLayerC), vp, vp, vp, vp, sz, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -671,3 +688,115 @@ class _PoolArena:
 
     def data_ptr(self):
         return self.pool.arena_ptr
+
+
+# ------------------------------------------------------------------ K3 latent MoE layer
+WF32, WBF16 = 0, 1
+
+
+def mmw(x, W, wdt, out=None, accumulate=False):
+    """k3c_mmw: y[t] = W x[t] for x [ntok][in] fp32 (ntok <= 32) and W [out][in] fp32
+    (wdt=WF32) or bf16 bit patterns (WBF16, a torch int16/uint16/bfloat16 tensor), in the
+    reference's k3_matmul summation order (bit-exact). accumulate adds into `out`."""
+    import torch
+    x = x.contiguous()
+    ntok, in_ = x.shape
+    out_ = W.shape[0]
+    if out is None:
+        out = torch.zeros((ntok, out_), dtype=torch.float32, device=x.device)
+    _check(lib().k3c_mmw(_ptr(out), out.stride(0), _ptr(x), in_, ntok, _ptr(W), wdt, in_, out_,
+                         1 if accumulate else 0, _stream()), "k3c_mmw")
+    return out
+
+
+def rmsnorm(x, w, eps=1e-5, out=None):
+    """k3c_rmsnorm over the rows of x [ntok][n] fp32."""
+    import torch
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    _check(lib().k3c_rmsnorm(_ptr(out), _ptr(x), _ptr(w), x.shape[1], x.shape[0], eps, _stream()),
+           "k3c_rmsnorm")
+    return out
+
+
+def situ_glu(gu, b1=4.0, b2=25.0):
+    """k3c_situ_glu: gu [ntok][2n] (gate | up) -> [ntok][n]."""
+    import torch
+    gu = gu.contiguous()
+    n = gu.shape[1] // 2
+    out = torch.empty((gu.shape[0], n), dtype=torch.float32, device=gu.device)
+    _check(lib().k3c_situ_glu(_ptr(out), _ptr(gu), n, gu.shape[0], b1, b2, _stream()), "k3c_situ_glu")
+    return out
+
+
+class LatentMoeLayer:
+    """The K3 latent MoE layer (k3c_moe_latent_decode): full-width routing, trunk down/up and
+    shared-expert matrices (fp32 or bf16), routed MXFP4 experts at the latent width in an HBM
+    arena of pool-format runs on the tensor-core path."""
+
+    def __init__(self, arena, n_runs, run_of, router_w, router_bias, down, up, sh1, sh3, sh2,
+                 latent_norm, wdt, hidden, latent, inter, n_shared, topk, terms=3, renorm=1,
+                 routed_scale=1.0, latent_norm_on=1, rms_eps=1e-5, situ_b1=4.0, situ_b2=25.0):
+        import torch
+        self._keep = (arena, run_of, router_w, router_bias, down, up, sh1, sh3, sh2, latent_norm)
+        ex = MoePoolLayerC(latent, inter, run_of.numel(), topk, renorm, ACT_SITU, routed_scale,
+                           router_w.data_ptr(), K3C_F32, None, arena.data_ptr(),
+                           pool_run_bytes(latent, inter), n_runs, run_of.data_ptr(), -1, terms)
+        p = lambda t: None if t is None else t.data_ptr()   # noqa: E731
+        self.c = MoeLatentLayerC(hidden, ex, p(router_w), p(router_bias), p(down), p(up), p(sh1),
+                                 p(sh3), p(sh2), p(latent_norm), wdt, n_shared, latent_norm_on,
+                                 rms_eps, situ_b1, situ_b2)
+        self._scratch = torch.empty(0, dtype=torch.uint8, device=arena.device)
+
+    @classmethod
+    def from_host(cls, layer: dict, device, terms=3):
+        """Upload a layer given as host numpy arrays in the oracle's form (router_w,
+        router_bias, latent_norm, down, up, sh1, sh3, sh2 as fp32 or uint16 bf16 patterns
+        per layer["wdt"], and ``experts``: MXFP4 expert dicts at the latent width)."""
+        import torch
+        dev = torch.device(device)
+        t = lambda a, dt=None: None if a is None else torch.from_numpy(   # noqa: E731
+            np.ascontiguousarray(a if dt is None else a.astype(dt))).to(dev)
+        wdt = int(layer["wdt"])
+        conv = (lambda a: t(a.view(np.int16))) if wdt == WBF16 else (lambda a: t(a, np.float32))
+        Lw, I = int(layer["latent"]), int(layer["inter"])
+        run = pool_run_bytes(Lw, I)
+        experts = layer["experts"]
+        arena = torch.empty(len(experts) * run, dtype=torch.uint8, device=dev)
+        for i, e in enumerate(experts):
+            de = DeviceExpert.from_host(e, dev)
+            pool_pack(arena[i * run:(i + 1) * run], de.q(), Lw, I)
+        torch.cuda.current_stream(dev).synchronize()
+        run_of = torch.arange(len(experts), dtype=torch.int32, device=dev)
+        return cls(arena, len(experts), run_of, t(layer["router_w"], np.float32),
+                   t(layer.get("router_bias"), np.float32), conv(layer["down"]), conv(layer["up"]),
+                   conv(layer["sh1"]), conv(layer["sh3"]), conv(layer["sh2"]),
+                   t(layer["latent_norm"], np.float32), wdt, int(layer["hidden"]), Lw, I,
+                   int(layer["n_shared"]), int(layer["topk"]), terms=terms,
+                   renorm=int(layer["renorm"]), routed_scale=float(layer["routed_scale"]),
+                   latent_norm_on=int(layer["latent_norm_on"]), rms_eps=float(layer["rms_eps"]),
+                   situ_b1=float(layer["situ_b1"]), situ_b2=float(layer["situ_b2"]))
+
+    def scratch_bytes(self, ntok):
+        return lib().k3c_moe_latent_scratch(C.byref(self.c), ntok)
+
+    def decode(self, x, out=None, idx=None, wt=None, drops=None):
+        import torch
+        x = x.contiguous()
+        ntok = x.shape[0]
+        need = self.scratch_bytes(ntok)
+        if self._scratch.numel() < need:
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        K = self.c.experts.topk
+        if out is None:
+            out = torch.empty((ntok, self.c.hidden), dtype=torch.float32, device=x.device)
+        if idx is None:
+            idx = torch.empty((ntok, K), dtype=torch.int32, device=x.device)
+        if wt is None:
+            wt = torch.empty((ntok, K), dtype=torch.float32, device=x.device)
+        _check(lib().k3c_moe_latent_decode(_ptr(out), _ptr(x), ntok, C.byref(self.c), _ptr(idx),
+                                           _ptr(wt), _ptr(drops), _ptr(self._scratch),
+                                           self._scratch.numel(), _stream()),
+               "k3c_moe_latent_decode")
+        return out, idx, wt

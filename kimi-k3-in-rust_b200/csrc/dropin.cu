@@ -1,7 +1,8 @@
 // dropin.cu -- the reference's kernel entry points over host pointers.
 //
-// k3_mxfp4_dequant, k3_matmul_mxfp4, k3_matmul_q8 and k3_router keep the reference's
-// signatures (include/k3/k3.h:241-243, 285, 559-566) and contract: void return, output
+// k3_mxfp4_dequant, k3_matmul_mxfp4, k3_matmul_q8, k3_matmul, k3_matmul_bf16 and k3_router
+// keep the reference's signatures (include/k3/k3.h:241-243, 281-285, 559-566; k3_matmul is
+// declared at src/core/k3_ops.c:265) and contract: void return, output
 // fully written on return, and a precondition violation aborts with a FATAL message
 // rather than returning with the output unwritten (src/core/k3_ops.c:37-78, 1366-1384).
 // Each call stages its inputs into a per-device workspace, runs the device kernel on a
@@ -29,6 +30,8 @@ int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
                   const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
                   int ntok, double *part, cudaStream_t s);
 size_t router_scratch_bytes(int hidden, int n_experts, int ntok);
+int launch_mmw(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int wdt, int in, int out,
+               int accumulate, cudaStream_t s);
 
 [[noreturn]] static void fatal(const char *what, const char *detail) {
     fprintf(stderr, "k3c: FATAL, %s: %s\n    Aborting rather than returning with the output "
@@ -152,6 +155,35 @@ void k3_matmul_q8(float *y, const float *x, const void *W, int in, int out) {
                          (const float *)(b + o_sc), ldw, in, out, w.stream), what);
     cuda_ok(cudaMemcpyAsync(y, b + o_y, nb_y, cudaMemcpyDeviceToHost, w.stream), what);
     cuda_ok(cudaStreamSynchronize(w.stream), what);
+}
+
+static void trunk_matmul(float *y, const float *x, const void *W, int wdt, int in, int out, const char *what) {
+    if (out <= 0) return;
+    if (in <= 0) {   // an empty sum is zero
+        memset(y, 0, (size_t)out * sizeof(float));
+        return;
+    }
+    const size_t esz = wdt == K3C_WBF16 ? 2 : 4;
+    const size_t nb_w = (size_t)out * in * esz, nb_x = (size_t)in * sizeof(float);
+    const size_t nb_y = (size_t)out * sizeof(float);
+    Workspace &w = ws_for_current(what);
+    std::lock_guard<std::mutex> lk(w.mu);
+    const size_t o_w = 0, o_x = align_up(nb_w, 256), o_y = align_up(o_x + nb_x, 256);
+    char *b = ws_reserve(w, o_y + nb_y, what);
+    cuda_ok(cudaMemcpyAsync(b + o_w, W, nb_w, cudaMemcpyHostToDevice, w.stream), what);
+    cuda_ok(cudaMemcpyAsync(b + o_x, x, nb_x, cudaMemcpyHostToDevice, w.stream), what);
+    rc_ok(launch_mmw((float *)(b + o_y), out, (const float *)(b + o_x), in, 1, b + o_w, wdt, in, out, 0, w.stream),
+          what);
+    cuda_ok(cudaMemcpyAsync(y, b + o_y, nb_y, cudaMemcpyDeviceToHost, w.stream), what);
+    cuda_ok(cudaStreamSynchronize(w.stream), what);
+}
+
+void k3_matmul(float *y, const float *x, const float *W, int in, int out) {
+    trunk_matmul(y, x, W, K3C_WF32, in, out, "k3_matmul");
+}
+
+void k3_matmul_bf16(float *y, const float *x, const uint16_t *W, int in, int out) {
+    trunk_matmul(y, x, W, K3C_WBF16, in, out, "k3_matmul_bf16");
 }
 
 void k3_router(int *idx, float *wout, const float *x, const float *W, const float *bias,

@@ -1,0 +1,364 @@
+// latent.cu -- the K3 latent MoE layer (src/core/k3_ops.c:556-656) on the GPU, and the
+// trunk matmuls it runs (k3_mmw, include/k3/k3.h:289-296: k3_matmul and k3_matmul_bf16,
+// src/core/k3_ops.c:265-291 and 1091-1196).
+//
+// Trunk matmuls are bit-exact with the reference. The reference fixes the summation order
+// of every output: element i of the first in - in%16 goes to double accumulator i%16 by a
+// fused multiply-add in element order, the sixteen accumulators are combined as
+// b_l = (a_l + a_{l+4}) + (a_{l+8} + a_{l+12}), l = 0..3, then (b0 + b1) + (b2 + b3), the
+// in%16 tail is fused onto the total in element order and the result is rounded once to
+// float. Here each output row belongs to 16 threads: thread l owns accumulator l and runs
+// its chain over the row in element order (double FMAs, exact widening of the fp32 or bf16
+// weight and the fp32 activation), and the row's threads combine the sixteen with width-16
+// shuffles in the same tree. The activations of up to NT tokens are staged in shared
+// memory as doubles, chunk by chunk, and every weight a thread loads is used for all of
+// them.
+//
+// The layer: route on the full-width input (the router of router.cu), z = down x, the
+// routed experts at the latent width through the tensor-core decode kernels with the routing
+// given (moe_pool.cu; their weighted top-k-order sum is the aggregate), RMSNorm of the
+// aggregate, out = up aggregate, then the full-width shared expert sh2(SiTU(sh1 x, sh3 x))
+// added without a weight.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "common.cuh"
+
+namespace k3c {
+
+int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
+                  const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
+                  int ntok, double *part, cudaStream_t s);
+size_t router_scratch_bytes(int hidden, int n_experts, int ntok);
+size_t moe_decode_tc_scratch(const k3c_moe_pool_layer *L, int ntok);
+int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const k3c_moe_pool_layer *L,
+                         int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
+                         cudaStream_t s, bool routed);
+
+// ------------------------------------------------------------------ trunk matmul
+constexpr int MW_THREADS = 256;
+constexpr int MW_GROUPS = MW_THREADS / 16;   // 16-thread groups per block
+constexpr int MW_UNROLL = 8;                 // K steps of 16 whose weights are loaded together
+
+template <int NT>
+struct MwCfg {
+    static constexpr int R = NT >= 32 ? 1 : 2;          // rows per 16-thread group
+    static constexpr int KC = NT >= 16 ? 512 : 1024;    // activation chunk (elements), multiple of 16*UNROLL
+    static constexpr int ROWS = MW_GROUPS * R;          // rows per block
+    static constexpr size_t SMEM = (size_t)NT * KC * sizeof(double);
+};
+
+template <bool BF16>
+__device__ __forceinline__ double mw_load(const void *row, int i) {
+    if constexpr (BF16) {
+        const unsigned short h = __ldg(reinterpret_cast<const unsigned short *>(row) + i);
+        return (double)__uint_as_float((uint32_t)h << 16);
+    } else {
+        return (double)__ldg(reinterpret_cast<const float *>(row) + i);
+    }
+}
+
+// y[t*ldy + o] = sum_i W[o][i] x[t*ldx + i] (accumulate: y += that, one float addition) for
+// o < out, t < ntok <= NT, in the reference's order (file comment).
+template <int NT, bool BF16>
+__global__ void __launch_bounds__(MW_THREADS) k_mmw(float *__restrict__ y, int ldy, const float *__restrict__ x,
+                                                   int ldx, const void *__restrict__ W, int in, int out,
+                                                   int ntok, int accumulate) {
+    using Cfg = MwCfg<NT>;
+    constexpr int R = Cfg::R, KC = Cfg::KC;
+    extern __shared__ double xs[];   // [NT][KC]
+    const int l = threadIdx.x & 15, grp = threadIdx.x >> 4;
+    const int row0 = blockIdx.x * Cfg::ROWS + grp * R;
+    const size_t esz = BF16 ? 2 : 4;
+    const char *wrow[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        const int o = row0 + r < out ? row0 + r : out - 1;   // rows past the end load row out-1
+        wrow[r] = reinterpret_cast<const char *>(W) + (size_t)o * in * esz;
+    }
+    double a[R][NT];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) a[r][t] = 0.0;
+
+    const int in16 = in & ~15;
+    for (int k0 = 0; k0 < in16; k0 += KC) {
+        const int kc = in16 - k0 < KC ? in16 - k0 : KC;   // a multiple of 16
+        __syncthreads();   // the previous chunk is consumed
+        for (int i = threadIdx.x; i < NT * kc; i += MW_THREADS) {
+            const int t = i / kc, k = i - t * kc;
+            xs[t * KC + k] = t < ntok ? (double)x[(size_t)t * ldx + k0 + k] : 0.0;
+        }
+        __syncthreads();
+        int m = 0;
+        for (; m + 16 * MW_UNROLL <= kc; m += 16 * MW_UNROLL) {
+            double w[MW_UNROLL][R];
+#pragma unroll
+            for (int u = 0; u < MW_UNROLL; u++)
+#pragma unroll
+                for (int r = 0; r < R; r++) w[u][r] = mw_load<BF16>(wrow[r], k0 + m + 16 * u + l);
+#pragma unroll
+            for (int u = 0; u < MW_UNROLL; u++) {
+                const int k = m + 16 * u + l;
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    const double xv = xs[t * KC + k];
+#pragma unroll
+                    for (int r = 0; r < R; r++) a[r][t] = fma(w[u][r], xv, a[r][t]);
+                }
+            }
+        }
+        for (; m < kc; m += 16) {
+            const int k = m + l;
+            double w[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) w[r] = mw_load<BF16>(wrow[r], k0 + k);
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                const double xv = xs[t * KC + k];
+#pragma unroll
+                for (int r = 0; r < R; r++) a[r][t] = fma(w[r], xv, a[r][t]);
+            }
+        }
+    }
+    // (a_l + a_{l+4}) + (a_{l+8} + a_{l+12}) at lanes 0..3, then (b0 + b1) + (b2 + b3) at lane 0
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        const int o = row0 + r;
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            double v = a[r][t];
+            v += __shfl_down_sync(0xffffffffu, v, 4, 16);
+            v += __shfl_down_sync(0xffffffffu, v, 8, 16);
+            v += __shfl_down_sync(0xffffffffu, v, 1, 16);
+            v += __shfl_down_sync(0xffffffffu, v, 2, 16);
+            if (l == 0 && o < out && t < ntok) {
+                const float *xt = x + (size_t)t * ldx;
+                for (int i = in16; i < in; i++) v = fma(mw_load<BF16>(wrow[r], i), (double)xt[i], v);
+                const float f = __double2float_rn(v);
+                float *dst = y + (size_t)t * ldy + o;
+                *dst = accumulate ? __fadd_rn(*dst, f) : f;
+            }
+        }
+    }
+}
+
+template <int NT, bool BF16>
+static int launch_mmw_nt(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int in, int out,
+                         int accumulate, cudaStream_t s) {
+    using Cfg = MwCfg<NT>;
+    auto k = k_mmw<NT, BF16>;
+    static bool attr_done[64] = {};
+    const int dev = cur_dev();
+    if (!attr_done[dev]) {
+        K3C_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
+        attr_done[dev] = true;
+    }
+    const int grid = (out + Cfg::ROWS - 1) / Cfg::ROWS;
+    k<<<grid, MW_THREADS, Cfg::SMEM, s>>>(y, ldy, x, ldx, W, in, out, ntok, accumulate);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
+template <bool BF16>
+static int launch_mmw_t(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int in, int out,
+                        int accumulate, cudaStream_t s) {
+    if (ntok <= 1) return launch_mmw_nt<1, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+    if (ntok <= 2) return launch_mmw_nt<2, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+    if (ntok <= 4) return launch_mmw_nt<4, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+    if (ntok <= 8) return launch_mmw_nt<8, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+    if (ntok <= 16) return launch_mmw_nt<16, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+    return launch_mmw_nt<32, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+}
+
+int launch_mmw(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int wdt, int in, int out,
+               int accumulate, cudaStream_t s) {
+    if (ntok <= 0 || out <= 0) return K3C_OK;
+    if (ntok > 32) return set_error(K3C_EINVAL, "mmw: ntok=%d > 32", ntok);
+    if (in <= 0 || !y || !x || !W || ldy < out || ldx < in)
+        return set_error(K3C_EINVAL, "mmw: bad arguments (in=%d out=%d ldx=%d ldy=%d)", in, out, ldx, ldy);
+    if (wdt == K3C_WBF16) return launch_mmw_t<true>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+    if (wdt == K3C_WF32) return launch_mmw_t<false>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+    return set_error(K3C_EINVAL, "mmw: wdt=%d (int8 trunk rows run through k3c_q8_pack/k3c_q8_gemv)", wdt);
+}
+
+// ------------------------------------------------------------------ RMSNorm, SiTU-GLU
+// y[t] = w * x[t] * inv, inv = 1/sqrt(mean(x[t]^2) + eps) computed in double and rounded to
+// float once (src/core/k3_ops.c:94-102). One block per token; the sum of squares is a block
+// reduction in double (the reference sums in element order: the two totals agree to a few
+// units of 2^-53 relative, which reaches the float inv only at a rounding boundary). y may
+// alias x.
+__global__ void __launch_bounds__(256) k_rmsnorm_rows(float *y, const float *x, const float *__restrict__ w,
+                                                      int n, float eps) {
+    __shared__ double part[8];
+    const float *xt = x + (size_t)blockIdx.x * n;
+    float *yt = y + (size_t)blockIdx.x * n;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double v = (double)xt[i];
+        ss = __dadd_rn(ss, __dmul_rn(v, v));
+    }
+    ss = warp_sum_d(ss);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) tot = __dadd_rn(tot, part[i]);
+    const float inv = __double2float_rn(1.0 / sqrt(tot / (double)n + (double)eps));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yt[i] = __fmul_rn(__fmul_rn(w[i], xt[i]), inv);
+}
+
+// y[t][i] = (b1 tanh(g/b1) sigmoid(g)) * (b2 tanh(u/b2)), g = gu[t][i], u = gu[t][n + i]
+// (src/core/k3_ops.c:110-122; the sigmoid takes the uncapped gate).
+__global__ void __launch_bounds__(256) k_situ_rows(float *__restrict__ y, const float *__restrict__ gu, int n,
+                                                   float b1, float b2) {
+    const float *g = gu + (size_t)blockIdx.y * 2 * n;
+    float *yt = y + (size_t)blockIdx.y * n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float gv = g[i], uv = g[n + i];
+        const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+        const float a = __fmul_rn(__fmul_rn(b1, tanhf(__fdiv_rn(gv, b1))), sg);
+        yt[i] = __fmul_rn(a, __fmul_rn(b2, tanhf(__fdiv_rn(uv, b2))));
+    }
+}
+
+// ------------------------------------------------------------------ the layer
+struct LatentBufs {
+    double *rpart;     // router logit chunks
+    float *z;          // [ntok][latent]
+    float *agg;        // [ntok][latent] weighted expert sum, then normalised
+    float *sgu;        // [ntok][2*SI]
+    float *sact;       // [ntok][SI]
+    int *idx;          // [ntok][topk] when the caller passes none
+    float *wt;
+    void *tc;          // tensor-core decode scratch
+    size_t tc_bytes;
+};
+
+static bool carve_latent(Carve &cv, LatentBufs &b, const k3c_moe_latent_layer *L, int ntok) {
+    const int SI = L->experts.inter * L->n_shared;
+    const int Lw = L->experts.hidden;
+    b.rpart = cv.take<double>(router_scratch_bytes(L->hidden, L->experts.n_experts, ntok) / sizeof(double) + 1);
+    b.z = cv.take<float>((size_t)ntok * Lw);
+    b.agg = cv.take<float>((size_t)ntok * Lw);
+    b.sgu = cv.take<float>((size_t)ntok * 2 * SI);
+    b.sact = cv.take<float>((size_t)ntok * SI);
+    b.idx = cv.take<int>((size_t)ntok * L->experts.topk);
+    b.wt = cv.take<float>((size_t)ntok * L->experts.topk);
+    b.tc_bytes = moe_decode_tc_scratch(&L->experts, ntok);
+    b.tc = cv.take<char>(b.tc_bytes, 1024);
+    return b.rpart && b.z && b.agg && b.sgu && b.sact && b.idx && b.wt && b.tc;
+}
+
+static int check_latent(const k3c_moe_latent_layer *L, int ntok) {
+    if (!L) return set_error(K3C_EINVAL, "moe_latent: null layer");
+    const k3c_moe_pool_layer &X = L->experts;
+    if (ntok > 32) return set_error(K3C_EINVAL, "moe_latent: ntok=%d > 32", ntok);
+    if (L->hidden <= 0 || X.hidden <= 0 || X.inter <= 0 || L->n_shared < 0)
+        return set_error(K3C_EINVAL, "moe_latent: hidden=%d latent=%d inter=%d n_shared=%d", L->hidden, X.hidden,
+                         X.inter, L->n_shared);
+    if (L->wdt != K3C_WF32 && L->wdt != K3C_WBF16) return set_error(K3C_EINVAL, "moe_latent: wdt=%d", L->wdt);
+    if (!L->router_w || !L->down || !L->up || (L->n_shared > 0 && (!L->sh1 || !L->sh3 || !L->sh2)) ||
+        (L->latent_norm_on && !L->latent_norm))
+        return set_error(K3C_EINVAL, "moe_latent: missing weights");
+    if (X.shared_run >= 0)
+        return set_error(K3C_EINVAL, "moe_latent: the latent layer's shared expert is the full-width trunk MLP; "
+                                     "experts.shared_run must be -1");
+    // the expert kernels apply SiTU with the K3 constants
+    if (X.act == K3C_ACT_SITU && (L->situ_b1 != 4.0f || L->situ_b2 != 25.0f))
+        return set_error(K3C_EINVAL, "moe_latent: expert SiTU runs with b1=4, b2=25 (got %g, %g)",
+                         (double)L->situ_b1, (double)L->situ_b2);
+    return K3C_OK;
+}
+
+size_t moe_latent_scratch(const k3c_moe_latent_layer *L, int ntok) {
+    Carve cv{reinterpret_cast<char *>(4096), (size_t)-1 / 2, 0};
+    LatentBufs b;
+    carve_latent(cv, b, L, ntok);
+    return cv.used + 1024;
+}
+
+int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L, int *idx_out,
+                      float *wt_out, int *drops, void *scratch, size_t scratch_bytes, cudaStream_t s) {
+    K3C_TRY(check_latent(L, ntok));
+    if (ntok <= 0) return K3C_OK;
+    Carve cv{(char *)scratch, scratch_bytes, 0};
+    LatentBufs b;
+    if (!carve_latent(cv, b, L, ntok))
+        return set_error(K3C_EINVAL, "moe_latent: scratch too small (%zu)", scratch_bytes);
+    const k3c_moe_pool_layer &X = L->experts;
+    const int H = L->hidden, Lw = X.hidden, SI = X.inter * L->n_shared, K = X.topk;
+    int *idx = idx_out ? idx_out : b.idx;
+    float *wt = wt_out ? wt_out : b.wt;
+    // 1. route on the full width
+    stage_begin(STAGE_ROUTER, s);
+    K3C_TRY(launch_router(idx, wt, nullptr, x, K3C_F32, L->router_w, K3C_F32, L->router_bias, H, X.n_experts, K,
+                          X.renorm, X.routed_scale, ntok, b.rpart, s));
+    stage_end(STAGE_ROUTER, s);
+    stage_begin(STAGE_Q8, s);   // trunk projections are reported with the trunk stage
+    // 2. z = down x
+    K3C_TRY(launch_mmw(b.z, Lw, x, H, ntok, L->down, L->wdt, H, Lw, 0, s));
+    stage_end(STAGE_Q8, s);
+    // 3. routed experts at the latent width, weighted top-k-order sum
+    K3C_TRY(launch_moe_decode_tc(b.agg, b.z, K3C_F32, ntok, &X, idx, wt, drops, b.tc, b.tc_bytes, s, true));
+    stage_begin(STAGE_Q8, s);
+    // 4. RMSNorm of the aggregate
+    if (L->latent_norm_on) {
+        k_rmsnorm_rows<<<ntok, 256, 0, s>>>(b.agg, b.agg, L->latent_norm, Lw, L->rms_eps);
+        K3C_CHECK_LAUNCH();
+    }
+    // 5. out = up aggregate
+    K3C_TRY(launch_mmw(out, H, b.agg, Lw, ntok, L->up, L->wdt, Lw, H, 0, s));
+    // 6. shared expert at full width, added without a weight
+    if (L->n_shared > 0) {
+        K3C_TRY(launch_mmw(b.sgu, 2 * SI, x, H, ntok, L->sh1, L->wdt, H, SI, 0, s));
+        K3C_TRY(launch_mmw(b.sgu + SI, 2 * SI, x, H, ntok, L->sh3, L->wdt, H, SI, 0, s));
+        dim3 gs((SI + 255) / 256 < 148 ? (SI + 255) / 256 : 148, ntok);
+        k_situ_rows<<<gs, 256, 0, s>>>(b.sact, b.sgu, SI, L->situ_b1, L->situ_b2);
+        K3C_CHECK_LAUNCH();
+        K3C_TRY(launch_mmw(out, H, b.sact, SI, ntok, L->sh2, L->wdt, SI, H, 1, s));
+    }
+    stage_end(STAGE_Q8, s);
+    return K3C_OK;
+}
+
+}  // namespace k3c
+
+extern "C" int k3c_mmw(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int wdt, int in,
+                       int out, int accumulate, k3c_stream_t stream) {
+    k3c::clear_error();
+    return k3c::launch_mmw(y, ldy, x, ldx, ntok, W, wdt, in, out, accumulate, (cudaStream_t)stream);
+}
+
+extern "C" int k3c_situ_glu(float *y, const float *gu, int n, int ntok, float b1, float b2,
+                            k3c_stream_t stream) {
+    k3c::clear_error();
+    if (n <= 0 || ntok <= 0) return K3C_OK;
+    if (!y || !gu) return k3c::set_error(K3C_EINVAL, "situ_glu: null pointer");
+    dim3 gs((n + 255) / 256 < 148 ? (n + 255) / 256 : 148, ntok);
+    k3c::k_situ_rows<<<gs, 256, 0, (cudaStream_t)stream>>>(y, gu, n, b1, b2);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
+extern "C" int k3c_rmsnorm(float *y, const float *x, const float *w, int n, int ntok, float eps,
+                           k3c_stream_t stream) {
+    k3c::clear_error();
+    if (n <= 0 || ntok <= 0) return K3C_OK;
+    if (!y || !x || !w) return k3c::set_error(K3C_EINVAL, "rmsnorm: null pointer");
+    k3c::k_rmsnorm_rows<<<ntok, 256, 0, (cudaStream_t)stream>>>(y, x, w, n, eps);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
+extern "C" size_t k3c_moe_latent_scratch(const k3c_moe_latent_layer *L, int ntok) {
+    return L ? k3c::moe_latent_scratch(L, ntok) : 0;
+}
+
+extern "C" int k3c_moe_latent_decode(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L,
+                                     int *idx, float *wt, int *drops, void *scratch, size_t scratch_bytes,
+                                     k3c_stream_t stream) {
+    k3c::clear_error();
+    return k3c::launch_moe_latent(out, x, ntok, L, idx, wt, drops, scratch, scratch_bytes, (cudaStream_t)stream);
+}

@@ -72,6 +72,7 @@ def lib():
         L.ora_matmul_mxfp4.argtypes = [_f32p, _f32p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]
         L.ora_matmul_f32.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int]
         L.ora_matmul_bf16.argtypes = [_f32p, _f32p, _u16p, C.c_int, C.c_int]
+        L.ora_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_float]
         L.ora_moe_latent.argtypes = [_f32p, _f32p, C.c_int, C.POINTER(OraLatent), _i32p, _f32p]
         L.ora_matmul_q8.argtypes = [_f32p, _f32p, _u8p, C.c_int, C.c_int]
         L.ora_router.argtypes = [_i32p, _f32p, _f32p, _f32p, C.c_void_p, C.c_int, C.c_int,
@@ -295,3 +296,29 @@ def moe_latent(x, layer: dict, use_ref=False):
                       **{k: float(layer[k]) for k in _LATENT_FLOATS})
         lib().ora_moe_latent(out, x, T, C.byref(c), idx, wt)
     return out, idx, wt
+
+
+def rmsnorm(x, w, eps=1e-5):
+    """k3_rmsnorm row by row (double sum of squares in element order)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    out = np.empty_like(rows)
+    for r in range(rows.shape[0]):
+        y = np.empty(rows.shape[1], np.float32)
+        lib().ora_rmsnorm(y, np.ascontiguousarray(rows[r]), np.ascontiguousarray(w, np.float32),
+                          rows.shape[1], eps)
+        out[r] = y
+    return out.reshape(x.shape)
+
+
+def situ_glu(gu, b1=4.0, b2=25.0):
+    """k3_situ_glu row by row: gu [..][2n] -> [..][n]."""
+    gu = np.ascontiguousarray(gu, np.float32)
+    rows = gu.reshape(-1, gu.shape[-1])
+    n = rows.shape[1] // 2
+    out = np.empty((rows.shape[0], n), np.float32)
+    for r in range(rows.shape[0]):
+        y = np.empty(n, np.float32)
+        lib().ora_situ_glu(y, np.ascontiguousarray(rows[r]), n, b1, b2)
+        out[r] = y
+    return out

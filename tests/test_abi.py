@@ -119,3 +119,56 @@ def test_ep_arguments_are_checked_without_a_gpu(k3):
     assert rc == -1 and b"buffers" in L.k3c_last_error()
     rc = L.k3c_moe_ep_combine(None, C.byref(peers), 512, None)
     assert rc == -1
+
+
+def test_latent_struct_layout_and_argument_checks(k3):
+    """The latent layer's ctypes mirror has the C layout, and the latent entry points reject
+    bad arguments before any CUDA call."""
+    prog = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "k3c.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu\n", sizeof(k3c_moe_latent_layer),
+         offsetof(k3c_moe_latent_layer, experts), offsetof(k3c_moe_latent_layer, router_w),
+         offsetof(k3c_moe_latent_layer, latent_norm), offsetof(k3c_moe_latent_layer, wdt),
+         offsetof(k3c_moe_latent_layer, situ_b2));
+  return 0; }
+"""
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(prog)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        got = [int(v) for v in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
+    M = k3.MoeLatentLayerC
+    assert got == [C.sizeof(M), M.experts.offset, M.router_w.offset, M.latent_norm.offset,
+                   M.wdt.offset, M.situ_b2.offset]
+
+    L = k3.lib()
+    lay = M()
+    lay.hidden, lay.wdt, lay.n_shared, lay.latent_norm_on = 256, 1, 2, 1
+    lay.situ_b1, lay.situ_b2, lay.rms_eps = 4.0, 25.0, 1e-5
+    ex = lay.experts
+    ex.hidden, ex.inter, ex.n_experts, ex.topk, ex.act, ex.terms, ex.shared_run = 128, 128, 8, 2, 1, 3, -1
+    dummy = 4096
+    lay.router_w = lay.down = lay.up = lay.sh1 = lay.sh3 = lay.sh2 = lay.latent_norm = dummy
+    rc = L.k3c_moe_latent_decode(None, None, 33, C.byref(lay), None, None, None, None, 0, None)
+    assert rc == -1 and b"ntok" in L.k3c_last_error()
+    lay.wdt = 2
+    rc = L.k3c_moe_latent_decode(None, None, 4, C.byref(lay), None, None, None, None, 0, None)
+    assert rc == -1 and b"wdt" in L.k3c_last_error()
+    lay.wdt, ex.shared_run = 1, 0
+    lay.experts = ex
+    rc = L.k3c_moe_latent_decode(None, None, 4, C.byref(lay), None, None, None, None, 0, None)
+    assert rc == -1 and b"shared_run" in L.k3c_last_error()
+    ex.shared_run = -1
+    lay.experts, lay.situ_b1 = ex, 3.0
+    rc = L.k3c_moe_latent_decode(None, None, 4, C.byref(lay), None, None, None, None, 0, None)
+    assert rc == -1 and b"SiTU" in L.k3c_last_error()
+    lay.situ_b1, lay.sh2 = 4.0, None
+    rc = L.k3c_moe_latent_decode(None, None, 4, C.byref(lay), None, None, None, None, 0, None)
+    assert rc == -1 and b"missing" in L.k3c_last_error()
+    assert L.k3c_mmw(None, 8, None, 8, 33, None, 1, 8, 8, 0, None) == -1
+    assert L.k3c_mmw(dummy, 8, dummy, 8, 2, dummy, 2, 8, 8, 0, None) == -1
+    assert b"int8" in L.k3c_last_error()
