@@ -887,9 +887,11 @@ def run_latent(args, ws, rank, local):
     dev = torch.device("cuda", local)
     g = torch.Generator(device=dev)
     g.manual_seed(5151 + rank)
+    # --distinct D < 384 (profiling only): D distinct expert runs tiled over the 896 ids
+    ND = args.distinct if args.distinct < E else LE
     lay, run = k3.pool_layout(LL, LI)
-    arena = torch.empty(LE * run, dtype=torch.uint8, device=dev)
-    a2 = arena.view(LE, run)
+    arena = torch.empty(ND * run, dtype=torch.uint8, device=dev)
+    a2 = arena.view(ND, run)
     for name, (off, nb) in lay.items():
         seg = a2[:, off:off + nb]
         if name.endswith("_p"):
@@ -904,8 +906,8 @@ def run_latent(args, ws, rank, local):
     router = (torch.randn((LE, LH), generator=g, device=dev) * 0.02).to(torch.bfloat16).float()
     down, up, sh1, sh3, sh2 = trunk(LL, LH), trunk(LH, LL), trunk(SI, LH), trunk(SI, LH), trunk(LH, SI)
     norm = torch.ones(LL, dtype=torch.float32, device=dev)
-    run_of = torch.arange(LE, dtype=torch.int32, device=dev)
-    lat = k3.LatentMoeLayer(arena, LE, run_of, router, None, down, up, sh1, sh3, sh2, norm, k3.WBF16,
+    run_of = torch.arange(LE, dtype=torch.int32, device=dev) % ND
+    lat = k3.LatentMoeLayer(arena, ND, run_of, router, None, down, up, sh1, sh3, sh2, norm, k3.WBF16,
                             LH, LL, LI, LS, LK, terms=args.terms)
     B, NB = 16, 32
     xs = [torch.randn((B, LH), generator=g, device=dev) for _ in range(NB)]

@@ -47,8 +47,9 @@ def test_mmw_accumulate_and_strides(k3, ora, dev):
     # write into columns 40..135 of a wider row, adding to what is there
     view = out[:, 40:136]
     L = k3.lib()
-    rc = L.k3c_mmw(C.c_void_p(view.data_ptr()), 160, C.c_void_p(T(x, dev).data_ptr()), 200, 4,
-                   C.c_void_p(T(W, dev).data_ptr()), k3.WF32, 200, 96, 1,
+    xd, Wd = T(x, dev), T(W, dev)          # held: the kernel reads them after this line
+    rc = L.k3c_mmw(C.c_void_p(view.data_ptr()), 160, C.c_void_p(xd.data_ptr()), 200, 4,
+                   C.c_void_p(Wd.data_ptr()), k3.WF32, 200, 96, 1,
                    C.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0
     got = out.cpu().numpy()
