@@ -22,6 +22,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace k3c {
@@ -36,45 +38,57 @@ int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const
                          cudaStream_t s, bool routed);
 
 // ------------------------------------------------------------------ trunk matmul
+// Pipeline: the activations of a chunk of KC elements (all tokens) sit in shared memory as
+// doubles, two buffers, the next chunk's values held in registers while the current chunk
+// runs; weights are loaded in blocks of 8 K-steps of 16 elements, the next block while the
+// current one is multiplied (across chunk boundaries too). None of this changes the order
+// in which any accumulator sees its elements.
 constexpr int MW_THREADS = 256;
 constexpr int MW_GROUPS = MW_THREADS / 16;   // 16-thread groups per block
-constexpr int MW_UNROLL = 8;                 // K steps of 16 whose weights are loaded together
+constexpr int MW_UNROLL = 8;                 // K steps of 16 per weight block
+constexpr int MW_UB = 16 * MW_UNROLL;        // elements per weight block
+constexpr int MW_XBUF = 4096;                // doubles per activation buffer (two buffers)
 
 template <int NT>
 struct MwCfg {
-    static constexpr int R = NT >= 32 ? 1 : 2;          // rows per 16-thread group
-    static constexpr int KC = NT >= 16 ? 512 : 1024;    // activation chunk (elements), multiple of 16*UNROLL
+    static constexpr int R = NT >= 16 ? 1 : 2;          // rows per 16-thread group
+    static constexpr int KC = MW_XBUF / NT;             // activation chunk (elements)
     static constexpr int ROWS = MW_GROUPS * R;          // rows per block
-    static constexpr size_t SMEM = (size_t)NT * KC * sizeof(double);
+    static constexpr int XPT = MW_XBUF / MW_THREADS;    // activations each thread stages per chunk
+    static constexpr size_t SMEM = 2 * (size_t)MW_XBUF * sizeof(double);
+    static_assert(KC % MW_UB == 0, "a chunk holds whole weight blocks");
 };
 
 template <bool BF16>
-__device__ __forceinline__ double mw_load(const void *row, int i) {
-    if constexpr (BF16) {
-        const unsigned short h = __ldg(reinterpret_cast<const unsigned short *>(row) + i);
-        return (double)__uint_as_float((uint32_t)h << 16);
-    } else {
-        return (double)__ldg(reinterpret_cast<const float *>(row) + i);
-    }
+using mw_raw_t = typename std::conditional<BF16, unsigned short, float>::type;
+
+template <bool BF16>
+__device__ __forceinline__ mw_raw_t<BF16> mw_raw(const char *row, int i) {
+    return __ldg(reinterpret_cast<const mw_raw_t<BF16> *>(row) + i);
+}
+template <bool BF16>
+__device__ __forceinline__ double mw_wide(mw_raw_t<BF16> v) {
+    if constexpr (BF16) return (double)__uint_as_float((uint32_t)v << 16);
+    else return (double)v;
 }
 
 // y[t*ldy + o] = sum_i W[o][i] x[t*ldx + i] (accumulate: y += that, one float addition) for
 // o < out, t < ntok <= NT, in the reference's order (file comment).
 template <int NT, bool BF16>
-__global__ void __launch_bounds__(MW_THREADS) k_mmw(float *__restrict__ y, int ldy, const float *__restrict__ x,
-                                                   int ldx, const void *__restrict__ W, int in, int out,
-                                                   int ntok, int accumulate) {
+__global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(float *__restrict__ y, int ldy, const float *__restrict__ x,
+                                                      int ldx, const void *__restrict__ W, int in, int out,
+                                                      int ntok, int accumulate) {
     using Cfg = MwCfg<NT>;
+    using raw_t = mw_raw_t<BF16>;
     constexpr int R = Cfg::R, KC = Cfg::KC;
-    extern __shared__ double xs[];   // [NT][KC]
+    extern __shared__ double xs[];   // [2][NT][KC]
     const int l = threadIdx.x & 15, grp = threadIdx.x >> 4;
     const int row0 = blockIdx.x * Cfg::ROWS + grp * R;
-    const size_t esz = BF16 ? 2 : 4;
     const char *wrow[R];
 #pragma unroll
     for (int r = 0; r < R; r++) {
         const int o = row0 + r < out ? row0 + r : out - 1;   // rows past the end load row out-1
-        wrow[r] = reinterpret_cast<const char *>(W) + (size_t)o * in * esz;
+        wrow[r] = reinterpret_cast<const char *>(W) + (size_t)o * in * sizeof(raw_t);
     }
     double a[R][NT];
 #pragma unroll
@@ -82,45 +96,88 @@ __global__ void __launch_bounds__(MW_THREADS) k_mmw(float *__restrict__ y, int l
 #pragma unroll
         for (int t = 0; t < NT; t++) a[r][t] = 0.0;
 
-    const int in16 = in & ~15;
-    for (int k0 = 0; k0 < in16; k0 += KC) {
-        const int kc = in16 - k0 < KC ? in16 - k0 : KC;   // a multiple of 16
-        __syncthreads();   // the previous chunk is consumed
-        for (int i = threadIdx.x; i < NT * kc; i += MW_THREADS) {
-            const int t = i / kc, k = i - t * kc;
-            xs[t * KC + k] = t < ntok ? (double)x[(size_t)t * ldx + k0 + k] : 0.0;
+    // this thread's share of a chunk: buffer element e = threadIdx.x + 256 j is (t, k) =
+    // (e / KC, e % KC), the layout of the [NT][KC] buffer
+    float xr[Cfg::XPT];
+    auto fetch_x = [&](int kb, int kcn) {
+#pragma unroll
+        for (int j = 0; j < Cfg::XPT; j++) {
+            const int e = threadIdx.x + MW_THREADS * j, t = e / KC, k = e - t * KC;
+            xr[j] = (t < ntok && k < kcn) ? x[(size_t)t * ldx + kb + k] : 0.0f;
         }
-        __syncthreads();
-        int m = 0;
-        for (; m + 16 * MW_UNROLL <= kc; m += 16 * MW_UNROLL) {
-            double w[MW_UNROLL][R];
+    };
+    auto store_x = [&](double *buf) {
 #pragma unroll
-            for (int u = 0; u < MW_UNROLL; u++)
+        for (int j = 0; j < Cfg::XPT; j++) buf[threadIdx.x + MW_THREADS * j] = (double)xr[j];
+    };
+    auto load_block = [&](raw_t (&w)[MW_UNROLL][R], int kb) {
 #pragma unroll
-                for (int r = 0; r < R; r++) w[u][r] = mw_load<BF16>(wrow[r], k0 + m + 16 * u + l);
+        for (int u = 0; u < MW_UNROLL; u++)
+#pragma unroll
+            for (int r = 0; r < R; r++) w[u][r] = mw_raw<BF16>(wrow[r], kb + 16 * u + l);
+    };
+
+    const int in16 = in & ~15;
+    const int nchunk = (in16 + KC - 1) / KC;
+    raw_t wc[MW_UNROLL][R];
+    if (in16 > 0) {
+        const int kc0 = in16 < KC ? in16 : KC;
+        fetch_x(0, kc0);
+        if (kc0 >= MW_UB) load_block(wc, 0);
+        store_x(xs);
+    }
+    __syncthreads();
+    for (int c = 0; c < nchunk; c++) {
+        const int k0 = c * KC;
+        const int kc = in16 - k0 < KC ? in16 - k0 : KC;
+        const double *xb = xs + (c & 1) * MW_XBUF;
+        const bool more = c + 1 < nchunk;
+        const int k0n = k0 + KC;
+        const int kcn = more ? (in16 - k0n < KC ? in16 - k0n : KC) : 0;
+        if (more) fetch_x(k0n, kcn);   // consumed after this chunk's products
+        const int nb = kc / MW_UB;
+        for (int b = 0; b < nb; b++) {
+            raw_t wn[MW_UNROLL][R];
+            const bool next_here = b + 1 < nb;
+            const bool next_there = !next_here && kcn >= MW_UB;
+            if (next_here) load_block(wn, k0 + (b + 1) * MW_UB);
+            else if (next_there) load_block(wn, k0n);
 #pragma unroll
             for (int u = 0; u < MW_UNROLL; u++) {
-                const int k = m + 16 * u + l;
+                const int k = b * MW_UB + 16 * u + l;
+                double wd[R];
+#pragma unroll
+                for (int r = 0; r < R; r++) wd[r] = mw_wide<BF16>(wc[u][r]);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
-                    const double xv = xs[t * KC + k];
+                    const double xv = xb[t * KC + k];
 #pragma unroll
-                    for (int r = 0; r < R; r++) a[r][t] = fma(w[u][r], xv, a[r][t]);
+                    for (int r = 0; r < R; r++) a[r][t] = fma(wd[r], xv, a[r][t]);
                 }
             }
-        }
-        for (; m < kc; m += 16) {
-            const int k = m + l;
-            double w[R];
+            if (next_here || next_there) {
 #pragma unroll
-            for (int r = 0; r < R; r++) w[r] = mw_load<BF16>(wrow[r], k0 + k);
+                for (int u = 0; u < MW_UNROLL; u++)
 #pragma unroll
-            for (int t = 0; t < NT; t++) {
-                const double xv = xs[t * KC + k];
-#pragma unroll
-                for (int r = 0; r < R; r++) a[r][t] = fma(w[r], xv, a[r][t]);
+                    for (int r = 0; r < R; r++) wc[u][r] = wn[u][r];
             }
         }
+        // the last chunk's K steps past its whole weight blocks
+        for (int m = nb * MW_UB; m < kc; m += 16) {
+            const int k = m + l;
+            double wd[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) wd[r] = mw_wide<BF16>(mw_raw<BF16>(wrow[r], k0 + k));
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                const double xv = xb[t * KC + k];
+#pragma unroll
+                for (int r = 0; r < R; r++) a[r][t] = fma(wd[r], xv, a[r][t]);
+            }
+        }
+        // the other buffer was last read in chunk c-1, which every thread has left
+        if (more) store_x(xs + ((c + 1) & 1) * MW_XBUF);
+        __syncthreads();
     }
     // (a_l + a_{l+4}) + (a_{l+8} + a_{l+12}) at lanes 0..3, then (b0 + b1) + (b2 + b3) at lane 0
 #pragma unroll
@@ -135,7 +192,7 @@ __global__ void __launch_bounds__(MW_THREADS) k_mmw(float *__restrict__ y, int l
             v += __shfl_down_sync(0xffffffffu, v, 2, 16);
             if (l == 0 && o < out && t < ntok) {
                 const float *xt = x + (size_t)t * ldx;
-                for (int i = in16; i < in; i++) v = fma(mw_load<BF16>(wrow[r], i), (double)xt[i], v);
+                for (int i = in16; i < in; i++) v = fma(mw_wide<BF16>(mw_raw<BF16>(wrow[r], i)), (double)xt[i], v);
                 const float f = __double2float_rn(v);
                 float *dst = y + (size_t)t * ldy + o;
                 *dst = accumulate ? __fadd_rn(*dst, f) : f;
