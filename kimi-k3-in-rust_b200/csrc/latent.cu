@@ -49,11 +49,17 @@ constexpr int MW_UNROLL = 8;                 // K steps of 16 per weight block
 constexpr int MW_UB = 16 * MW_UNROLL;        // elements per weight block
 constexpr int MW_XBUF = 4096;                // doubles per activation buffer (two buffers)
 
+// Each 16-thread group owns R rows and NTT of the NT tokens. From 16 tokens up the two
+// groups of a warp share their rows and split the tokens (TS = 2), so an activation read
+// from shared memory feeds R rows' FMAs in both halves of the warp; below that the two groups
+// take different rows (TS = 1).
 template <int NT>
 struct MwCfg {
-    static constexpr int R = NT >= 16 ? 1 : 2;          // rows per 16-thread group
+    static constexpr int TS = NT >= 16 ? 2 : 1;         // token split across a warp's groups
+    static constexpr int NTT = NT / TS;                 // tokens per group
+    static constexpr int R = NTT >= 16 ? 1 : 2;         // rows per group
     static constexpr int KC = MW_XBUF / NT;             // activation chunk (elements)
-    static constexpr int ROWS = MW_GROUPS * R;          // rows per block
+    static constexpr int ROWS = MW_GROUPS * R / TS;     // rows per block
     static constexpr int XPT = MW_XBUF / MW_THREADS;    // activations each thread stages per chunk
     static constexpr size_t SMEM = 2 * (size_t)MW_XBUF * sizeof(double);
     static_assert(KC % MW_UB == 0, "a chunk holds whole weight blocks");
@@ -80,21 +86,22 @@ __global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(float *__restrict__ y, in
                                                       int ntok, int accumulate) {
     using Cfg = MwCfg<NT>;
     using raw_t = mw_raw_t<BF16>;
-    constexpr int R = Cfg::R, KC = Cfg::KC;
+    constexpr int R = Cfg::R, KC = Cfg::KC, NTT = Cfg::NTT;
     extern __shared__ double xs[];   // [2][NT][KC]
     const int l = threadIdx.x & 15, grp = threadIdx.x >> 4;
-    const int row0 = blockIdx.x * Cfg::ROWS + grp * R;
+    const int row0 = blockIdx.x * Cfg::ROWS + (Cfg::TS == 2 ? (grp >> 1) : grp) * R;
+    const int tok0 = Cfg::TS == 2 ? (grp & 1) * NTT : 0;
     const char *wrow[R];
 #pragma unroll
     for (int r = 0; r < R; r++) {
         const int o = row0 + r < out ? row0 + r : out - 1;   // rows past the end load row out-1
         wrow[r] = reinterpret_cast<const char *>(W) + (size_t)o * in * sizeof(raw_t);
     }
-    double a[R][NT];
+    double a[R][NTT];
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
-        for (int t = 0; t < NT; t++) a[r][t] = 0.0;
+        for (int t = 0; t < NTT; t++) a[r][t] = 0.0;
 
     // this thread's share of a chunk: buffer element e = threadIdx.x + 256 j is (t, k) =
     // (e / KC, e % KC), the layout of the [NT][KC] buffer
@@ -149,8 +156,8 @@ __global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(float *__restrict__ y, in
 #pragma unroll
                 for (int r = 0; r < R; r++) wd[r] = mw_wide<BF16>(wc[u][r]);
 #pragma unroll
-                for (int t = 0; t < NT; t++) {
-                    const double xv = xb[t * KC + k];
+                for (int t = 0; t < NTT; t++) {
+                    const double xv = xb[(tok0 + t) * KC + k];
 #pragma unroll
                     for (int r = 0; r < R; r++) a[r][t] = fma(wd[r], xv, a[r][t]);
                 }
@@ -169,8 +176,8 @@ __global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(float *__restrict__ y, in
 #pragma unroll
             for (int r = 0; r < R; r++) wd[r] = mw_wide<BF16>(mw_raw<BF16>(wrow[r], k0 + k));
 #pragma unroll
-            for (int t = 0; t < NT; t++) {
-                const double xv = xb[t * KC + k];
+            for (int t = 0; t < NTT; t++) {
+                const double xv = xb[(tok0 + t) * KC + k];
 #pragma unroll
                 for (int r = 0; r < R; r++) a[r][t] = fma(wd[r], xv, a[r][t]);
             }
@@ -184,8 +191,9 @@ __global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(float *__restrict__ y, in
     for (int r = 0; r < R; r++) {
         const int o = row0 + r;
 #pragma unroll
-        for (int t = 0; t < NT; t++) {
-            double v = a[r][t];
+        for (int tt = 0; tt < NTT; tt++) {
+            const int t = tok0 + tt;
+            double v = a[r][tt];
             v += __shfl_down_sync(0xffffffffu, v, 4, 16);
             v += __shfl_down_sync(0xffffffffu, v, 8, 16);
             v += __shfl_down_sync(0xffffffffu, v, 1, 16);
