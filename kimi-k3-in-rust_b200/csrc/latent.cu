@@ -78,18 +78,46 @@ __device__ __forceinline__ double mw_wide(mw_raw_t<BF16> v) {
     else return (double)v;
 }
 
-// y[t*ldy + o] = sum_i W[o][i] x[t*ldx + i] (accumulate: y += that, one float addition) for
-// o < out, t < ntok <= NT, in the reference's order (file comment).
+// One matrix of a launch: y[t*ldy + o] = sum_i W[o][i] x[t*ldx + i] (accumulate: y += that,
+// one float addition) for o < out, t < ntok.
+struct MwSeg {
+    const float *x;
+    const void *W;
+    float *y;
+    int ldx, ldy, in, out, accumulate, blocks;
+};
+constexpr int MW_MAXSEG = 3;
+// Up to three matrices of the same weight type and token count run as one grid (blocks of
+// segment 0 first): the blocks of several small launches fill the SMs' slots together
+// instead of each launch ending in its own partial wave.
+struct MwSegs {
+    MwSeg s[MW_MAXSEG];
+    int n;
+};
+
+// Each segment's products for t < ntok <= NT, in the reference's order (file comment).
 template <int NT, bool BF16>
-__global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(float *__restrict__ y, int ldy, const float *__restrict__ x,
-                                                      int ldx, const void *__restrict__ W, int in, int out,
-                                                      int ntok, int accumulate) {
+__global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(const MwSegs segs, int ntok) {
+    int blk = blockIdx.x;
+    MwSeg sg = segs.s[0];
+    if (segs.n > 1 && blk >= segs.s[0].blocks) {
+        blk -= segs.s[0].blocks;
+        sg = segs.s[1];
+        if (segs.n > 2 && blk >= segs.s[1].blocks) {
+            blk -= segs.s[1].blocks;
+            sg = segs.s[2];
+        }
+    }
+    const float *__restrict__ x = sg.x;
+    const void *__restrict__ W = sg.W;
+    float *__restrict__ y = sg.y;
+    const int ldx = sg.ldx, ldy = sg.ldy, in = sg.in, out = sg.out, accumulate = sg.accumulate;
     using Cfg = MwCfg<NT>;
     using raw_t = mw_raw_t<BF16>;
     constexpr int R = Cfg::R, KC = Cfg::KC, NTT = Cfg::NTT;
     extern __shared__ double xs[];   // [2][NT][KC]
     const int l = threadIdx.x & 15, grp = threadIdx.x >> 4;
-    const int row0 = blockIdx.x * Cfg::ROWS + (Cfg::TS == 2 ? (grp >> 1) : grp) * R;
+    const int row0 = blk * Cfg::ROWS + (Cfg::TS == 2 ? (grp >> 1) : grp) * R;
     const int tok0 = Cfg::TS == 2 ? (grp & 1) * NTT : 0;
     const char *wrow[R];
 #pragma unroll
@@ -210,8 +238,7 @@ __global__ void __launch_bounds__(MW_THREADS, 2) k_mmw(float *__restrict__ y, in
 }
 
 template <int NT, bool BF16>
-static int launch_mmw_nt(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int in, int out,
-                         int accumulate, cudaStream_t s) {
+static int launch_mmw_nt(MwSegs segs, int ntok, cudaStream_t s) {
     using Cfg = MwCfg<NT>;
     auto k = k_mmw<NT, BF16>;
     static bool attr_done[64] = {};
@@ -220,32 +247,50 @@ static int launch_mmw_nt(float *y, int ldy, const float *x, int ldx, int ntok, c
         K3C_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
         attr_done[dev] = true;
     }
-    const int grid = (out + Cfg::ROWS - 1) / Cfg::ROWS;
-    k<<<grid, MW_THREADS, Cfg::SMEM, s>>>(y, ldy, x, ldx, W, in, out, ntok, accumulate);
+    int grid = 0;
+    for (int i = 0; i < segs.n; i++) {
+        segs.s[i].blocks = (segs.s[i].out + Cfg::ROWS - 1) / Cfg::ROWS;
+        grid += segs.s[i].blocks;
+    }
+    k<<<grid, MW_THREADS, Cfg::SMEM, s>>>(segs, ntok);
     K3C_CHECK_LAUNCH();
     return K3C_OK;
 }
 
 template <bool BF16>
-static int launch_mmw_t(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int in, int out,
-                        int accumulate, cudaStream_t s) {
-    if (ntok <= 1) return launch_mmw_nt<1, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
-    if (ntok <= 2) return launch_mmw_nt<2, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
-    if (ntok <= 4) return launch_mmw_nt<4, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
-    if (ntok <= 8) return launch_mmw_nt<8, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
-    if (ntok <= 16) return launch_mmw_nt<16, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
-    return launch_mmw_nt<32, BF16>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
+static int launch_mmw_t(const MwSegs &segs, int ntok, cudaStream_t s) {
+    if (ntok <= 1) return launch_mmw_nt<1, BF16>(segs, ntok, s);
+    if (ntok <= 2) return launch_mmw_nt<2, BF16>(segs, ntok, s);
+    if (ntok <= 4) return launch_mmw_nt<4, BF16>(segs, ntok, s);
+    if (ntok <= 8) return launch_mmw_nt<8, BF16>(segs, ntok, s);
+    if (ntok <= 16) return launch_mmw_nt<16, BF16>(segs, ntok, s);
+    return launch_mmw_nt<32, BF16>(segs, ntok, s);
+}
+
+// Matrices with out == 0 are dropped; every other one is checked before anything launches.
+static int launch_mmw_segs(const MwSeg *list, int n, int ntok, int wdt, cudaStream_t s) {
+    if (ntok <= 0) return K3C_OK;
+    if (ntok > 32) return set_error(K3C_EINVAL, "mmw: ntok=%d > 32", ntok);
+    if (wdt != K3C_WBF16 && wdt != K3C_WF32)
+        return set_error(K3C_EINVAL, "mmw: wdt=%d (int8 trunk rows run through k3c_q8_pack/k3c_q8_gemv)", wdt);
+    MwSegs segs = {};
+    for (int i = 0; i < n; i++) {
+        const MwSeg &g = list[i];
+        if (g.out <= 0) continue;
+        if (g.in <= 0 || !g.y || !g.x || !g.W || g.ldy < g.out || g.ldx < g.in)
+            return set_error(K3C_EINVAL, "mmw: bad arguments (in=%d out=%d ldx=%d ldy=%d)", g.in, g.out, g.ldx,
+                             g.ldy);
+        if (segs.n == MW_MAXSEG) return set_error(K3C_EINVAL, "mmw: more than %d matrices", MW_MAXSEG);
+        segs.s[segs.n++] = g;
+    }
+    if (segs.n == 0) return K3C_OK;
+    return wdt == K3C_WBF16 ? launch_mmw_t<true>(segs, ntok, s) : launch_mmw_t<false>(segs, ntok, s);
 }
 
 int launch_mmw(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int wdt, int in, int out,
                int accumulate, cudaStream_t s) {
-    if (ntok <= 0 || out <= 0) return K3C_OK;
-    if (ntok > 32) return set_error(K3C_EINVAL, "mmw: ntok=%d > 32", ntok);
-    if (in <= 0 || !y || !x || !W || ldy < out || ldx < in)
-        return set_error(K3C_EINVAL, "mmw: bad arguments (in=%d out=%d ldx=%d ldy=%d)", in, out, ldx, ldy);
-    if (wdt == K3C_WBF16) return launch_mmw_t<true>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
-    if (wdt == K3C_WF32) return launch_mmw_t<false>(y, ldy, x, ldx, ntok, W, in, out, accumulate, s);
-    return set_error(K3C_EINVAL, "mmw: wdt=%d (int8 trunk rows run through k3c_q8_pack/k3c_q8_gemv)", wdt);
+    const MwSeg g = {x, W, y, ldx, ldy, in, out, accumulate, 0};
+    return launch_mmw_segs(&g, 1, ntok, wdt, s);
 }
 
 // ------------------------------------------------------------------ RMSNorm, SiTU-GLU
@@ -288,6 +333,12 @@ __global__ void __launch_bounds__(256) k_situ_rows(float *__restrict__ y, const 
     }
 }
 
+// y[i] = y[i] + d[i] (one float addition each), n elements.
+__global__ void __launch_bounds__(256) k_add_f32(float *__restrict__ y, const float *__restrict__ d, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __fadd_rn(y[i], d[i]);
+}
+
 // ------------------------------------------------------------------ the layer
 struct LatentBufs {
     double *rpart;     // router logit chunks
@@ -295,6 +346,7 @@ struct LatentBufs {
     float *agg;        // [ntok][latent] weighted expert sum, then normalised
     float *sgu;        // [ntok][2*SI]
     float *sact;       // [ntok][SI]
+    float *sdn;        // [ntok][hidden] shared expert output
     int *idx;          // [ntok][topk] when the caller passes none
     float *wt;
     void *tc;          // tensor-core decode scratch
@@ -309,11 +361,12 @@ static bool carve_latent(Carve &cv, LatentBufs &b, const k3c_moe_latent_layer *L
     b.agg = cv.take<float>((size_t)ntok * Lw);
     b.sgu = cv.take<float>((size_t)ntok * 2 * SI);
     b.sact = cv.take<float>((size_t)ntok * SI);
+    b.sdn = cv.take<float>((size_t)ntok * L->hidden);
     b.idx = cv.take<int>((size_t)ntok * L->experts.topk);
     b.wt = cv.take<float>((size_t)ntok * L->experts.topk);
     b.tc_bytes = moe_decode_tc_scratch(&L->experts, ntok);
     b.tc = cv.take<char>(b.tc_bytes, 1024);
-    return b.rpart && b.z && b.agg && b.sgu && b.sact && b.idx && b.wt && b.tc;
+    return b.rpart && b.z && b.agg && b.sgu && b.sact && b.sdn && b.idx && b.wt && b.tc;
 }
 
 static int check_latent(const k3c_moe_latent_layer *L, int ntok) {
@@ -362,8 +415,19 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
                           X.renorm, X.routed_scale, ntok, b.rpart, s));
     stage_end(STAGE_ROUTER, s);
     stage_begin(STAGE_Q8, s);   // trunk projections are reported with the trunk stage
-    // 2. z = down x
-    K3C_TRY(launch_mmw(b.z, Lw, x, H, ntok, L->down, L->wdt, H, Lw, 0, s));
+    // 2. z = down x, and the shared expert's gate and up projections of the same x in the same
+    //    launch (the shared branch depends on nothing else, so computing it first changes no
+    //    result)
+    const bool sh = L->n_shared > 0;
+    const MwSeg first[3] = {{x, L->down, b.z, H, Lw, H, Lw, 0, 0},
+                            {x, L->sh1, b.sgu, H, 2 * SI, H, sh ? SI : 0, 0, 0},
+                            {x, L->sh3, b.sgu + SI, H, 2 * SI, H, sh ? SI : 0, 0, 0}};
+    K3C_TRY(launch_mmw_segs(first, 3, ntok, L->wdt, s));
+    if (sh) {
+        dim3 gs((SI + 255) / 256 < 148 ? (SI + 255) / 256 : 148, ntok);
+        k_situ_rows<<<gs, 256, 0, s>>>(b.sact, b.sgu, SI, L->situ_b1, L->situ_b2);
+        K3C_CHECK_LAUNCH();
+    }
     stage_end(STAGE_Q8, s);
     // 3. routed experts at the latent width, weighted top-k-order sum
     K3C_TRY(launch_moe_decode_tc(b.agg, b.z, K3C_F32, ntok, &X, idx, wt, drops, b.tc, b.tc_bytes, s, true));
@@ -373,16 +437,16 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
         k_rmsnorm_rows<<<ntok, 256, 0, s>>>(b.agg, b.agg, L->latent_norm, Lw, L->rms_eps);
         K3C_CHECK_LAUNCH();
     }
-    // 5. out = up aggregate
-    K3C_TRY(launch_mmw(out, H, b.agg, Lw, ntok, L->up, L->wdt, Lw, H, 0, s));
-    // 6. shared expert at full width, added without a weight
-    if (L->n_shared > 0) {
-        K3C_TRY(launch_mmw(b.sgu, 2 * SI, x, H, ntok, L->sh1, L->wdt, H, SI, 0, s));
-        K3C_TRY(launch_mmw(b.sgu + SI, 2 * SI, x, H, ntok, L->sh3, L->wdt, H, SI, 0, s));
-        dim3 gs((SI + 255) / 256 < 148 ? (SI + 255) / 256 : 148, ntok);
-        k_situ_rows<<<gs, 256, 0, s>>>(b.sact, b.sgu, SI, L->situ_b1, L->situ_b2);
+    // 5. out = up aggregate, and the shared expert's down projection in the same launch (its
+    //    longer rows first); 6. out += shared output, one float addition per element, the
+    //    reference's `ot[i] += sdn[i]`
+    const MwSeg second[2] = {{b.sact, L->sh2, b.sdn, SI, H, SI, sh ? H : 0, 0, 0},
+                             {b.agg, L->up, out, Lw, H, Lw, H, 0, 0}};
+    K3C_TRY(launch_mmw_segs(second, 2, ntok, L->wdt, s));
+    if (sh) {
+        const size_t n = (size_t)ntok * H;
+        k_add_f32<<<(unsigned)((n + 255) / 256 < 296 ? (n + 255) / 256 : 296), 256, 0, s>>>(out, b.sdn, n);
         K3C_CHECK_LAUNCH();
-        K3C_TRY(launch_mmw(out, H, b.sact, SI, ntok, L->sh2, L->wdt, SI, H, 1, s));
     }
     stage_end(STAGE_Q8, s);
     return K3C_OK;
