@@ -14,11 +14,13 @@
 // memory as doubles, chunk by chunk, and every weight a thread loads is used for all of
 // them.
 //
-// The layer: route on the full-width input (the router of router.cu), z = down x, the
-// routed experts at the latent width through the tensor-core decode kernels with the routing
-// given (moe_pool.cu; their weighted top-k-order sum is the aggregate), RMSNorm of the
-// aggregate, out = up aggregate, then the full-width shared expert sh2(SiTU(sh1 x, sh3 x))
-// added without a weight.
+// The layer: route on the full-width input (the router of router.cu); one trunk launch for
+// z = down x and the shared expert's sh1 x, sh3 x (same input), then SiTU; the routed experts
+// at the latent width through the tensor-core decode kernels with the routing given
+// (moe_pool.cu; their weighted top-k-order sum is the aggregate); RMSNorm of the aggregate;
+// one trunk launch for sdn = sh2 SiTU(...) and out = up aggregate; out += sdn, one float add
+// per element. The shared branch depends only on x, so computing it early changes no bit of
+// the result against the reference's order of steps.
 #include <cuda_runtime.h>
 #include <math.h>
 
