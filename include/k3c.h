@@ -290,12 +290,14 @@ typedef struct {
     float rms_eps, situ_b1, situ_b2;
 } k3c_moe_latent_layer;
 
-/* k3_moe (src/core/k3_ops.c:556-656) for ntok <= 32 tokens: out [ntok][hidden] fp32 from x
- * [ntok][hidden] fp32. Per token: route on x; z = down x; the top-k experts on z at the
- * latent width, summed with their weights in top-k order (tensor-core decode kernels, the
- * activation as experts.terms E4M3 terms); RMSNorm of the sum; out = up sum; plus the
- * shared expert sh2(SiTU(sh1 x, sh3 x)) unweighted. idx/wt (device, may be NULL) receive
- * the routing [ntok][topk]; drops counts selected experts without a resident run. */
+/* k3_moe (src/core/k3_ops.c:556-656) for ntok <= 65535 tokens: out [ntok][hidden] fp32 from
+ * x [ntok][hidden] fp32. Per token: route on x; z = down x; the top-k experts on z at the
+ * latent width, summed with their weights in top-k order; RMSNorm of the sum; out = up sum;
+ * plus the shared expert sh2(SiTU(sh1 x, sh3 x)) unweighted. Up to 32 tokens the experts run
+ * on the tensor-core decode kernels (the activation as experts.terms E4M3 terms); more tokens
+ * run them on the prefill kernels (two E4M3 terms; the latent width must then be a multiple of
+ * 256) and the trunk matrices 32 tokens at a time. idx/wt (device, may be NULL) receive the
+ * routing [ntok][topk]; drops counts selected experts without a resident run. */
 size_t k3c_moe_latent_scratch(const k3c_moe_latent_layer *L, int ntok);
 int k3c_moe_latent_decode(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L,
                           int *idx, float *wt, int *drops, void *scratch, size_t scratch_bytes,

@@ -38,6 +38,10 @@ size_t moe_decode_tc_scratch(const k3c_moe_pool_layer *L, int ntok);
 int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const k3c_moe_pool_layer *L,
                          int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
                          cudaStream_t s, bool routed);
+size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contrib);
+int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k3c_moe_pool_layer *L,
+                          int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
+                          cudaStream_t s, bool routed, const k3c_ep_peers *ep);
 
 // ------------------------------------------------------------------ trunk matmul
 // Pipeline: the activations of a chunk of KC elements (all tokens) sit in shared memory as
@@ -342,12 +346,18 @@ __global__ void __launch_bounds__(256) k_add_f32(float *__restrict__ y, const fl
 }
 
 // ------------------------------------------------------------------ the layer
+// Up to LAT_CHUNK tokens go through the decode kernels and one trunk launch per step; more
+// tokens run the trunk matrices LAT_CHUNK tokens at a time and the routed experts through the
+// prefill kernels (each expert read once for all of its tokens).
+constexpr int LAT_CHUNK = 32;
+constexpr int LAT_MAX_TOKENS = 65535;
+
 struct LatentBufs {
     double *rpart;     // router logit chunks
     float *z;          // [ntok][latent]
     float *agg;        // [ntok][latent] weighted expert sum, then normalised
-    float *sgu;        // [ntok][2*SI]
-    float *sact;       // [ntok][SI]
+    float *sgu;        // [chunk][2*SI]
+    float *sact;       // [chunk][SI]
     float *sdn;        // [ntok][hidden] shared expert output
     int *idx;          // [ntok][topk] when the caller passes none
     float *wt;
@@ -358,15 +368,17 @@ struct LatentBufs {
 static bool carve_latent(Carve &cv, LatentBufs &b, const k3c_moe_latent_layer *L, int ntok) {
     const int SI = L->experts.inter * L->n_shared;
     const int Lw = L->experts.hidden;
+    const int C = ntok < LAT_CHUNK ? ntok : LAT_CHUNK;
     b.rpart = cv.take<double>(router_scratch_bytes(L->hidden, L->experts.n_experts, ntok) / sizeof(double) + 1);
     b.z = cv.take<float>((size_t)ntok * Lw);
     b.agg = cv.take<float>((size_t)ntok * Lw);
-    b.sgu = cv.take<float>((size_t)ntok * 2 * SI);
-    b.sact = cv.take<float>((size_t)ntok * SI);
+    b.sgu = cv.take<float>((size_t)C * 2 * SI);
+    b.sact = cv.take<float>((size_t)C * SI);
     b.sdn = cv.take<float>((size_t)ntok * L->hidden);
     b.idx = cv.take<int>((size_t)ntok * L->experts.topk);
     b.wt = cv.take<float>((size_t)ntok * L->experts.topk);
-    b.tc_bytes = moe_decode_tc_scratch(&L->experts, ntok);
+    b.tc_bytes = ntok <= LAT_CHUNK ? moe_decode_tc_scratch(&L->experts, ntok)
+                                   : moe_prefill_tc_scratch(&L->experts, ntok, true);
     b.tc = cv.take<char>(b.tc_bytes, 1024);
     return b.rpart && b.z && b.agg && b.sgu && b.sact && b.sdn && b.idx && b.wt && b.tc;
 }
@@ -374,7 +386,7 @@ static bool carve_latent(Carve &cv, LatentBufs &b, const k3c_moe_latent_layer *L
 static int check_latent(const k3c_moe_latent_layer *L, int ntok) {
     if (!L) return set_error(K3C_EINVAL, "moe_latent: null layer");
     const k3c_moe_pool_layer &X = L->experts;
-    if (ntok > 32) return set_error(K3C_EINVAL, "moe_latent: ntok=%d > 32", ntok);
+    if (ntok > LAT_MAX_TOKENS) return set_error(K3C_EINVAL, "moe_latent: ntok=%d > %d", ntok, LAT_MAX_TOKENS);
     if (L->hidden <= 0 || X.hidden <= 0 || X.inter <= 0 || L->n_shared < 0)
         return set_error(K3C_EINVAL, "moe_latent: hidden=%d latent=%d inter=%d n_shared=%d", L->hidden, X.hidden,
                          X.inter, L->n_shared);
@@ -416,11 +428,49 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
     K3C_TRY(launch_router(idx, wt, nullptr, x, K3C_F32, L->router_w, K3C_F32, L->router_bias, H, X.n_experts, K,
                           X.renorm, X.routed_scale, ntok, b.rpart, s));
     stage_end(STAGE_ROUTER, s);
+    const bool sh = L->n_shared > 0;
+    if (ntok > LAT_CHUNK) {
+        // the same steps for many tokens: trunk matrices (and the shared branch) 32 tokens at
+        // a time, the routed experts through the prefill kernels
+        stage_begin(STAGE_Q8, s);
+        for (int t0 = 0; t0 < ntok; t0 += LAT_CHUNK) {
+            const int c = ntok - t0 < LAT_CHUNK ? ntok - t0 : LAT_CHUNK;
+            const float *xc = x + (size_t)t0 * H;
+            const MwSeg first[3] = {{xc, L->down, b.z + (size_t)t0 * Lw, H, Lw, H, Lw, 0, 0},
+                                    {xc, L->sh1, b.sgu, H, 2 * SI, H, sh ? SI : 0, 0, 0},
+                                    {xc, L->sh3, b.sgu + SI, H, 2 * SI, H, sh ? SI : 0, 0, 0}};
+            K3C_TRY(launch_mmw_segs(first, 3, c, L->wdt, s));
+            if (sh) {
+                dim3 gs((SI + 255) / 256 < 148 ? (SI + 255) / 256 : 148, c);
+                k_situ_rows<<<gs, 256, 0, s>>>(b.sact, b.sgu, SI, L->situ_b1, L->situ_b2);
+                K3C_CHECK_LAUNCH();
+                K3C_TRY(launch_mmw(b.sdn + (size_t)t0 * H, H, b.sact, SI, c, L->sh2, L->wdt, SI, H, 0, s));
+            }
+        }
+        stage_end(STAGE_Q8, s);
+        K3C_TRY(launch_moe_prefill_tc(b.agg, b.z, K3C_F32, ntok, &X, idx, wt, drops, b.tc, b.tc_bytes, s, true,
+                                      nullptr));
+        stage_begin(STAGE_Q8, s);
+        if (L->latent_norm_on) {
+            k_rmsnorm_rows<<<ntok, 256, 0, s>>>(b.agg, b.agg, L->latent_norm, Lw, L->rms_eps);
+            K3C_CHECK_LAUNCH();
+        }
+        for (int t0 = 0; t0 < ntok; t0 += LAT_CHUNK) {
+            const int c = ntok - t0 < LAT_CHUNK ? ntok - t0 : LAT_CHUNK;
+            K3C_TRY(launch_mmw(out + (size_t)t0 * H, H, b.agg + (size_t)t0 * Lw, Lw, c, L->up, L->wdt, Lw, H, 0, s));
+        }
+        if (sh) {
+            const size_t n = (size_t)ntok * H;
+            k_add_f32<<<(unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, s>>>(out, b.sdn, n);
+            K3C_CHECK_LAUNCH();
+        }
+        stage_end(STAGE_Q8, s);
+        return K3C_OK;
+    }
     stage_begin(STAGE_Q8, s);   // trunk projections are reported with the trunk stage
     // 2. z = down x, and the shared expert's gate and up projections of the same x in the same
     //    launch (the shared branch depends on nothing else, so computing it first changes no
     //    result)
-    const bool sh = L->n_shared > 0;
     const MwSeg first[3] = {{x, L->down, b.z, H, Lw, H, Lw, 0, 0},
                             {x, L->sh1, b.sgu, H, 2 * SI, H, sh ? SI : 0, 0, 0},
                             {x, L->sh3, b.sgu + SI, H, 2 * SI, H, sh ? SI : 0, 0, 0}};

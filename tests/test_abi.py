@@ -153,7 +153,7 @@ int main(void) {
     ex.hidden, ex.inter, ex.n_experts, ex.topk, ex.act, ex.terms, ex.shared_run = 128, 128, 8, 2, 1, 3, -1
     dummy = 4096
     lay.router_w = lay.down = lay.up = lay.sh1 = lay.sh3 = lay.sh2 = lay.latent_norm = dummy
-    rc = L.k3c_moe_latent_decode(None, None, 33, C.byref(lay), None, None, None, None, 0, None)
+    rc = L.k3c_moe_latent_decode(None, None, 70000, C.byref(lay), None, None, None, None, 0, None)
     assert rc == -1 and b"ntok" in L.k3c_last_error()
     lay.wdt = 2
     rc = L.k3c_moe_latent_decode(None, None, 4, C.byref(lay), None, None, None, None, 0, None)
