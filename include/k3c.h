@@ -254,6 +254,64 @@ int k3c_moe_decode_tc_routed(float *out, const void *x, int x_dtype, int ntok,
                              int *drops, void *scratch, size_t scratch_bytes, k3c_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * Routed experts from the checkpoint's safetensors shards (src/io/k3_st.h, src/io/k3_load.h).
+ * Host functions except k3c_expert_upload; none of them allocates device memory.
+ * ------------------------------------------------------------------------------------ */
+/* Tensor element types of a shard (the reference's K3Dtype values, src/io/k3_st.h:35). */
+enum { K3C_DT_U8 = 1, K3C_DT_BF16 = 2, K3C_DT_F16 = 3, K3C_DT_F32 = 4 };
+typedef struct {
+    int shard, dtype, ndim;
+    int64_t off;          /* absolute byte offset in its shard file */
+    int64_t nbytes;
+    int64_t shape[4];
+} k3c_tensor;
+typedef struct k3c_ckpt k3c_ckpt;   /* the indexed shards of one checkpoint directory */
+/* k3_st_open / k3_st_close (src/io/k3_st.h:70-71): index every *.safetensors file of dir
+ * (shard i is the i-th name in sorted order). NULL on failure, k3c_last_error() says why:
+ * an impossible header length, a tensor whose byte span is not its shape's, a span past the
+ * end of the file, an unsupported dtype (U8, BF16, F16, F32 are read), a name twice. */
+k3c_ckpt *k3c_ckpt_open(const char *dir);
+void k3c_ckpt_close(k3c_ckpt *c);
+int k3c_ckpt_shards(const k3c_ckpt *c);
+/* 1 when the shard could be opened for O_DIRECT reads (expert reads then bypass the page
+ * cache); 0 when reads fall back to the buffered descriptor. */
+int k3c_ckpt_direct(const k3c_ckpt *c, int shard);
+/* k3_st_find (src/io/k3_st.h:76): K3C_ENOTFOUND when absent. */
+int k3c_ckpt_find(const k3c_ckpt *c, const char *name, k3c_tensor *t);
+
+/* K3QMat / K3ExpertRef (src/io/k3_load.h:29-45), same fields in the same order. */
+typedef struct {
+    int64_t p_off, p_bytes;   /* packed nibbles, offset within the run */
+    int64_t s_off, s_bytes;   /* E8M0 scales, offset within the run */
+    int rows, pcols, scols;
+} k3c_qmat;
+typedef struct {
+    int layer, expert, shard;
+    int64_t off, nbytes;      /* run start in the shard, run bytes */
+    int contiguous;           /* 1: the six tensors tile one span, read with one call */
+    k3c_qmat m[3];            /* w1, w2, w3 */
+} k3c_expert_run;
+/* k3_expert_ref (src/io/k3_load.c:15-105): resolve the six tensors of
+ * "language_model.model.layers.L.block_sparse_moe.experts.E.{w1,w2,w3}.{weight_packed,
+ * weight_scale}" and check them: U8, 2-D, equal row counts, one scale per 32 elements, one
+ * shard. A contiguous run keeps the file's offsets; otherwise the run is assembled in the
+ * order w1.packed w1.scale w2.packed w2.scale w3.packed w3.scale. */
+int k3c_expert_ref(const k3c_ckpt *c, int layer, int expert, k3c_expert_run *r);
+/* k3_expert_load_direct (src/io/k3_load.c:137-145): a contiguous run is one O_DIRECT read
+ * widened to 4096-byte boundaries, so buf must be page aligned and hold nbytes + 8192; the run
+ * then starts at buf + *payload_off (0 when the shard has no O_DIRECT descriptor). Scattered
+ * tensors are six buffered reads into the canonical order at buf. Returns payload bytes. */
+int64_t k3c_expert_read(const k3c_ckpt *c, const k3c_expert_run *r, void *buf, int64_t bufcap,
+                        int64_t *payload_off);
+/* Copy a run read by k3c_expert_read (payload = buf + payload_off; pinned memory makes the
+ * copy asynchronous) into dev_staging (r->nbytes device bytes) and pack it into the
+ * pool-format device run dev_run (k3c_pool_pack_expert): one routed expert from the
+ * checkpoint into an HBM pool slot or arena run. The tensors' offsets within the run must be
+ * multiples of 16 bytes, as they are for every K3 shape. */
+int k3c_expert_upload(uint8_t *dev_run, const k3c_expert_run *r, const void *payload,
+                      uint8_t *dev_staging, k3c_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * The K3 latent MoE layer (src/core/k3_ops.c:556-656) and its trunk operations.
  * ------------------------------------------------------------------------------------ */
 

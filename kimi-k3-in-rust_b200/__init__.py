@@ -60,6 +60,27 @@ class MoeLatentLayerC(C.Structure):
                 + [(n, C.c_float) for n in ("rms_eps", "situ_b1", "situ_b2")])
 
 
+class TensorC(C.Structure):
+    """Mirror of k3c_tensor (include/k3c.h)."""
+
+    _fields_ = [("shard", C.c_int), ("dtype", C.c_int), ("ndim", C.c_int), ("off", C.c_int64),
+                ("nbytes", C.c_int64), ("shape", C.c_int64 * 4)]
+
+
+class QMatC(C.Structure):
+    """Mirror of k3c_qmat (the reference's K3QMat)."""
+
+    _fields_ = [("p_off", C.c_int64), ("p_bytes", C.c_int64), ("s_off", C.c_int64),
+                ("s_bytes", C.c_int64), ("rows", C.c_int), ("pcols", C.c_int), ("scols", C.c_int)]
+
+
+class ExpertRunC(C.Structure):
+    """Mirror of k3c_expert_run (the reference's K3ExpertRef)."""
+
+    _fields_ = [("layer", C.c_int), ("expert", C.c_int), ("shard", C.c_int), ("off", C.c_int64),
+                ("nbytes", C.c_int64), ("contiguous", C.c_int), ("m", QMatC * 3)]
+
+
 EP_MAX = 8
 
 
@@ -159,6 +180,14 @@ def lib():
         "k3c_situ_glu": ([vp, vp, i, i, f, f, vp], i),
         "k3c_rmsnorm": ([vp, vp, vp, i, i, f, vp], i),
         "k3c_moe_latent_scratch": ([C.POINTER(MoeLatentLayerC), i], sz),
+        "k3c_ckpt_open": ([C.c_char_p], vp),
+        "k3c_ckpt_close": ([vp], None),
+        "k3c_ckpt_shards": ([vp], i),
+        "k3c_ckpt_direct": ([vp, i], i),
+        "k3c_ckpt_find": ([vp, C.c_char_p, C.POINTER(TensorC)], i),
+        "k3c_expert_ref": ([vp, i, i, C.POINTER(ExpertRunC)], i),
+        "k3c_expert_read": ([vp, C.POINTER(ExpertRunC), vp, C.c_int64, C.POINTER(C.c_int64)], C.c_int64),
+        "k3c_expert_upload": ([vp, C.POINTER(ExpertRunC), vp, vp, vp], i),
         "k3c_moe_latent_decode": ([vp, vp, i, C.POINTER(MoeLatentLayerC), vp, vp, vp, vp, sz, vp], i),
     }
     for name, (args, res) in sig.items():
@@ -800,3 +829,68 @@ class LatentMoeLayer:
                                            self._scratch.numel(), _stream()),
                "k3c_moe_latent_decode")
         return out, idx, wt
+
+
+# ------------------------------------------------------------------ checkpoint experts
+CKPT_ALIGN = 4096
+
+
+def aligned_host_buffer(nbytes, align=CKPT_ALIGN):
+    """A numpy uint8 buffer of nbytes whose address is a multiple of align (for O_DIRECT)."""
+    raw = np.empty(nbytes + align, np.uint8)
+    off = (-raw.ctypes.data) % align
+    return raw[off:off + nbytes]
+
+
+class Checkpoint:
+    """The safetensors shards of one checkpoint directory (k3c_ckpt_*): tensor lookup and
+    routed-expert runs read from the files (O_DIRECT where the file system allows it) and
+    uploaded into pool-format device runs."""
+
+    def __init__(self, directory):
+        self.h = lib().k3c_ckpt_open(os.fsencode(directory))
+        if not self.h:
+            raise K3CError(f"k3c_ckpt_open({directory}): {lib().k3c_last_error().decode()}")
+
+    def close(self):
+        if self.h:
+            lib().k3c_ckpt_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def shards(self):
+        return lib().k3c_ckpt_shards(self.h)
+
+    def direct(self, shard):
+        return bool(lib().k3c_ckpt_direct(self.h, shard))
+
+    def find(self, name):
+        t = TensorC()
+        _check(lib().k3c_ckpt_find(self.h, name.encode(), C.byref(t)), "k3c_ckpt_find")
+        return t
+
+    def expert_ref(self, layer, expert):
+        r = ExpertRunC()
+        _check(lib().k3c_expert_ref(self.h, layer, expert, C.byref(r)), "k3c_expert_ref")
+        return r
+
+    def read_expert(self, run, buf=None):
+        """The run's bytes (a view into buf, a page-aligned host buffer of at least
+        run.nbytes + 8192 bytes; allocated when None)."""
+        if buf is None:
+            buf = aligned_host_buffer(run.nbytes + 2 * CKPT_ALIGN)
+        po = C.c_int64(0)
+        n = lib().k3c_expert_read(self.h, C.byref(run), C.c_void_p(buf.ctypes.data), buf.size, C.byref(po))
+        if n != run.nbytes:
+            raise K3CError(f"k3c_expert_read: {lib().k3c_last_error().decode()}")
+        return buf[po.value:po.value + n]
+
+    def upload(self, run, payload, dev_run, dev_staging):
+        """Pack a run read by read_expert into the pool-format device run dev_run (a torch
+        uint8 view of pool_run_bytes bytes), through dev_staging (run.nbytes device bytes)."""
+        ptr = payload.data_ptr() if hasattr(payload, "data_ptr") else payload.ctypes.data
+        _check(lib().k3c_expert_upload(_ptr(dev_run), C.byref(run), C.c_void_p(ptr), _ptr(dev_staging),
+                                       _stream()), "k3c_expert_upload")

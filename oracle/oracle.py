@@ -123,6 +123,9 @@ def ref():
                                      C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
                                      _i32p, _f32p]
         L.refh_threads.restype = C.c_int
+        L.refh_expert_read.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_longlong,
+                                       C.c_void_p, C.POINTER(C.c_longlong)]
+        L.refh_expert_read.restype = C.c_longlong
         _ref = L
     return _ref
 
@@ -322,3 +325,20 @@ def situ_glu(gu, b1=4.0, b2=25.0):
         lib().ora_situ_glu(y, np.ascontiguousarray(rows[r]), n, b1, b2)
         out[r] = y
     return out
+
+
+def ref_expert_read(directory, layer, expert, run_struct_type, cap):
+    """The reference's own k3_st_open + k3_expert_ref + k3_expert_load_direct. Returns
+    (status, run, payload bytes): status -1 when the shards do not open, -2 when the expert is
+    rejected, else the bytes read. run_struct_type is a ctypes mirror of K3ExpertRef."""
+    import os as _os
+    raw = np.empty(cap + 4096, np.uint8)
+    off = (-raw.ctypes.data) % 4096
+    buf = raw[off:off + cap]
+    run = run_struct_type()
+    po = C.c_longlong(0)
+    n = ref().refh_expert_read(_os.fsencode(directory), layer, expert, buf.ctypes.data, cap,
+                               C.addressof(run), C.byref(po))
+    if n < 0:
+        return int(n), None, None
+    return int(n), run, buf[po.value:po.value + n].copy()

@@ -16,10 +16,12 @@
  * bench.py times refh_moe_layer as the reference arm (cpu_baseline kind "reference").
  */
 #include <math.h>
+#include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 
 #include "k3.h"
+#include "k3_load.h"
 
 static float refh_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
 
@@ -157,6 +159,25 @@ int refh_moe_latent(float *out, const float *x, int ntok, const float *router_w,
     }
     free(idx); free(wt); free(scratch);
     return 0;
+}
+
+/* The reference's own shard index and expert loader on a checkpoint directory: k3_st_open,
+ * k3_expert_ref and k3_expert_load_direct (src/io/k3_st.c, src/io/k3_load.c). Returns the
+ * payload bytes read, -1 when k3_st_open fails, -2 when k3_expert_ref rejects the expert. */
+long long refh_expert_read(const char *dir, int layer, int expert, unsigned char *buf, long long cap,
+                           K3ExpertRef *ref_out, long long *payload_off)
+{
+    K3St s;
+    memset(&s, 0, sizeof s);
+    if (k3_st_open(&s, dir) != 0) return -1;
+    K3ExpertRef r;
+    if (k3_expert_ref(&s, layer, expert, &r) != 0) { k3_st_close(&s); return -2; }
+    if (ref_out) *ref_out = r;
+    int64_t po = 0;
+    const int64_t n = k3_expert_load_direct(&s, &r, buf, cap, &po);
+    if (payload_off) *payload_off = po;
+    k3_st_close(&s);
+    return (long long)n;
 }
 
 /* Thread count the reference's OpenMP loops will use, for the cpu_baseline record. */

@@ -1,0 +1,81 @@
+"""A small safetensors writer for tests: shards laid out exactly as asked (tensor order,
+filler tensors between them), so the expert loader meets contiguous, reordered, scattered and
+cross-shard runs. Test infrastructure only."""
+import json
+import os
+import struct
+
+import numpy as np
+
+EXPERT = "language_model.model.layers.{}.block_sparse_moe.experts.{}.{}.{}"
+_DT = {np.uint8: "U8", np.float32: "F32", np.uint16: "BF16", np.float16: "F16"}
+
+
+def write_shard(path, tensors, metadata=None, header_pad=0):
+    """tensors: list of (name, numpy array, dtype string or None) written in list order,
+    back to back. header_pad adds spaces to the JSON header (shifts every data offset)."""
+    hdr, off, blobs = {}, 0, []
+    if metadata is not None:
+        hdr["__metadata__"] = metadata
+    for name, a, dt in tensors:
+        a = np.ascontiguousarray(a)
+        b = a.tobytes()
+        hdr[name] = {"dtype": dt or _DT[a.dtype.type], "shape": list(a.shape),
+                     "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    js = json.dumps(hdr).encode() + b" " * header_pad
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(js)))
+        f.write(js)
+        for b in blobs:
+            f.write(b)
+
+
+def expert_tensors(g, layer, expert, hidden, inter, order=("w1", "w2", "w3")):
+    """The six tensors of one expert (packed U8 [rows][cols/2], scales U8 [rows][cols/32]) in
+    the given matrix order, and their canonical run bytes (w1.p w1.s w2.p w2.s w3.p w3.s)."""
+    shapes = {"w1": (inter, hidden), "w3": (inter, hidden), "w2": (hidden, inter)}
+    arrs = {}
+    for w, (r, c) in shapes.items():
+        arrs[w] = (g.integers(0, 256, (r, c // 2), dtype=np.uint8),
+                   g.integers(118, 125, (r, c // 32), dtype=np.uint8))
+    out = []
+    for w in order:
+        out.append((EXPERT.format(layer, expert, w, "weight_packed"), arrs[w][0], None))
+        out.append((EXPERT.format(layer, expert, w, "weight_scale"), arrs[w][1], None))
+    canon = b"".join(arrs[w][0].tobytes() + arrs[w][1].tobytes() for w in ("w1", "w2", "w3"))
+    expert_dict = dict(gate_p=arrs["w1"][0], gate_s=arrs["w1"][1], up_p=arrs["w3"][0],
+                       up_s=arrs["w3"][1], down_p=arrs["w2"][0], down_s=arrs["w2"][1])
+    return out, canon, expert_dict
+
+
+def build_checkpoint(d, g, hidden=256, inter=128):
+    """Two shards. Layer 1 experts: 0 contiguous in canonical order after an odd-sized filler
+    (an unaligned run start); 1 contiguous with its matrices in the order w3, w1, w2; 2 with a
+    filler between w1 and w2 (scattered); 3 with w3 in the second shard. Layer 2 expert 0
+    contiguous in the second shard. Returns {(layer, expert): (canonical bytes, expert dict)}."""
+    os.makedirs(d, exist_ok=True)
+    want = {}
+    a, b = [], []
+    a.append(("model.filler_a", g.integers(0, 256, 37, dtype=np.uint8), None))
+    t, c, e = expert_tensors(g, 1, 0, hidden, inter)
+    a += t
+    want[(1, 0)] = (c, e)
+    t, c, e = expert_tensors(g, 1, 1, hidden, inter, order=("w3", "w1", "w2"))
+    a += t
+    want[(1, 1)] = (c, e)
+    t, c, e = expert_tensors(g, 1, 2, hidden, inter)
+    a += t[:2] + [("model.filler_b", np.arange(5, dtype=np.float32), None)] + t[2:]
+    want[(1, 2)] = (c, e)
+    t, c, e = expert_tensors(g, 1, 3, hidden, inter)
+    a += t[:4]
+    b += t[4:]
+    a.append(("model.norm_bf16", np.arange(7, dtype=np.uint16), "BF16"))
+    t, c, e = expert_tensors(g, 2, 0, hidden, inter)
+    b = [("model.filler_c", g.integers(0, 256, 4099, dtype=np.uint8), None)] + b + t
+    want[(2, 0)] = (c, e)
+    write_shard(os.path.join(d, "model-00001-of-00002.safetensors"), a,
+                metadata={"format": "pt", "note": 'a {nested} "value", [1, 2]'}, header_pad=3)
+    write_shard(os.path.join(d, "model-00002-of-00002.safetensors"), b)
+    return want

@@ -1,0 +1,106 @@
+"""Routed experts read from safetensors shards (k3c_ckpt_*, k3c_expert_ref / _read) against
+the reference's own shard index and expert loader (k3_st_open, k3_expert_ref,
+k3_expert_load_direct compiled into oracle/_ref) and against the bytes the test wrote."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from ckpt_util import EXPERT, build_checkpoint, write_shard
+
+REF = pytest.mark.skipif("not __import__('oracle.oracle', fromlist=['x']).ref_available()")
+
+
+@pytest.fixture(scope="module")
+def ckpt_dir(tmp_path_factory, k3):
+    d = str(tmp_path_factory.mktemp("ckpt"))
+    want = build_checkpoint(d, k3.synth.rng(2026))
+    return d, want
+
+
+def test_index_and_find(k3, ckpt_dir):
+    d, _ = ckpt_dir
+    ck = k3.Checkpoint(d)
+    assert ck.shards == 2
+    t = ck.find("model.norm_bf16")
+    assert (t.shard, t.dtype, t.ndim, t.shape[0], t.nbytes) == (0, 2, 1, 7, 14)   # K3C_DT_BF16
+    t = ck.find(EXPERT.format(2, 0, "w2", "weight_scale"))
+    assert t.shard == 1 and t.ndim == 2 and (t.shape[0], t.shape[1]) == (256, 4)
+    with pytest.raises(k3.K3CError):
+        ck.find("model.absent")
+    ck.close()
+
+
+def test_expert_runs_match_written_bytes(k3, ckpt_dir):
+    d, want = ckpt_dir
+    ck = k3.Checkpoint(d)
+    for (layer, expert), (canon, _) in want.items():
+        r = ck.expert_ref(layer, expert)
+        payload = ck.read_expert(r)
+        # assemble the canonical order from the run's own offsets
+        got = b"".join(payload[r.m[i].p_off:r.m[i].p_off + r.m[i].p_bytes].tobytes() +
+                       payload[r.m[i].s_off:r.m[i].s_off + r.m[i].s_bytes].tobytes() for i in range(3))
+        assert got == canon
+        assert r.nbytes == len(canon)
+    assert ck.expert_ref(1, 0).contiguous == 1 and ck.expert_ref(1, 1).contiguous == 1
+    assert ck.expert_ref(1, 2).contiguous == 0
+    assert ck.expert_ref(1, 1).m[2].p_off == 0          # w3 first in the file
+    with pytest.raises(k3.K3CError, match="spans shards"):
+        ck.expert_ref(1, 3)
+    with pytest.raises(k3.K3CError, match="missing"):
+        ck.expert_ref(1, 9)
+
+
+@REF
+def test_expert_runs_match_reference_loader(k3, ora, ckpt_dir):
+    d, want = ckpt_dir
+    ck = k3.Checkpoint(d)
+    for layer, expert in list(want) + [(1, 3), (1, 9)]:
+        st, rr, rb = ora.ref_expert_read(d, layer, expert, k3.ExpertRunC, 1 << 20)
+        try:
+            r = ck.expert_ref(layer, expert)
+        except k3.K3CError:
+            assert st == -2, (layer, expert)
+            continue
+        assert st == r.nbytes
+        assert bytes(r) == bytes(rr)                    # every field of K3ExpertRef
+        assert ck.read_expert(r).tobytes() == rb.tobytes()
+
+
+def _bad(d, name, tensors, hdr_len=None, **kw):
+    os.makedirs(d, exist_ok=True)
+    p = os.path.join(d, name)
+    write_shard(p, tensors, **kw)
+    if hdr_len is not None:
+        with open(p, "r+b") as f:
+            f.write(int(hdr_len).to_bytes(8, "little"))
+    return d
+
+
+@pytest.mark.parametrize("case", ["hdr_len", "span", "eof", "dtype", "dup"])
+def test_malformed_shards_are_rejected(k3, ora, tmp_path, case):
+    d = str(tmp_path / case)
+    a = np.arange(16, dtype=np.uint8)
+    if case == "hdr_len":
+        _bad(d, "m.safetensors", [("x", a, None)], hdr_len=1 << 40)
+    elif case == "span":       # shape says 4 bytes, the offsets 16
+        _bad(d, "m.safetensors", [("x", a, None)])
+        p = os.path.join(d, "m.safetensors")
+        raw = open(p, "rb").read().replace(b'"shape": [16]', b'"shape": [4] ')
+        open(p, "wb").write(raw)
+    elif case == "eof":
+        _bad(d, "m.safetensors", [("x", a, None)])
+        p = os.path.join(d, "m.safetensors")
+        raw = open(p, "rb").read()
+        open(p, "wb").write(raw[:-3])
+    elif case == "dtype":
+        _bad(d, "m.safetensors", [("x", a.view(np.uint64), "F64")])
+    else:                      # the same name in two shards
+        _bad(d, "a.safetensors", [("x", a, None)])
+        _bad(d, "b.safetensors", [("x", a, None)])
+    with pytest.raises(k3.K3CError):
+        k3.Checkpoint(d)
+    if ora.ref_available():
+        st, _, _ = ora.ref_expert_read(d, 0, 0, k3.ExpertRunC, 4096)
+        assert st == -1
