@@ -80,8 +80,15 @@ int k3c_timing_read(double *ms, long long *count, int nstage);
 enum { K3C_F32 = 0, K3C_BF16 = 1 };
 /* Expert activation functions. */
 enum { K3C_ACT_SWIGLU = 0, K3C_ACT_SITU = 1 };
-/* Trunk weight types, the reference's K3_WF32 / K3_WBF16 (include/k3/k3.h:270). */
-enum { K3C_WF32 = 0, K3C_WBF16 = 1 };
+/* Trunk weight types, the reference's K3_WF32 / K3_WBF16 / K3_WI8 (include/k3/k3.h:270). */
+enum { K3C_WF32 = 0, K3C_WBF16 = 1, K3C_WI8 = 2 };
+/* A per-row int8 trunk matrix in the layout k3c_q8_pack makes (device arrays): the draft
+ * model's K3_WI8 weights (rows [f32 scale][int8 * in] in its files, tools/int8_trunk.py:33-45). */
+typedef struct {
+    const int8_t *wq;       /* [out][ldw] */
+    const float *wscale;    /* [out] */
+    int ldw;
+} k3c_q8_mat;
 
 /* ====================================================================================
  * 1. DROP-IN ENTRY POINTS (host pointers)
@@ -335,7 +342,9 @@ int k3c_rmsnorm(float *y, const float *x, const float *w, int n, int ntok, float
  * experts.inter = moe_inter; its n_experts, topk, renorm, routed_scale, act and terms apply;
  * its router fields are not used; shared_run must be -1). The trunk matrices have type
  * wdt: down [latent][hidden], up [hidden][latent], sh1/sh3 [inter*n_shared][hidden],
- * sh2 [hidden][inter*n_shared]. All pointers are device addresses. */
+ * sh2 [hidden][inter*n_shared]; device addresses for K3C_WF32 / K3C_WBF16 (matmuls in the
+ * reference's order, bit-exact), and for K3C_WI8 (the draft model) each is the address of a
+ * host k3c_q8_mat (the int8 tensor-core GEMV, exact int32 sums, one scale per row). */
 typedef struct {
     int hidden;
     k3c_moe_pool_layer experts;

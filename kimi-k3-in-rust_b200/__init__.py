@@ -50,6 +50,12 @@ class MoePoolLayerC(C.Structure):
                 ("run_of", C.c_void_p), ("shared_run", C.c_int), ("terms", C.c_int)]
 
 
+class Q8MatC(C.Structure):
+    """Mirror of k3c_q8_mat (include/k3c.h): a packed int8 trunk matrix on the device."""
+
+    _fields_ = [("wq", C.c_void_p), ("wscale", C.c_void_p), ("ldw", C.c_int)]
+
+
 class MoeLatentLayerC(C.Structure):
     """Mirror of k3c_moe_latent_layer (include/k3c.h)."""
 
@@ -720,7 +726,7 @@ class _PoolArena:
 
 
 # ------------------------------------------------------------------ K3 latent MoE layer
-WF32, WBF16 = 0, 1
+WF32, WBF16, WI8 = 0, 1, 2
 
 
 def mmw(x, W, wdt, out=None, accumulate=False):
@@ -772,7 +778,11 @@ class LatentMoeLayer:
         ex = MoePoolLayerC(latent, inter, run_of.numel(), topk, renorm, ACT_SITU, routed_scale,
                            router_w.data_ptr(), K3C_F32, None, arena.data_ptr(),
                            pool_run_bytes(latent, inter), n_runs, run_of.data_ptr(), -1, terms)
-        p = lambda t: None if t is None else t.data_ptr()   # noqa: E731
+
+        def p(t):   # a device tensor's address, or the host address of a k3c_q8_mat (WI8)
+            if t is None:
+                return None
+            return C.addressof(t) if isinstance(t, Q8MatC) else t.data_ptr()
         self.c = MoeLatentLayerC(hidden, ex, p(router_w), p(router_bias), p(down), p(up), p(sh1),
                                  p(sh3), p(sh2), p(latent_norm), wdt, n_shared, latent_norm_on,
                                  rms_eps, situ_b1, situ_b2)
@@ -788,8 +798,18 @@ class LatentMoeLayer:
         t = lambda a, dt=None: None if a is None else torch.from_numpy(   # noqa: E731
             np.ascontiguousarray(a if dt is None else a.astype(dt))).to(dev)
         wdt = int(layer["wdt"])
-        conv = (lambda a: t(a.view(np.int16))) if wdt == WBF16 else (lambda a: t(a, np.float32))
         Lw, I = int(layer["latent"]), int(layer["inter"])
+        keep = []
+
+        def conv(a):
+            if wdt == WBF16:
+                return t(a.view(np.int16))
+            if wdt == WI8:   # reference rows [f32 scale][int8 * in] -> packed on the device
+                out_, row = a.shape
+                wq, ws, ldw = q8_pack(t(np.ascontiguousarray(a, np.uint8)), row - 4, out_)
+                keep.append((wq, ws))
+                return Q8MatC(wq.data_ptr(), ws.data_ptr(), ldw)
+            return t(a, np.float32)
         run = pool_run_bytes(Lw, I)
         experts = layer["experts"]
         arena = torch.empty(len(experts) * run, dtype=torch.uint8, device=dev)
@@ -798,14 +818,16 @@ class LatentMoeLayer:
             pool_pack(arena[i * run:(i + 1) * run], de.q(), Lw, I)
         torch.cuda.current_stream(dev).synchronize()
         run_of = torch.arange(len(experts), dtype=torch.int32, device=dev)
-        return cls(arena, len(experts), run_of, t(layer["router_w"], np.float32),
-                   t(layer.get("router_bias"), np.float32), conv(layer["down"]), conv(layer["up"]),
-                   conv(layer["sh1"]), conv(layer["sh3"]), conv(layer["sh2"]),
-                   t(layer["latent_norm"], np.float32), wdt, int(layer["hidden"]), Lw, I,
-                   int(layer["n_shared"]), int(layer["topk"]), terms=terms,
-                   renorm=int(layer["renorm"]), routed_scale=float(layer["routed_scale"]),
-                   latent_norm_on=int(layer["latent_norm_on"]), rms_eps=float(layer["rms_eps"]),
-                   situ_b1=float(layer["situ_b1"]), situ_b2=float(layer["situ_b2"]))
+        obj = cls(arena, len(experts), run_of, t(layer["router_w"], np.float32),
+                  t(layer.get("router_bias"), np.float32), conv(layer["down"]), conv(layer["up"]),
+                  conv(layer["sh1"]), conv(layer["sh3"]), conv(layer["sh2"]),
+                  t(layer["latent_norm"], np.float32), wdt, int(layer["hidden"]), Lw, I,
+                  int(layer["n_shared"]), int(layer["topk"]), terms=terms,
+                  renorm=int(layer["renorm"]), routed_scale=float(layer["routed_scale"]),
+                  latent_norm_on=int(layer["latent_norm_on"]), rms_eps=float(layer["rms_eps"]),
+                  situ_b1=float(layer["situ_b1"]), situ_b2=float(layer["situ_b2"]))
+        obj._packed = keep   # the int8 arrays the k3c_q8_mat records point at
+        return obj
 
     def scratch_bytes(self, ntok):
         return lib().k3c_moe_latent_scratch(C.byref(self.c), ntok)

@@ -39,6 +39,8 @@ int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const
                          int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
                          cudaStream_t s, bool routed);
 size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contrib);
+int launch_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok, const int8_t *wq,
+                   const float *wscale, int ldw, int in, int out, cudaStream_t s);
 int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k3c_moe_pool_layer *L,
                           int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
                           cudaStream_t s, bool routed, const k3c_ep_peers *ep);
@@ -339,6 +341,21 @@ __global__ void __launch_bounds__(256) k_situ_rows(float *__restrict__ y, const 
     }
 }
 
+// The trunk matrices of one step: fp32 / bf16 through the batched k_mmw grid; int8 rows (the
+// draft model) one k3c_q8_gemv each, W being the address of a host k3c_q8_mat.
+static int trunk_segs(const MwSeg *list, int n, int ntok, int wdt, cudaStream_t s) {
+    if (wdt != K3C_WI8) return launch_mmw_segs(list, n, ntok, wdt, s);
+    for (int i = 0; i < n; i++) {
+        const MwSeg &g = list[i];
+        if (g.out <= 0) continue;
+        const k3c_q8_mat *m = static_cast<const k3c_q8_mat *>(g.W);
+        if (!m || !m->wq || !m->wscale || g.accumulate)
+            return set_error(K3C_EINVAL, "moe_latent: int8 trunk matrix %d is not a k3c_q8_mat", i);
+        K3C_TRY(launch_q8_gemv(g.y, g.ldy, g.x, K3C_F32, g.ldx, ntok, m->wq, m->wscale, m->ldw, g.in, g.out, s));
+    }
+    return K3C_OK;
+}
+
 // y[i] = y[i] + d[i] (one float addition each), n elements.
 __global__ void __launch_bounds__(256) k_add_f32(float *__restrict__ y, const float *__restrict__ d, size_t n) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -390,7 +407,8 @@ static int check_latent(const k3c_moe_latent_layer *L, int ntok) {
     if (L->hidden <= 0 || X.hidden <= 0 || X.inter <= 0 || L->n_shared < 0)
         return set_error(K3C_EINVAL, "moe_latent: hidden=%d latent=%d inter=%d n_shared=%d", L->hidden, X.hidden,
                          X.inter, L->n_shared);
-    if (L->wdt != K3C_WF32 && L->wdt != K3C_WBF16) return set_error(K3C_EINVAL, "moe_latent: wdt=%d", L->wdt);
+    if (L->wdt != K3C_WF32 && L->wdt != K3C_WBF16 && L->wdt != K3C_WI8)
+        return set_error(K3C_EINVAL, "moe_latent: wdt=%d", L->wdt);
     if (!L->router_w || !L->down || !L->up || (L->n_shared > 0 && (!L->sh1 || !L->sh3 || !L->sh2)) ||
         (L->latent_norm_on && !L->latent_norm))
         return set_error(K3C_EINVAL, "moe_latent: missing weights");
@@ -439,12 +457,13 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
             const MwSeg first[3] = {{xc, L->down, b.z + (size_t)t0 * Lw, H, Lw, H, Lw, 0, 0},
                                     {xc, L->sh1, b.sgu, H, 2 * SI, H, sh ? SI : 0, 0, 0},
                                     {xc, L->sh3, b.sgu + SI, H, 2 * SI, H, sh ? SI : 0, 0, 0}};
-            K3C_TRY(launch_mmw_segs(first, 3, c, L->wdt, s));
+            K3C_TRY(trunk_segs(first, 3, c, L->wdt, s));
             if (sh) {
                 dim3 gs((SI + 255) / 256 < 148 ? (SI + 255) / 256 : 148, c);
                 k_situ_rows<<<gs, 256, 0, s>>>(b.sact, b.sgu, SI, L->situ_b1, L->situ_b2);
                 K3C_CHECK_LAUNCH();
-                K3C_TRY(launch_mmw(b.sdn + (size_t)t0 * H, H, b.sact, SI, c, L->sh2, L->wdt, SI, H, 0, s));
+                const MwSeg down2 = {b.sact, L->sh2, b.sdn + (size_t)t0 * H, SI, H, SI, H, 0, 0};
+                K3C_TRY(trunk_segs(&down2, 1, c, L->wdt, s));
             }
         }
         stage_end(STAGE_Q8, s);
@@ -457,7 +476,8 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
         }
         for (int t0 = 0; t0 < ntok; t0 += LAT_CHUNK) {
             const int c = ntok - t0 < LAT_CHUNK ? ntok - t0 : LAT_CHUNK;
-            K3C_TRY(launch_mmw(out + (size_t)t0 * H, H, b.agg + (size_t)t0 * Lw, Lw, c, L->up, L->wdt, Lw, H, 0, s));
+            const MwSeg up = {b.agg + (size_t)t0 * Lw, L->up, out + (size_t)t0 * H, Lw, H, Lw, H, 0, 0};
+            K3C_TRY(trunk_segs(&up, 1, c, L->wdt, s));
         }
         if (sh) {
             const size_t n = (size_t)ntok * H;
@@ -474,7 +494,7 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
     const MwSeg first[3] = {{x, L->down, b.z, H, Lw, H, Lw, 0, 0},
                             {x, L->sh1, b.sgu, H, 2 * SI, H, sh ? SI : 0, 0, 0},
                             {x, L->sh3, b.sgu + SI, H, 2 * SI, H, sh ? SI : 0, 0, 0}};
-    K3C_TRY(launch_mmw_segs(first, 3, ntok, L->wdt, s));
+    K3C_TRY(trunk_segs(first, 3, ntok, L->wdt, s));
     if (sh) {
         dim3 gs((SI + 255) / 256 < 148 ? (SI + 255) / 256 : 148, ntok);
         k_situ_rows<<<gs, 256, 0, s>>>(b.sact, b.sgu, SI, L->situ_b1, L->situ_b2);
@@ -494,7 +514,7 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
     //    reference's `ot[i] += sdn[i]`
     const MwSeg second[2] = {{b.sact, L->sh2, b.sdn, SI, H, SI, sh ? H : 0, 0, 0},
                              {b.agg, L->up, out, Lw, H, Lw, H, 0, 0}};
-    K3C_TRY(launch_mmw_segs(second, 2, ntok, L->wdt, s));
+    K3C_TRY(trunk_segs(second, 2, ntok, L->wdt, s));
     if (sh) {
         const size_t n = (size_t)ntok * H;
         k_add_f32<<<(unsigned)((n + 255) / 256 < 296 ? (n + 255) / 256 : 296), 256, 0, s>>>(out, b.sdn, n);

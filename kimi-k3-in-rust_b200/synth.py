@@ -148,10 +148,19 @@ def latent_layer(g: np.random.Generator, hidden: int, latent: int, inter: int,
     [n_experts][hidden] (spread so routing is decisive), routed MXFP4 experts at the latent
     width (``experts``), trunk matrices down [latent][hidden], up [hidden][latent],
     sh1/sh3 [inter*n_shared][hidden], sh2 [hidden][inter*n_shared] as bf16 bit patterns
-    (wdt=1) or fp32 (wdt=0), each ~N(0, 1/in), and latent-norm weights near 1."""
+    (wdt=1), fp32 (wdt=0), each ~N(0, 1/in), or per-row int8 in the reference's row layout
+    [f32 scale][int8 * in] (wdt=2, the draft model's trunk; scale ~ 1/(64 sqrt(in)) so the
+    rows have the same spread), and latent-norm weights near 1."""
     SI = inter * n_shared
 
     def trunk(out_, in_):
+        if wdt == 2:
+            w = g.integers(-127, 128, size=(out_, in_), dtype=np.int8)
+            sc = (g.uniform(0.5, 1.5, out_) / (64 * np.sqrt(in_))).astype(np.float32)
+            rows = np.empty((out_, 4 + in_), np.uint8)
+            rows[:, :4] = sc.view(np.uint8).reshape(out_, 4)
+            rows[:, 4:] = w.view(np.uint8)
+            return rows
         w = g.standard_normal((out_, in_), dtype=np.float32) * np.float32(1.0 / np.sqrt(in_))
         return bf16_bits(w) if wdt == 1 else w
 

@@ -155,7 +155,7 @@ int main(void) {
     lay.router_w = lay.down = lay.up = lay.sh1 = lay.sh3 = lay.sh2 = lay.latent_norm = dummy
     rc = L.k3c_moe_latent_decode(None, None, 70000, C.byref(lay), None, None, None, None, 0, None)
     assert rc == -1 and b"ntok" in L.k3c_last_error()
-    lay.wdt = 2
+    lay.wdt = 3
     rc = L.k3c_moe_latent_decode(None, None, 4, C.byref(lay), None, None, None, None, 0, None)
     assert rc == -1 and b"wdt" in L.k3c_last_error()
     lay.wdt, ex.shared_run = 1, 0

@@ -99,7 +99,7 @@ def test_latent_layer_matches_reference_k3_moe(k3, golden, golden_gen, dev):
     assert maxrel(out.cpu().numpy(), r["out"]) < 2e-2
 
 
-@pytest.mark.parametrize("ntok,wdt", [(1, 1), (16, 1), (32, 0), (100, 1), (300, 0)])
+@pytest.mark.parametrize("ntok,wdt", [(1, 1), (16, 1), (32, 0), (100, 1), (300, 0), (16, 2), (70, 2)])
 def test_latent_layer_vs_oracle(k3, ora, dev, ntok, wdt):
     g = k3.synth.rng(100 + ntok)
     layer = k3.synth.latent_layer(g, 1024, 512, 256, 32, 4, n_shared=2, wdt=wdt)

@@ -72,3 +72,17 @@ def test_latent_live_reference_fp32_trunk(ora, k3):
     b = ora.moe_latent(x, layer, use_ref=True)
     for u, v in zip(a, b):
         assert np.array_equal(u, v)
+
+
+@REF
+def test_latent_live_reference_int8_trunk(ora, k3):
+    # the draft model's trunk: per-row int8 rows through k3_matmul_q8. The reference states no
+    # determinism contract for that kernel (float sums), so the bar is a tolerance and the
+    # routing, which runs on the fp32 input, is exact.
+    g = k3.synth.rng(63)
+    layer = k3.synth.latent_layer(g, 384, 256, 128, 16, 4, n_shared=2, wdt=2)
+    x = g.standard_normal((3, 384), dtype=np.float32)
+    a, ai, aw = ora.moe_latent(x, layer)
+    b, bi, bw = ora.moe_latent(x, layer, use_ref=True)
+    assert np.array_equal(ai, bi) and np.array_equal(aw, bw)
+    assert np.abs(a - b).max() <= 1e-5 * np.abs(b).max()
