@@ -306,7 +306,8 @@ typedef struct {
 int k3c_expert_ref(const k3c_ckpt *c, int layer, int expert, k3c_expert_run *r);
 /* k3_expert_load_direct (src/io/k3_load.c:137-145): a contiguous run is one O_DIRECT read
  * widened to 4096-byte boundaries, so buf must be page aligned and hold nbytes + 8192; the run
- * then starts at buf + *payload_off (0 when the shard has no O_DIRECT descriptor). Scattered
+ * then starts at buf + *payload_off (0, by a buffered read, when the shard has no O_DIRECT
+ * descriptor or buf is not page aligned). Scattered
  * tensors are six buffered reads into the canonical order at buf. Returns payload bytes. */
 int64_t k3c_expert_read(const k3c_ckpt *c, const k3c_expert_run *r, void *buf, int64_t bufcap,
                         int64_t *payload_off);

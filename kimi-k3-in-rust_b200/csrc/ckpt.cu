@@ -272,10 +272,12 @@ static int index_shard(k3c_ckpt *c, int shard, const std::string &path) {
 }
 
 // Widened O_DIRECT read of [off, off + n) into buf (page aligned, bufcap bytes); the payload
-// starts at *pad. Without an O_DIRECT descriptor, a buffered read at buf + 0.
+// starts at *pad. Without an O_DIRECT descriptor, or into a buffer that is not page aligned, a
+// buffered read at buf + 0.
 static int64_t read_span(const k3c_ckpt *c, int shard, int64_t off, int64_t n, void *buf, int64_t bufcap,
                          int64_t *pad) {
-    const int dfd = c->dfd[shard];
+    // O_DIRECT also needs the destination aligned: a buffer that is not takes the buffered path
+    const int dfd = ((uintptr_t)buf % CK_ALIGN) ? -1 : c->dfd[shard];
     if (dfd < 0) {
         if (pad) *pad = 0;
         if (bufcap < n) return 0;

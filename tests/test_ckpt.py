@@ -104,3 +104,17 @@ def test_malformed_shards_are_rejected(k3, ora, tmp_path, case):
     if ora.ref_available():
         st, _, _ = ora.ref_expert_read(d, 0, 0, k3.ExpertRunC, 4096)
         assert st == -1
+
+
+def test_unaligned_buffer_reads_buffered(k3, ckpt_dir):
+    """A destination that is not page aligned cannot take an O_DIRECT read: the run is read
+    through the page cache into the buffer's start instead."""
+    d, want = ckpt_dir
+    ck = k3.Checkpoint(d)
+    r = ck.expert_ref(1, 0)
+    aligned = k3.aligned_host_buffer(r.nbytes + 2 * 4096 + 64)
+    buf = aligned[8:]                                    # 8 bytes past a page boundary
+    po = C.c_int64(-1)
+    n = k3.lib().k3c_expert_read(ck.h, C.byref(r), C.c_void_p(buf.ctypes.data), buf.size, C.byref(po))
+    assert n == r.nbytes and po.value == 0
+    assert buf[:n].tobytes() == ck.read_expert(r).tobytes()
