@@ -802,6 +802,8 @@ class LatentMoeLayer:
         keep = []
 
         def conv(a):
+            if a is None:   # the shared expert's matrices of a layer with n_shared = 0
+                return None
             if wdt == WBF16:
                 return t(a.view(np.int16))
             if wdt == WI8:   # reference rows [f32 scale][int8 * in] -> packed on the device

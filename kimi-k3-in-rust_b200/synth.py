@@ -174,7 +174,8 @@ def latent_layer(g: np.random.Generator, hidden: int, latent: int, inter: int,
                  for _ in range(n_experts)],
         latent_norm=(1.0 + 0.1 * g.standard_normal(latent, dtype=np.float32)).astype(np.float32),
         down=trunk(latent, hidden), up=trunk(hidden, latent),
-        sh1=trunk(SI, hidden), sh3=trunk(SI, hidden), sh2=trunk(hidden, SI),
+        sh1=trunk(SI, hidden) if SI else None, sh3=trunk(SI, hidden) if SI else None,
+        sh2=trunk(hidden, SI) if SI else None,
         wdt=wdt, hidden=hidden, latent=latent, inter=inter, n_shared=n_shared,
         n_experts=n_experts, topk=topk, renorm=1, latent_norm_on=1,
         routed_scale=1.0, rms_eps=1e-5, situ_b1=4.0, situ_b2=25.0)

@@ -113,3 +113,25 @@ def test_latent_layer_vs_oracle(k3, ora, dev, ntok, wdt):
     assert np.array_equal(wt.cpu().numpy(), wwt)
     assert int(drops.item()) == 0
     assert maxrel(out.cpu().numpy(), want) < 2e-2
+
+
+@pytest.mark.parametrize("ntok", [8, 48])
+@pytest.mark.parametrize("variant", ["no_shared", "no_norm", "no_bias"])
+def test_latent_layer_optional_parts(k3, ora, dev, ntok, variant):
+    """The layer's optional parts: no shared expert (n_shared = 0), no aggregate RMSNorm,
+    no router bias; through the decode kernels (8 tokens) and the prefill kernels (48)."""
+    g = k3.synth.rng(200 + ntok)
+    layer = k3.synth.latent_layer(g, 512, 256, 128, 16, 4, n_shared=0 if variant == "no_shared" else 1,
+                                  wdt=1)
+    if variant == "no_norm":
+        layer["latent_norm_on"] = 0
+    if variant == "no_bias":
+        layer["router_bias"] = None
+    if variant == "no_shared":
+        for k in ("sh1", "sh3", "sh2"):
+            layer[k] = None
+    x = g.standard_normal((ntok, 512), dtype=np.float32)
+    want, widx, _ = ora.moe_latent(x, layer)
+    out, idx, _ = k3.LatentMoeLayer.from_host(layer, dev).decode(T(x, dev))
+    assert np.array_equal(idx.cpu().numpy(), widx)
+    assert maxrel(out.cpu().numpy(), want) < 2e-2
