@@ -909,7 +909,8 @@ def run_latent(args, ws, rank, local):
     run_of = torch.arange(LE, dtype=torch.int32, device=dev) % ND
     lat = k3.LatentMoeLayer(arena, ND, run_of, router, None, down, up, sh1, sh3, sh2, norm, k3.WBF16,
                             LH, LL, LI, LS, LK, terms=args.terms)
-    B, NB = 16, 32
+    B = args.batch
+    NB = 32 if B <= 32 else 4          # rotating token batches (each larger than L2 above 32)
     xs = [torch.randn((B, LH), generator=g, device=dev) for _ in range(NB)]
     out = torch.empty((B, LH), dtype=torch.float32, device=dev)
     idx_log = [torch.empty((B, LK), dtype=torch.int32, device=dev) for _ in range(args.steps)]
@@ -978,8 +979,10 @@ def run_latent(args, ws, rank, local):
         "dtype": (f"experts mxfp4 x e4m3 ({args.terms} terms, tcgen05 kind::mxf8f6f4); trunk bf16 weights x fp32 "
                   "activations, fp64 accumulate in the reference's order (bit-exact)"),
         "data": "synthetic",
-        "config": {"workload": LAT_WORKLOAD, "batch": B, "hidden": LH, "latent": LL, "inter": LI, "experts": LE,
-                   "topk": LK, "n_shared": LS, "l2": "inputs larger than L2: ~230 distinct experts (~4 GB) per step"},
+        "config": {"workload": LAT_WORKLOAD.replace("decode: B=16", f"{'decode' if B <= 32 else 'prefill'}: B={B}"),
+                   "batch": B, "hidden": LH, "latent": LL, "inter": LI, "experts": LE,
+                   "topk": LK, "n_shared": LS, "l2": "inputs larger than L2: each step reads its distinct experts (unique_experts_per_step x 17.5 MB) "
+                         "and a rotating token batch"},
         "unique_experts_per_step": float(np.mean(uniq)),
         "stages_ms_per_step": {"experts": exp_ms / args.steps, "router": ms_buf[1] / args.steps,
                                "trunk": trunk_ms / args.steps},
@@ -1151,6 +1154,8 @@ def main():
     ap.add_argument("--path", default="tc", choices=["tc", "cuda"],
                     help="tc: tcgen05 block-scaled MMA path; cuda: CUDA-core GEMV path")
     ap.add_argument("--terms", type=int, default=3, help="E4M3 activation terms (tc path)")
+    ap.add_argument("--batch", type=int, default=16,
+                    help="latent workload: tokens per step (above 32 the many-token path)")
     ap.add_argument("--ep-place", default="balanced", choices=["balanced", "contiguous"],
                     help="ep workload: expert placement balanced on a routing sample's pair counts, or "
                          "contiguous id ranges")
