@@ -367,6 +367,10 @@ __global__ void __launch_bounds__(256) k_add_f32(float *__restrict__ y, const fl
 // tokens run the trunk matrices LAT_CHUNK tokens at a time and the routed experts through the
 // prefill kernels (each expert read once for all of its tokens).
 constexpr int LAT_CHUNK = 32;
+// trunk launches of the many-token path: at 16 tokens the two 16-lane groups of a warp share
+// two rows (each shared-memory read of an activation feeds two rows' FMAs); at 32 they take one
+// row each. Re-reading the weights per launch costs far less than that difference.
+constexpr int LAT_TRUNK_CHUNK = 16;
 constexpr int LAT_MAX_TOKENS = 65535;
 
 struct LatentBufs {
@@ -448,11 +452,11 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
     stage_end(STAGE_ROUTER, s);
     const bool sh = L->n_shared > 0;
     if (ntok > LAT_CHUNK) {
-        // the same steps for many tokens: trunk matrices (and the shared branch) 32 tokens at
+        // the same steps for many tokens: trunk matrices (and the shared branch) 16 tokens at
         // a time, the routed experts through the prefill kernels
         stage_begin(STAGE_Q8, s);
-        for (int t0 = 0; t0 < ntok; t0 += LAT_CHUNK) {
-            const int c = ntok - t0 < LAT_CHUNK ? ntok - t0 : LAT_CHUNK;
+        for (int t0 = 0; t0 < ntok; t0 += LAT_TRUNK_CHUNK) {
+            const int c = ntok - t0 < LAT_TRUNK_CHUNK ? ntok - t0 : LAT_TRUNK_CHUNK;
             const float *xc = x + (size_t)t0 * H;
             const MwSeg first[3] = {{xc, L->down, b.z + (size_t)t0 * Lw, H, Lw, H, Lw, 0, 0},
                                     {xc, L->sh1, b.sgu, H, 2 * SI, H, sh ? SI : 0, 0, 0},
@@ -474,8 +478,8 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
             k_rmsnorm_rows<<<ntok, 256, 0, s>>>(b.agg, b.agg, L->latent_norm, Lw, L->rms_eps);
             K3C_CHECK_LAUNCH();
         }
-        for (int t0 = 0; t0 < ntok; t0 += LAT_CHUNK) {
-            const int c = ntok - t0 < LAT_CHUNK ? ntok - t0 : LAT_CHUNK;
+        for (int t0 = 0; t0 < ntok; t0 += LAT_TRUNK_CHUNK) {
+            const int c = ntok - t0 < LAT_TRUNK_CHUNK ? ntok - t0 : LAT_TRUNK_CHUNK;
             const MwSeg up = {b.agg + (size_t)t0 * Lw, L->up, out + (size_t)t0 * H, Lw, H, Lw, H, 0, 0};
             K3C_TRY(trunk_segs(&up, 1, c, L->wdt, s));
         }
