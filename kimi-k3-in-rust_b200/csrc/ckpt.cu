@@ -57,10 +57,6 @@ class HeaderScan {
         }
         return false;
     }
-    bool peek(char c) {
-        space();
-        return p_ < e_ && *p_ == c;
-    }
     bool string(std::string &out) {
         if (!eat('"')) return false;
         out.clear();
@@ -76,19 +72,19 @@ class HeaderScan {
                 case 'b': c = '\b'; break;
                 case 'f': c = '\f'; break;
                 case 'u': {
-                    // names in this format are ASCII; a \u escape is kept only when it is
-                    // an ASCII code point
+                    // names in this format are ASCII: an ASCII code point is kept, any other
+                    // becomes '?' (the name still resolves, as the reference's index does)
                     if (e_ - p_ < 4) return false;
                     unsigned v = 0;
                     for (int i = 0; i < 4; i++) {
                         const char h = p_[i];
-                        v = v * 16 + (h >= '0' && h <= '9' ? h - '0' : h >= 'a' && h <= 'f' ? h - 'a' + 10
-                                      : h >= 'A' && h <= 'F' ? h - 'A' + 10 : 99);
-                        if (v >= 0x10000) return false;
+                        const int d = h >= '0' && h <= '9' ? h - '0' : h >= 'a' && h <= 'f' ? h - 'a' + 10
+                                      : h >= 'A' && h <= 'F' ? h - 'A' + 10 : -1;
+                        if (d < 0) return false;
+                        v = v * 16 + (unsigned)d;
                     }
                     p_ += 4;
-                    if (v > 0x7f) return false;
-                    c = (char)v;
+                    c = v < 0x80 ? (char)v : '?';
                     break;
                 }
                 default: c = esc; break;   // \" \\ \/

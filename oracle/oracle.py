@@ -126,6 +126,8 @@ def ref():
         L.refh_expert_read.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_longlong,
                                        C.c_void_p, C.POINTER(C.c_longlong)]
         L.refh_expert_read.restype = C.c_longlong
+        L.refh_st_find.argtypes = [C.c_char_p, C.POINTER(C.c_char_p), C.c_int, C.POINTER(C.c_longlong)]
+        L.refh_st_find.restype = C.c_int
         _ref = L
     return _ref
 
@@ -342,3 +344,14 @@ def ref_expert_read(directory, layer, expert, run_struct_type, cap):
     if n < 0:
         return int(n), None, None
     return int(n), run, buf[po.value:po.value + n].copy()
+
+
+def ref_st_find(directory, names):
+    """The reference's own k3_st_open + k3_st_find. Returns None when the shards do not open,
+    else one tuple per name: (found, shard, dtype, ndim, offset, nbytes, shape0, shape1)."""
+    import os as _os
+    arr = (C.c_char_p * len(names))(*[n.encode() for n in names])
+    info = (C.c_longlong * (8 * len(names)))()
+    if ref().refh_st_find(_os.fsencode(directory), arr, len(names), info) != 0:
+        return None
+    return [tuple(info[8 * i:8 * i + 8]) for i in range(len(names))]

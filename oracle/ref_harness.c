@@ -180,6 +180,26 @@ long long refh_expert_read(const char *dir, int layer, int expert, unsigned char
     return (long long)n;
 }
 
+/* The reference's own shard index: k3_st_open then k3_st_find for each of n names. For name
+ * i, info[8*i .. 8*i+7] = found, shard, dtype, ndim, offset, nbytes, shape[0], shape[1].
+ * Returns 0, or -1 when k3_st_open fails. */
+int refh_st_find(const char *dir, const char *const *names, int n, long long *info)
+{
+    K3St s;
+    memset(&s, 0, sizeof s);
+    if (k3_st_open(&s, dir) != 0) return -1;
+    for (int i = 0; i < n; i++) {
+        long long *o = info + 8 * (size_t)i;
+        const K3Tensor *t = k3_st_find(&s, names[i]);
+        memset(o, 0, 8 * sizeof(long long));
+        if (!t) continue;
+        o[0] = 1; o[1] = t->shard; o[2] = t->dtype; o[3] = t->ndim; o[4] = t->off; o[5] = t->nbytes;
+        o[6] = t->ndim > 0 ? t->shape[0] : 0; o[7] = t->ndim > 1 ? t->shape[1] : 0;
+    }
+    k3_st_close(&s);
+    return 0;
+}
+
 /* Thread count the reference's OpenMP loops will use, for the cpu_baseline record. */
 #ifdef _OPENMP
 #include <omp.h>

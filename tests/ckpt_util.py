@@ -79,3 +79,13 @@ def build_checkpoint(d, g, hidden=256, inter=128):
                 metadata={"format": "pt", "note": 'a {nested} "value", [1, 2]'}, header_pad=3)
     write_shard(os.path.join(d, "model-00002-of-00002.safetensors"), b)
     return want
+
+
+def write_raw(path, header, data):
+    """A shard from a header given as raw JSON text (for headers no serializer writes:
+    escapes, trailing commas, odd whitespace) and its data bytes."""
+    js = header.encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(js)))
+        f.write(js)
+        f.write(data)

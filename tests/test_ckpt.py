@@ -7,7 +7,7 @@ import os
 import numpy as np
 import pytest
 
-from ckpt_util import EXPERT, build_checkpoint, write_shard
+from ckpt_util import EXPERT, build_checkpoint, write_raw, write_shard
 
 REF = pytest.mark.skipif("not __import__('oracle.oracle', fromlist=['x']).ref_available()")
 
@@ -118,3 +118,48 @@ def test_unaligned_buffer_reads_buffered(k3, ckpt_dir):
     n = k3.lib().k3c_expert_read(ck.h, C.byref(r), C.c_void_p(buf.ctypes.data), buf.size, C.byref(po))
     assert n == r.nbytes and po.value == 0
     assert buf[:n].tobytes() == ck.read_expert(r).tobytes()
+
+
+QUIRKS = (
+    '{ "__metadata__" : {"a": [1, 2.5e3, {"b": "x\\"y]}"}], "n": null, "t": true},\n'
+    ' "we\\"ird\\\\name\\/u\\u0041\\u00e9" : {"dtype":"U8","shape":[3],"data_offsets":[0,3]},\n'
+    '\t"scalar": {"shape": [], "dtype": "F32", "data_offsets": [3, 7]},'
+    ' "empty": {"dtype": "BF16", "shape": [0, 5], "data_offsets": [7, 7]},'
+    ' "extra": {"dtype":"U8","shape":[2,2],"data_offsets":[7,11], "other": {"k": [1, "]"]}}, }'
+)
+QUIRK_NAMES = ['we"ird\\name/uA?', "scalar", "empty", "extra", "missing"]
+
+
+def test_header_quirks_match_reference_index(k3, ora, tmp_path):
+    """Escapes in names (a non-ASCII code point reads as '?'), nested metadata holding
+    brackets inside strings, tabs and newlines, a scalar, a zero-size tensor, an unknown key
+    holding an object, a trailing comma: every name resolves as in the reference's index."""
+    d = str(tmp_path)
+    write_raw(f"{d}/m.safetensors", QUIRKS, bytes(range(11)))
+    ck = k3.Checkpoint(d)
+    got = []
+    for n in QUIRK_NAMES:
+        try:
+            t = ck.find(n)
+            got.append((1, t.shard, t.dtype, t.ndim, t.off, t.nbytes,
+                        t.shape[0] if t.ndim > 0 else 0, t.shape[1] if t.ndim > 1 else 0))
+        except k3.K3CError:
+            got.append((0,) * 8)
+    assert got[0][0] == 1 and got[1][3] == 0 and got[2][5] == 0 and got[4][0] == 0
+    if ora.ref_available():
+        assert got == ora.ref_st_find(d, QUIRK_NAMES)
+
+
+@pytest.mark.parametrize("hdr", [
+    '{"x": {"dtype": "U8", "shape": [1, 1, 1, 1, 1], "data_offsets": [0, 1]}}',   # rank 5
+    '{"x": {"dtype": "U8", "shape": [1], "data_offsets": [0, 1]}, "x": {"dtype": "U8", "shape": [1], "data_offsets": [1, 2]}}',
+    '{"x": {"dtype": "U8", "shape": [2]}}',                                       # no offsets
+    '["x"]',                                                                      # not an object
+])
+def test_bad_headers_rejected_like_reference(k3, ora, tmp_path, hdr):
+    d = str(tmp_path)
+    write_raw(f"{d}/m.safetensors", hdr, b"\0\0")
+    with pytest.raises(k3.K3CError):
+        k3.Checkpoint(d)
+    if ora.ref_available():
+        assert ora.ref_st_find(d, ["x"]) is None
