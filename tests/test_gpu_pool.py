@@ -151,3 +151,44 @@ def test_streamed_decode_matches_resident_layers(k3, dev):
     st = pool.stats()
     assert st["evictions"] > 0
     pool.close()
+
+
+def test_streamed_prefill_matches_resident_layers(k3, dev):
+    """The reference's streamed prefill (k3_moe_prefill with an expert source,
+    src/core/k3_ops.c:689-808: each distinct expert of the chunk fetched once): layers of 40
+    tokens whose distinct experts are acquired through a pool that cannot hold all layers at
+    once, run by the routed prefill kernels; every output equals the resident layer's bit for
+    bit, and the pool evicts on the way."""
+    import torch
+    H, I, NL, NE, K, T_ = 256, 128, 3, 8, 3, 40
+    host = HostRuns(k3, dev, H, I, NL, NE, seed=15)
+    g = k3.synth.rng(16)
+    pool = k3.ExpertPool(H, I, NL, NE, NE + 2, host)
+    wf, wb = k3.synth.router_weights(g, NE, H)
+    W = T(wb.view(np.int16), dev).view(torch.bfloat16)
+    _, xb = k3.synth.activations(g, T_, H)
+    x0 = T(xb.view(np.int16), dev).view(torch.bfloat16)
+    refs, routes, x = [], [], x0
+    for l in range(NL):
+        lay = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in host.experts[l * NE:(l + 1) * NE]],
+                                   None, W, None, H, I, K, dev)
+        out, idx, wt = lay.prefill(x)
+        refs.append(out.clone())
+        routes.append((idx.clone(), wt.clone()))
+        x = out.to(torch.bfloat16)
+    torch.cuda.synchronize()
+    run_ofs = [pool.run_table() for _ in range(NL)]
+    layers = [pool.layer(W, H, I, K, NE, run_ofs[l]) for l in range(NL)]
+    outs, x = [], x0
+    for l in range(NL):
+        idx, wt = routes[l]
+        ids = sorted(set(idx.cpu().numpy().ravel().tolist()))
+        pool.acquire(l, ids, run_of=run_ofs[l])
+        outs.append(layers[l].prefill_routed(x, idx, wt))
+        pool.release(l, ids)
+        x = outs[-1].to(torch.bfloat16)
+    torch.cuda.synchronize()
+    for l in range(NL):
+        assert np.array_equal(outs[l].cpu().numpy().view(np.uint32), refs[l].cpu().numpy().view(np.uint32)), l
+    assert pool.stats()["evictions"] > 0
+    pool.close()
