@@ -163,6 +163,15 @@ int k3c_router_ws(int *idx, float *w, float *scores, const void *x, int x_dtype,
                   const void *W, int w_dtype, const float *bias, int hidden, int n_experts,
                   int topk, int renorm, float routed_scale, int ntok, void *scratch,
                   size_t scratch_bytes, k3c_stream_t stream);
+/* The draft model's cache-only routing (src/core/k3_ops.c:580-593), on the device: for each
+ * token of idx/wt [ntok][topk] (as a router wrote them), keep the entries whose expert has a
+ * resident run (run_of[e] >= 0, device [n_experts]) in their top-k order, divide the kept
+ * weights by their float sum when it is positive, and set the remaining entries to expert -1
+ * with weight 0. Run the layer with that routing through a routed entry point
+ * (k3c_moe_decode_tc_routed, k3c_moe_prefill_tc_routed) with drops = NULL: the emptied entries
+ * are skipped, and the reference counts no drops in this mode. */
+int k3c_route_cache_only(int *idx, float *wt, int ntok, int topk, const int *run_of, int n_experts,
+                         k3c_stream_t stream);
 /* Selection stage alone, on given fp32 scores [ntok][n_experts]: the parity boundary at
  * which indices must match the reference bit-exactly. */
 int k3c_router_select(int *idx, float *w, const float *scores, const float *bias,

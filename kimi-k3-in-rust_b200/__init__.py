@@ -186,6 +186,7 @@ def lib():
         "k3c_situ_glu": ([vp, vp, i, i, f, f, vp], i),
         "k3c_rmsnorm": ([vp, vp, vp, i, i, f, vp], i),
         "k3c_moe_latent_scratch": ([C.POINTER(MoeLatentLayerC), i], sz),
+        "k3c_route_cache_only": ([vp, vp, i, i, vp, i, vp], i),
         "k3c_ckpt_open": ([C.c_char_p], vp),
         "k3c_ckpt_close": ([vp], None),
         "k3c_ckpt_shards": ([vp], i),
@@ -291,6 +292,15 @@ def router(x, W, bias, topk, renorm=1, routed_scale=1.0):
                             _dtype_code(W), _ptr(bias), H, E, topk, renorm, routed_scale, ntok,
                             _stream()), "k3c_router")
     return idx, w, sc
+
+
+def route_cache_only(idx, wt, run_of):
+    """k3c_route_cache_only in place on device idx/wt [ntok][topk] (the draft model's routing
+    among resident experts); run_of: device int32 [n_experts], -1 = not resident."""
+    ntok, topk = idx.shape
+    _check(lib().k3c_route_cache_only(_ptr(idx), _ptr(wt), ntok, topk, _ptr(run_of), run_of.numel(),
+                                      _stream()), "k3c_route_cache_only")
+    return idx, wt
 
 
 def router_select(scores, bias, topk, renorm=1, routed_scale=1.0):

@@ -521,6 +521,50 @@ int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
 
 }  // namespace k3c
 
+namespace k3c {
+// The draft model's cache-only routing (src/core/k3_ops.c:580-593), one warp per token (lane
+// 0 works, in top-k order): keep the entries whose expert has a run, divide their weights by
+// the float sum of the kept weights when it is positive, and empty the remaining entries
+// (expert -1, weight 0).
+__global__ void __launch_bounds__(128) k_route_cache_only(int *__restrict__ idx, float *__restrict__ wt, int ntok,
+                                                          int topk, const int *__restrict__ run_of, int n_experts) {
+    __shared__ int si[4][K3_MAX_TOPK];
+    __shared__ float sw[4][K3_MAX_TOPK];
+    const int wl = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 4 + wl;
+    if (t >= ntok || lane != 0) return;
+    int *ti = idx + (size_t)t * topk;
+    float *tw = wt + (size_t)t * topk;
+    int m = 0;
+    float wsum = 0.0f;
+    for (int j = 0; j < topk; j++) {
+        const int e = ti[j];
+        if (e >= 0 && e < n_experts && run_of[e] >= 0) {
+            si[wl][m] = e;
+            sw[wl][m] = tw[j];
+            wsum = __fadd_rn(wsum, tw[j]);
+            m++;
+        }
+    }
+    for (int j = 0; j < topk; j++) {
+        ti[j] = j < m ? si[wl][j] : -1;
+        tw[j] = j < m ? (wsum > 0.0f ? __fdiv_rn(sw[wl][j], wsum) : sw[wl][j]) : 0.0f;
+    }
+}
+}  // namespace k3c
+
+extern "C" int k3c_route_cache_only(int *idx, float *wt, int ntok, int topk, const int *run_of, int n_experts,
+                                    k3c_stream_t stream) {
+    k3c::clear_error();
+    if (ntok < 0 || topk <= 0 || topk > K3_MAX_TOPK || n_experts <= 0)
+        return k3c::set_error(K3C_EINVAL, "route_cache_only: ntok=%d topk=%d n_experts=%d", ntok, topk, n_experts);
+    if (ntok == 0) return K3C_OK;
+    if (!idx || !wt || !run_of) return k3c::set_error(K3C_EINVAL, "route_cache_only: null pointer");
+    k3c::k_route_cache_only<<<(ntok + 3) / 4, 128, 0, (cudaStream_t)stream>>>(idx, wt, ntok, topk, run_of, n_experts);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
 extern "C" int k3c_router_select(int *idx, float *w, const float *scores, const float *bias,
                                  int n_experts, int topk, int renorm, float routed_scale,
                                  int ntok, k3c_stream_t stream) {

@@ -192,3 +192,52 @@ def test_streamed_prefill_matches_resident_layers(k3, dev):
         assert np.array_equal(outs[l].cpu().numpy().view(np.uint32), refs[l].cpu().numpy().view(np.uint32)), l
     assert pool.stats()["evictions"] > 0
     pool.close()
+
+
+def test_cache_only_routing(k3, ora, dev):
+    """The draft model's cache-only routing (src/core/k3_ops.c:580-593): kept entries and their
+    renormalised weights equal a host restatement bit for bit, and the layer run with them
+    equals the oracle's sum over the resident experts (plus the shared expert)."""
+    import torch
+    from conftest import maxrel
+    H, I, E, K, T_ = 256, 128, 16, 4, 8
+    g = k3.synth.rng(21)
+    experts = [k3.synth.expert(g, H, I) for _ in range(E)]
+    shared = k3.synth.expert(g, H, I)
+    wf, wb = k3.synth.router_weights(g, E, H)
+    wf = (wf * 20).astype(np.float32)
+    wb = k3.synth.bf16_bits(wf)
+    W = T(wb.view(np.int16), dev).view(torch.bfloat16)
+    xf, xb = k3.synth.activations(g, T_, H)
+    x = T(xb.view(np.int16), dev).view(torch.bfloat16)
+    full = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in experts],
+                                k3.DeviceExpert.from_host(shared, dev), W, None, H, I, K, dev)
+    _, idx, wt = full.decode(x)
+    resident = np.array([e % 3 != 0 for e in range(E)])
+    run_of = T(np.where(resident, np.arange(E), -1).astype(np.int32), dev)
+    idx2, wt2 = idx.clone(), wt.clone()
+    k3.route_cache_only(idx2, wt2, run_of)
+    hi, hw = idx.cpu().numpy(), wt.cpu().numpy()
+    want_i = np.full_like(hi, -1)
+    want_w = np.zeros_like(hw)
+    for t in range(T_):
+        kept = [(e, w) for e, w in zip(hi[t], hw[t]) if resident[e]]
+        s = np.float32(0)
+        for _, w in kept:
+            s = np.float32(s + w)
+        for j, (e, w) in enumerate(kept):
+            want_i[t, j] = e
+            want_w[t, j] = np.float32(w / s) if s > 0 else w
+    assert np.array_equal(idx2.cpu().numpy(), want_i)
+    assert np.array_equal(wt2.cpu().numpy().view(np.uint32), want_w.view(np.uint32))
+    draft = k3.PoolMoeLayer(full.arena, full.c.n_runs, run_of, full.c.shared_run, W, None, H, I, K)
+    out = draft.decode_routed(x, idx2, wt2).cpu().numpy()
+    want = np.zeros((T_, H), np.float32)
+    for t in range(T_):
+        for j in range(K):
+            if want_i[t, j] >= 0:
+                y = ora.expert_ffn(xf[t:t + 1], experts[want_i[t, j]], H, I)[0]
+                want[t] = want[t] + np.float32(want_w[t, j]) * y
+        want[t] = want[t] + ora.expert_ffn(xf[t:t + 1], shared, H, I)[0]
+    assert (want_i < 0).any()
+    assert maxrel(out, want) < 2e-2
