@@ -17,8 +17,14 @@ touches ~110 different experts (~2.6 GB): inputs larger than L2.
   python bench.py --workload latent [--steps K] [--warmup W]    (K3 latent MoE layer, one line)
 
 N > 1 (torchrun) runs N independent replicas (decode does not shard; scaling "weak").
+The same line carries, under "ep", BASELINE config[3] on the same N GPUs: the expert-parallel
+MoE prefill of 16384 tokens with the 384 experts sharded 384/N per GPU (scaling "strong"),
+timed as the max over ranks, with its NVLink bytes, per-stage times and a parity check after
+the timed region (64 tokens per rank against the single-GPU layer over the same weights, and
+8 tokens on rank 0 against the reference's own CPU path). --no-ep leaves it out.
 --impl reference times the reference's own CPU kernels (oracle/_ref, built from its
-sources) on the same workload with every host thread.
+sources) on the same workload with every host core (also under torchrun, which exports
+OMP_NUM_THREADS=1).
 """
 from __future__ import annotations
 
@@ -171,6 +177,7 @@ def cpu_moe_tokens_per_s(budget_s, steps=None, warmup=0, seed=7):
     import ctypes as C
     from oracle import oracle as ora
     R = ora.ref()
+    ora.ref_use_all_cores()
     distinct, shared, wf, q8rows, batches = host_workload(seed)
     experts = [distinct[i % len(distinct)] for i in range(E)]
     arr = (ora.Expert6 * E)(*[ora.expert6(e) for e in experts])
@@ -213,7 +220,7 @@ def run_reference(args, ws, rank):
         "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
         "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 * el / n, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp64 accumulate (reference CPU)",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "batch": 16},
+        "data": "synthetic", "config": decode_config(args.gpus),
         "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
@@ -255,7 +262,40 @@ def build_device_workload(k3, dev, seed, distinct=E, path="tc", terms=3):
     return blob, layer, wq, ws
 
 
+def decode_config(ws):
+    """The config of the headline line (both arms print the same dict)."""
+    return {"workload": WORKLOAD, "batch": 16, "hidden": H, "inter": I, "experts": E, "topk": K,
+            "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+            "l2": "inputs larger than L2: each step reads ~110 different experts (~2.6 GB) "
+                  "from a rotating pool of 32 token batches"}
+
+
 def run_ours(args, ws, rank, local):
+    """The headline line: config[1] decode (replicas at N > 1) and, under "ep", the config[3]
+    expert-parallel layer across the same N GPUs."""
+    import gc
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    line = decode_line(args, ws, rank, local)
+    gc.collect()
+    torch.cuda.empty_cache()
+    if not args.no_ep and args.path == "tc":
+        k3 = ge.load_package()
+        dev = torch.device("cuda", local)
+        ep = ep_layer(args, k3, k3.lib(), dev, ws, rank, local, args.ep_steps, 3, parity=not args.no_parity)
+        if line is not None:
+            line["ep"] = ep
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def decode_line(args, ws, rank, local):
+    """config[1]: returns the line on rank 0 (None on the others); leaves the process group
+    open."""
     import torch
     import __graft_entry__ as ge
     k3 = ge.load_package()
@@ -387,9 +427,8 @@ def run_ours(args, ws, rank, local):
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
-        dist.destroy_process_group()
     if rank != 0:
-        return
+        return None
     cpu = None
     if ws == 1 and not args.no_cpu:
         from oracle import oracle as ora
@@ -405,11 +444,8 @@ def run_ours(args, ws, rank, local):
                   "(tcgen05 kind::mxf8f6f4)") if args.path == "tc" else
                  "fp32 (MXFP4 weights, bf16 inputs widened exactly, fp32 accumulate)",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": B, "hidden": H, "inter": I, "experts": E,
-                   "topk": K, "path": args.path, "terms": args.terms if args.path == "tc" else None,
-                   "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
-                   "l2": "inputs larger than L2: each step reads ~110 different experts (~2.6 GB) "
-                         "from a rotating pool of 32 token batches"},
+        "config": decode_config(ws),
+        "impl": {"path": args.path, "terms": args.terms if args.path == "tc" else None},
         "decode_hbm_gbs": layer_bytes / dt / 1e9,
         "unique_experts_per_step": float(np.mean(uniq)),
         "batches": batches,
@@ -432,7 +468,7 @@ def run_ours(args, ws, rank, local):
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
-    print(json.dumps(line))
+    return line
 
 
 # DRAM bytes the two k_tc_moe launches of a config[1] step move, over the step's algorithmic
@@ -1008,75 +1044,100 @@ EP_WORKLOAD = "config[3] expert-parallel MoE prefill: 16384 bf16 tokens sharded 
               "the ids); dispatch and combine over NVLink peer memory inside the expert kernels (--ep-impl a2a: NCCL all-to-all)"
 
 
-def run_ep(args, ws, rank, local):
+def ep_init_group(ws, dev):
+    """The process group of the expert-parallel layer: NCCL across ranks, or a one-rank gloo
+    group in memory (no network) when this process is alone."""
     import datetime
-    import ctypes as C
-    import torch
     import torch.distributed as dist
-    import __graft_entry__ as ge
-    k3 = ge.load_package()
-    L = k3.lib()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    if dist.is_initialized():
+        return
     if ws > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     else:
-        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29577", rank=0, world_size=1)
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+
+
+def ep_cpu_leg(k3, ref_runs, W, bias, x, out_ep, idx_ep, ntok=8):
+    """The reference's own CPU path (oracle/_ref: k3_router + k3_matmul_mxfp4 experts, SwiGLU,
+    the top-k-order combine; every host core) on `ntok` of this rank's tokens: times it as the
+    layer's CPU baseline and, as the checker, compares its routing and outputs with the
+    expert-parallel layer's. Rank 0 only, after the timed region."""
+    from oracle import oracle as ora
+    if not ora.ref_available():
+        return None, {"unavailable": "oracle/_ref/libk3ref.so not built"}
+    import torch
+    threads = ora.ref_use_all_cores()
+    ids = sorted(set(int(v) for v in idx_ep[:ntok].reshape(-1).tolist()))
+    host = {e: k3.synth.host_expert(ref_runs, e, H, I) for e in ids}
+    shared = k3.synth.host_expert(ref_runs, E, H, I)
+    experts = [host.get(e, host[ids[0]]) for e in range(E)]   # the others are never selected
+    xf = x[:ntok].float().cpu().numpy()
+    wf = W.float().cpu().numpy()
+    t0 = time.perf_counter()
+    ro, ri, _ = ora.moe_layer(xf, wf, bias.cpu().numpy(), experts, shared, H, I, K, use_ref=True)
+    el = time.perf_counter() - t0
+    got = out_ep[:ntok].cpu().numpy().astype(np.float64)
+    err = float(np.abs(got - ro).max() / np.abs(ro).max())
+    cpu = {"value": ntok / el, "unit": UNIT, "cores": threads, "kind": "reference",
+           "sample": f"{ntok} config[3] tokens through the reference's k3_router and k3_matmul_mxfp4 "
+                     f"experts ({el:.2f} s)"}
+    return cpu, {"tokens": ntok, "indices_equal": bool(np.array_equal(ri, idx_ep[:ntok].cpu().numpy())),
+                 "maxrel": err, "checker": "the reference's own kernels (oracle/_ref)"}
+
+
+def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced", impl="fused",
+             parity=True):
+    """BASELINE config[3] on this process group: 16384 tokens in total, EP_T / ws per rank, the
+    384 routed experts sharded 384 / ws per rank, top-8 under the Zipf(1.1) selection bias.
+    Every rank generates the same 384 + 1 experts (same seed) and keeps its share in its
+    arena; the full bank stays resident only for the parity check after the timed region,
+    which runs 64 of each rank's tokens through the single-GPU layer built from the same
+    weights (and, on rank 0, 8 of them through the reference's own CPU path).
+    Returns the result dict on rank 0 (None elsewhere)."""
+    import ctypes as C
+    import torch
+    import torch.distributed as dist
+    ep_init_group(ws, dev)
     assert E % ws == 0
     per = E // ws
-    lo, hi = rank * per, (rank + 1) * per
-    owner = torch.arange(E, device=dev) // per
-    # this rank's experts (distinct weights per id) + the shared expert, pool format
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
-    lay, run = k3.pool_layout(H, I)
-    blob = torch.empty((per + 1) * run, dtype=torch.uint8, device=dev)
-    b2 = blob.view(per + 1, run)
-    for name, (off, nb) in lay.items():
-        seg = b2[:, off:off + nb]
-        if name.endswith("_p"):
-            seg.copy_(torch.randint(0, 256, seg.shape, generator=g, device=dev, dtype=torch.uint8))
-        else:
-            seg.copy_(torch.randint(118, 125, seg.shape, generator=g, device=dev, dtype=torch.uint8))
-    gw = torch.Generator(device=dev)
-    gw.manual_seed(77)                                     # router W identical on every rank
-    W = (torch.randn((E, H), generator=gw, device=dev) * 0.02).to(torch.bfloat16)
-    sample = torch.randn((2048, H), generator=gw, device=dev).to(torch.bfloat16)
-    scores = torch.sigmoid(sample.float() @ W.float().T)
-    perm = torch.randperm(E, generator=torch.Generator().manual_seed(5)).to(dev)   # rank -> id
-    bias_rank = k3.synth.zipf_fit_bias(scores[:, perm], s=1.1, topk=K, iters=600)
-    bias = torch.empty_like(bias_rank)
-    bias[perm] = bias_rank
+    ref_runs, arena_all = k3.synth.device_bank(k3, E + 1, H, I, dev, seed=4242)   # index E: shared
+    stride = k3.pool_run_bytes(H, I)
+    W, bias, sample = k3.synth.zipf_router(dev, E, H, K)
     if ws > 1:
         dist.broadcast(bias, 0)
-    run_of = torch.full((E,), -1, dtype=torch.int32, device=dev)
-    if args.ep_place == "balanced" and ws > 1:
+    if place == "balanced" and ws > 1:
         # expert placement from the pair counts of a routing sample (the sample the bias was
         # fitted on, routed with it): greedy, heaviest expert to the least-loaded rank
         sidx, _, _ = k3.router(sample, W, bias, K)
         load = torch.bincount(sidx.reshape(-1).long(), minlength=E).double()
         dist.broadcast(load, 0)
         owner_l, lists = k3.ep.balanced_placement(load.cpu().tolist(), ws)
-        owner = torch.tensor(owner_l, dtype=torch.int64, device=dev)
-        mine = torch.tensor(lists[rank], dtype=torch.int64, device=dev)
-        run_of[mine] = torch.arange(per, dtype=torch.int32, device=dev)
     else:
-        run_of[lo:hi] = torch.arange(per, dtype=torch.int32, device=dev)
+        owner_l = [e // per for e in range(E)]
+        lists = [list(range(q * per, (q + 1) * per)) for q in range(ws)]
+    owner = torch.tensor(owner_l, dtype=torch.int64, device=dev)
+    mine = torch.tensor(lists[rank] + [E], dtype=torch.int64, device=dev)
+    if ws == 1:
+        arena = arena_all
+    else:
+        arena = arena_all.view(E + 1, stride).index_select(0, mine).reshape(-1)
+    run_of = torch.full((E,), -1, dtype=torch.int32, device=dev)
+    run_of[mine[:-1]] = torch.arange(per, dtype=torch.int32, device=dev)
     none = torch.full((E,), -1, dtype=torch.int32, device=dev)
     T = EP_T // ws
-    if args.ep_impl == "fused":
-        layer = k3.PoolMoeLayer(blob, per + 1, run_of, per, W, bias, H, I, K, terms=2)
+    if impl == "fused":
+        layer = k3.PoolMoeLayer(arena, per + 1, run_of, per, W, bias, H, I, K, terms=2)
         epl = k3.ep.FusedExpertParallel(k3, layer, t_max=T)
     else:
-        lr = k3.PoolMoeLayer(blob, per + 1, run_of, -1, W, bias, H, I, K, terms=2)
-        lsh = k3.PoolMoeLayer(blob, per + 1, none, per, W, bias, H, I, K, terms=2)
+        lr = k3.PoolMoeLayer(arena, per + 1, run_of, -1, W, bias, H, I, K, terms=2)
+        lsh = k3.PoolMoeLayer(arena, per + 1, none, per, W, bias, H, I, K, terms=2)
         route, routed, shared = k3.ep.gpu_layer_fns(k3, lr, lsh, W, bias, K)
         epl = k3.ep.ExpertParallel(owner, route, routed, shared)
     gx = torch.Generator(device=dev)
     gx.manual_seed(99 + rank)
     xs = [torch.randn((T, H), generator=gx, device=dev).to(torch.bfloat16) for _ in range(2)]
-    fwd_kw = {"counts": [T] * ws} if args.ep_impl == "fused" else {}   # equal splits: no count exchange
-    for i in range(args.warmup):
+    fwd_kw = {"counts": [T] * ws} if impl == "fused" else {}   # equal splits: no count exchange
+    for i in range(warmup):
         epl.forward(xs[i % 2], **fwd_kw)
     torch.cuda.synchronize()
     dist.barrier()
@@ -1089,56 +1150,103 @@ def run_ep(args, ws, rank, local):
     launches0 = L.k3c_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    sent = 0
-    for i in range(args.steps):
+    for i in range(steps):
         epl.forward(xs[i % 2], **fwd_kw)
-        sent += epl.last.get("sent_tokens", epl.last.get("remote_rows_read", 0))
     e1.record()
     torch.cuda.synchronize()
+    launches = L.k3c_launch_count() - launches0
     L.k3c_timing_enable(0)
     L.k3c_timing_read(ms_buf, n_buf, 4)
-    stages = {name: ms_buf[j] / args.steps for j, name in enumerate(("experts", "router", "partial_rows", "q8"))
-              if j != 3}
+    stages = {name: ms_buf[j] / steps for j, name in enumerate(("experts", "router", "partial_rows"))}
     dist.barrier()
     torch.cuda.synchronize()
     clocks = clk.stop()
     dt_local = e0.elapsed_time(e1) / 1e3
-    t = torch.tensor([dt_local, float(sent)], dtype=torch.float64, device=dev)
+    # NVLink traffic of one layer, from this rank's tokens' routing: a token is read once by
+    # every other rank that owns one of its experts, and that rank stores one partial row back
+    out_ep = epl.forward(xs[0], **fwd_kw)
+    idx_ep = (epl.idx_buf[:T].clone() if impl == "fused" else k3.router(xs[0], W, bias, K)[0])
+    dest = owner[idx_ep.long()]
+    member = torch.zeros((T, ws), dtype=torch.bool, device=dev)
+    member.scatter_(1, dest, True)
+    member[:, rank] = False
+    remote_rows = float(member.sum().item())
+    # parity: 64 of this rank's tokens against the single-GPU layer over the full bank
+    maxrel, idx_ok = 0.0, 1.0
+    sel = None
+    if parity:
+        full = k3.PoolMoeLayer(arena_all, E + 1, torch.arange(E, dtype=torch.int32, device=dev), E, W, bias,
+                               H, I, K, terms=2)
+        pick = np.random.default_rng(rank).choice(np.arange(1, T - 1), 62, replace=False)
+        sel = torch.from_numpy(np.sort(np.concatenate([[0, T - 1], pick]))).to(dev)
+        ref_o, ref_i, _ = full.prefill(xs[0][sel])
+        got = out_ep[sel].double()
+        maxrel = float(((got - ref_o.double()).abs().max() / ref_o.double().abs().max()).item())
+        idx_ok = float(torch.equal(ref_i, idx_ep[sel]))
+        del full
+    t = torch.tensor([dt_local, remote_rows, maxrel, -idx_ok], dtype=torch.float64, device=dev)
     if ws > 1:
         mx = t.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         sm = t.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        dt, sent_all = float(mx[0]), float(sm[1])
+        dt, rows_all, maxrel_all, idx_all = float(mx[0]), float(sm[1]), float(mx[2]), -float(mx[3])
     else:
-        dt, sent_all = dt_local, sent
-    launches = L.k3c_launch_count() - launches0
-    if args.ep_impl == "fused":
+        dt, rows_all, maxrel_all, idx_all = dt_local, remote_rows, maxrel, idx_ok
+    if impl == "fused":
         epl.close()
+    if rank != 0:
+        return None
+    cpu, ora_par = (None, None)
+    if parity and not args.no_cpu:
+        cpu, ora_par = ep_cpu_leg(k3, ref_runs, W, bias, xs[0][sel], out_ep[sel], idx_ep[sel])
+    flop = (EP_T * K + EP_T) * 2 * 3 * I * H
+    return {
+        "workload": EP_WORKLOAD, "tokens": EP_T, "n_gpus": ws, "steps": steps, "warmup": warmup,
+        "tokens_per_s": EP_T * steps / dt, "unit": UNIT, "ms_per_step": 1e3 * dt / steps,
+        "scaling": "strong", "parallelism": f"ep{ws}",
+        "placement": place if ws > 1 else "all experts", "impl": impl,
+        "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
+        "useful_tflops": flop * steps / dt / 1e12,
+        "stages_ms_per_step_rank0": stages,
+        "nvlink_per_step": {"remote_token_rows_read": rows_all, "bytes_read": rows_all * H * 2,
+                            "partial_rows_written": rows_all, "bytes_written": rows_all * (H * 4 + 4),
+                            "how": "bf16 token rows read by each rank that owns one of the token's experts; "
+                                   "one fp32 partial row (and its flag) stored back per (token, rank)"}
+        if impl == "fused" else None,
+        "parity": {"tokens_per_rank": 64 if parity else 0, "maxrel_vs_single_gpu": maxrel_all if parity else None,
+                   "indices_equal_single_gpu": bool(idx_all == 1.0) if parity else None,
+                   "single_gpu_layer": "k3c_moe_prefill_tc over all 384 experts, same weights",
+                   "tolerance": 2e-2, "oracle": ora_par},
+        "cpu_baseline": cpu,
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+
+
+def run_ep(args, ws, rank, local):
+    """--workload ep: config[3] as its own line (the same section the default line carries
+    under "ep")."""
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    r = ep_layer(args, k3, L, dev, ws, rank, local, args.steps, args.warmup, args.ep_place, args.ep_impl,
+                 parity=not args.no_parity)
     dist.destroy_process_group()
     if rank != 0:
         return
-    flop = (EP_T * K + EP_T) * 2 * 3 * I * H
     print(json.dumps({
-        "metric": METRIC, "value": EP_T * args.steps / dt, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None,
-        "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
-        "data": "synthetic",
+        "metric": METRIC, "value": r["tokens_per_s"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": r["dtype"], "data": "synthetic",
         "config": {"workload": EP_WORKLOAD, "tokens": EP_T, "hidden": H, "inter": I, "experts": E, "topk": K,
-                   "parallelism": f"ep{ws}", "placement": args.ep_place if ws > 1 else "all experts"},
-        "useful_tflops": flop * args.steps / dt / 1e12,
-        "stages_ms_per_step_rank0": stages if args.ep_impl == "fused" else None,
-        "dispatch": ({"impl": "fused: peers' token rows read by the quantisation kernel, per-rank partial rows stored at the token owner, over NVLink",
-                      "remote_token_rows_read_per_step": sent_all / args.steps,
-                      "sync": "two one-element NCCL all-reduces per layer"} if args.ep_impl == "fused" else
-                     {"impl": "torch.distributed all_to_all_single (NCCL)" if ws > 1 else "none (1 GPU)",
-                      "token_rows_per_step": sent_all / args.steps,
-                      "dispatch_gb_per_step": sent_all / args.steps * H * 2 / 1e9,
-                      "combine_gb_per_step": sent_all / args.steps * H * 4 / 1e9}),
-        "gpu_launches": int(launches),
-        "clocks": clocks,
-    }))
+                   "parallelism": f"ep{ws}", "placement": r["placement"]},
+        **{k: r[k] for k in ("useful_tflops", "stages_ms_per_step_rank0", "nvlink_per_step", "parity",
+                             "cpu_baseline", "gpu_launches", "clocks")}}))
 
 
 def main():
@@ -1161,6 +1269,10 @@ def main():
                          "contiguous id ranges")
     ap.add_argument("--ep-impl", default="fused", choices=["fused", "a2a"],
                     help="ep workload: fused peer-memory exchange in the expert kernels, or NCCL all-to-all")
+    ap.add_argument("--ep-steps", type=int, default=10,
+                    help="default line: timed steps of the config[3] expert-parallel layer (its 'ep' object)")
+    ap.add_argument("--no-ep", action="store_true", help="default line without the 'ep' object")
+    ap.add_argument("--no-parity", action="store_true", help="ep: skip the parity check after the timed region")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "streamed", "ep", "expert", "latent"],
                     help="decode: config[1] (the headline line); prefill: config[2]; streamed: config[4]; "

@@ -179,3 +179,68 @@ def latent_layer(g: np.random.Generator, hidden: int, latent: int, inter: int,
         wdt=wdt, hidden=hidden, latent=latent, inter=inter, n_shared=n_shared,
         n_experts=n_experts, topk=topk, renorm=1, latent_norm_on=1,
         routed_scale=1.0, rms_eps=1e-5, situ_b1=4.0, situ_b2=25.0)
+
+
+def zipf_router(device, n_experts: int = N_EXPERTS, hidden: int = HIDDEN, topk: int = TOPK,
+                s: float = 1.1, seed: int = 77, sample: int = 2048, perm_seed: int = 5,
+                iters: int = 600):
+    """The Zipf(s)-skewed router of BASELINE configs [2] and [3], generated on `device`:
+    W_r ~ N(0, 0.02) in bf16 and a selection bias fitted (zipf_fit_bias) on a separate sample
+    of `sample` bf16 tokens so that expert popularity follows Zipf(s) over a fixed random
+    permutation of the expert ids. The same seeds give the same tensors on every process of
+    one device type. Returns (W bf16 [E][H], bias fp32 [E], the sample tokens bf16)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    W = (torch.randn((n_experts, hidden), generator=g, device=device) * 0.02).to(torch.bfloat16)
+    smp = torch.randn((sample, hidden), generator=g, device=device).to(torch.bfloat16)
+    scores = torch.sigmoid(smp.float() @ W.float().T)
+    perm = torch.randperm(n_experts, generator=torch.Generator().manual_seed(perm_seed)).to(device)
+    b_rank = zipf_fit_bias(scores[:, perm], s=s, topk=topk, iters=iters)
+    bias = torch.empty_like(b_rank)
+    bias[perm] = b_rank
+    return W, bias, smp
+
+
+def device_bank(k3, n: int, hidden: int = HIDDEN, inter: int = INTER, device="cuda", seed: int = 4242):
+    """n MXFP4 experts generated on the device with the BASELINE distributions (packed bytes
+    uniform over 0..255, scale bytes uniform in [118, 124]) in the reference's expert-run
+    layout, and the same experts packed into pool-format runs for the tensor-core kernels.
+    The same seed gives the same bytes on every process of one device type, so ranks that
+    each hold a share of the experts agree on every expert's weights.
+    Returns (ref_runs uint8 [n][run], arena uint8 [n * pool_run_bytes])."""
+    import torch
+    lay, run = k3.expert_run_layout(hidden, inter)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    ref = torch.empty((n, run), dtype=torch.uint8, device=device)
+    for name, (off, nb) in lay.items():
+        seg = ref[:, off:off + nb]
+        if name.endswith("_p"):
+            seg.random_(0, 256, generator=g)
+        else:
+            seg.random_(SCALE_LO, SCALE_HI + 1, generator=g)
+    stride = k3.pool_run_bytes(hidden, inter)
+    arena = torch.empty(n * stride, dtype=torch.uint8, device=device)
+    for i, q in enumerate(k3.experts_from_blob(ref, n, hidden, inter)):
+        k3.pool_pack(arena[i * stride:(i + 1) * stride], q, hidden, inter)
+    return ref, arena
+
+
+def host_expert(ref_runs, i: int, hidden: int = HIDDEN, inter: int = INTER, layout=None) -> dict:
+    """Expert i of a device_bank as the host dict of expert(): numpy uint8 arrays in the
+    reference layout (gate/up [inter][hidden/2] + [inter][hidden/32], down [hidden][inter/2] +
+    [hidden][inter/32])."""
+    if layout is None:
+        parts = [("gate_p", inter * hidden // 2), ("gate_s", inter * hidden // 32),
+                 ("down_p", hidden * inter // 2), ("down_s", hidden * inter // 32),
+                 ("up_p", inter * hidden // 2), ("up_s", inter * hidden // 32)]
+        off, layout = 0, {}
+        for name, nb in parts:
+            layout[name] = (off, nb)
+            off += nb
+    run = ref_runs[i].cpu().numpy()
+    shapes = {"gate_p": (inter, hidden // 2), "gate_s": (inter, hidden // GROUP),
+              "up_p": (inter, hidden // 2), "up_s": (inter, hidden // GROUP),
+              "down_p": (hidden, inter // 2), "down_s": (hidden, inter // GROUP)}
+    return {k: np.ascontiguousarray(run[o:o + nb].reshape(shapes[k])) for k, (o, nb) in layout.items()}

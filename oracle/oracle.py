@@ -123,6 +123,8 @@ def ref():
                                      C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
                                      _i32p, _f32p]
         L.refh_threads.restype = C.c_int
+        L.refh_set_threads.argtypes = [C.c_int]
+        L.refh_set_threads.restype = None
         L.refh_expert_read.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_longlong,
                                        C.c_void_p, C.POINTER(C.c_longlong)]
         L.refh_expert_read.restype = C.c_longlong
@@ -130,6 +132,23 @@ def ref():
         L.refh_st_find.restype = C.c_int
         _ref = L
     return _ref
+
+
+def host_cores() -> int:
+    """Host cores this process may run on (its CPU affinity)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def ref_use_all_cores() -> int:
+    """Make the reference's OpenMP loops use every host core of this process and return that
+    count. A launcher such as torch.distributed.run exports OMP_NUM_THREADS=1 to every rank;
+    the CPU baseline runs on rank 0 alone and may use the whole host."""
+    n = host_cores()
+    ref().refh_set_threads(n)
+    return ref().refh_threads()
 
 
 def _ptr_or_null(a):

@@ -200,10 +200,14 @@ int refh_st_find(const char *dir, const char *const *names, int n, long long *in
     return 0;
 }
 
-/* Thread count the reference's OpenMP loops will use, for the cpu_baseline record. */
+/* Thread count the reference's OpenMP loops will use, for the cpu_baseline record.
+ * refh_set_threads sets it for this process (a launcher such as torch.distributed.run exports
+ * OMP_NUM_THREADS=1 to every rank; the baseline runs on rank 0 alone and may use the host). */
 #ifdef _OPENMP
 #include <omp.h>
 int refh_threads(void) { return omp_get_max_threads(); }
+void refh_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
 #else
 int refh_threads(void) { return 1; }
+void refh_set_threads(int n) { (void)n; }
 #endif
