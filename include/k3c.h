@@ -46,6 +46,57 @@ typedef struct K3ExpertSrc {
     int (*resident)(struct K3ExpertSrc *self, int layer, int expert, K3ExpertQ *out);
     void *ctx;
 } K3ExpertSrc;
+
+/* Model configuration, include/k3/k3.h:73-116, field for field (k3_moe reads hidden,
+ * rms_eps, n_experts, topk, n_shared, latent, moe_inter, routed_scale, moe_renorm,
+ * latent_norm, situ_b1, situ_b2). */
+typedef struct {
+    int hidden;
+    int n_layers;
+    int vocab;
+    float rms_eps;
+    int kda_heads;
+    int kda_head_dim;
+    int conv_k;
+    float gate_lb;
+    int n_heads;
+    int q_lora;
+    int kv_lora;
+    int qk_nope;
+    int qk_rope;
+    int v_head;
+    int mla_out_gate;
+    int n_experts;
+    int topk;
+    int n_shared;
+    int latent;
+    int moe_inter;
+    float routed_scale;
+    int moe_renorm;
+    int latent_norm;
+    int first_dense;
+    int dense_inter;
+    int attn_res_block;
+    float situ_b1;
+    float situ_b2;
+    int n_full_attn;
+    int *full_attn;
+} K3Cfg;
+
+/* Latent MoE layer weights, include/k3/k3.h:357-380, field for field. HOST addresses.
+ * gate/bias fp32; w1/w3/w2 the fp32 resident bank ([e][moe_inter][latent] gate and up,
+ * [e][latent][moe_inter] down), used when src is NULL; down/up/sh1/sh3/sh2 tagged by wdt. */
+typedef struct {
+    const float *gate, *bias;
+    const float *w1, *w3, *w2;
+    const float *latent_norm;
+    const void *down, *up;
+    const void *sh1, *sh3, *sh2;
+    int wdt;
+    struct K3ExpertSrc *src;
+    int layer;
+    int cache_only;
+} K3MoeW;
 #endif /* K3_H */
 
 /* Binary-compatible with cudaStream_t; NULL is the legacy default stream. */
@@ -124,6 +175,52 @@ void k3_router(int *idx, float *w, const float *x, const float *W,
 /* include/k3/k3.h:388: routed experts dropped from a sum because they failed to load. */
 extern long k3_expert_drops;
 
+/* include/k3/k3.h:382, src/core/k3_ops.c:556-656. The K3 latent MoE layer for T tokens:
+ * out[T][hidden] from x[T][hidden] (host fp32). Per token: route on the full width
+ * (w->gate, w->bias); with w->cache_only and w->src->resident, keep only the resident top-k
+ * experts and renormalise their weights; z = down x; the selected experts on z at the latent
+ * width (from w->src: getmany of the top-k, then get() -- or resident() when cache_only --
+ * for each; a failed get is counted in k3_expert_drops with the reference's message and
+ * skipped; without a source, the fp32 bank w->w1/w3/w2), summed with their weights in top-k
+ * order; RMSNorm of the sum (c->latent_norm); up; plus the full-width shared expert
+ * unweighted. idx/wt (host, topk entries) are left as the reference leaves them: the last
+ * token's routing. scratch is accepted and not used (the work space is on the GPU), so
+ * callers size it with k3_moe_scratch exactly as before.
+ *
+ * Experts run on the tcgen05 tensor cores (the routed-expert kernels of the k3c_* layer:
+ * activations as three E4M3 terms up to 32 tokens, two above) when the latent width and
+ * moe_inter are multiples of 128 (the latent width of 256 above 32 tokens) and SiTU has the
+ * K3 bounds 4 and 25: within 2e-2 of the reference's output (measured ~1e-5 up to 32 tokens).
+ * Otherwise, for the fp32 bank, or with K3C_DROPIN_FP32=1 in the environment, they run as
+ * fp32 GEMVs (k3_matmul's order for the bank, 1e-5 for MXFP4). Trunk matrices always run
+ * bit-exact (k3_matmul / k3_matmul_bf16 order) or, for K3_WI8, as exact int32 sums.
+ *
+ * Experts from a source other than k3c_pool_source are copied (host or device memory) into
+ * device staging right after each get(), within the reference's validity window; experts
+ * from a k3c_pool_source are used in their pool slots (no copy) and released once the call's
+ * kernels are enqueued. Weights are uploaded on every call unless
+ * k3c_dropin_keep_weights(1) promises that weight arrays do not change at a given address.
+ * Aborts, as the reference does, on a precondition violation or a CUDA failure. */
+void k3_moe(float *out, const float *x, const K3MoeW *w, const K3Cfg *c, int T, int *idx,
+            float *wt, float *scratch);
+/* include/k3/k3.h:418-426, src/core/k3_ops.c:689-808. Same outputs as k3_moe; with a source,
+ * more than one token, no cache_only and K3_NO_BATCH_PREFILL unset, the source sees the
+ * reference's batched pattern: per 64-token chunk, getmany of the chunk's distinct experts
+ * in first-seen order, then one get() per distinct expert (a failure drops that expert for the
+ * whole chunk: one k3_expert_drops count, "this chunk is CORRUPT"); idx/wt are written only by
+ * a final one-token chunk, as in the reference. Otherwise it is k3_moe. */
+void k3_moe_prefill(float *out, const float *x, const K3MoeW *w, const K3Cfg *c, int T,
+                    int *idx, float *wt, float *scratch);
+/* include/k3/k3.h:381, src/core/k3_ops.c:658-666: the reference's scratch size in floats. */
+size_t k3_moe_scratch(const K3Cfg *c);
+/* No counterpart in the reference. 1: the drop-ins above keep a device copy of each weight
+ * array (router, norm, trunk matrices, fp32 bank) keyed by its host address and size, so a
+ * weight is uploaded once per process -- for callers whose weights stay put (the engine);
+ * 0 (the default): every call uploads what it reads. k3c_dropin_forget_weights() frees the
+ * kept copies. */
+void k3c_dropin_keep_weights(int on);
+void k3c_dropin_forget_weights(void);
+
 /* ====================================================================================
  * 2. DEVICE ENTRY POINTS (device pointers, explicit stream)
  * ==================================================================================== */
@@ -165,13 +262,15 @@ int k3c_router_ws(int *idx, float *w, float *scores, const void *x, int x_dtype,
                   size_t scratch_bytes, k3c_stream_t stream);
 /* The draft model's cache-only routing (src/core/k3_ops.c:580-593), on the device: for each
  * token of idx/wt [ntok][topk] (as a router wrote them), keep the entries whose expert has a
- * resident run (run_of[e] >= 0, device [n_experts]) in their top-k order, divide the kept
- * weights by their float sum when it is positive, and set the remaining entries to expert -1
- * with weight 0. Run the layer with that routing through a routed entry point
- * (k3c_moe_decode_tc_routed, k3c_moe_prefill_tc_routed) with drops = NULL: the emptied entries
- * are skipped, and the reference counts no drops in this mode. */
+ * resident run (0 <= run_of[e] < n_runs, run_of device [n_experts]: the test the expert
+ * kernels apply) in their top-k order, divide the kept weights by their float sum when it is
+ * positive, and set the remaining entries to expert -1 with weight 0. Run the layer with that
+ * routing through a routed entry point (k3c_moe_decode_tc_routed, k3c_moe_prefill_tc_routed,
+ * k3c_moe_latent_decode_routed) with drops = NULL: the emptied entries are skipped, and the
+ * reference counts no drops in this mode. The run table of resident experts comes from
+ * k3c_pool_acquire_resident (pinned, copies complete on the stream). */
 int k3c_route_cache_only(int *idx, float *wt, int ntok, int topk, const int *run_of, int n_experts,
-                         k3c_stream_t stream);
+                         int n_runs, k3c_stream_t stream);
 /* Selection stage alone, on given fp32 scores [ntok][n_experts]: the parity boundary at
  * which indices must match the reference bit-exactly. */
 int k3c_router_select(int *idx, float *w, const float *scores, const float *bias,
@@ -365,6 +464,11 @@ typedef struct {
     const float *latent_norm;     /* [latent] (used when latent_norm_on) */
     int wdt, n_shared, latent_norm_on;
     float rms_eps, situ_b1, situ_b2;
+    /* The draft model's K3MoeW.cache_only (src/core/k3_ops.c:580-593): route among the experts
+     * with a run in experts.run_of only (k3c_route_cache_only after the router) and count no
+     * drops. experts.run_of must then hold only runs that are pinned and filled on the stream
+     * (k3c_pool_acquire_resident). */
+    int cache_only;
 } k3c_moe_latent_layer;
 
 /* k3_moe (src/core/k3_ops.c:556-656) for ntok <= 65535 tokens: out [ntok][hidden] fp32 from
@@ -379,6 +483,13 @@ size_t k3c_moe_latent_scratch(const k3c_moe_latent_layer *L, int ntok);
 int k3c_moe_latent_decode(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L,
                           int *idx, float *wt, int *drops, void *scratch, size_t scratch_bytes,
                           k3c_stream_t stream);
+/* The same layer with the routing given: idx/wt [ntok][topk] on the device are used as they are
+ * (the router and L->cache_only are not applied; entries < 0 or without a run are skipped and
+ * counted in drops when it is not NULL). The k3_moe drop-in runs this after the expert source
+ * has been asked for every selected expert. */
+int k3c_moe_latent_decode_routed(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L,
+                                 const int *idx, const float *wt, int *drops, void *scratch,
+                                 size_t scratch_bytes, k3c_stream_t stream);
 
 /* MoE prefill over ntok tokens: the reference's k3_moe_prefill / moe_prefill_chunk
  * (src/core/k3_ops.c:689-808) for the non-latent shape -- route, group the (token, expert)
@@ -473,8 +584,22 @@ void k3c_pool_destroy(k3c_expert_pool *pool);
 uint8_t *k3c_pool_arena(k3c_expert_pool *pool);            /* slot s at arena + s*stride */
 size_t k3c_pool_slot_stride(const k3c_expert_pool *pool);
 int k3c_pool_slots(const k3c_expert_pool *pool);
-/* Slot holding (layer, expert) -- possibly still filling -- or -1 (reference: resident). */
+/* The expert shape the pool's runs hold (hidden = the experts' input width). */
+int k3c_pool_shape(const k3c_expert_pool *pool, int *hidden, int *inter);
+/* Slot holding (layer, expert) -- possibly still filling -- or -1. A query only: it pins
+ * nothing and orders nothing, so a kernel must not read the slot on its word; use
+ * k3c_pool_acquire_resident (or a k3c_pool_source's resident()) for that. */
 int k3c_pool_resident(k3c_expert_pool *pool, int layer, int expert);
+/* The draft model's resident set (reference: K3ExpertSrc.resident, src/cache/k3_cache.c:239-250,
+ * used by k3_moe's cache-only routing, src/core/k3_ops.c:580-593): every expert of `layer`
+ * that has a slot, pinned until k3c_pool_release, with `stream` made to wait for any of their
+ * copies still in flight (no new copy is issued and no hit or miss is counted). ids (host, may
+ * be NULL, cap entries) receives the pinned expert ids -- pass them to k3c_pool_release;
+ * dev_run_of (device, n_experts ints, may be NULL) receives run_of[e] = slot for those and -1
+ * elsewhere, ordered on `stream`: the run table for k3c_route_cache_only and the routed entry
+ * points. Returns the count (>= 0; K3C_EFULL if it exceeds cap, nothing pinned) or a status. */
+int k3c_pool_acquire_resident(k3c_expert_pool *pool, int layer, int *ids, int cap, int *dev_run_of,
+                              k3c_stream_t stream);
 /* Batch hint (reference: getmany): start the copies of the ids not resident; returns how
  * many were started. Counted as prefetch reads, not as hits or misses. */
 int k3c_pool_getmany(k3c_expert_pool *pool, int layer, const int *ids, int n);
@@ -491,6 +616,51 @@ int k3c_pool_release(k3c_expert_pool *pool, int layer, const int *ids, int n, k3
 int k3c_pool_pin(k3c_expert_pool *pool, int layer, int expert, k3c_stream_t stream);
 int k3c_pool_stats(k3c_expert_pool *pool, k3c_pool_stats_t *out);
 int k3c_pool_sync(k3c_expert_pool *pool);                  /* waits for the copy stream */
+/* The reference cache's bookkeeping around the counters (src/cache/k3_cache.c:235-261, 355-455):
+ * every get request (k3c_pool_acquire, a pool source's get) appends (layer, expert) to an
+ * access trace of int32 pairs and counts it in a per-key request histogram, both recording
+ * what was asked for, hit or miss.
+ *   k3c_pool_trace: copies up to cap int32 values (pairs) of the trace into out (may be NULL)
+ *     and returns the trace's length in int32 values;
+ *   k3c_pool_hist: copies the histogram [n_layers * n_experts] (uint32) into out;
+ *   k3c_pool_dump_trace: the trace as a flat binary file of int32 pairs, the format
+ *     k3_cache_dump_trace writes and tools/sim_cache.py replays (-1 if there is none);
+ *   k3c_pool_dump_hist: the histogram as JSON {"n_layers","n_experts","counts":{"L,e":n}},
+ *     nonzero entries only, as k3_cache_dump_hist;
+ *   k3c_pool_set_pin: k3_cache_pin -- pin (1) or unpin (0) the slot of a resident expert so
+ *     eviction skips it (the payoff of the histogram); 0 if the expert is not resident;
+ *   k3c_pool_reset_stats: k3_cache_reset_stats (hits, misses, evictions, bytes and
+ *     prefetch reads together);
+ *   k3c_pool_report: k3_cache_report's summary on stdout, host bytes in place of disk. */
+int64_t k3c_pool_trace(k3c_expert_pool *pool, int32_t *out, int64_t cap);
+int k3c_pool_hist(k3c_expert_pool *pool, uint32_t *out);
+int k3c_pool_dump_trace(k3c_expert_pool *pool, const char *path);
+int k3c_pool_dump_hist(k3c_expert_pool *pool, const char *path);
+int k3c_pool_set_pin(k3c_expert_pool *pool, int layer, int expert, int pin);
+void k3c_pool_reset_stats(k3c_expert_pool *pool);
+void k3c_pool_report(k3c_expert_pool *pool, const char *label);
+
+/* ---- The pool as the reference's K3ExpertSrc (include/k3/k3.h:332-355), for the k3_moe /
+ * k3_moe_prefill drop-ins and any caller of the reference's interface.
+ *   get(layer, e, q)      = k3c_pool_acquire of one expert (hit/miss counted, trace, copy on a
+ *                           miss): pins its slot and makes the source's stream wait for the
+ *                           copy; q receives DEVICE addresses into the slot's pool-format run:
+ *                           p1/s1 = the interleaved gate/up matrix and its scale atoms, p2/s2 =
+ *                           down and its atoms, p3 = s3 = NULL (up lives inside p1). 0 or -1.
+ *   getmany(layer, ids, n)= k3c_pool_getmany (prefetch copies; returns the count started).
+ *   resident(layer, e, q) = 1 if e has a slot; with q non-NULL the slot is also pinned and the
+ *                           stream made to wait for its copy, as get() but without counting.
+ * Pins taken by get/resident hold until k3c_pool_source_release, which orders the slots'
+ * reuse after the work enqueued on the source's stream so far -- the reference's "valid until
+ * the caller finishes the token" made explicit for asynchronous consumers. A kernel reading
+ * the slots must run on k3c_pool_source_stream. Not thread-safe (as the reference's cache). */
+K3ExpertSrc *k3c_pool_source_create(k3c_expert_pool *pool, k3c_stream_t stream);
+void k3c_pool_source_destroy(K3ExpertSrc *src);     /* releases its pins first */
+int k3c_pool_source_release(K3ExpertSrc *src);
+k3c_stream_t k3c_pool_source_stream(const K3ExpertSrc *src);
+k3c_expert_pool *k3c_pool_source_pool(const K3ExpertSrc *src);   /* NULL: not a pool source */
+/* Slot of a q that this source's get/resident returned, or -1. */
+int k3c_pool_source_slot(const K3ExpertSrc *src, const K3ExpertQ *q);
 
 #ifdef __cplusplus
 }

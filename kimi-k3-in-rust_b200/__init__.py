@@ -63,7 +63,8 @@ class MoeLatentLayerC(C.Structure):
                 + [(n, C.c_void_p) for n in ("router_w", "router_bias", "down", "up", "sh1", "sh3",
                                              "sh2", "latent_norm")]
                 + [(n, C.c_int) for n in ("wdt", "n_shared", "latent_norm_on")]
-                + [(n, C.c_float) for n in ("rms_eps", "situ_b1", "situ_b2")])
+                + [(n, C.c_float) for n in ("rms_eps", "situ_b1", "situ_b2")]
+                + [("cache_only", C.c_int)])
 
 
 class TensorC(C.Structure):
@@ -106,6 +107,40 @@ class EpPeersC(C.Structure):
 
 class K3CError(RuntimeError):
     pass
+
+
+class K3CfgC(C.Structure):
+    """Mirror of the reference's K3Cfg (include/k3/k3.h:73-116; include/k3c.h)."""
+
+    _fields_ = ([(n, C.c_int) for n in ("hidden", "n_layers", "vocab")] + [("rms_eps", C.c_float)]
+                + [(n, C.c_int) for n in ("kda_heads", "kda_head_dim", "conv_k")] + [("gate_lb", C.c_float)]
+                + [(n, C.c_int) for n in ("n_heads", "q_lora", "kv_lora", "qk_nope", "qk_rope", "v_head",
+                                          "mla_out_gate", "n_experts", "topk", "n_shared", "latent",
+                                          "moe_inter")]
+                + [("routed_scale", C.c_float)]
+                + [(n, C.c_int) for n in ("moe_renorm", "latent_norm", "first_dense", "dense_inter",
+                                          "attn_res_block")]
+                + [("situ_b1", C.c_float), ("situ_b2", C.c_float), ("n_full_attn", C.c_int),
+                   ("full_attn", C.POINTER(C.c_int))])
+
+
+class K3ExpertSrcC(C.Structure):
+    """Mirror of the reference's K3ExpertSrc vtable (include/k3/k3.h:332-355)."""
+
+
+SRC_GET_FN = C.CFUNCTYPE(C.c_int, C.POINTER(K3ExpertSrcC), C.c_int, C.c_int, C.POINTER(K3ExpertQ))
+SRC_GETMANY_FN = C.CFUNCTYPE(C.c_int, C.POINTER(K3ExpertSrcC), C.c_int, C.POINTER(C.c_int), C.c_int)
+K3ExpertSrcC._fields_ = [("get", SRC_GET_FN), ("getmany", SRC_GETMANY_FN), ("resident", SRC_GET_FN),
+                         ("ctx", C.c_void_p)]
+
+
+class K3MoeWC(C.Structure):
+    """Mirror of the reference's K3MoeW (include/k3/k3.h:357-380; include/k3c.h): host addresses."""
+
+    _fields_ = ([(n, C.c_void_p) for n in ("gate", "bias", "w1", "w3", "w2", "latent_norm", "down", "up",
+                                           "sh1", "sh3", "sh2")]
+                + [("wdt", C.c_int), ("src", C.POINTER(K3ExpertSrcC)), ("layer", C.c_int),
+                   ("cache_only", C.c_int)])
 
 
 _lib = None
@@ -186,7 +221,28 @@ def lib():
         "k3c_situ_glu": ([vp, vp, i, i, f, f, vp], i),
         "k3c_rmsnorm": ([vp, vp, vp, i, i, f, vp], i),
         "k3c_moe_latent_scratch": ([C.POINTER(MoeLatentLayerC), i], sz),
-        "k3c_route_cache_only": ([vp, vp, i, i, vp, i, vp], i),
+        "k3c_route_cache_only": ([vp, vp, i, i, vp, i, i, vp], i),
+        "k3c_moe_latent_decode_routed": ([vp, vp, i, C.POINTER(MoeLatentLayerC), vp, vp, vp, vp, sz, vp], i),
+        "k3c_pool_acquire_resident": ([vp, i, vp, i, vp, vp], i),
+        "k3c_pool_trace": ([vp, vp, C.c_int64], C.c_int64),
+        "k3c_pool_hist": ([vp, vp], i),
+        "k3c_pool_dump_trace": ([vp, C.c_char_p], i),
+        "k3c_pool_dump_hist": ([vp, C.c_char_p], i),
+        "k3c_pool_set_pin": ([vp, i, i, i], i),
+        "k3c_pool_reset_stats": ([vp], None),
+        "k3c_pool_report": ([vp, C.c_char_p], None),
+        "k3c_pool_source_create": ([vp, vp], vp),
+        "k3c_pool_source_destroy": ([vp], None),
+        "k3c_pool_source_release": ([vp], i),
+        "k3c_pool_source_stream": ([vp], vp),
+        "k3c_pool_source_pool": ([vp], vp),
+        "k3c_pool_source_slot": ([vp, C.POINTER(K3ExpertQ)], i),
+        "k3c_pool_shape": ([vp, C.POINTER(i), C.POINTER(i)], i),
+        "k3_moe": ([vp, vp, C.POINTER(K3MoeWC), C.POINTER(K3CfgC), i, vp, vp, vp], None),
+        "k3_moe_prefill": ([vp, vp, C.POINTER(K3MoeWC), C.POINTER(K3CfgC), i, vp, vp, vp], None),
+        "k3_moe_scratch": ([C.POINTER(K3CfgC)], sz),
+        "k3c_dropin_keep_weights": ([i], None),
+        "k3c_dropin_forget_weights": ([], None),
         "k3c_ckpt_open": ([C.c_char_p], vp),
         "k3c_ckpt_close": ([vp], None),
         "k3c_ckpt_shards": ([vp], i),
@@ -294,12 +350,13 @@ def router(x, W, bias, topk, renorm=1, routed_scale=1.0):
     return idx, w, sc
 
 
-def route_cache_only(idx, wt, run_of):
+def route_cache_only(idx, wt, run_of, n_runs):
     """k3c_route_cache_only in place on device idx/wt [ntok][topk] (the draft model's routing
-    among resident experts); run_of: device int32 [n_experts], -1 = not resident."""
+    among resident experts); run_of: device int32 [n_experts], an expert is resident when
+    0 <= run_of[e] < n_runs."""
     ntok, topk = idx.shape
     _check(lib().k3c_route_cache_only(_ptr(idx), _ptr(wt), ntok, topk, _ptr(run_of), run_of.numel(),
-                                      _stream()), "k3c_route_cache_only")
+                                      int(n_runs), _stream()), "k3c_route_cache_only")
     return idx, wt
 
 
@@ -782,7 +839,8 @@ class LatentMoeLayer:
 
     def __init__(self, arena, n_runs, run_of, router_w, router_bias, down, up, sh1, sh3, sh2,
                  latent_norm, wdt, hidden, latent, inter, n_shared, topk, terms=3, renorm=1,
-                 routed_scale=1.0, latent_norm_on=1, rms_eps=1e-5, situ_b1=4.0, situ_b2=25.0):
+                 routed_scale=1.0, latent_norm_on=1, rms_eps=1e-5, situ_b1=4.0, situ_b2=25.0,
+                 cache_only=0):
         import torch
         self._keep = (arena, run_of, router_w, router_bias, down, up, sh1, sh3, sh2, latent_norm)
         ex = MoePoolLayerC(latent, inter, run_of.numel(), topk, renorm, ACT_SITU, routed_scale,
@@ -795,11 +853,11 @@ class LatentMoeLayer:
             return C.addressof(t) if isinstance(t, Q8MatC) else t.data_ptr()
         self.c = MoeLatentLayerC(hidden, ex, p(router_w), p(router_bias), p(down), p(up), p(sh1),
                                  p(sh3), p(sh2), p(latent_norm), wdt, n_shared, latent_norm_on,
-                                 rms_eps, situ_b1, situ_b2)
+                                 rms_eps, situ_b1, situ_b2, int(cache_only))
         self._scratch = torch.empty(0, dtype=torch.uint8, device=arena.device)
 
     @classmethod
-    def from_host(cls, layer: dict, device, terms=3):
+    def from_host(cls, layer: dict, device, terms=3, cache_only=0):
         """Upload a layer given as host numpy arrays in the oracle's form (router_w,
         router_bias, latent_norm, down, up, sh1, sh3, sh2 as fp32 or uint16 bf16 patterns
         per layer["wdt"], and ``experts``: MXFP4 expert dicts at the latent width)."""
@@ -837,7 +895,7 @@ class LatentMoeLayer:
                   int(layer["n_shared"]), int(layer["topk"]), terms=terms,
                   renorm=int(layer["renorm"]), routed_scale=float(layer["routed_scale"]),
                   latent_norm_on=int(layer["latent_norm_on"]), rms_eps=float(layer["rms_eps"]),
-                  situ_b1=float(layer["situ_b1"]), situ_b2=float(layer["situ_b2"]))
+                  situ_b1=float(layer["situ_b1"]), situ_b2=float(layer["situ_b2"]), cache_only=cache_only)
         obj._packed = keep   # the int8 arrays the k3c_q8_mat records point at
         return obj
 
@@ -863,6 +921,22 @@ class LatentMoeLayer:
                                            self._scratch.numel(), _stream()),
                "k3c_moe_latent_decode")
         return out, idx, wt
+
+    def decode_routed(self, x, idx, wt, out=None, drops=None):
+        """The layer with the routing given (k3c_moe_latent_decode_routed)."""
+        import torch
+        x = x.contiguous()
+        ntok = x.shape[0]
+        need = self.scratch_bytes(ntok)
+        if self._scratch.numel() < need:
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=x.device)
+        if out is None:
+            out = torch.empty((ntok, self.c.hidden), dtype=torch.float32, device=x.device)
+        _check(lib().k3c_moe_latent_decode_routed(_ptr(out), _ptr(x), ntok, C.byref(self.c), _ptr(idx),
+                                                  _ptr(wt), _ptr(drops), _ptr(self._scratch),
+                                                  self._scratch.numel(), _stream()),
+               "k3c_moe_latent_decode_routed")
+        return out
 
 
 # ------------------------------------------------------------------ checkpoint experts

@@ -22,6 +22,8 @@ int launch_mx_gemv(float *y, int ldy, const float *x, int ldx, int ntok, const u
                    const uint8_t *scales, int in, int rows, int group, cudaStream_t s);
 int launch_mx_dequant(float *out, const uint8_t *packed, const uint8_t *scales, int rows,
                       int pcols, int group, cudaStream_t s);
+int launch_mx_exact(float *y, int ldy, const float *x, int ldx, int ntok, const uint8_t *packed,
+                    const uint8_t *scales, int in, int rows, int group, cudaStream_t s);
 int launch_q8_pack(int8_t *wq, float *wscale, int ldw, const void *rows, int in, int out,
                    cudaStream_t s);
 int launch_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
@@ -129,9 +131,10 @@ void k3_matmul_mxfp4(float *y, const float *x, const unsigned char *packed,
     cuda_ok(cudaMemcpyAsync(b + o_x, x, nb_x, cudaMemcpyHostToDevice, w.stream), what);
     cuda_ok(cudaMemcpyAsync(b + o_p, packed, nb_p, cudaMemcpyHostToDevice, w.stream), what);
     cuda_ok(cudaMemcpyAsync(b + o_s, scales, nb_s, cudaMemcpyHostToDevice, w.stream), what);
-    rc_ok(launch_mx_gemv((float *)(b + o_y), rows, (const float *)(b + o_x), in, 1,
-                         (const uint8_t *)(b + o_p), (const uint8_t *)(b + o_s), in, rows, group,
-                         w.stream), what);
+    // the reference's own summation order: bit-identical for a group that is a multiple of 16
+    rc_ok(launch_mx_exact((float *)(b + o_y), rows, (const float *)(b + o_x), in, 1,
+                          (const uint8_t *)(b + o_p), (const uint8_t *)(b + o_s), in, rows, group,
+                          w.stream), what);
     cuda_ok(cudaMemcpyAsync(y, b + o_y, nb_y, cudaMemcpyDeviceToHost, w.stream), what);
     cuda_ok(cudaStreamSynchronize(w.stream), what);
 }

@@ -39,6 +39,8 @@ int launch_moe_decode_tc(float *out, const void *x, int x_dtype, int ntok, const
                          int *idx_out, float *wt_out, int *drops, void *scratch, size_t scratch_bytes,
                          cudaStream_t s, bool routed);
 size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contrib);
+int launch_route_cache_only(int *idx, float *wt, int ntok, int topk, const int *run_of, int n_experts, int n_runs,
+                            cudaStream_t s);
 int launch_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok, const int8_t *wq,
                    const float *wscale, int ldw, int in, int out, cudaStream_t s);
 int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k3c_moe_pool_layer *L,
@@ -434,7 +436,8 @@ size_t moe_latent_scratch(const k3c_moe_latent_layer *L, int ntok) {
 }
 
 int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L, int *idx_out,
-                      float *wt_out, int *drops, void *scratch, size_t scratch_bytes, cudaStream_t s) {
+                      float *wt_out, int *drops, void *scratch, size_t scratch_bytes, cudaStream_t s,
+                      bool routed = false) {
     K3C_TRY(check_latent(L, ntok));
     if (ntok <= 0) return K3C_OK;
     Carve cv{(char *)scratch, scratch_bytes, 0};
@@ -443,13 +446,21 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
         return set_error(K3C_EINVAL, "moe_latent: scratch too small (%zu)", scratch_bytes);
     const k3c_moe_pool_layer &X = L->experts;
     const int H = L->hidden, Lw = X.hidden, SI = X.inter * L->n_shared, K = X.topk;
+    if (routed && (!idx_out || !wt_out)) return set_error(K3C_EINVAL, "moe_latent_routed: null routing");
     int *idx = idx_out ? idx_out : b.idx;
     float *wt = wt_out ? wt_out : b.wt;
-    // 1. route on the full width
-    stage_begin(STAGE_ROUTER, s);
-    K3C_TRY(launch_router(idx, wt, nullptr, x, K3C_F32, L->router_w, K3C_F32, L->router_bias, H, X.n_experts, K,
-                          X.renorm, X.routed_scale, ntok, b.rpart, s));
-    stage_end(STAGE_ROUTER, s);
+    if (!routed) {
+        // 1. route on the full width
+        stage_begin(STAGE_ROUTER, s);
+        K3C_TRY(launch_router(idx, wt, nullptr, x, K3C_F32, L->router_w, K3C_F32, L->router_bias, H, X.n_experts,
+                              K, X.renorm, X.routed_scale, ntok, b.rpart, s));
+        if (L->cache_only) {
+            // the draft model: keep the resident experts, renormalise, count no drops
+            K3C_TRY(launch_route_cache_only(idx, wt, ntok, K, X.run_of, X.n_experts, X.n_runs, s));
+            drops = nullptr;
+        }
+        stage_end(STAGE_ROUTER, s);
+    }
     const bool sh = L->n_shared > 0;
     if (ntok > LAT_CHUNK) {
         // the same steps for many tokens: trunk matrices (and the shared branch) 16 tokens at
@@ -566,4 +577,12 @@ extern "C" int k3c_moe_latent_decode(float *out, const float *x, int ntok, const
                                      k3c_stream_t stream) {
     k3c::clear_error();
     return k3c::launch_moe_latent(out, x, ntok, L, idx, wt, drops, scratch, scratch_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int k3c_moe_latent_decode_routed(float *out, const float *x, int ntok, const k3c_moe_latent_layer *L,
+                                            const int *idx, const float *wt, int *drops, void *scratch,
+                                            size_t scratch_bytes, k3c_stream_t stream) {
+    k3c::clear_error();
+    return k3c::launch_moe_latent(out, x, ntok, L, const_cast<int *>(idx), const_cast<float *>(wt), drops, scratch,
+                                  scratch_bytes, (cudaStream_t)stream, true);
 }

@@ -97,6 +97,57 @@ __global__ void __launch_bounds__(256) k_mx_gemv_generic(float *__restrict__ y, 
     if (lane == 0) y[(size_t)t * ldy + r] = (float)acc;
 }
 
+// The reference's AVX2 flat row path reproduced bit for bit (src/core/k3_ops.c:1418-1508; taken
+// there when group is a multiple of 16): lane l of a 16-thread group accumulates the elements
+// i = l (mod 16) of whole 16-element chunks as fma((double)w, (double)x[i], a_l) in element
+// order, w = E2M1(nibble) * 2^(s-127) formed in fp32 (exact, or +-inf where it overflows);
+// a chunk whose scale byte is 255 contributes no operation at all. The lanes are combined as
+// q_l = (a_l + a_{l+8}) + (a_{l+4} + a_{l+12}) and then (q_0 + q_2) + (q_1 + q_3), the
+// in % 16 tail is fused in element order with w = E2M1 * E8M0 (255 -> 0), and the sum is
+// rounded to float once.
+template <int NT>
+__global__ void __launch_bounds__(256) k_mx_exact(float *__restrict__ y, int ldy, const float *__restrict__ x,
+                                                  int ldx, int ntok, const uint8_t *__restrict__ packed,
+                                                  const uint8_t *__restrict__ scales, int in, int rows, int group) {
+    const int l = threadIdx.x & 15;
+    const int row = blockIdx.x * 16 + (threadIdx.x >> 4);
+    const int r = row < rows ? row : rows - 1;   // rows past the end compute row rows-1, unstored
+    const int pcols = in / 2, ngrp = (in + group - 1) / group, in16 = in & ~15;
+    const uint8_t *pr = packed + (size_t)r * pcols;
+    const uint8_t *sr = scales + (size_t)r * ngrp;
+    for (int t0 = blockIdx.y * NT; t0 < ntok; t0 += gridDim.y * NT) {
+        double a[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) a[t] = 0.0;
+        for (int i = l; i < in16; i += 16) {
+            const uint32_t sb = sr[i / group];
+            if (sb == 255u) continue;
+            const uint32_t byte = pr[i >> 1];
+            const double w = (double)(e2m1_to_f32((i & 1) ? byte >> 4 : byte & 15u) * e8m0_to_f32(sb));
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+                if (t0 + t < ntok) a[t] = fma(w, (double)x[(size_t)(t0 + t) * ldx + i], a[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            double v = a[t];
+            v += __shfl_down_sync(0xffffffffu, v, 8, 16);
+            v += __shfl_down_sync(0xffffffffu, v, 4, 16);
+            v += __shfl_down_sync(0xffffffffu, v, 2, 16);
+            v += __shfl_down_sync(0xffffffffu, v, 1, 16);
+            if (l == 0 && row < rows && t0 + t < ntok) {
+                const float *xt = x + (size_t)(t0 + t) * ldx;
+                for (int i = in16; i < in; i++) {
+                    const uint32_t byte = pr[i >> 1];
+                    const float w = e2m1_to_f32((i & 1) ? byte >> 4 : byte & 15u) * e8m0_to_f32(sr[i / group]);
+                    v = fma((double)w, (double)xt[i], v);
+                }
+                y[(size_t)(t0 + t) * ldy + row] = __double2float_rn(v);
+            }
+        }
+    }
+}
+
 int mx_check(int in, int rows, int group) {
     if (in <= 0 || rows <= 0) return set_error(K3C_EINVAL, "mxfp4: in=%d rows=%d", in, rows);
     if (in & 1) return set_error(K3C_EINVAL, "mxfp4: odd in=%d", in);
@@ -126,6 +177,24 @@ int launch_mx_gemv(float *y, int ldy, const float *x, int ldx, int ntok,
         const long long items = (long long)rows * ntok;
         k_mx_gemv_generic<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(y, ldy, x, ldx, ntok,
                                                                     packed, scales, in, rows, group);
+    }
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
+
+// k3_matmul_mxfp4's result bit for bit when group is a multiple of 16 (k_mx_exact); other
+// groups take the generic kernel (double sums in another order, within a few ulps of double).
+int launch_mx_exact(float *y, int ldy, const float *x, int ldx, int ntok, const uint8_t *packed,
+                    const uint8_t *scales, int in, int rows, int group, cudaStream_t s) {
+    K3C_TRY(mx_check(in, rows, group));
+    if (ntok <= 0) return K3C_OK;
+    if (group % 16) return launch_mx_gemv(y, ldy, x, ldx, ntok, packed, scales, in, rows, group, s);
+    dim3 grid((rows + 15) / 16, 1);
+    if (ntok == 1) {
+        k_mx_exact<1><<<grid, 256, 0, s>>>(y, ldy, x, ldx, ntok, packed, scales, in, rows, group);
+    } else {
+        grid.y = (ntok + 3) / 4 < 16 ? (ntok + 3) / 4 : 16;
+        k_mx_exact<4><<<grid, 256, 0, s>>>(y, ldy, x, ldx, ntok, packed, scales, in, rows, group);
     }
     K3C_CHECK_LAUNCH();
     return K3C_OK;

@@ -18,11 +18,14 @@
 // A slot is pinned from acquire to release, so the experts of a layer in flight cannot be
 // evicted under it (the reference's "pointers stay valid until the token finishes").
 #include <cuda_runtime.h>
+#include <stdio.h>
 
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
+#include "pool_common.cuh"
 
 struct k3c_expert_pool {
     int hidden = 0, inter = 0, n_layers = 0, n_experts = 0, nslot = 0;
@@ -35,6 +38,9 @@ struct k3c_expert_pool {
     std::vector<int> key_of;        // slot -> key, K3C_SLOT_EMPTY or K3C_SLOT_INFLIGHT
     std::vector<int> pins;          // acquire count + permanent pins
     std::vector<char> pinned_forever;
+    std::vector<char> user_pin;     // k3c_pool_set_pin (the reference's k3_cache_pin)
+    std::vector<int32_t> trace;     // (layer, expert) of every get request, in order
+    std::vector<uint32_t> hist;     // get requests per key
     std::vector<unsigned long long> used_at;
     std::vector<cudaEvent_t> fill_ev, use_ev;
     std::vector<char> fill_pending, use_pending;
@@ -57,7 +63,7 @@ int pick_victim(k3c_expert_pool *p) {
     for (int i = 0; i < p->nslot; i++) {
         if (p->key_of[i] == K3C_SLOT_INFLIGHT) continue;
         if (p->key_of[i] == K3C_SLOT_EMPTY) return i;
-        if (p->pins[i] > 0) continue;
+        if (p->pins[i] > 0 || p->user_pin[i]) continue;
         if (p->used_at[i] < oldest) {
             oldest = p->used_at[i];
             best = i;
@@ -135,6 +141,8 @@ k3c_expert_pool *k3c_pool_create(int hidden, int inter, int n_layers, int n_expe
     p->key_of.assign(n_slots, K3C_SLOT_EMPTY);
     p->pins.assign(n_slots, 0);
     p->pinned_forever.assign(n_slots, 0);
+    p->user_pin.assign(n_slots, 0);
+    p->hist.assign((size_t)n_layers * n_experts, 0);
     p->used_at.assign(n_slots, 0);
     p->fill_ev.assign(n_slots, nullptr);
     p->use_ev.assign(n_slots, nullptr);
@@ -181,6 +189,13 @@ uint8_t *k3c_pool_arena(k3c_expert_pool *p) { return p ? p->arena : nullptr; }
 size_t k3c_pool_slot_stride(const k3c_expert_pool *p) { return p ? p->stride : 0; }
 int k3c_pool_slots(const k3c_expert_pool *p) { return p ? p->nslot : 0; }
 
+int k3c_pool_shape(const k3c_expert_pool *p, int *hidden, int *inter) {
+    if (!p) return K3C_EINVAL;
+    if (hidden) *hidden = p->hidden;
+    if (inter) *inter = p->inter;
+    return K3C_OK;
+}
+
 int k3c_pool_resident(k3c_expert_pool *p, int layer, int expert) {
     if (!p || !key_ok(p, layer, expert)) return -1;
     std::lock_guard<std::mutex> lk(p->mu);
@@ -218,6 +233,9 @@ int k3c_pool_acquire(k3c_expert_pool *p, int layer, const int *ids, int n, int *
             break;
         }
         const int key = layer * p->n_experts + ids[i];
+        p->hist[key]++;   // what was asked for, before it is served (k3_cache.c:235-249)
+        p->trace.push_back(layer);
+        p->trace.push_back(ids[i]);
         int slot = p->slot_of[key];
         if (slot >= 0) {
             p->st.hits++;
@@ -300,6 +318,264 @@ int k3c_pool_stats(k3c_expert_pool *p, k3c_pool_stats_t *out) {
 int k3c_pool_sync(k3c_expert_pool *p) {
     if (!p) return K3C_EINVAL;
     return cudaStreamSynchronize(p->copy) == cudaSuccess ? K3C_OK : K3C_ECUDA;
+}
+
+int k3c_pool_acquire_resident(k3c_expert_pool *p, int layer, int *ids, int cap, int *dev_run_of,
+                              k3c_stream_t stream) {
+    k3c::clear_error();
+    if (!p || layer < 0 || layer >= p->n_layers) return k3c::set_error(K3C_EINVAL, "pool_acquire_resident: bad layer");
+    cudaStream_t s = (cudaStream_t)stream;
+    std::lock_guard<std::mutex> lk(p->mu);
+    std::vector<int> es;
+    for (int e = 0; e < p->n_experts; e++)
+        if (p->slot_of[layer * p->n_experts + e] >= 0) es.push_back(e);
+    const int n = (int)es.size();
+    if (ids && n > cap) return k3c::set_error(K3C_EFULL, "pool_acquire_resident: %d resident, room for %d", n, cap);
+    for (int e : es) {
+        const int slot = p->slot_of[layer * p->n_experts + e];
+        if (p->fill_pending[slot]) {
+            if (cudaEventQuery(p->fill_ev[slot]) == cudaSuccess) {
+                p->fill_pending[slot] = 0;
+            } else {
+                cudaError_t err = cudaStreamWaitEvent(s, p->fill_ev[slot], 0);
+                if (err != cudaSuccess) return k3c::set_error(K3C_ECUDA, "pool_acquire_resident: %s", cudaGetErrorString(err));
+            }
+        }
+    }
+    cudaGetLastError();   // a not-ready event query is not an error
+    for (int i = 0; i < n; i++) {
+        p->pins[p->slot_of[layer * p->n_experts + es[i]]]++;
+        if (ids) ids[i] = es[i];
+    }
+    if (dev_run_of) {
+        const int b = p->stage_next;
+        p->stage_next = (b + 1) % kStageRing;
+        cudaEventSynchronize(p->stage_ev[b]);
+        int *h = p->stage[b];
+        for (int e = 0; e < p->n_experts; e++) h[e] = -1;
+        for (int e : es) h[e] = p->slot_of[layer * p->n_experts + e];
+        cudaError_t err = cudaMemcpyAsync(dev_run_of, h, (size_t)p->n_experts * sizeof(int), cudaMemcpyHostToDevice, s);
+        if (err == cudaSuccess) err = cudaEventRecord(p->stage_ev[b], s);
+        if (err != cudaSuccess) return k3c::set_error(K3C_ECUDA, "pool_acquire_resident: %s", cudaGetErrorString(err));
+    }
+    return n;
+}
+
+int64_t k3c_pool_trace(k3c_expert_pool *p, int32_t *out, int64_t cap) {
+    if (!p) return -1;
+    std::lock_guard<std::mutex> lk(p->mu);
+    const int64_t n = (int64_t)p->trace.size();
+    if (out)
+        for (int64_t i = 0; i < n && i < cap; i++) out[i] = p->trace[(size_t)i];
+    return n;
+}
+
+int k3c_pool_hist(k3c_expert_pool *p, uint32_t *out) {
+    if (!p || !out) return K3C_EINVAL;
+    std::lock_guard<std::mutex> lk(p->mu);
+    for (size_t i = 0; i < p->hist.size(); i++) out[i] = p->hist[i];
+    return K3C_OK;
+}
+
+int k3c_pool_dump_trace(k3c_expert_pool *p, const char *path) {
+    if (!p || !path) return -1;
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (p->trace.empty()) return -1;
+    FILE *f = fopen(path, "wb");
+    if (!f) return -1;
+    const size_t n = fwrite(p->trace.data(), sizeof(int32_t), p->trace.size(), f);
+    fclose(f);
+    return n == p->trace.size() ? 0 : -1;
+}
+
+int k3c_pool_dump_hist(k3c_expert_pool *p, const char *path) {
+    if (!p || !path) return -1;
+    std::lock_guard<std::mutex> lk(p->mu);
+    FILE *f = fopen(path, "w");
+    if (!f) return -1;
+    fprintf(f, "{\"n_layers\":%d,\"n_experts\":%d,\"counts\":{", p->n_layers, p->n_experts);
+    bool first = true;
+    for (int L = 0; L < p->n_layers; L++)
+        for (int e = 0; e < p->n_experts; e++) {
+            const uint32_t v = p->hist[(size_t)L * p->n_experts + e];
+            if (!v) continue;
+            fprintf(f, "%s\"%d,%d\":%u", first ? "" : ",", L, e, v);
+            first = false;
+        }
+    fprintf(f, "}}\n");
+    fclose(f);
+    return 0;
+}
+
+int k3c_pool_set_pin(k3c_expert_pool *p, int layer, int expert, int pin) {
+    if (!p || !key_ok(p, layer, expert)) return 0;
+    std::lock_guard<std::mutex> lk(p->mu);
+    const int slot = p->slot_of[layer * p->n_experts + expert];
+    if (slot < 0) return 0;
+    p->user_pin[slot] = pin ? 1 : 0;
+    return 1;
+}
+
+void k3c_pool_reset_stats(k3c_expert_pool *p) {
+    if (!p) return;
+    std::lock_guard<std::mutex> lk(p->mu);
+    p->st = k3c_pool_stats_t{};   // prefetch reads reset with the hits they are subtracted from
+}
+
+void k3c_pool_report(k3c_expert_pool *p, const char *label) {
+    if (!p) return;
+    std::lock_guard<std::mutex> lk(p->mu);
+    const long long n = p->st.hits + p->st.misses;
+    int resident = 0, pinned = 0;
+    for (int i = 0; i < p->nslot; i++) {
+        if (p->key_of[i] >= 0) resident++;
+        if (p->user_pin[i] || p->pinned_forever[i]) pinned++;
+    }
+    printf("pool [%s]\n", label ? label : "");
+    printf("  slots        : %d of %.2f MB = %.2f GB HBM (%d resident, %d pinned)\n", p->nslot,
+           (double)p->stride / 1e6, (double)p->stride * p->nslot / 1e9, resident, pinned);
+    printf("  requests     : %lld  hits %lld (%.2f%%)  misses %lld  evictions %lld\n", n, p->st.hits,
+           n ? 100.0 * p->st.hits / n : 0.0, p->st.misses, p->st.evictions);
+    if (p->st.prefetch_reads) {
+        const long long served = p->st.hits > p->st.prefetch_reads ? p->st.hits - p->st.prefetch_reads : 0;
+        printf("  of those hits : %lld came from the batch prefetch, i.e. copied from the host\n"
+               "                  this token; TRUE resident hit rate %.2f%%\n",
+               p->st.prefetch_reads, n ? 100.0 * served / n : 0.0);
+    }
+    printf("  copied from host: %.2f GB\n", (double)p->st.bytes_h2d / 1e9);
+    fflush(stdout);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ K3ExpertSrc adapter
+namespace {
+
+struct PoolSource {
+    K3ExpertSrc src;   // first member: a K3ExpertSrc* is a PoolSource*
+    k3c_expert_pool *pool;
+    cudaStream_t stream;
+    std::vector<std::pair<int, int>> held;   // (layer, expert) pinned for the caller
+    uint32_t magic;
+};
+constexpr uint32_t kPoolSourceMagic = 0x6b337073u;
+
+void fill_q(const k3c_expert_pool *p, int slot, K3ExpertQ *q) {
+    const k3c::PoolGeom g = k3c::pool_geom(p->hidden, p->inter);
+    const unsigned char *b = p->arena + (size_t)slot * p->stride;
+    q->p1 = b + g.gu_p;
+    q->s1 = b + g.gu_s;
+    q->p3 = nullptr;   // up is interleaved with gate inside p1 (pool format)
+    q->s3 = nullptr;
+    q->p2 = b + g.d_p;
+    q->s2 = b + g.d_s;
+}
+
+int src_get(K3ExpertSrc *self, int layer, int expert, K3ExpertQ *out) {
+    PoolSource *ps = reinterpret_cast<PoolSource *>(self);
+    int slot = -1;
+    if (k3c_pool_acquire(ps->pool, layer, &expert, 1, &slot, nullptr, (k3c_stream_t)ps->stream) != K3C_OK)
+        return -1;
+    ps->held.emplace_back(layer, expert);
+    if (out) fill_q(ps->pool, slot, out);
+    return 0;
+}
+
+int src_getmany(K3ExpertSrc *self, int layer, const int *ids, int n) {
+    PoolSource *ps = reinterpret_cast<PoolSource *>(self);
+    const int r = k3c_pool_getmany(ps->pool, layer, ids, n);
+    return r < 0 ? -1 : r;
+}
+
+int src_resident(K3ExpertSrc *self, int layer, int expert, K3ExpertQ *out) {
+    PoolSource *ps = reinterpret_cast<PoolSource *>(self);
+    k3c_expert_pool *p = ps->pool;
+    if (!key_ok(p, layer, expert)) return 0;
+    std::lock_guard<std::mutex> lk(p->mu);
+    const int slot = p->slot_of[layer * p->n_experts + expert];
+    if (slot < 0) return 0;
+    if (!out) return 1;
+    if (p->fill_pending[slot]) {
+        if (cudaEventQuery(p->fill_ev[slot]) == cudaSuccess) {
+            p->fill_pending[slot] = 0;
+        } else if (cudaStreamWaitEvent(ps->stream, p->fill_ev[slot], 0) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cudaGetLastError();
+    }
+    p->pins[slot]++;
+    ps->held.emplace_back(layer, expert);
+    fill_q(p, slot, out);
+    return 1;
+}
+
+PoolSource *as_pool_source(const K3ExpertSrc *s) {
+    if (!s || s->get != src_get) return nullptr;
+    PoolSource *ps = reinterpret_cast<PoolSource *>(const_cast<K3ExpertSrc *>(s));
+    return ps->magic == kPoolSourceMagic ? ps : nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+K3ExpertSrc *k3c_pool_source_create(k3c_expert_pool *pool, k3c_stream_t stream) {
+    k3c::clear_error();
+    if (!pool) {
+        k3c::set_error(K3C_EINVAL, "pool_source_create: null pool");
+        return nullptr;
+    }
+    PoolSource *ps = new PoolSource;
+    ps->src.get = src_get;
+    ps->src.getmany = src_getmany;
+    ps->src.resident = src_resident;
+    ps->src.ctx = ps;
+    ps->pool = pool;
+    ps->stream = (cudaStream_t)stream;
+    ps->magic = kPoolSourceMagic;
+    return &ps->src;
+}
+
+int k3c_pool_source_release(K3ExpertSrc *src) {
+    k3c::clear_error();
+    PoolSource *ps = as_pool_source(src);
+    if (!ps) return k3c::set_error(K3C_EINVAL, "pool_source_release: not a pool source");
+    int rc = K3C_OK;
+    for (const auto &h : ps->held) {
+        const int r = k3c_pool_release(ps->pool, h.first, &h.second, 1, (k3c_stream_t)ps->stream);
+        if (r != K3C_OK) rc = r;
+    }
+    ps->held.clear();
+    return rc;
+}
+
+void k3c_pool_source_destroy(K3ExpertSrc *src) {
+    PoolSource *ps = as_pool_source(src);
+    if (!ps) return;
+    k3c_pool_source_release(src);
+    ps->magic = 0;
+    delete ps;
+}
+
+k3c_stream_t k3c_pool_source_stream(const K3ExpertSrc *src) {
+    PoolSource *ps = as_pool_source(src);
+    return ps ? (k3c_stream_t)ps->stream : nullptr;
+}
+
+k3c_expert_pool *k3c_pool_source_pool(const K3ExpertSrc *src) {
+    PoolSource *ps = as_pool_source(src);
+    return ps ? ps->pool : nullptr;
+}
+
+int k3c_pool_source_slot(const K3ExpertSrc *src, const K3ExpertQ *q) {
+    PoolSource *ps = as_pool_source(src);
+    if (!ps || !q || !q->p1) return -1;
+    const k3c_expert_pool *p = ps->pool;
+    const unsigned char *a = p->arena;
+    if (q->p1 < a || q->p1 >= a + (size_t)p->nslot * p->stride) return -1;
+    const size_t off = (size_t)(q->p1 - a);
+    return off % p->stride == 0 ? (int)(off / p->stride) : -1;
 }
 
 }  // extern "C"

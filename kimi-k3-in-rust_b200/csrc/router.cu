@@ -523,11 +523,12 @@ int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype,
 
 namespace k3c {
 // The draft model's cache-only routing (src/core/k3_ops.c:580-593), one warp per token (lane
-// 0 works, in top-k order): keep the entries whose expert has a run, divide their weights by
-// the float sum of the kept weights when it is positive, and empty the remaining entries
-// (expert -1, weight 0).
+// 0 works, in top-k order): keep the entries whose expert has a run (run_of[e] in [0, n_runs),
+// the test the expert kernels apply), divide their weights by the float sum of the kept
+// weights when it is positive, and empty the remaining entries (expert -1, weight 0).
 __global__ void __launch_bounds__(128) k_route_cache_only(int *__restrict__ idx, float *__restrict__ wt, int ntok,
-                                                          int topk, const int *__restrict__ run_of, int n_experts) {
+                                                          int topk, const int *__restrict__ run_of, int n_experts,
+                                                          int n_runs) {
     __shared__ int si[4][K3_MAX_TOPK];
     __shared__ float sw[4][K3_MAX_TOPK];
     const int wl = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -539,7 +540,8 @@ __global__ void __launch_bounds__(128) k_route_cache_only(int *__restrict__ idx,
     float wsum = 0.0f;
     for (int j = 0; j < topk; j++) {
         const int e = ti[j];
-        if (e >= 0 && e < n_experts && run_of[e] >= 0) {
+        const int r = e >= 0 && e < n_experts ? run_of[e] : -1;
+        if (r >= 0 && r < n_runs) {
             si[wl][m] = e;
             sw[wl][m] = tw[j];
             wsum = __fadd_rn(wsum, tw[j]);
@@ -551,18 +553,24 @@ __global__ void __launch_bounds__(128) k_route_cache_only(int *__restrict__ idx,
         tw[j] = j < m ? (wsum > 0.0f ? __fdiv_rn(sw[wl][j], wsum) : sw[wl][j]) : 0.0f;
     }
 }
+
+int launch_route_cache_only(int *idx, float *wt, int ntok, int topk, const int *run_of, int n_experts, int n_runs,
+                            cudaStream_t s) {
+    if (ntok < 0 || topk <= 0 || topk > K3_MAX_TOPK || n_experts <= 0 || n_runs < 0)
+        return set_error(K3C_EINVAL, "route_cache_only: ntok=%d topk=%d n_experts=%d n_runs=%d", ntok, topk,
+                         n_experts, n_runs);
+    if (ntok == 0) return K3C_OK;
+    if (!idx || !wt || !run_of) return set_error(K3C_EINVAL, "route_cache_only: null pointer");
+    k_route_cache_only<<<(ntok + 3) / 4, 128, 0, s>>>(idx, wt, ntok, topk, run_of, n_experts, n_runs);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
+}
 }  // namespace k3c
 
 extern "C" int k3c_route_cache_only(int *idx, float *wt, int ntok, int topk, const int *run_of, int n_experts,
-                                    k3c_stream_t stream) {
+                                    int n_runs, k3c_stream_t stream) {
     k3c::clear_error();
-    if (ntok < 0 || topk <= 0 || topk > K3_MAX_TOPK || n_experts <= 0)
-        return k3c::set_error(K3C_EINVAL, "route_cache_only: ntok=%d topk=%d n_experts=%d", ntok, topk, n_experts);
-    if (ntok == 0) return K3C_OK;
-    if (!idx || !wt || !run_of) return k3c::set_error(K3C_EINVAL, "route_cache_only: null pointer");
-    k3c::k_route_cache_only<<<(ntok + 3) / 4, 128, 0, (cudaStream_t)stream>>>(idx, wt, ntok, topk, run_of, n_experts);
-    K3C_CHECK_LAUNCH();
-    return K3C_OK;
+    return k3c::launch_route_cache_only(idx, wt, ntok, topk, run_of, n_experts, n_runs, (cudaStream_t)stream);
 }
 
 extern "C" int k3c_router_select(int *idx, float *w, const float *scores, const float *bias,

@@ -122,6 +122,9 @@ def ref():
                                      C.POINTER(Expert6), C.c_void_p, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
                                      _i32p, _f32p]
+        L.refh_moe_call.argtypes = [C.c_int, _f32p, _f32p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p]
+        L.refh_moe_call.restype = C.c_long
         L.refh_threads.restype = C.c_int
         L.refh_set_threads.argtypes = [C.c_int]
         L.refh_set_threads.restype = None

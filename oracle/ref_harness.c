@@ -211,3 +211,19 @@ void refh_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
 int refh_threads(void) { return 1; }
 void refh_set_threads(int n) { (void)n; }
 #endif
+
+/* The reference's OWN k3_moe (prefill = 0) or k3_moe_prefill (prefill = 1) on caller-built
+ * K3MoeW / K3Cfg (the test builds them through the mirrored layouts of include/k3c.h, which is
+ * itself an ABI check) and the caller's expert source; scratch sized by k3_moe_scratch. Returns
+ * the reference's k3_expert_drops counted during the call, or -1 on allocation failure. */
+long refh_moe_call(int prefill, float *out, const float *x, int T, const K3MoeW *w, const K3Cfg *c,
+                   int *idx, float *wt)
+{
+    float *scratch = (float *)malloc(k3_moe_scratch(c) * sizeof(float));
+    if (!scratch) return -1;
+    const long d0 = k3_expert_drops;
+    if (prefill) k3_moe_prefill(out, x, w, c, T, idx, wt, scratch);
+    else         k3_moe(out, x, w, c, T, idx, wt, scratch);
+    free(scratch);
+    return k3_expert_drops - d0;
+}

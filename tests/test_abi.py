@@ -172,3 +172,74 @@ int main(void) {
     assert L.k3c_mmw(None, 8, None, 8, 33, None, 1, 8, 8, 0, None) == -1
     assert L.k3c_mmw(dummy, 8, dummy, 8, 2, dummy, 2, 8, 8, 0, None) == -1
     assert b"int8" in L.k3c_last_error()
+
+
+REF_DIR = os.path.join(ROOT, "oracle", "_ref")
+
+
+def test_reference_types_have_the_reference_layout(k3):
+    """K3ExpertQ, K3ExpertSrc, K3Cfg and K3MoeW as include/k3c.h mirrors them have the
+    offsets and sizes of the reference's include/k3/k3.h (oracle/_ref/abi_ref, built against
+    the reference's header), and the ctypes mirrors have the same."""
+    ref_exe = os.path.join(REF_DIR, "abi_ref")
+    if not os.path.exists(ref_exe):
+        import pytest
+        pytest.skip("oracle/_ref/abi_ref not built (needs the reference tree)")
+    with tempfile.TemporaryDirectory() as d:
+        exe = os.path.join(d, "abi_ours")
+        subprocess.run(["gcc", "-O1", "-std=gnu99", "-DUSE_K3C", "-I", os.path.join(ROOT, "include"),
+                        os.path.join(ROOT, "oracle", "abi_layout.c"), "-o", exe], check=True)
+        ours = subprocess.run([exe], capture_output=True, text=True, check=True).stdout
+    ref = subprocess.run([ref_exe], capture_output=True, text=True, check=True).stdout
+    assert ours == ref
+    lay = {}
+    for line in ref.splitlines():
+        parts = line.split()
+        if "." in parts[0] and len(parts) == 3:
+            lay[parts[0]] = int(parts[1])
+        elif len(parts) == 2 and parts[1].isdigit():
+            lay[parts[0]] = int(parts[1])
+    for cname, ct in (("K3Cfg", k3.K3CfgC), ("K3MoeW", k3.K3MoeWC), ("K3ExpertSrc", k3.K3ExpertSrcC),
+                      ("K3ExpertQ", k3.K3ExpertQ)):
+        assert C.sizeof(ct) == lay[cname], cname
+        for f, _ in ct._fields_:
+            assert getattr(ct, f).offset == lay[f"{cname}.{f}"], (cname, f)
+
+
+def test_k3_moe_scratch_is_the_references(k3, ora):
+    """k3_moe_scratch (no GPU needed) returns the reference's float count, so callers size
+    their scratch exactly as before."""
+    if not ora.ref_available():
+        import pytest
+        pytest.skip("oracle/_ref not built")
+    R = ora.ref()
+    R.k3_moe_scratch.restype = C.c_size_t
+    R.k3_moe_scratch.argtypes = [C.c_void_p]
+    for hidden, latent, inter, n_shared in ((128, 64, 48, 2), (7168, 3584, 3072, 2), (512, 256, 256, 0)):
+        c = k3.K3CfgC()
+        c.hidden, c.latent, c.moe_inter, c.n_shared = hidden, latent, inter, n_shared
+        assert k3.lib().k3_moe_scratch(C.byref(c)) == R.k3_moe_scratch(C.addressof(c))
+
+
+def test_reference_programs_bind_to_the_library():
+    """The reference's own test_ops and bench_kernels built against libk3cuda.so
+    (oracle/Makefile): every k3_* entry point the library defines resolves to it, both from the
+    test program and from the reference's k3_ops.c (interposition), checked by the dynamic
+    linker with all bindings resolved at start-up."""
+    exe = os.path.join(REF_DIR, "test_ops_gpu")
+    if not os.path.exists(exe):
+        import pytest
+        pytest.skip("oracle/_ref/test_ops_gpu not built")
+    env = dict(os.environ, LD_BIND_NOW="1", LD_DEBUG="bindings")
+    r = subprocess.run([exe, "/nonexistent"], capture_output=True, text=True, env=env, timeout=120)
+    bind = {}
+    for line in r.stderr.splitlines():
+        m = re.search(r"binding file (\S+) \[0\] to (\S+) \[0\]: normal symbol `(k3_\w+)'", line)
+        if m:
+            bind[(os.path.basename(m.group(1)), m.group(3))] = os.path.basename(m.group(2))
+    for sym in ("k3_moe", "k3_router", "k3_matmul", "k3_matmul_bf16", "k3_mxfp4_dequant", "k3_moe_scratch"):
+        assert bind.get(("test_ops_gpu", sym)) == "libk3cuda.so", sym
+    for sym in ("k3_moe", "k3_moe_prefill", "k3_router", "k3_matmul", "k3_matmul_bf16", "k3_matmul_mxfp4",
+                "k3_matmul_q8", "k3_expert_drops"):
+        assert bind.get(("libk3ops.so", sym)) == "libk3cuda.so", sym
+    assert bind.get(("libk3ops.so", "k3_rmsnorm")) == "libk3ops.so"   # the rest stays the reference's

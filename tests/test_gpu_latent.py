@@ -135,3 +135,33 @@ def test_latent_layer_optional_parts(k3, ora, dev, ntok, variant):
     out, idx, _ = k3.LatentMoeLayer.from_host(layer, dev).decode(T(x, dev))
     assert np.array_equal(idx.cpu().numpy(), widx)
     assert maxrel(out.cpu().numpy(), want) < 2e-2
+
+
+@pytest.mark.parametrize("ntok", [8, 48])
+def test_latent_layer_cache_only(k3, ora, dev, ntok):
+    """The draft model's cache-only routing inside the latent layer (k3c_moe_latent_layer
+    .cache_only): route among the experts with a run only, renormalise, count no drops --
+    against the reference's own k3_moe with cache_only set and an expert source whose
+    resident() reports the same set (src/core/k3_ops.c:580-593)."""
+    if not ora.ref_available():
+        pytest.skip("oracle/_ref not built")
+    import torch
+    from dropin_util import HostSource, MoeArgs, reference
+    g = k3.synth.rng(600 + ntok)
+    layer = k3.synth.latent_layer(g, 512, 256, 128, 16, 6, n_shared=1, wdt=1)
+    x = g.standard_normal((ntok, 512), dtype=np.float32)
+    resident = [e for e in range(16) if e % 4 != 2]
+    lat = k3.LatentMoeLayer.from_host(layer, dev, cache_only=1)
+    run_of = lat._keep[1]
+    run_of.copy_(torch.tensor([e if e in resident else -1 for e in range(16)], dtype=torch.int32))
+    drops = torch.zeros(1, dtype=torch.int32, device=dev)
+    out, idx, wt = lat.decode(T(x, dev), drops=drops)
+    src = HostSource(k3, layer["experts"], resident=set(resident))
+    rout, ridx, rwt, rd = reference(ora, MoeArgs(k3, layer, src.src, cache_only=1), x)
+    idx = idx.cpu().numpy()
+    assert int(drops.item()) == 0 and rd == 0
+    assert np.isin(idx[idx >= 0], resident).all() and (idx < 0).any()
+    m = int((idx[-1] >= 0).sum())
+    assert np.array_equal(idx[-1, :m], ridx[:m])
+    assert np.array_equal(wt.cpu().numpy()[-1, :m].view(np.uint32), rwt[:m].view(np.uint32))
+    assert maxrel(out.cpu().numpy(), rout) < 2e-2
