@@ -126,6 +126,12 @@ const char *k3c_version(void);
 long long k3c_launch_count(void);
 void k3c_timing_enable(int on);
 int k3c_timing_read(double *ms, long long *count, int nstage);
+/* No reference counterpart (the reference has no device waits). Runs the bounded-wait helpers
+ * every pipelined kernel here uses on a wait nothing satisfies -- kind 0: an mbarrier phase,
+ * kind 1: a release/acquire counter -- with a limit of limit_ms (<= 2000; the kernels use
+ * 2000): returns K3C_ETIMEOUT and the context stays usable. kind 2 (a satisfied counter)
+ * returns K3C_OK. Synchronises `stream`. */
+int k3c_selftest_wait(int kind, double limit_ms, k3c_stream_t stream);
 
 /* Activation / weight element types used by the k3c_* entry points. */
 enum { K3C_F32 = 0, K3C_BF16 = 1 };
@@ -373,7 +379,10 @@ int k3c_moe_decode_tc_routed(float *out, const void *x, int x_dtype, int ntok,
  * Host functions except k3c_expert_upload; none of them allocates device memory.
  * ------------------------------------------------------------------------------------ */
 /* Tensor element types of a shard (the reference's K3Dtype values, src/io/k3_st.h:35). */
-enum { K3C_DT_U8 = 1, K3C_DT_BF16 = 2, K3C_DT_F16 = 3, K3C_DT_F32 = 4 };
+enum { K3C_DT_U8 = 1, K3C_DT_BF16 = 2, K3C_DT_F16 = 3, K3C_DT_F32 = 4,
+       /* K3_DT_I8R: the draft trunk's per-row int8 rows [f32 scale][int8 * cols]; only in a
+        * packed trunk (below), never in a safetensors shard */
+       K3C_DT_I8R = 5 };
 typedef struct {
     int shard, dtype, ndim;
     int64_t off;          /* absolute byte offset in its shard file */
@@ -387,6 +396,25 @@ typedef struct k3c_ckpt k3c_ckpt;   /* the indexed shards of one checkpoint dire
  * end of the file, an unsupported dtype (U8, BF16, F16, F32 are read), a name twice. */
 k3c_ckpt *k3c_ckpt_open(const char *dir);
 void k3c_ckpt_close(k3c_ckpt *c);
+/* A packed trunk directory (src/io/k3_trunk.c:98-200; written by the reference's
+ * tools/pack_trunk.py, and as the draft model's int8 trunk by tools/int8_trunk.py): trunk.json
+ * lists per layer its run's file_off / nbytes in trunk.bin and its tensors (off within the run,
+ * nbytes, dtype, shape); dtypes BF16, F32, U8, F16 and I8R. k3c_trunk_open refuses a manifest
+ * whose tensor spans leave their run or the file, whose I8R tensor is not rows * (4 + cols)
+ * bytes for its shape [rows, cols], or whose other tensors' spans are not their shape's bytes.
+ * k3c_trunk_find: tensor `name` of `layer` with off made absolute in trunk.bin (shard 0).
+ * k3c_trunk_read: that tensor's bytes (one O_DIRECT read widened to 4096-byte boundaries when
+ * buf is page aligned and the manifest's align is 4096, as k3_trunk_open decides; a buffered
+ * read otherwise); the payload starts at buf + *payload_off. An I8R tensor feeds the draft
+ * model's K3C_WI8 trunk: copy its rows to the device and k3c_q8_pack them (in = cols,
+ * out = rows) into the k3c_q8_mat of a k3c_moe_latent_layer. */
+typedef struct k3c_trunk k3c_trunk;
+k3c_trunk *k3c_trunk_open(const char *dir);
+void k3c_trunk_close(k3c_trunk *tr);
+int k3c_trunk_layers(const k3c_trunk *tr);
+int k3c_trunk_find(const k3c_trunk *tr, int layer, const char *name, k3c_tensor *t);
+int64_t k3c_trunk_read(const k3c_trunk *tr, const k3c_tensor *t, void *buf, int64_t bufcap,
+                       int64_t *payload_off);
 int k3c_ckpt_shards(const k3c_ckpt *c);
 /* 1 when the shard could be opened for O_DIRECT reads (expert reads then bypass the page
  * cache); 0 when reads fall back to the buffered descriptor. */

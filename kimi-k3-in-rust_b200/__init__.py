@@ -243,6 +243,12 @@ def lib():
         "k3_moe_scratch": ([C.POINTER(K3CfgC)], sz),
         "k3c_dropin_keep_weights": ([i], None),
         "k3c_dropin_forget_weights": ([], None),
+        "k3c_selftest_wait": ([i, C.c_double, vp], i),
+        "k3c_trunk_open": ([C.c_char_p], vp),
+        "k3c_trunk_close": ([vp], None),
+        "k3c_trunk_layers": ([vp], i),
+        "k3c_trunk_find": ([vp, i, C.c_char_p, C.POINTER(TensorC)], i),
+        "k3c_trunk_read": ([vp, C.POINTER(TensorC), vp, C.c_int64, C.POINTER(C.c_int64)], C.c_int64),
         "k3c_ckpt_open": ([C.c_char_p], vp),
         "k3c_ckpt_close": ([vp], None),
         "k3c_ckpt_shards": ([vp], i),
@@ -948,6 +954,60 @@ def aligned_host_buffer(nbytes, align=CKPT_ALIGN):
     raw = np.empty(nbytes + align, np.uint8)
     off = (-raw.ctypes.data) % align
     return raw[off:off + nbytes]
+
+
+DT_I8R = 5
+
+
+class Trunk:
+    """A packed trunk directory (k3c_trunk_*): trunk.json + trunk.bin as the reference's
+    tools/pack_trunk.py and tools/int8_trunk.py write them; tensors by (layer, name), I8R
+    rows (the draft model's int8 trunk) included."""
+
+    def __init__(self, directory):
+        self.p = lib().k3c_trunk_open(directory.encode())
+        if not self.p:
+            raise K3CError(f"k3c_trunk_open: {lib().k3c_last_error().decode()}")
+
+    def close(self):
+        if self.p:
+            lib().k3c_trunk_close(self.p)
+            self.p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def layers(self):
+        return lib().k3c_trunk_layers(self.p)
+
+    def find(self, layer, name):
+        t = TensorC()
+        _check(lib().k3c_trunk_find(self.p, layer, name.encode(), C.byref(t)), "k3c_trunk_find")
+        return t
+
+    def read(self, t):
+        """The tensor's bytes (numpy uint8), read with O_DIRECT where the trunk allows it."""
+        buf = aligned_host_buffer(int(t.nbytes) + 2 * CKPT_ALIGN)
+        off = C.c_int64(0)
+        got = lib().k3c_trunk_read(self.p, C.byref(t), buf.ctypes.data, buf.size, C.byref(off))
+        if got != t.nbytes:
+            raise K3CError(f"k3c_trunk_read: {lib().k3c_last_error().decode()}")
+        return buf[off.value:off.value + int(t.nbytes)].copy()
+
+    def q8_mat(self, layer, name, device):
+        """An I8R tensor as the draft model's K3C_WI8 trunk matrix: its rows copied to the device
+        and packed (k3c_q8_pack). Returns (Q8MatC, the device arrays it points at)."""
+        import torch
+        t = self.find(layer, name)
+        if t.dtype != DT_I8R:
+            raise K3CError(f"{name} is dtype {t.dtype}, not I8R")
+        rows = torch.from_numpy(self.read(t)).to(device)
+        wq, ws, ldw = q8_pack(rows, int(t.shape[1]), int(t.shape[0]))
+        return Q8MatC(wq.data_ptr(), ws.data_ptr(), ldw), (wq, ws)
 
 
 class Checkpoint:

@@ -270,17 +270,16 @@ static int index_shard(k3c_ckpt *c, int shard, const std::string &path) {
 // Widened O_DIRECT read of [off, off + n) into buf (page aligned, bufcap bytes); the payload
 // starts at *pad. Without an O_DIRECT descriptor, or into a buffer that is not page aligned, a
 // buffered read at buf + 0.
-static int64_t read_span(const k3c_ckpt *c, int shard, int64_t off, int64_t n, void *buf, int64_t bufcap,
-                         int64_t *pad) {
+static int64_t read_fd_span(int fd, int dfd_in, int64_t off, int64_t n, void *buf, int64_t bufcap, int64_t *pad) {
     // O_DIRECT also needs the destination aligned: a buffer that is not takes the buffered path
-    const int dfd = ((uintptr_t)buf % CK_ALIGN) ? -1 : c->dfd[shard];
+    const int dfd = ((uintptr_t)buf % CK_ALIGN) ? -1 : dfd_in;
     if (dfd < 0) {
         if (pad) *pad = 0;
         if (bufcap < n) return 0;
         int64_t got = 0;
         while (got < n) {
             const int64_t want = std::min(n - got, CK_READ_MAX);
-            const ssize_t r = pread(c->fd[shard], (char *)buf + got, (size_t)want, (off_t)(off + got));
+            const ssize_t r = pread(fd, (char *)buf + got, (size_t)want, (off_t)(off + got));
             if (r <= 0) break;
             got += r;
         }
@@ -299,6 +298,11 @@ static int64_t read_span(const k3c_ckpt *c, int shard, int64_t off, int64_t n, v
     }
     const int64_t pl = off - lo;
     return got >= pl + n ? n : (got > pl ? got - pl : 0);
+}
+
+static int64_t read_span(const k3c_ckpt *c, int shard, int64_t off, int64_t n, void *buf, int64_t bufcap,
+                         int64_t *pad) {
+    return read_fd_span(c->fd[shard], c->dfd[shard], off, n, buf, bufcap, pad);
 }
 
 }  // namespace k3c
@@ -498,4 +502,218 @@ extern "C" int k3c_expert_upload(uint8_t *dev_run, const k3c_expert_run *r, cons
     q.p2 = dev_staging + r->m[1].p_off;
     q.s2 = dev_staging + r->m[1].s_off;
     return k3c_pool_pack_expert(dev_run, &q, hidden, inter, stream);
+}
+
+// ------------------------------------------------------------------ packed trunk
+// trunk.json: {"align": 4096, "layers": [{"file_off": F, "nbytes": N, "tensors": {name: {"off": o,
+// "nbytes": n, "dtype": "BF16" | "F32" | "U8" | "F16" | "I8R", "shape": [...]}}, ...}, ...]}
+// (src/io/k3_trunk.c:98-148; other keys are skipped as there).
+struct k3c_trunk {
+    int fd = -1, dfd = -1;
+    int64_t align = 0;
+    struct Layer {
+        int64_t file_off = 0, nbytes = 0;
+        std::unordered_map<std::string, k3c_tensor> t;
+    };
+    std::vector<Layer> lay;
+};
+
+namespace k3c {
+
+static int trunk_dtype(const std::string &s) {
+    if (s == "I8R") return K3C_DT_I8R;
+    return dtype_code(s);
+}
+
+static int parse_trunk_tensor(HeaderScan &sc, k3c_tensor &t, const std::string &nm) {
+    memset(&t, 0, sizeof t);
+    if (!sc.eat('{')) return set_error(K3C_EINVAL, "trunk: tensor %s is not an object", nm.c_str());
+    bool f1 = true, got_dt = false;
+    while (!sc.eat('}')) {
+        if (!f1 && !sc.eat(',')) return set_error(K3C_EINVAL, "trunk: malformed tensor %s", nm.c_str());
+        f1 = false;
+        std::string key;
+        if (!sc.string(key) || !sc.eat(':')) return set_error(K3C_EINVAL, "trunk: malformed tensor %s", nm.c_str());
+        if (key == "off" || key == "nbytes") {
+            int64_t v;
+            if (!sc.integer(v) || v < 0) return set_error(K3C_EINVAL, "trunk: bad %s on %s", key.c_str(), nm.c_str());
+            (key == "off" ? t.off : t.nbytes) = v;
+        } else if (key == "dtype") {
+            std::string dv;
+            if (!sc.string(dv)) return set_error(K3C_EINVAL, "trunk: bad dtype on %s", nm.c_str());
+            t.dtype = trunk_dtype(dv);
+            if (!t.dtype) return set_error(K3C_EINVAL, "trunk: unsupported dtype '%s' on %s", dv.c_str(), nm.c_str());
+            got_dt = true;
+        } else if (key == "shape") {
+            if (!sc.eat('[')) return set_error(K3C_EINVAL, "trunk: bad shape on %s", nm.c_str());
+            if (!sc.eat(']'))
+                for (;;) {
+                    int64_t d;
+                    if (!sc.integer(d) || d < 0 || t.ndim == 4)
+                        return set_error(K3C_EINVAL, "trunk: bad shape on %s", nm.c_str());
+                    t.shape[t.ndim++] = d;
+                    if (sc.eat(',')) continue;
+                    if (sc.eat(']')) break;
+                    return set_error(K3C_EINVAL, "trunk: bad shape on %s", nm.c_str());
+                }
+        } else if (!sc.skip()) {
+            return set_error(K3C_EINVAL, "trunk: malformed tensor %s", nm.c_str());
+        }
+    }
+    if (!got_dt) return set_error(K3C_EINVAL, "trunk: %s has no dtype", nm.c_str());
+    // the span must be the shape's bytes; an I8R matrix is rows x (4-byte scale + cols int8)
+    int64_t want;
+    if (t.dtype == K3C_DT_I8R) {
+        if (t.ndim != 2) return set_error(K3C_EINVAL, "trunk: I8R tensor %s is not 2-D", nm.c_str());
+        want = t.shape[0] * (4 + t.shape[1]);
+    } else {
+        want = dtype_size(t.dtype);
+        for (int i = 0; i < t.ndim; i++) want *= t.shape[i];
+    }
+    if (t.nbytes != want)
+        return set_error(K3C_EINVAL, "trunk: %s spans %lld bytes, its shape needs %lld", nm.c_str(),
+                         (long long)t.nbytes, (long long)want);
+    return K3C_OK;
+}
+
+static int parse_trunk(k3c_trunk *tr, const std::string &txt) {
+    HeaderScan sc(txt.data(), txt.data() + txt.size());
+    if (!sc.eat('{')) return set_error(K3C_EINVAL, "trunk: trunk.json is not an object");
+    bool f1 = true, got_layers = false;
+    while (!sc.eat('}')) {
+        if (!f1 && !sc.eat(',')) return set_error(K3C_EINVAL, "trunk: malformed trunk.json");
+        f1 = false;
+        std::string key;
+        if (!sc.string(key) || !sc.eat(':')) return set_error(K3C_EINVAL, "trunk: malformed trunk.json");
+        if (key == "align") {
+            if (!sc.integer(tr->align)) return set_error(K3C_EINVAL, "trunk: bad align");
+        } else if (key == "layers") {
+            got_layers = true;
+            if (!sc.eat('[')) return set_error(K3C_EINVAL, "trunk: layers is not an array");
+            if (sc.eat(']')) continue;
+            for (;;) {
+                k3c_trunk::Layer L;
+                if (!sc.eat('{')) return set_error(K3C_EINVAL, "trunk: layer %zu is not an object", tr->lay.size());
+                bool g1 = true, got_t = false;
+                while (!sc.eat('}')) {
+                    if (!g1 && !sc.eat(',')) return set_error(K3C_EINVAL, "trunk: malformed layer %zu", tr->lay.size());
+                    g1 = false;
+                    std::string lk;
+                    if (!sc.string(lk) || !sc.eat(':'))
+                        return set_error(K3C_EINVAL, "trunk: malformed layer %zu", tr->lay.size());
+                    if (lk == "file_off" || lk == "nbytes") {
+                        int64_t v;
+                        if (!sc.integer(v) || v < 0) return set_error(K3C_EINVAL, "trunk: bad %s", lk.c_str());
+                        (lk == "file_off" ? L.file_off : L.nbytes) = v;
+                    } else if (lk == "tensors") {
+                        got_t = true;
+                        if (!sc.eat('{')) return set_error(K3C_EINVAL, "trunk: layer %zu tensors", tr->lay.size());
+                        bool h1 = true;
+                        while (!sc.eat('}')) {
+                            if (!h1 && !sc.eat(',')) return set_error(K3C_EINVAL, "trunk: malformed tensors");
+                            h1 = false;
+                            std::string nm;
+                            if (!sc.string(nm) || !sc.eat(':')) return set_error(K3C_EINVAL, "trunk: malformed tensors");
+                            k3c_tensor t;
+                            K3C_TRY(parse_trunk_tensor(sc, t, nm));
+                            if (!L.t.emplace(nm, t).second)
+                                return set_error(K3C_EINVAL, "trunk: %s appears twice in layer %zu", nm.c_str(),
+                                                 tr->lay.size());
+                        }
+                    } else if (!sc.skip()) {
+                        return set_error(K3C_EINVAL, "trunk: malformed layer %zu", tr->lay.size());
+                    }
+                }
+                if (!got_t) return set_error(K3C_EINVAL, "trunk: layer %zu has no tensors", tr->lay.size());
+                for (auto &kv : L.t)
+                    if (kv.second.off + kv.second.nbytes > L.nbytes)
+                        return set_error(K3C_EINVAL, "trunk: %s runs past its layer's %lld bytes", kv.first.c_str(),
+                                         (long long)L.nbytes);
+                tr->lay.push_back(std::move(L));
+                if (sc.eat(',')) continue;
+                if (sc.eat(']')) break;
+                return set_error(K3C_EINVAL, "trunk: malformed layers array");
+            }
+        } else if (!sc.skip()) {
+            return set_error(K3C_EINVAL, "trunk: malformed trunk.json");
+        }
+    }
+    if (!got_layers) return set_error(K3C_EINVAL, "trunk: no layers array");
+    return K3C_OK;
+}
+
+}  // namespace k3c
+
+extern "C" void k3c_trunk_close(k3c_trunk *tr) {
+    if (!tr) return;
+    if (tr->fd >= 0) close(tr->fd);
+    if (tr->dfd >= 0) close(tr->dfd);
+    delete tr;
+}
+
+extern "C" k3c_trunk *k3c_trunk_open(const char *dir) {
+    clear_error();
+    if (!dir) {
+        set_error(K3C_EINVAL, "trunk_open: null directory");
+        return nullptr;
+    }
+    const std::string jp = std::string(dir) + "/trunk.json", bp = std::string(dir) + "/trunk.bin";
+    FILE *f = fopen(jp.c_str(), "rb");
+    if (!f) {
+        set_error(K3C_EINVAL, "trunk_open: cannot read %s", jp.c_str());
+        return nullptr;
+    }
+    std::string txt;
+    char chunk[65536];
+    for (size_t n; (n = fread(chunk, 1, sizeof chunk, f)) > 0;) txt.append(chunk, n);
+    fclose(f);
+    k3c_trunk *tr = new k3c_trunk;
+    if (parse_trunk(tr, txt) != K3C_OK) {
+        k3c_trunk_close(tr);
+        return nullptr;
+    }
+    tr->fd = open(bp.c_str(), O_RDONLY);
+    if (tr->fd < 0) {
+        set_error(K3C_EINVAL, "trunk_open: cannot open %s", bp.c_str());
+        k3c_trunk_close(tr);
+        return nullptr;
+    }
+    struct stat st;
+    const int64_t fsize = fstat(tr->fd, &st) == 0 ? (int64_t)st.st_size : -1;
+    for (size_t i = 0; i < tr->lay.size(); i++)
+        if (tr->lay[i].file_off + tr->lay[i].nbytes > fsize) {
+            set_error(K3C_EINVAL, "trunk_open: layer %zu runs past the end of %s", i, bp.c_str());
+            k3c_trunk_close(tr);
+            return nullptr;
+        }
+    // O_DIRECT only for a trunk packed on 4096-byte boundaries (k3_trunk_open's rule)
+    if (tr->align == CK_ALIGN) tr->dfd = open(bp.c_str(), O_RDONLY | O_DIRECT);
+    return tr;
+}
+
+extern "C" int k3c_trunk_layers(const k3c_trunk *tr) { return tr ? (int)tr->lay.size() : 0; }
+
+extern "C" int k3c_trunk_find(const k3c_trunk *tr, int layer, const char *name, k3c_tensor *t) {
+    clear_error();
+    if (!tr || !name || !t || layer < 0 || layer >= (int)tr->lay.size())
+        return set_error(K3C_EINVAL, "trunk_find: bad arguments (layer %d)", layer);
+    const auto &L = tr->lay[(size_t)layer];
+    auto it = L.t.find(name);
+    if (it == L.t.end()) return set_error(K3C_ENOTFOUND, "trunk_find: %s not in layer %d", name, layer);
+    *t = it->second;
+    t->off += L.file_off;
+    t->shard = 0;
+    return K3C_OK;
+}
+
+extern "C" int64_t k3c_trunk_read(const k3c_trunk *tr, const k3c_tensor *t, void *buf, int64_t bufcap,
+                                  int64_t *payload_off) {
+    clear_error();
+    if (!tr || !t || !buf || bufcap <= 0) return set_error(K3C_EINVAL, "trunk_read: bad arguments");
+    int64_t pad = 0;
+    const int64_t got = read_fd_span(tr->fd, tr->dfd, t->off, t->nbytes, buf, bufcap, &pad);
+    if (payload_off) *payload_off = pad;
+    if (got != t->nbytes)
+        set_error(K3C_EINVAL, "trunk_read: read %lld of %lld bytes", (long long)got, (long long)t->nbytes);
+    return got;
 }

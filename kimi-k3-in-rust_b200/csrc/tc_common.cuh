@@ -57,16 +57,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, int *err, int code, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0 && globaltimer_ns() - t0 > 2000000000ull) {
+        if ((it & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
             if (err) atomicExch(err, code);
             return false;
         }
     }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    return mbar_wait_ns(bar, parity, err, code, kWaitLimitNs);
 }
 
 // ------------------------------------------------------------------ TMA / bulk copies
@@ -235,19 +239,22 @@ __device__ __forceinline__ void red_release_add1(int *ctr) {
 // between CTAs of different kernels that run at the same time. Gives up after ~2 s of device
 // time, or as soon as another thread has recorded an error, and returns false (recording
 // `code` on a timeout).
-__device__ __forceinline__ bool wait_count(const int *ctr, int target, int *err, int code) {
+__device__ __forceinline__ bool wait_count_ns(const int *ctr, int target, int *err, int code, uint64_t limit_ns) {
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 0;; ++it) {
         int v;
         asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
         if (v >= target) return true;
         if (*(volatile int *)err) return false;
-        if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+        if ((it & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) {
             atomicExch(err, code);
             return false;
         }
         __nanosleep(128);
     }
+}
+__device__ __forceinline__ bool wait_count(const int *ctr, int target, int *err, int code) {
+    return wait_count_ns(ctr, target, err, code, kWaitLimitNs);
 }
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;

@@ -89,3 +89,89 @@ def write_raw(path, header, data):
         f.write(struct.pack("<Q", len(js)))
         f.write(js)
         f.write(data)
+
+
+# ------------------------------------------------------------------ packed trunk
+TRUNK_ALIGN = 4096
+
+
+def bf16_bits_np(a):
+    """fp32 -> bf16 bit patterns, round to nearest even (finite values)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def write_bf16_trunk(directory, layers):
+    """A packed trunk in the layout tools/pack_trunk.py writes: trunk.bin with one run per
+    layer starting and ending on a 4096-byte boundary, trunk.json {"n_layers", "align",
+    "layers": [{"layer", "shard", "run_start", "nbytes", "file_off", "tensors": {name: {"off",
+    "nbytes", "dtype", "shape"}}}]}. layers: list of lists of (name, array) -- uint16 arrays
+    are BF16 bit patterns, float32 arrays F32."""
+    os.makedirs(directory, exist_ok=True)
+    man = {"n_layers": len(layers), "align": TRUNK_ALIGN, "layers": []}
+    with open(os.path.join(directory, "trunk.bin"), "wb") as f:
+        for li, tensors in enumerate(layers):
+            f.write(b"\0" * ((-f.tell()) % TRUNK_ALIGN))
+            file_off, off, ts = f.tell(), 0, {}
+            for name, a in tensors:
+                a = np.ascontiguousarray(a)
+                b = a.tobytes()
+                ts[name] = {"off": off, "nbytes": len(b), "dtype": _DT[a.dtype.type], "shape": list(a.shape)}
+                f.write(b)
+                off += len(b)
+            f.write(b"\0" * ((-f.tell()) % TRUNK_ALIGN))
+            man["layers"].append({"layer": li, "shard": "model.safetensors", "run_start": 0,
+                                  "nbytes": (off + TRUNK_ALIGN - 1) & ~(TRUNK_ALIGN - 1),
+                                  "file_off": file_off, "tensors": dict(sorted(ts.items()))})
+    with open(os.path.join(directory, "trunk.json"), "w") as f:
+        json.dump(man, f)
+    return man
+
+
+def quant_rows_int8(f32_2d):
+    """Per-row int8 rows [f32 scale][int8 * cols]: scale = max|row| / 127 in fp32 (1 for an all-zero
+    row), q = round-half-even(f / scale) clipped to [-128, 127] -- tools/int8_trunk.py:33-45."""
+    amax = np.abs(f32_2d).max(axis=1)
+    scale = (amax / np.float32(127.0)).astype(np.float32)
+    scale[scale == 0] = np.float32(1.0)
+    q = np.rint(f32_2d / scale[:, None]).clip(-128, 127).astype(np.int8)
+    rows = np.empty((f32_2d.shape[0], 4 + f32_2d.shape[1]), np.uint8)
+    rows[:, :4] = scale.view(np.uint8).reshape(-1, 4)
+    rows[:, 4:] = q.view(np.uint8)
+    return rows
+
+
+def int8_trunk(src, out):
+    """The draft trunk from a bf16 packed trunk, as tools/int8_trunk.py:58-98 makes it: every
+    2-D BF16 tensor becomes I8R rows, everything else is copied; runs keep their order and
+    4096-byte alignment, tensors are laid out in ascending source offset."""
+    os.makedirs(out, exist_ok=True)
+    man = json.load(open(os.path.join(src, "trunk.json")))
+    raw = open(os.path.join(src, "trunk.bin"), "rb").read()
+    new = {k: v for k, v in man.items() if k != "layers"}
+    new["layers"] = []
+    with open(os.path.join(out, "trunk.bin"), "wb") as f:
+        for lay in man["layers"]:
+            run = raw[lay["file_off"]:lay["file_off"] + lay["nbytes"]]
+            f.write(b"\0" * ((-f.tell()) % TRUNK_ALIGN))
+            file_off, pos, ts = f.tell(), 0, {}
+            for name, t in sorted(lay["tensors"].items(), key=lambda kv: kv[1]["off"]):
+                b = run[t["off"]:t["off"] + t["nbytes"]]
+                shape = t.get("shape", [])
+                if t["dtype"] == "BF16" and len(shape) == 2:
+                    u = np.frombuffer(b, np.uint16).reshape(shape)
+                    enc = quant_rows_int8((u.astype(np.uint32) << 16).view(np.float32)).tobytes()
+                    ts[name] = {"off": pos, "nbytes": len(enc), "dtype": "I8R", "shape": shape}
+                    f.write(enc)
+                    pos += len(enc)
+                else:
+                    ts[name] = {"off": pos, "nbytes": len(b), "dtype": t["dtype"], "shape": shape}
+                    f.write(b)
+                    pos += len(b)
+            f.write(b"\0" * ((-f.tell()) % TRUNK_ALIGN))
+            nl = {k: v for k, v in lay.items() if k not in ("file_off", "nbytes", "tensors")}
+            nl.update({"file_off": file_off, "nbytes": (pos + TRUNK_ALIGN - 1) & ~(TRUNK_ALIGN - 1), "tensors": ts})
+            new["layers"].append(nl)
+    with open(os.path.join(out, "trunk.json"), "w") as f:
+        json.dump(new, f)
+    return new

@@ -2,11 +2,13 @@
 the reference's own shard index and expert loader (k3_st_open, k3_expert_ref,
 k3_expert_load_direct compiled into oracle/_ref) and against the bytes the test wrote."""
 import ctypes as C
+import json
 import os
 
 import numpy as np
 import pytest
 
+import ckpt_util as ck
 from ckpt_util import EXPERT, build_checkpoint, write_raw, write_shard
 
 REF = pytest.mark.skipif("not __import__('oracle.oracle', fromlist=['x']).ref_available()")
@@ -163,3 +165,82 @@ def test_bad_headers_rejected_like_reference(k3, ora, tmp_path, hdr):
         k3.Checkpoint(d)
     if ora.ref_available():
         assert ora.ref_st_find(d, ["x"]) is None
+
+
+# ------------------------------------------------------------------ packed (draft) trunk
+REF_INT8_TRUNK = "/root/reference/tools/int8_trunk.py"
+
+
+def _trunk_layers(seed):
+    g = np.random.default_rng(seed)
+
+    def bf(r, c):
+        return ck.bf16_bits_np(g.standard_normal((r, c), dtype=np.float32) * np.float32(0.05))
+
+    layers = []
+    for li in range(2):
+        p = f"language_model.model.layers.{li}."
+        down = bf(64, 96) if li == 0 else np.zeros((64, 96), np.uint16)   # an all-zero matrix: scale 1
+        layers.append([(p + "block_sparse_moe.down_proj.weight", down),
+                       (p + "block_sparse_moe.up_proj.weight", bf(96, 64)),
+                       (p + "block_sparse_moe.shared_experts.w1.weight", bf(32, 96)),
+                       (p + "post_attention_layernorm.weight", np.ones(96, np.float32)),
+                       (p + "block_sparse_moe.gate.e_score_correction_bias", g.standard_normal(8, dtype=np.float32))])
+    return layers
+
+
+def test_int8_trunk_restatement_matches_reference_tool(tmp_path):
+    """tests/ckpt_util.int8_trunk (the draft trunk the layer tests read) writes the same bytes and
+    manifest as the reference's own tools/int8_trunk.py on the same bf16 packed trunk, including
+    an all-zero matrix (scale 1)."""
+    import os
+    import subprocess
+    import sys
+    if not os.path.exists(REF_INT8_TRUNK):
+        pytest.skip("the reference tree is not present")
+    src = str(tmp_path / "bf16")
+    ck.write_bf16_trunk(src, _trunk_layers(1))
+    ck.int8_trunk(src, str(tmp_path / "ours"))
+    subprocess.run([sys.executable, REF_INT8_TRUNK, src, str(tmp_path / "ref")], check=True, capture_output=True)
+    assert open(tmp_path / "ours" / "trunk.bin", "rb").read() == open(tmp_path / "ref" / "trunk.bin", "rb").read()
+    assert json.load(open(tmp_path / "ours" / "trunk.json")) == json.load(open(tmp_path / "ref" / "trunk.json"))
+
+
+def test_trunk_reader_knows_i8r(k3, tmp_path):
+    """k3c_trunk_*: every tensor of a draft trunk by (layer, name) with its dtype (I8R for the
+    quantised matrices, F32 for the rest), absolute offset and shape; the bytes read (O_DIRECT
+    into an aligned buffer, buffered otherwise) are the file's."""
+    src, out = str(tmp_path / "bf16"), str(tmp_path / "i8")
+    ck.write_bf16_trunk(src, _trunk_layers(2))
+    man = ck.int8_trunk(src, out)
+    raw = open(tmp_path / "i8" / "trunk.bin", "rb").read()
+    tr = k3.Trunk(out)
+    assert tr.layers == 2
+    for li, lay in enumerate(man["layers"]):
+        for name, t in lay["tensors"].items():
+            got = tr.find(li, name)
+            assert got.dtype == (k3.DT_I8R if t["dtype"] == "I8R" else {"F32": 4, "BF16": 2}[t["dtype"]])
+            assert got.off == lay["file_off"] + t["off"] and got.nbytes == t["nbytes"]
+            assert [got.shape[i] for i in range(got.ndim)] == t["shape"]
+            assert tr.read(got).tobytes() == raw[got.off:got.off + got.nbytes]
+    rows = tr.read(tr.find(0, "language_model.model.layers.0.block_sparse_moe.down_proj.weight")).reshape(64, 100)
+    assert np.all(rows[:, :4].view(np.float32) > 0)
+    with pytest.raises(k3.K3CError, match="not in layer"):
+        tr.find(1, "nope")
+    tr.close()
+
+
+@pytest.mark.parametrize("edit,match", [
+    (lambda t: t.update(nbytes=t["nbytes"] - 1), "spans"),
+    (lambda t: t.update(dtype="Q4"), "unsupported dtype"),
+    (lambda t: t.update(off=10 ** 9), "runs past"),
+    (lambda t: t.update(shape=[64]), "not 2-D"),
+])
+def test_trunk_reader_refuses_bad_manifests(k3, tmp_path, edit, match):
+    src, out = str(tmp_path / "bf16"), str(tmp_path / "i8")
+    ck.write_bf16_trunk(src, _trunk_layers(3))
+    man = ck.int8_trunk(src, out)
+    edit(man["layers"][0]["tensors"]["language_model.model.layers.0.block_sparse_moe.down_proj.weight"])
+    json.dump(man, open(tmp_path / "i8" / "trunk.json", "w"))
+    with pytest.raises(k3.K3CError, match=match):
+        k3.Trunk(out)

@@ -58,3 +58,32 @@ def test_decode_from_checkpoint_runs(k3, ora, tmp_path):
     ref, ridx, _ = ora.moe_layer(xf, k3.synth.bf16_to_f32(wb), None, experts, None, H, I, K)
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert maxrel(out.cpu().numpy(), ref) < 2e-2
+
+
+def test_latent_layer_from_an_int8_draft_trunk(k3, ora, tmp_path):
+    """The draft model's layer fed from a packed int8 trunk (the I8R tensors tools/int8_trunk.py
+    writes, read by k3c_trunk_*): its down/up/shared matrices packed for the int8 tensor-core
+    GEMV, the layer within 2e-2 of the oracle's k3_moe on the same int8 rows, routing exact."""
+    import torch
+    import ckpt_util as ck
+    from conftest import maxrel
+    g = k3.synth.rng(808)
+    lay = k3.synth.latent_layer(g, 512, 256, 128, 16, 4, n_shared=1, wdt=1)
+    names = {k: f"language_model.model.layers.0.block_sparse_moe.{k}.weight" for k in ("down", "up", "sh1", "sh3", "sh2")}
+    ck.write_bf16_trunk(str(tmp_path / "bf16"), [[(names[k], lay[k]) for k in names]])
+    ck.int8_trunk(str(tmp_path / "bf16"), str(tmp_path / "i8"))
+    tr = k3.Trunk(str(tmp_path / "i8"))
+    i8 = dict(lay, wdt=2)
+    for k, n in names.items():
+        t = tr.find(0, n)
+        assert t.dtype == k3.DT_I8R
+        i8[k] = tr.read(t).reshape(int(t.shape[0]), 4 + int(t.shape[1]))
+    mat, keep = tr.q8_mat(0, names["down"], "cuda")
+    wq, ws, ldw = k3.q8_pack(torch.from_numpy(i8["down"]).cuda(), 512, 256)
+    assert torch.equal(keep[0], wq) and torch.equal(keep[1], ws) and mat.ldw == ldw
+    x = g.standard_normal((5, 512), dtype=np.float32)
+    want, widx, _ = ora.moe_latent(x, i8)
+    out, idx, _ = k3.LatentMoeLayer.from_host(i8, "cuda").decode(torch.from_numpy(x).cuda())
+    assert np.array_equal(idx.cpu().numpy(), widx)
+    assert maxrel(out.cpu().numpy(), want) < 2e-2
+    tr.close()
