@@ -1106,10 +1106,12 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     if ws > 1:
         dist.broadcast(bias, 0)
     if place == "balanced" and ws > 1:
-        # expert placement from the pair counts of a routing sample (the sample the bias was
-        # fitted on, routed with it): greedy, heaviest expert to the least-loaded rank
+        # expert placement from a routing sample (the sample the bias was fitted on, routed with
+        # it): an expert's GEMM time goes with its 128-row slots, so its load is its expected
+        # slot count at the full batch; greedy, heaviest expert to the least-loaded rank
         sidx, _, _ = k3.router(sample, W, bias, K)
-        load = torch.bincount(sidx.reshape(-1).long(), minlength=E).double()
+        pairs = torch.bincount(sidx.reshape(-1).long(), minlength=E).double() * (EP_T / sample.shape[0])
+        load = torch.ceil(pairs / 128.0)
         dist.broadcast(load, 0)
         owner_l, lists = k3.ep.balanced_placement(load.cpu().tolist(), ws)
     else:
@@ -1157,13 +1159,14 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     launches = L.k3c_launch_count() - launches0
     L.k3c_timing_enable(0)
     L.k3c_timing_read(ms_buf, n_buf, 4)
-    stages = {name: ms_buf[j] / steps for j, name in enumerate(("experts", "router", "partial_rows"))}
+    stages = {name: ms_buf[j] / steps for j, name in enumerate(("experts", "router", "combine"))}
     dist.barrier()
     torch.cuda.synchronize()
     clocks = clk.stop()
     dt_local = e0.elapsed_time(e1) / 1e3
     # NVLink traffic of one layer, from this rank's tokens' routing: a token is read once by
-    # every other rank that owns one of its experts, and that rank stores one partial row back
+    # every other rank that owns one of its experts, and each of its pairs computed elsewhere
+    # comes back as one bf16 row
     out_ep = epl.forward(xs[0], **fwd_kw)
     idx_ep = (epl.idx_buf[:T].clone() if impl == "fused" else k3.router(xs[0], W, bias, K)[0])
     dest = owner[idx_ep.long()]
@@ -1171,6 +1174,7 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     member.scatter_(1, dest, True)
     member[:, rank] = False
     remote_rows = float(member.sum().item())
+    remote_pairs = float((dest != rank).sum().item())
     # parity: 64 of this rank's tokens against the single-GPU layer over the full bank
     maxrel, idx_ok = 0.0, 1.0
     sel = None
@@ -1184,15 +1188,18 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
         maxrel = float(((got - ref_o.double()).abs().max() / ref_o.double().abs().max()).item())
         idx_ok = float(torch.equal(ref_i, idx_ep[sel]))
         del full
-    t = torch.tensor([dt_local, remote_rows, maxrel, -idx_ok], dtype=torch.float64, device=dev)
+    t = torch.tensor([dt_local, remote_rows, maxrel, -idx_ok, remote_pairs, stages["experts"]], dtype=torch.float64,
+                     device=dev)
     if ws > 1:
         mx = t.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         sm = t.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         dt, rows_all, maxrel_all, idx_all = float(mx[0]), float(sm[1]), float(mx[2]), -float(mx[3])
+        pairs_all, exp_max, exp_mean = float(sm[4]), float(mx[5]), float(sm[5]) / ws
     else:
         dt, rows_all, maxrel_all, idx_all = dt_local, remote_rows, maxrel, idx_ok
+        pairs_all, exp_max, exp_mean = remote_pairs, stages["experts"], stages["experts"]
     if impl == "fused":
         epl.close()
     if rank != 0:
@@ -1200,6 +1207,8 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     cpu, ora_par = (None, None)
     if parity and not args.no_cpu:
         cpu, ora_par = ep_cpu_leg(k3, ref_runs, W, bias, xs[0][sel], out_ep[sel], idx_ep[sel])
+        if ws > 1:
+            cpu = None   # a CPU baseline is reported at N = 1 only; the check above still ran
     flop = (EP_T * K + EP_T) * 2 * 3 * I * H
     return {
         "workload": EP_WORKLOAD, "tokens": EP_T, "n_gpus": ws, "steps": steps, "warmup": warmup,
@@ -1209,10 +1218,11 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
         "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
         "useful_tflops": flop * steps / dt / 1e12,
         "stages_ms_per_step_rank0": stages,
+        "expert_stage_ms_max_over_ranks": exp_max, "expert_stage_ms_mean_over_ranks": exp_mean,
         "nvlink_per_step": {"remote_token_rows_read": rows_all, "bytes_read": rows_all * H * 2,
-                            "partial_rows_written": rows_all, "bytes_written": rows_all * (H * 4 + 4),
+                            "pair_rows_written": pairs_all, "bytes_written": pairs_all * H * 2,
                             "how": "bf16 token rows read by each rank that owns one of the token's experts; "
-                                   "one fp32 partial row (and its flag) stored back per (token, rank)"}
+                                   "one bf16 pair row stored at the token's owner per pair computed elsewhere"}
         if impl == "fused" else None,
         "parity": {"tokens_per_rank": 64 if parity else 0, "maxrel_vs_single_gpu": maxrel_all if parity else None,
                    "indices_equal_single_gpu": bool(idx_all == 1.0) if parity else None,

@@ -546,23 +546,23 @@ int k3c_moe_combine(float *out, const float *contrib, const float *wt, const int
 
 /* ---- Expert-parallel prefill over peer memory (no reference counterpart: the reference is
  * a single-process CPU engine). The ranks of one node each own a set of routed experts (the
- * layer's run table marks the others -1; every id must be owned by exactly one rank) and
- * their own tokens. Per layer, with a cross-rank barrier (a one-element NCCL all-reduce on
- * the stream) between the steps:
+ * layer's run table marks the others -1) and their own tokens. Per layer, with a cross-rank
+ * barrier (a one-element NCCL all-reduce on the stream) between the steps:
  *   1. each rank writes its tokens' bf16 or fp32 activations into its x buffer and their
  *      top-k ids and weights into its idx and wt buffers (k3c_router_ws);  -- barrier
  *   2. k3c_moe_prefill_ep_experts on every rank: plans over all ranks' pairs (reading the
  *      peers' idx), quantises the tokens it needs straight out of the peers' x buffers
- *      (loads over NVLink), runs its own experts and its own tokens' shared expert, adds each
- *      token's pairs on this rank in top-k order (weights read from the token owner's wt)
- *      and stores that partial row into the owner's partial buffer, setting the owner's flag
- *      for (this rank, token) (stores over NVLink);                          -- barrier
- *   3. k3c_moe_ep_combine on every rank: its tokens' flagged partials added in rank order;
- *      the flags are cleared for the next layer.
+ *      (loads over NVLink), runs its own experts over them and its own tokens' shared expert;
+ *      the down-projection epilogue stores each pair's output as a bf16 row at [t][k] of the
+ *      token owner's receive buffer (stores over NVLink, overlapping the MMAs of the next
+ *      tiles; the shared expert's row at [t][topk]);                          -- barrier
+ *   3. k3c_moe_ep_combine on every rank: its tokens' rows added in top-k order with its own
+ *      weights, then the shared row -- the single-GPU combine, so the result equals
+ *      k3c_moe_prefill_tc of the same layer bit for bit. A pair whose expert no rank holds
+ *      (expert_rank[e] < 0) is skipped.
  * Buffers are exchanged once per process: k3c_ep_alloc gives device memory and its IPC
- * handle, k3c_ep_open maps a peer's handle (same node). The partial buffer holds
- * [world][t_max][hidden] fp32, the flag buffer [world][t_max] ints (zero before the first
- * layer). ---- */
+ * handle, k3c_ep_open maps a peer's handle (same node). The receive buffer holds
+ * [t_max][topk+1][hidden] bf16 (2 bytes each). ---- */
 #define K3C_EP_MAX 8
 typedef struct {
     unsigned char bytes[64];
@@ -580,14 +580,15 @@ typedef struct {
     const void *x[K3C_EP_MAX];    /* each rank's activations [t_max][hidden] */
     const int *idx[K3C_EP_MAX];   /* each rank's top-k ids [t_max][topk] */
     const float *wt[K3C_EP_MAX];  /* each rank's top-k weights [t_max][topk] */
-    float *partial[K3C_EP_MAX];   /* each rank's received partial rows [world][t_max][hidden] */
-    int *flag[K3C_EP_MAX];        /* each rank's received-row flags [world][t_max] */
+    uint16_t *recv[K3C_EP_MAX];   /* each rank's pair rows [t_max][topk+1][hidden], bf16 */
 } k3c_ep_peers;
 size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers);
 int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers,
                                void *scratch, size_t scratch_bytes, k3c_stream_t stream);
-/* Step 3: out [ntok of this rank][hidden] fp32. */
-int k3c_moe_ep_combine(float *out, const k3c_ep_peers *peers, int hidden, k3c_stream_t stream);
+/* Step 3: out [ntok of this rank][hidden] fp32; expert_rank (device, n_experts ints): the rank
+ * holding each expert, -1 for none; has_shared: the layer has a shared expert. */
+int k3c_moe_ep_combine(float *out, const k3c_ep_peers *peers, int hidden, int topk,
+                       const int *expert_rank, int n_experts, int has_shared, k3c_stream_t stream);
 
 /* ---- HBM expert pool: the reference's expert cache (src/cache/k3_cache.c:24-261) with
  * experts streamed from pinned host memory. A slot holds one pool-format run

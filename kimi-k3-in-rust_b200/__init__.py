@@ -102,7 +102,7 @@ class EpPeersC(C.Structure):
 
     _fields_ = [("world", C.c_int), ("rank", C.c_int), ("t_max", C.c_int), ("x_dtype", C.c_int),
                 ("ntok", C.c_int * EP_MAX), ("x", C.c_void_p * EP_MAX), ("idx", C.c_void_p * EP_MAX),
-                ("wt", C.c_void_p * EP_MAX), ("partial", C.c_void_p * EP_MAX), ("flag", C.c_void_p * EP_MAX)]
+                ("wt", C.c_void_p * EP_MAX), ("recv", C.c_void_p * EP_MAX)]
 
 
 class K3CError(RuntimeError):
@@ -210,7 +210,7 @@ def lib():
         "k3c_ep_close": ([vp], i),
         "k3c_moe_prefill_ep_scratch": ([C.POINTER(MoePoolLayerC), C.POINTER(EpPeersC)], sz),
         "k3c_moe_prefill_ep_experts": ([C.POINTER(MoePoolLayerC), C.POINTER(EpPeersC), vp, sz, vp], i),
-        "k3c_moe_ep_combine": ([vp, C.POINTER(EpPeersC), i, vp], i),
+        "k3c_moe_ep_combine": ([vp, C.POINTER(EpPeersC), i, i, vp, i, i, vp], i),
         "k3_mxfp4_dequant": ([vp, vp, vp, i, i, i], None),
         "k3_matmul_mxfp4": ([vp, vp, vp, vp, i, i, i], None),
         "k3_matmul_q8": ([vp, vp, vp, i, i], None),

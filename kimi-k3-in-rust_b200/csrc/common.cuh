@@ -146,6 +146,13 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
     return __int_as_float((int)((uint32_t)h << 16));
 }
 
+// Two floats rounded to bf16 (nearest even), lo in bits 0..15, hi in bits 16..31.
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
 __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -19,9 +19,11 @@
 //           32-column block, which lies inside one thread, into the down stage's operand
 //           (same compact rows).
 //   D       per work item (slot, 256 hidden rows): the same MMA over the requantised
-//           activations; the epilogue writes each pair's unweighted expert output.
-//   combine the decode path's fixed-order weighted sum (k3_ops.c:641-642) plus the shared
-//           expert.
+//           activations; the epilogue writes each pair's unweighted expert output as a bf16
+//           row (rounded to nearest) into the token's [topk+1][H] pair rows -- in the token
+//           owner's receive buffer, over NVLink, under expert parallelism.
+//   combine the decode path's fixed-order weighted sum (k3_ops.c:641-642, fp32 products and
+//           sums of the bf16 rows) plus the shared expert.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdlib.h>
@@ -241,7 +243,7 @@ struct PfArgs {
     const uint8_t *sfa;       // A scale atoms [slot][J][KT][512]
     uint8_t *act_q;           // GU out: [J][rows_cap][I] E4M3, compact rows
     uint8_t *act_sf;          // GU out: [slot][J][I/128][512]
-    float *contrib[K3C_EP_MAX];   // D out: rank q's [tmax][topk+1][H] (one rank: [0] = [T][..])
+    uint16_t *contrib[K3C_EP_MAX];   // D out, bf16: rank q's [tmax][topk+1][H] (one rank: [0] = [T][..])
     int tmax;                     // pair token g lives on rank g / tmax, row g % tmax
     int kstride, T, H, I, act, rows_cap;
     int *err;
@@ -520,15 +522,20 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
                 if (ok && m < sl.ntok) {
                     const size_t pr = (size_t)s * PF_M + m;
                     const int g = p.pair_tok[pr];
-                    float *dst = p.contrib[g / p.tmax] + ((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H +
-                                 (size_t)nt * PF_N;
+                    uint16_t *dst = p.contrib[g / p.tmax] + ((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H +
+                                    (size_t)nt * PF_N;
 #pragma unroll
                     for (int cc = 0; cc < NC; cc++) {
-                        float4 *d4 = reinterpret_cast<float4 *>(dst + 32 * (half * NC + cc));
+                        uint4 *d4 = reinterpret_cast<uint4 *>(dst + 32 * (half * NC + cc));
 #pragma unroll
-                        for (int i = 0; i < 8; i++)
-                            d4[i] = make_float4(__uint_as_float(v[cc][4 * i]), __uint_as_float(v[cc][4 * i + 1]),
-                                                __uint_as_float(v[cc][4 * i + 2]), __uint_as_float(v[cc][4 * i + 3]));
+                        for (int i = 0; i < 4; i++) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int k = 0; k < 4; k++)
+                                w[k] = f32x2_to_bf16x2(__uint_as_float(v[cc][8 * i + 2 * k]),
+                                                       __uint_as_float(v[cc][8 * i + 2 * k + 1]));
+                            d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
                     }
                 }
             }
@@ -760,8 +767,9 @@ __global__ void __launch_bounds__(PT_THREADS) k_pf_tail(const __grid_constant__ 
                         if (i >= cn) break;
                         const size_t pr = (size_t)s * PF_M + c0 + i;
                         const int g = p.pair_tok[pr];
+                        const float f = __uint_as_float(v[i]);
                         p.contrib[g / p.tmax][((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H + h] =
-                            __uint_as_float(v[i]);
+                            (uint16_t)(f32x2_to_bf16x2(f, 0.0f) & 0xFFFFu);
                     }
                 }
             }
@@ -781,7 +789,8 @@ __global__ void __launch_bounds__(PT_THREADS) k_pf_tail(const __grid_constant__ 
 struct PfBufs {
     int *idx, *pe, *rank, *cnt, *chunk_base, *slot_base, *eoff, *n_slots, *n_rows, *err, *pair_tok, *pair_k,
         *row_tok, *full_ids, *tail_ids, *n_full, *n_tail;
-    float *wt, *contrib;
+    float *wt;
+    uint16_t *contrib;
     double *rpart;
     uint8_t *dropped, *xq, *tq, *xsf, *sfa_x, *actq, *actsf;
     SlotPf *slots;
@@ -821,7 +830,7 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T, b
     b.sfa_x = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (H / 128) * 512);
     b.actq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * I, 1024);
     b.actsf = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (I / 128) * 512);
-    b.contrib = own_contrib ? cv.take<float>((size_t)T * (K + 1) * H) : reinterpret_cast<float *>(16);
+    b.contrib = own_contrib ? cv.take<uint16_t>((size_t)T * (K + 1) * H) : reinterpret_cast<uint16_t *>(16);
     return b.idx && b.wt && b.rpart && b.pe && b.rank && b.dropped && b.cnt && b.chunk_base && b.slot_base &&
            b.eoff && b.n_slots && b.n_rows && b.err && b.slots && b.full_ids && b.tail_ids && b.n_full && b.n_tail &&
            b.pair_tok && b.pair_k && b.row_tok && b.xq &&
@@ -830,72 +839,69 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T, b
 
 static char *const kPfSizing = reinterpret_cast<char *>(4096);
 
-// Expert-parallel step 2, last kernel: one block per virtual token g (rank g / t_max, row
-// g % t_max). The token's pairs that ran on this rank (dropped = not resident here) are added
-// in top-k order with the owner's weights, the shared expert's row after them for this
-// rank's own tokens (the single-GPU combine's operations, k3_ops.c:641-642), and the partial
-// row is stored into the owner's partial buffer at [this rank][row] with its flag set. A
-// token with nothing on this rank sends nothing.
-__global__ void __launch_bounds__(128) k_ep_partial(k3c_ep_peers ep, const float *__restrict__ contrib,
-                                                    const uint8_t *__restrict__ dropped, int topk, int H,
-                                                    int has_shared) {
-    const int g = blockIdx.x, q = g / ep.t_max, t = g % ep.t_max;
-    if (t >= ep.ntok[q]) return;
-    const bool own_sh = has_shared && q == ep.rank;
-    bool any = own_sh;
-    for (int k = 0; k < topk; k++) any |= !dropped[(size_t)g * topk + k];
-    if (!any) return;
-    const float *wq = ep.wt[q] + (size_t)t * topk;
-    const int ks = topk + 1, h4 = H / 4;
-    const float4 *c4 = reinterpret_cast<const float4 *>(contrib) + (size_t)g * ks * h4;
-    float4 *dst = reinterpret_cast<float4 *>(ep.partial[q] + ((size_t)ep.rank * ep.t_max + t) * H);
-    for (int h = threadIdx.x; h < h4; h += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = 0; k < topk; k++) {
-            if (dropped[(size_t)g * topk + k]) continue;
-            const float w = wq[k];
-            const float4 c = c4[(size_t)k * h4 + h];
-            acc.x = __fadd_rn(acc.x, __fmul_rn(w, c.x));
-            acc.y = __fadd_rn(acc.y, __fmul_rn(w, c.y));
-            acc.z = __fadd_rn(acc.z, __fmul_rn(w, c.z));
-            acc.w = __fadd_rn(acc.w, __fmul_rn(w, c.w));
+// The combine over bf16 pair rows [ntok][topk+1][H]: out[t] = sum over k in top-k order of
+// wt[t][k] * row[t][k] (fp32 product and sum, each rounded, as k3_ops.c:641-642 with
+// -ffp-contract=off), then + row[t][topk] (the shared expert, unweighted). A pair is skipped
+// when dropped[t*topk+k] is set (single GPU: the expert has no run here) or, under expert
+// parallelism, when its expert id is outside [0, n_experts) or no rank holds it
+// (expert_rank[e] < 0). Eight columns per thread (one 16-byte load per row).
+__global__ void __launch_bounds__(128) k_pair_combine(float *__restrict__ out, const uint16_t *__restrict__ rows,
+                                                      const float *__restrict__ wt, const uint8_t *__restrict__ dropped,
+                                                      const int *__restrict__ ids, const int *__restrict__ expert_rank,
+                                                      int n_experts, int topk, int h8, int has_shared) {
+    const int t = blockIdx.y, ks = topk + 1;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= h8) return;
+    const uint4 *r4 = reinterpret_cast<const uint4 *>(rows) + (size_t)t * ks * h8 + c;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.0f;
+    auto add = [&](uint4 u, float w, bool weighted) {
+        const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float lo = __uint_as_float(v[i] << 16), hi = __uint_as_float(v[i] & 0xFFFF0000u);
+            acc[2 * i] = __fadd_rn(acc[2 * i], weighted ? __fmul_rn(w, lo) : lo);
+            acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], weighted ? __fmul_rn(w, hi) : hi);
         }
-        if (own_sh) {
-            const float4 c = c4[(size_t)topk * h4 + h];
-            acc.x = __fadd_rn(acc.x, c.x);
-            acc.y = __fadd_rn(acc.y, c.y);
-            acc.z = __fadd_rn(acc.z, c.z);
-            acc.w = __fadd_rn(acc.w, c.w);
+    };
+    constexpr int JM = 8;   // rows loaded ahead of their use
+    for (int j0 = 0; j0 < topk; j0 += JM) {
+        uint4 cj[JM];
+        bool use[JM];
+#pragma unroll
+        for (int i = 0; i < JM; i++) {
+            const int j = j0 + i, pi = t * topk + j;
+            bool u = j < topk;
+            if (u && dropped) u = !dropped[pi];
+            if (u && ids) {
+                const int e = ids[pi];
+                u = (unsigned)e < (unsigned)n_experts && expert_rank[e] >= 0;
+            }
+            use[i] = u;
+            if (u) cj[i] = r4[(size_t)j * h8];
         }
-        dst[h] = acc;
+#pragma unroll
+        for (int i = 0; i < JM; i++)
+            if (use[i]) add(cj[i], wt[t * topk + j0 + i], true);
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        ep.flag[q][(size_t)ep.rank * ep.t_max + t] = 1;
-    }
+    if (has_shared) add(r4[(size_t)topk * h8], 1.0f, false);
+    float4 *o = reinterpret_cast<float4 *>(out + (size_t)t * 8 * h8) + 2 * c;
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-// Expert-parallel step 3: this rank's tokens, the flagged partial rows added in rank order;
-// the flags are cleared for the next layer.
-__global__ void __launch_bounds__(128) k_ep_combine(float *__restrict__ out, k3c_ep_peers ep, int H) {
-    const int t = blockIdx.x, h4 = H / 4;
-    const float *part = ep.partial[ep.rank];
-    int *flag = ep.flag[ep.rank];
-    for (int h = threadIdx.x; h < h4; h += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int q = 0; q < ep.world; q++) {
-            if (!flag[(size_t)q * ep.t_max + t]) continue;
-            const float4 c = reinterpret_cast<const float4 *>(part + ((size_t)q * ep.t_max + t) * H)[h];
-            acc.x = __fadd_rn(acc.x, c.x);
-            acc.y = __fadd_rn(acc.y, c.y);
-            acc.z = __fadd_rn(acc.z, c.z);
-            acc.w = __fadd_rn(acc.w, c.w);
-        }
-        reinterpret_cast<float4 *>(out + (size_t)t * H)[h] = acc;
-    }
-    __syncthreads();
-    if (threadIdx.x < ep.world) flag[(size_t)threadIdx.x * ep.t_max + t] = 0;
+static int launch_pair_combine(float *out, const uint16_t *rows, const float *wt, const uint8_t *dropped,
+                               const int *ids, const int *expert_rank, int n_experts, int ntok, int topk, int hidden,
+                               int has_shared, cudaStream_t s) {
+    if (ntok <= 0) return K3C_OK;
+    if (hidden % 8 || ((uintptr_t)out & 15) || ((uintptr_t)rows & 15))
+        return set_error(K3C_EINVAL, "pair_combine: hidden=%d (a multiple of 8) and 16-byte aligned rows", hidden);
+    const int h8 = hidden / 8;
+    k_pair_combine<<<dim3((h8 + 127) / 128, ntok), 128, 0, s>>>(out, rows, wt, dropped, ids, expert_rank, n_experts,
+                                                                 topk, h8, has_shared);
+    K3C_CHECK_LAUNCH();
+    return K3C_OK;
 }
 
 size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contrib = true) {
@@ -949,7 +955,7 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         return set_error(K3C_EINVAL, "moe_prefill_tc: bad arena");
     Carve cv{(char *)scratch, scratch_bytes, 0};
     PfBufs b;
-    if (!carve_pf(cv, b, L, T))
+    if (!carve_pf(cv, b, L, T, !ep))
         return set_error(K3C_EINVAL, "moe_prefill_tc: scratch too small (%zu)", scratch_bytes);
     int *idx = idx_out ? idx_out : b.idx;
     float *wt = wt_out ? wt_out : b.wt;
@@ -1046,7 +1052,9 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     a.run_stride = L->run_stride;
     a.act_q = b.actq;
     a.act_sf = b.actsf;
-    a.contrib[0] = b.contrib;   // pair outputs stay on this rank ([T][topk+1][H])
+    a.contrib[0] = b.contrib;   // one rank: the pair rows stay here ([T][topk+1][H])
+    if (ep)                     // expert parallelism: each pair's row goes to its token's owner
+        for (int q = 0; q < ep->world; q++) a.contrib[q] = ep->recv[q];
     a.tmax = T;
     a.kstride = K + 1;
     a.T = T;
@@ -1088,13 +1096,8 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     stage_end(STAGE_EXPERTS, s);
     if (!ep) {
         stage_begin(STAGE_COMBINE, s);
-        K3C_TRY(launch_moe_combine(out, b.contrib, wt, b.dropped, T, K, H, L->shared_run >= 0 ? 1 : 0, s));
-        stage_end(STAGE_COMBINE, s);
-    } else {
-        // this rank's pairs of every token, summed per token and stored at the token's owner
-        stage_begin(STAGE_COMBINE, s);
-        k_ep_partial<<<T, 128, 0, s>>>(*ep, b.contrib, b.dropped, K, H, L->shared_run >= 0 ? 1 : 0);
-        K3C_CHECK_LAUNCH();
+        K3C_TRY(launch_pair_combine(out, b.contrib, wt, b.dropped, nullptr, nullptr, 0, T, K, H,
+                                    L->shared_run >= 0 ? 1 : 0, s));
         stage_end(STAGE_COMBINE, s);
     }
     // K3C_SYNC_CHECK=1: synchronise and report the kernels' own error code (a bounded wait
@@ -1139,27 +1142,30 @@ static int check_ep(const k3c_moe_pool_layer *L, const k3c_ep_peers *ep) {
         return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: x_dtype=%d", ep->x_dtype);
     for (int q = 0; q < ep->world; q++)
         if (ep->ntok[q] < 0 || ep->ntok[q] > ep->t_max || !ep->x[q] || !ep->idx[q] || !ep->wt[q] ||
-            !ep->partial[q] || !ep->flag[q] || ((uintptr_t)ep->x[q] & 15) || ((uintptr_t)ep->partial[q] & 15))
+            !ep->recv[q] || ((uintptr_t)ep->x[q] & 15) || ((uintptr_t)ep->recv[q] & 15))
             return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: rank %d's buffers (ntok %d)", q, ep->ntok[q]);
-    if (L->hidden % 4) return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: hidden=%d", L->hidden);
+    if (L->hidden % 8) return k3c::set_error(K3C_EINVAL, "moe_prefill_ep: hidden=%d", L->hidden);
     return K3C_OK;
 }
 
 extern "C" size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers) {
     if (check_ep(L, peers)) return 0;
-    return k3c::moe_prefill_tc_scratch(L, peers->world * peers->t_max);
+    return k3c::moe_prefill_tc_scratch(L, peers->world * peers->t_max, false);   // pair rows go to peers
 }
 
-extern "C" int k3c_moe_ep_combine(float *out, const k3c_ep_peers *peers, int hidden, k3c_stream_t stream) {
+extern "C" int k3c_moe_ep_combine(float *out, const k3c_ep_peers *peers, int hidden, int topk,
+                                  const int *expert_rank, int n_experts, int has_shared, k3c_stream_t stream) {
     k3c::clear_error();
     if (!peers || peers->world < 1 || peers->world > K3C_EP_MAX || peers->rank < 0 || peers->rank >= peers->world ||
-        hidden <= 0 || hidden % 4 || ((uintptr_t)out & 15) || !peers->partial[peers->rank] || !peers->flag[peers->rank])
+        hidden <= 0 || topk <= 0 || topk > K3_MAX_TOPK || !expert_rank || n_experts <= 0 ||
+        !peers->recv[peers->rank] || !peers->idx[peers->rank] || !peers->wt[peers->rank])
         return k3c::set_error(K3C_EINVAL, "moe_ep_combine: bad arguments");
-    const int n = peers->ntok[peers->rank];
-    if (n <= 0) return K3C_OK;
-    k3c::k_ep_combine<<<n, 128, 0, (cudaStream_t)stream>>>(out, *peers, hidden);
-    K3C_CHECK_LAUNCH();
-    return K3C_OK;
+    const int r = peers->rank;
+    k3c::stage_begin(k3c::STAGE_COMBINE, (cudaStream_t)stream);
+    const int rc = k3c::launch_pair_combine(out, peers->recv[r], peers->wt[r], nullptr, peers->idx[r], expert_rank,
+                                            n_experts, peers->ntok[r], topk, hidden, has_shared, (cudaStream_t)stream);
+    k3c::stage_end(k3c::STAGE_COMBINE, (cudaStream_t)stream);
+    return rc;
 }
 
 extern "C" int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers, void *scratch,

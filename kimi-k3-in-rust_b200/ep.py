@@ -119,16 +119,16 @@ class FusedExpertParallel:
 
     Per layer: (1) this rank copies its tokens into its shared x buffer and routes them into
     its shared idx / wt buffers; (2) after a barrier, every rank runs its own experts over the
-    pairs of ALL ranks (its quantisation kernel reads the peers' token rows over NVLink), adds
-    each token's pairs that ran here in top-k order and stores that one partial row into the
-    token owner's partial buffer (stores over NVLink); (3) after a second barrier, each rank
-    adds its tokens' partial rows in rank order. The result equals the single-GPU layer up to
-    the grouping of the fp32 additions (per rank, then across ranks); on one rank it is the
-    single-GPU combine.
+    pairs of ALL ranks (its quantisation kernel reads the peers' token rows over NVLink) and
+    its down-projection epilogue stores each pair's output as a bf16 row into the token
+    owner's receive buffer (stores over NVLink, overlapping the following tiles' MMAs);
+    (3) after a second barrier, each rank adds its tokens' rows in top-k order with its own
+    weights, then the shared expert's row -- the single-GPU combine, so the result equals the
+    single-GPU layer bit for bit.
 
     The barriers are one-element NCCL all-reduces on the current stream: a rank's step-2
     kernels start only after every rank's step-1 writes are complete, and its combine only
-    after every rank has stored its partial rows.
+    after every rank has stored its pair rows.
 
     layer: a PoolMoeLayer whose run table marks the other ranks' experts -1 and whose shared
     run is the shared expert (each rank computes its own tokens' shared expert).
@@ -150,7 +150,7 @@ class FusedExpertParallel:
         esize = torch.empty(0, dtype=self.x_dtype).element_size()
         W_, T_ = self.world, self.t_max
         sizes = {"x": T_ * self.H * esize, "idx": T_ * self.K * 4, "wt": T_ * self.K * 4,
-                 "partial": W_ * T_ * self.H * 4, "flag": W_ * T_ * 4}
+                 "recv": T_ * (self.K + 1) * self.H * 2}
         self._own, handles = {}, {}
         for name, nb in sizes.items():
             ptr, h = C.c_void_p(), k3.IpcHandleC()
@@ -161,7 +161,15 @@ class FusedExpertParallel:
         self.x_buf = k3.device_view(self._own["x"], (T_, self.H), self.x_dtype)
         self.idx_buf = k3.device_view(self._own["idx"], (T_, self.K), torch.int32)
         self.wt_buf = k3.device_view(self._own["wt"], (T_, self.K), torch.float32)
-        k3.device_view(self._own["flag"], (W_, T_), torch.int32).zero_()
+        # the rank holding each expert (every rank's run table marks its own experts)
+        mine = (layer.run_of >= 0).to(torch.int32)
+        every = [torch.empty_like(mine) for _ in range(W_)] if W_ > 1 else [mine]
+        if W_ > 1:
+            dist.all_gather(every, mine, group=group)
+        rank_of = torch.full((self.E,), -1, dtype=torch.int32, device=dev)
+        for q in reversed(range(W_)):
+            rank_of[every[q].bool()] = q
+        self.expert_rank = rank_of
         torch.cuda.synchronize()
         everyone = [None] * W_
         dist.all_gather_object(everyone, handles, group=group)
@@ -227,7 +235,7 @@ class FusedExpertParallel:
                                       c.routed_scale, T, k3._ptr(self._rscratch), self._rscratch.numel(),
                                       k3._stream()), "k3c_router_ws")
         self._barrier()
-        # 2. every rank's pairs through this rank's experts; partial rows to the tokens' owners
+        # 2. every rank's pairs through this rank's experts; pair rows to the tokens' owners
         need = L.k3c_moe_prefill_ep_scratch(C.byref(c), C.byref(self.peers))
         if need == 0:
             raise k3.K3CError(f"k3c_moe_prefill_ep_scratch: {L.k3c_last_error().decode()}")
@@ -237,10 +245,11 @@ class FusedExpertParallel:
                                                self._scratch.numel(), k3._stream()),
                   "k3c_moe_prefill_ep_experts")
         self._barrier()
-        # 3. this rank's tokens: the partial rows in rank order
+        # 3. this rank's tokens: their pair rows in top-k order, then the shared row
         out = torch.empty((T, self.H), dtype=torch.float32, device=x.device)
-        k3._check(L.k3c_moe_ep_combine(k3._ptr(out), C.byref(self.peers), self.H, k3._stream()),
-                  "k3c_moe_ep_combine")
+        k3._check(L.k3c_moe_ep_combine(k3._ptr(out), C.byref(self.peers), self.H, self.K,
+                                       k3._ptr(self.expert_rank), self.E, 1 if c.shared_run >= 0 else 0,
+                                       k3._stream()), "k3c_moe_ep_combine")
         self.last = {"tokens": counts, "remote_rows_read": sum(counts) - T}
         return out
 

@@ -83,12 +83,12 @@ def test_pool_and_ep_struct_layouts_match_header(k3):
 #include <stddef.h>
 #include "k3c.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n",
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n",
          sizeof(k3c_moe_pool_layer), offsetof(k3c_moe_pool_layer, run_of),
          offsetof(k3c_moe_pool_layer, shared_run), offsetof(k3c_moe_pool_layer, terms),
          sizeof(k3c_ep_peers), offsetof(k3c_ep_peers, ntok), offsetof(k3c_ep_peers, x),
-         offsetof(k3c_ep_peers, idx), offsetof(k3c_ep_peers, wt), offsetof(k3c_ep_peers, partial),
-         offsetof(k3c_ep_peers, flag), sizeof(k3c_ipc_handle));
+         offsetof(k3c_ep_peers, idx), offsetof(k3c_ep_peers, wt), offsetof(k3c_ep_peers, recv),
+         sizeof(k3c_ipc_handle));
   return 0; }
 """
     with tempfile.TemporaryDirectory() as d:
@@ -99,8 +99,8 @@ int main(void) {
         got = [int(v) for v in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
     P, E = k3.MoePoolLayerC, k3.EpPeersC
     want = [C.sizeof(P), P.run_of.offset, P.shared_run.offset, P.terms.offset,
-            C.sizeof(E), E.ntok.offset, E.x.offset, E.idx.offset, E.wt.offset, E.partial.offset,
-            E.flag.offset, C.sizeof(k3.IpcHandleC)]
+            C.sizeof(E), E.ntok.offset, E.x.offset, E.idx.offset, E.wt.offset, E.recv.offset,
+            C.sizeof(k3.IpcHandleC)]
     assert got == want
 
 
@@ -117,7 +117,7 @@ def test_ep_arguments_are_checked_without_a_gpu(k3):
     peers.world = 2                                                   # buffers missing
     rc = L.k3c_moe_prefill_ep_experts(C.byref(layer), C.byref(peers), None, 0, None)
     assert rc == -1 and b"buffers" in L.k3c_last_error()
-    rc = L.k3c_moe_ep_combine(None, C.byref(peers), 512, None)
+    rc = L.k3c_moe_ep_combine(None, C.byref(peers), 512, 2, None, 8, 1, None)
     assert rc == -1
 
 

@@ -2,10 +2,11 @@
 prefill of the same layer on its tokens.
 - NCCL all-to-all path (ep.ExpertParallel): same activation terms, only the order in which
   the per-rank partial sums are added differs (1e-5).
-- Peer-memory path (ep.FusedExpertParallel: token rows read and per-rank partial rows
-  stored over NVLink by this library's kernels): every pair output is the single-GPU one and
-  the combine adds the same products, grouped per rank (1e-5), for two layer calls in a row
-  with different token counts per rank."""
+- Peer-memory path (ep.FusedExpertParallel: token rows read and every pair's bf16 output row
+  stored at its token's owner over NVLink by this library's kernels): every pair row is the
+  single-GPU one and the owner's combine is the single-GPU combine, so the output equals the
+  single-GPU layer (within 1e-5, bit for bit in practice), for two layer calls in a row with
+  different token counts per rank."""
 import os
 import sys
 
@@ -134,9 +135,9 @@ def test_ep_two_gpus_matches_single_gpu():
 
 
 def test_ep_fused_one_rank_equals_single_gpu():
-    """The peer-memory path's kernels (id gather, token quantisation from the x buffer,
-    per-rank partial rows, owner combine) on a one-rank group: one partial row per token, so
-    the output equals the single-GPU layer bit for bit (up to the sign of zeros)."""
+    """The peer-memory path's kernels (id gather, token quantisation from the x buffer, pair
+    rows into the receive buffer, owner combine) on a one-rank group: the output equals the
+    single-GPU layer bit for bit."""
     import datetime
     import torch
     import torch.distributed as dist
