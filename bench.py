@@ -1160,6 +1160,20 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     L.k3c_timing_enable(0)
     L.k3c_timing_read(ms_buf, n_buf, 4)
     stages = {name: ms_buf[j] / steps for j, name in enumerate(("experts", "router", "combine"))}
+    # the layer's phases, timed in separate steps after the timed region (events between them)
+    phases = None
+    if impl == "fused":
+        epl.phase_timing(True)
+        for i in range(3):
+            epl.forward(xs[i % 2], **fwd_kw)
+        phases = epl.phase_read()
+        epl.phase_timing(False)
+        ph = torch.tensor([phases[k] for k in epl.PHASES], dtype=torch.float64, device=dev)
+        if ws > 1:
+            dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+        phases = {"rank0": phases, "max_over_ranks": dict(zip(epl.PHASES, ph.tolist())),
+                  "experts_call_parts_rank0": {"grouped_gemms": stages["experts"],
+                                               "plan_dispatch_other": phases["experts_call"] - stages["experts"]}}
     dist.barrier()
     torch.cuda.synchronize()
     clocks = clk.stop()
@@ -1218,6 +1232,7 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
         "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
         "useful_tflops": flop * steps / dt / 1e12,
         "stages_ms_per_step_rank0": stages,
+        "phases_ms": phases,
         "expert_stage_ms_max_over_ranks": exp_max, "expert_stage_ms_mean_over_ranks": exp_mean,
         "nvlink_per_step": {"remote_token_rows_read": rows_all, "bytes_read": rows_all * H * 2,
                             "pair_rows_written": pairs_all, "bytes_written": pairs_all * H * 2,
@@ -1255,8 +1270,9 @@ def run_ep(args, ws, rank, local):
         "scaling": "strong", "vs_baseline": None, "dtype": r["dtype"], "data": "synthetic",
         "config": {"workload": EP_WORKLOAD, "tokens": EP_T, "hidden": H, "inter": I, "experts": E, "topk": K,
                    "parallelism": f"ep{ws}", "placement": r["placement"]},
-        **{k: r[k] for k in ("useful_tflops", "stages_ms_per_step_rank0", "nvlink_per_step", "parity",
-                             "cpu_baseline", "gpu_launches", "clocks")}}))
+        **{k: r[k] for k in ("useful_tflops", "stages_ms_per_step_rank0", "phases_ms", "expert_stage_ms_max_over_ranks",
+                             "expert_stage_ms_mean_over_ranks", "nvlink_per_step", "parity", "cpu_baseline",
+                             "gpu_launches", "clocks")}}))
 
 
 def main():

@@ -194,7 +194,33 @@ class FusedExpertParallel:
         self._scratch = torch.empty(0, dtype=torch.uint8, device=dev)
         self._rscratch = torch.empty(0, dtype=torch.uint8, device=dev)
         self._counts = None
+        self._ph = None
         self.last = {}
+
+    PHASES = ("route", "barrier1", "experts_call", "barrier2", "combine")
+
+    def phase_timing(self, on=True):
+        """Record CUDA events between the layer's phases on the current stream (route: token copy
+        and router; barrier1; experts_call: planning, dispatch, the grouped GEMMs and the pair
+        rows; barrier2; combine); phase_read() returns their mean milliseconds."""
+        self._ph = [] if on else None
+
+    def phase_read(self):
+        import torch
+        if not self._ph:
+            return None
+        torch.cuda.synchronize()
+        tot = [0.0] * len(self.PHASES)
+        for ev in self._ph:
+            for i in range(len(self.PHASES)):
+                tot[i] += ev[i].elapsed_time(ev[i + 1])
+        n = len(self._ph)
+        self._ph = []
+        return {name: tot[i] / n for i, name in enumerate(self.PHASES)}
+
+    def _mark(self, ev, i):
+        if ev is not None:
+            ev[i].record()
 
     def _barrier(self):
         import torch.distributed as dist
@@ -223,6 +249,11 @@ class FusedExpertParallel:
             counts = [T]
         for q in range(self.world):
             self.peers.ntok[q] = int(counts[q])
+        ev = None
+        if self._ph is not None:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)]
+            self._ph.append(ev)
+        self._mark(ev, 0)
         # 1. this rank's tokens and their routing into the shared buffers
         self.x_buf[:T].copy_(x)
         if T:
@@ -234,7 +265,9 @@ class FusedExpertParallel:
                                       C.c_void_p(c.router_bias), self.H, self.E, self.K, c.renorm,
                                       c.routed_scale, T, k3._ptr(self._rscratch), self._rscratch.numel(),
                                       k3._stream()), "k3c_router_ws")
+        self._mark(ev, 1)
         self._barrier()
+        self._mark(ev, 2)
         # 2. every rank's pairs through this rank's experts; pair rows to the tokens' owners
         need = L.k3c_moe_prefill_ep_scratch(C.byref(c), C.byref(self.peers))
         if need == 0:
@@ -244,12 +277,15 @@ class FusedExpertParallel:
         k3._check(L.k3c_moe_prefill_ep_experts(C.byref(c), C.byref(self.peers), k3._ptr(self._scratch),
                                                self._scratch.numel(), k3._stream()),
                   "k3c_moe_prefill_ep_experts")
+        self._mark(ev, 3)
         self._barrier()
+        self._mark(ev, 4)
         # 3. this rank's tokens: their pair rows in top-k order, then the shared row
         out = torch.empty((T, self.H), dtype=torch.float32, device=x.device)
         k3._check(L.k3c_moe_ep_combine(k3._ptr(out), C.byref(self.peers), self.H, self.K,
                                        k3._ptr(self.expert_rank), self.E, 1 if c.shared_run >= 0 else 0,
                                        k3._stream()), "k3c_moe_ep_combine")
+        self._mark(ev, 5)
         self.last = {"tokens": counts, "remote_rows_read": sum(counts) - T}
         return out
 
