@@ -133,6 +133,11 @@ def ref():
         L.refh_expert_read.restype = C.c_longlong
         L.refh_st_find.argtypes = [C.c_char_p, C.POINTER(C.c_char_p), C.c_int, C.POINTER(C.c_longlong)]
         L.refh_st_find.restype = C.c_int
+        L.refh_cache_replay.argtypes = [C.c_char_p, C.c_void_p, C.c_int, C.POINTER(C.c_int), C.c_int, C.c_int,
+                                        C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_ulonglong),
+                                        C.POINTER(C.c_int), C.c_longlong, C.POINTER(C.c_longlong),
+                                        C.POINTER(C.c_uint)]
+        L.refh_cache_replay.restype = C.c_int
         _ref = L
     return _ref
 
@@ -377,3 +382,32 @@ def ref_st_find(directory, names):
     if ref().refh_st_find(_os.fsencode(directory), arr, len(names), info) != 0:
         return None
     return [tuple(info[8 * i:8 * i + 8]) for i in range(len(names))]
+
+
+def ref_cache_replay(directory, cfg, nslot, records):
+    """The reference's own expert cache (src/cache/k3_cache.c) over the checkpoint in
+    `directory`, with exactly nslot slots, replaying records [(kind, layer, ids)]: kind 0 get
+    of ids[0], 1 getmany of ids, 2 pin ids[0], 3 unpin ids[0]. cfg: a K3Cfg ctypes structure
+    (n_layers, n_experts, topk, first_dense are read). Returns a dict: key_of after each
+    record, rc of each call, hits/misses/evictions/prefetch_reads, the (layer, expert) trace
+    and the request histogram; None when the checkpoint or the cache does not open."""
+    flat = []
+    for kind, layer, ids in records:
+        flat += [kind, layer, len(ids)] + list(ids)
+    nrec = len(records)
+    ops = (C.c_int * max(1, len(flat)))(*flat)
+    key_of = (C.c_int * (nrec * nslot))()
+    rc = (C.c_int * max(1, nrec))()
+    stats = (C.c_ulonglong * 4)()
+    cap = 2 * nrec + 2
+    trace = (C.c_int * cap)()
+    ntrace = C.c_longlong(0)
+    hist = (C.c_uint * (cfg.n_layers * cfg.n_experts))()
+    n = ref().refh_cache_replay(os.fsencode(directory), C.addressof(cfg), nslot, ops, len(flat), nrec, key_of, rc,
+                                stats, trace, cap, C.byref(ntrace), hist)
+    if n != nrec:
+        return None
+    return {"key_of": [list(key_of[i * nslot:(i + 1) * nslot]) for i in range(nrec)], "rc": list(rc[:nrec]),
+            "hits": stats[0], "misses": stats[1], "evictions": stats[2], "prefetch_reads": stats[3],
+            "trace": [(trace[2 * i], trace[2 * i + 1]) for i in range(ntrace.value // 2)],
+            "hist": list(hist)}

@@ -21,6 +21,7 @@
 #include <string.h>
 
 #include "k3.h"
+#include "k3_cache.h"
 #include "k3_load.h"
 
 static float refh_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
@@ -226,4 +227,53 @@ long refh_moe_call(int prefill, float *out, const float *x, int T, const K3MoeW 
     else         k3_moe(out, x, w, c, T, idx, wt, scratch);
     free(scratch);
     return k3_expert_drops - d0;
+}
+
+/* The reference's OWN expert cache (src/cache/k3_cache.c) replaying a request sequence, for
+ * pinning the bookkeeping restatement oracle/cache_model.py. The cache is built by
+ * k3_cache_init over the checkpoint in dir with room for exactly nslot slots. ops is a flat
+ * stream of records [kind, layer, n, ids[n]]: kind 0 = src.get of ids[0], 1 = src.getmany of
+ * the n ids, 2 = k3_cache_pin(ids[0], 1), 3 = k3_cache_pin(ids[0], 0). After record i,
+ * key_of[i*nslot .. +nslot) receives the cache's key_of table and rc[i] the call's return
+ * value. stats = {hits, misses, evictions, prefetch_reads}; trace (cap trace_cap int32) and
+ * hist (n_layers*n_experts) are the cache's own records; *ntrace their int32 count.
+ * Returns the number of records replayed, or -1 (checkpoint), -2 (cache init), -3 (ops). */
+int refh_cache_replay(const char *dir, const K3Cfg *cfg, int nslot, const int *ops, int n_ops, int n_rec,
+                      int *key_of, int *rc, unsigned long long *stats, int *trace, long long trace_cap,
+                      long long *ntrace, unsigned *hist)
+{
+    K3St st;
+    memset(&st, 0, sizeof st);
+    if (k3_st_open(&st, dir) != 0) return -1;
+    K3ExpertRef probe;
+    if (k3_expert_ref(&st, cfg->first_dense, 0, &probe) != 0) { k3_st_close(&st); return -1; }
+    int64_t slot_bytes = probe.nbytes + 2 * K3_ST_ALIGN;          /* the init's own sizing rule */
+    slot_bytes = (slot_bytes + K3_ST_ALIGN - 1) & ~(int64_t)(K3_ST_ALIGN - 1);
+    K3Cache c;
+    if (k3_cache_init(&c, &st, cfg, (int64_t)nslot * slot_bytes) != 0 || c.nslot != nslot) {
+        k3_st_close(&st);
+        return -2;
+    }
+    int pos = 0, i = 0;
+    for (; i < n_rec && pos + 3 <= n_ops; i++) {
+        const int kind = ops[pos], layer = ops[pos + 1], n = ops[pos + 2];
+        const int *ids = ops + pos + 3;
+        if (n < 1 || pos + 3 + n > n_ops) { i = -3; break; }
+        K3ExpertQ q;
+        if (kind == 0) rc[i] = c.src.get(&c.src, layer, ids[0], &q);
+        else if (kind == 1) rc[i] = c.src.getmany ? c.src.getmany(&c.src, layer, ids, n) : -1;
+        else rc[i] = k3_cache_pin(&c, layer, ids[0], kind == 2);
+        memcpy(key_of + (size_t)i * nslot, c.key_of, (size_t)nslot * sizeof(int));
+        pos += 3 + n;
+    }
+    stats[0] = c.hits;
+    stats[1] = c.misses;
+    stats[2] = c.evictions;
+    stats[3] = c.prefetch_reads;
+    *ntrace = c.ntrace;
+    if (trace && c.trace) memcpy(trace, c.trace, (size_t)(c.ntrace < trace_cap ? c.ntrace : trace_cap) * 4);
+    if (hist) memcpy(hist, c.hist, (size_t)c.n_layers * c.n_experts * sizeof(unsigned));
+    k3_cache_free(&c);
+    k3_st_close(&st);
+    return i;
 }
