@@ -327,10 +327,13 @@ def decode_line(args, ws, rank, local):
     side = torch.cuda.Stream()
     side_h = C.c_void_p(side.cuda_stream)
 
+    q8_ws = torch.empty(k3.q8_gemv_scratch(B, H, H), dtype=torch.uint8, device=dev)   # caller-owned scratch
+
     def compute(x, o, y, idx):
         side.wait_stream(main)
-        rc = L.k3c_q8_gemv(C.c_void_p(y.data_ptr()), H, C.c_void_p(x.data_ptr()), k3.K3C_BF16, H,
-                           B, C.c_void_p(wq.data_ptr()), C.c_void_p(wsc.data_ptr()), H, H, H, side_h)
+        rc = L.k3c_q8_gemv_ws(C.c_void_p(y.data_ptr()), H, C.c_void_p(x.data_ptr()), k3.K3C_BF16, H,
+                              B, C.c_void_p(wq.data_ptr()), C.c_void_p(wsc.data_ptr()), H, H, H,
+                              C.c_void_p(q8_ws.data_ptr()), q8_ws.numel(), side_h)
         assert rc == 0, L.k3c_last_error()
         layer.decode(x, out=o, idx=idx, wt=wt)
         main.wait_stream(side)

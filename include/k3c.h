@@ -251,6 +251,12 @@ int k3c_q8_pack(int8_t *wq, float *wscale, int ldw, const void *w_rows, int in, 
 int k3c_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
                 const int8_t *wq, const float *wscale, int ldw, int in, int out,
                 k3c_stream_t stream);
+/* k3c_q8_gemv with caller-owned device scratch (k3c_q8_gemv_scratch bytes; depends on ntok,
+ * in and out) instead of a stream-ordered allocation per call: K3C_EINVAL when too small. */
+size_t k3c_q8_gemv_scratch(int ntok, int in, int out);
+int k3c_q8_gemv_ws(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
+                   const int8_t *wq, const float *wscale, int ldw, int in, int out,
+                   void *scratch, size_t scratch_bytes, k3c_stream_t stream);
 
 /* Router for ntok tokens: logits W.x accumulated in double, sigmoid as in the reference,
  * top-k selection on score+bias with strict-greater first-index ties, renorm, scale.

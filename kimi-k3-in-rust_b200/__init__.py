@@ -175,6 +175,8 @@ def lib():
         "k3c_mxfp4_gemv": ([vp, i, vp, i, i, vp, vp, i, i, i, vp], i),
         "k3c_q8_pack": ([vp, vp, i, vp, i, i, vp], i),
         "k3c_q8_gemv": ([vp, i, vp, i, i, i, vp, vp, i, i, i, vp], i),
+        "k3c_q8_gemv_scratch": ([i, i, i], sz),
+        "k3c_q8_gemv_ws": ([vp, i, vp, i, i, i, vp, vp, i, i, i, vp, sz, vp], i),
         "k3c_router": ([vp, vp, vp, vp, i, vp, i, vp, i, i, i, i, f, i, vp], i),
         "k3c_router_select": ([vp, vp, vp, vp, i, i, i, f, i, vp], i),
         "k3c_expert_ffn_scratch": ([i, i, i], sz),
@@ -327,16 +329,27 @@ def q8_pack(rows_u8, in_, out):
     return wq, ws, ldw
 
 
-def q8_gemv(x, wq, ws, ldw, in_, out):
+def q8_gemv(x, wq, ws, ldw, in_, out, scratch=None):
+    """scratch: a uint8 device tensor of at least q8_gemv_scratch(ntok, in_, out) bytes
+    (k3c_q8_gemv_ws), or None for a per-call stream-ordered allocation (k3c_q8_gemv)."""
     import torch
     if x.dim() == 1:
         x = x.unsqueeze(0)
     x = x.contiguous()
     ntok = x.shape[0]
     y = torch.empty((ntok, out), dtype=torch.float32, device=x.device)
-    _check(lib().k3c_q8_gemv(_ptr(y), out, _ptr(x), _dtype_code(x), x.shape[1], ntok, _ptr(wq),
-                             _ptr(ws), ldw, in_, out, _stream()), "k3c_q8_gemv")
+    if scratch is None:
+        _check(lib().k3c_q8_gemv(_ptr(y), out, _ptr(x), _dtype_code(x), x.shape[1], ntok, _ptr(wq),
+                                 _ptr(ws), ldw, in_, out, _stream()), "k3c_q8_gemv")
+    else:
+        _check(lib().k3c_q8_gemv_ws(_ptr(y), out, _ptr(x), _dtype_code(x), x.shape[1], ntok, _ptr(wq), _ptr(ws),
+                                    ldw, in_, out, _ptr(scratch), scratch.numel() * scratch.element_size(),
+                                    _stream()), "k3c_q8_gemv_ws")
     return y
+
+
+def q8_gemv_scratch(ntok, in_, out):
+    return int(lib().k3c_q8_gemv_scratch(ntok, in_, out))
 
 
 def router(x, W, bias, topk, renorm=1, routed_scale=1.0):

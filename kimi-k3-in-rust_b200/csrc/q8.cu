@@ -410,22 +410,43 @@ static int q8_split(int tiles, int KT, int per_sm) {
     return S < 1 ? 1 : S;
 }
 
+// The launch geometry and the device scratch of one projection: split-K partials (double),
+// the activation terms, their exponents and the per-tile arrival counters.
+struct Q8Plan {
+    int KT, kpad, MT, TB, stages, S;
+    size_t term_bytes, part_bytes, texp_bytes, total;
+};
+static Q8Plan q8_plan(int ntok, int in, int out) {
+    Q8Plan p;
+    p.KT = (in + 127) / 128;
+    p.kpad = p.KT * 128;
+    p.MT = (out + 127) / 128;
+    p.TB = (ntok + Q8_NT - 1) / Q8_NT;
+    p.stages = q8_stages();
+    p.S = q8_split(p.MT * p.TB, p.KT, p.stages == 8 ? 1 : 2);
+    p.term_bytes = (size_t)p.TB * Q8_N * p.kpad;
+    p.part_bytes = p.S > 1 ? (size_t)p.TB * p.MT * p.S * Q8_NT * 128 * sizeof(double) : 0;
+    p.texp_bytes = align_up((size_t)p.S * p.TB * Q8_NT * sizeof(int), 256);
+    p.total = p.part_bytes + p.term_bytes + p.texp_bytes + (size_t)p.TB * p.MT * sizeof(int);
+    return p;
+}
+
+// scratch: caller-owned device memory of at least q8_plan().total bytes, 256-byte aligned, or
+// nullptr to take it from the stream-ordered pool for this call.
 template <typename XT>
 static int launch_q8_tc(float *y, int ldy, const void *x, int ldx, int ntok, const int8_t *wq,
-                        const float *wscale, int ldw, int in, int out, cudaStream_t s) {
+                        const float *wscale, int ldw, int in, int out, void *scratch, cudaStream_t s) {
     static int *err_of[64] = {};
     int *&err = err_of[cur_dev()];
     if (!err) K3C_TRY_CUDA(cudaGetSymbolAddress((void **)&err, g_q8_err));
-    const int KT = (in + 127) / 128, kpad = KT * 128;
-    const int MT = (out + 127) / 128, TB = (ntok + Q8_NT - 1) / Q8_NT;
-    const int stages = q8_stages();
-    const int S = q8_split(MT * TB, KT, stages == 8 ? 1 : 2);
-    const size_t term_bytes = (size_t)TB * Q8_N * kpad;
-    const size_t part_bytes = S > 1 ? (size_t)TB * MT * S * Q8_NT * 128 * sizeof(double) : 0;
-    const size_t texp_bytes = align_up((size_t)S * TB * Q8_NT * sizeof(int), 256);
-    char *buf = nullptr;
-    k3c::keep_async_pool();
-    K3C_TRY_CUDA(cudaMallocAsync((void **)&buf, part_bytes + term_bytes + texp_bytes + (size_t)TB * MT * sizeof(int), s));
+    const Q8Plan p = q8_plan(ntok, in, out);
+    const int KT = p.KT, kpad = p.kpad, MT = p.MT, TB = p.TB, stages = p.stages, S = p.S;
+    const size_t term_bytes = p.term_bytes, part_bytes = p.part_bytes, texp_bytes = p.texp_bytes;
+    char *buf = reinterpret_cast<char *>(scratch);
+    if (!buf) {
+        k3c::keep_async_pool();
+        K3C_TRY_CUDA(cudaMallocAsync((void **)&buf, p.total, s));
+    }
     double *part = reinterpret_cast<double *>(buf);
     int8_t *terms = reinterpret_cast<int8_t *>(buf + part_bytes);
     int *texp = reinterpret_cast<int *>(buf + part_bytes + term_bytes);
@@ -474,7 +495,7 @@ static int launch_q8_tc(float *y, int ldy, const void *x, int ldx, int ntok, con
         count_launch();
         if (ce != cudaSuccess) rc = set_error(K3C_ECUDA, "q8_gemv: %s", cudaGetErrorString(ce));
     } while (0);
-    cudaFreeAsync(buf, s);
+    if (!scratch) cudaFreeAsync(buf, s);
     if (rc) return rc;
     // K3C_SYNC_CHECK=1: synchronise and report the kernel's own error code (a bounded wait
     // that gave up, or a failed alignment self-check).
@@ -492,18 +513,41 @@ static int launch_q8_tc(float *y, int ldy, const void *x, int ldx, int ntok, con
     return K3C_OK;
 }
 
-int launch_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
-                   const int8_t *wq, const float *wscale, int ldw, int in, int out,
-                   cudaStream_t s) {
+static int launch_q8_gemv_impl(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
+                               const int8_t *wq, const float *wscale, int ldw, int in, int out, void *scratch,
+                               cudaStream_t s) {
     if (in <= 0 || out <= 0 || ldw < in || (ldw % 32) || ((uintptr_t)wq & 15) || in > 262144)
         return set_error(K3C_EINVAL, "q8_gemv: in=%d out=%d ldw=%d (ldw must be a multiple of 32, in <= 262144)",
                          in, out, ldw);
     if (ntok < 0 || (ntok > 0 && (ldy < out || ldx < in)))
         return set_error(K3C_EINVAL, "q8_gemv: ntok=%d ldy=%d ldx=%d", ntok, ldy, ldx);
     if (ntok == 0) return K3C_OK;
-    if (x_dtype == K3C_BF16) return launch_q8_tc<uint16_t>(y, ldy, x, ldx, ntok, wq, wscale, ldw, in, out, s);
-    if (x_dtype == K3C_F32) return launch_q8_tc<float>(y, ldy, x, ldx, ntok, wq, wscale, ldw, in, out, s);
+    if (x_dtype == K3C_BF16) return launch_q8_tc<uint16_t>(y, ldy, x, ldx, ntok, wq, wscale, ldw, in, out, scratch, s);
+    if (x_dtype == K3C_F32) return launch_q8_tc<float>(y, ldy, x, ldx, ntok, wq, wscale, ldw, in, out, scratch, s);
     return set_error(K3C_EINVAL, "q8_gemv: x_dtype=%d", x_dtype);
+}
+
+int launch_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok,
+                   const int8_t *wq, const float *wscale, int ldw, int in, int out,
+                   cudaStream_t s) {
+    return launch_q8_gemv_impl(y, ldy, x, x_dtype, ldx, ntok, wq, wscale, ldw, in, out, nullptr, s);
+}
+
+size_t q8_scratch_bytes(int ntok, int in, int out) {
+    if (ntok <= 0 || in <= 0 || out <= 0) return 0;
+    return q8_plan(ntok, in, out).total + 256;
+}
+
+int launch_q8_gemv_ws(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok, const int8_t *wq,
+                      const float *wscale, int ldw, int in, int out, void *scratch, size_t scratch_bytes,
+                      cudaStream_t s) {
+    if (ntok <= 0 || in <= 0 || out <= 0)
+        return launch_q8_gemv_impl(y, ldy, x, x_dtype, ldx, ntok, wq, wscale, ldw, in, out, nullptr, s);
+    const size_t need = q8_plan(ntok, in, out).total;
+    char *base = reinterpret_cast<char *>(((uintptr_t)scratch + 255) & ~(uintptr_t)255);
+    if (!scratch || (size_t)(base - (char *)scratch) + need > scratch_bytes)
+        return set_error(K3C_EINVAL, "q8_gemv: scratch of %zu bytes, %zu needed", scratch_bytes, need + 256);
+    return launch_q8_gemv_impl(y, ldy, x, x_dtype, ldx, ntok, wq, wscale, ldw, in, out, base, s);
 }
 
 }  // namespace k3c
@@ -521,6 +565,19 @@ extern "C" int k3c_q8_gemv(float *y, int ldy, const void *x, int x_dtype, int ld
     k3c::stage_begin(k3c::STAGE_Q8, (cudaStream_t)stream);
     int rc = k3c::launch_q8_gemv(y, ldy, x, x_dtype, ldx, ntok, wq, wscale, ldw, in, out,
                                  (cudaStream_t)stream);
+    k3c::stage_end(k3c::STAGE_Q8, (cudaStream_t)stream);
+    return rc;
+}
+
+extern "C" size_t k3c_q8_gemv_scratch(int ntok, int in, int out) { return k3c::q8_scratch_bytes(ntok, in, out); }
+
+extern "C" int k3c_q8_gemv_ws(float *y, int ldy, const void *x, int x_dtype, int ldx, int ntok, const int8_t *wq,
+                              const float *wscale, int ldw, int in, int out, void *scratch, size_t scratch_bytes,
+                              k3c_stream_t stream) {
+    k3c::clear_error();
+    k3c::stage_begin(k3c::STAGE_Q8, (cudaStream_t)stream);
+    int rc = k3c::launch_q8_gemv_ws(y, ldy, x, x_dtype, ldx, ntok, wq, wscale, ldw, in, out, scratch, scratch_bytes,
+                                    (cudaStream_t)stream);
     k3c::stage_end(k3c::STAGE_Q8, (cudaStream_t)stream);
     return rc;
 }

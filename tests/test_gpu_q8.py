@@ -87,3 +87,30 @@ def test_q8_tc_nonfinite_token(k3, ora, dev):
     assert np.all(np.isnan(got[1]))
     for t in (0, 2):
         assert maxrel(got[t], ora.matmul_q8(xf[t], rows, in_, out)) < TOL, t
+
+
+@pytest.mark.parametrize("in_,out,ntok", [(7168, 7168, 16), (1000, 129, 33), (300, 260, 1)])
+def test_q8_caller_scratch_equals_pooled(k3, dev, in_, out, ntok):
+    """k3c_q8_gemv_ws with caller-owned scratch (offset by 8 bytes: the entry point aligns it)
+    gives the bits of k3c_q8_gemv; a buffer too short is refused with K3C_EINVAL before any
+    launch."""
+    import torch
+    g = k3.synth.rng(900 + ntok)
+    _, _, rows = k3.synth.q8_matrix(g, out, in_)
+    wq, ws, ldw = k3.q8_pack(T(rows, dev), in_, out)
+    xb = k3.synth.bf16_bits(g.standard_normal((ntok, in_), dtype=np.float32))
+    xd = T(xb.view(np.int16), dev).view(torch.bfloat16)
+    want = run(k3, xd, wq, ws, ldw, in_, out, ntok, in_)
+    need = k3.q8_gemv_scratch(ntok, in_, out)
+    buf = torch.empty(need + 8, dtype=torch.uint8, device=dev)
+    y = torch.full((ntok, out), float("nan"), dtype=torch.float32, device=dev)
+    L = k3.lib()
+    rc = L.k3c_q8_gemv_ws(y.data_ptr(), out, xd.data_ptr(), k3.K3C_BF16, in_, ntok, wq.data_ptr(), ws.data_ptr(),
+                          ldw, in_, out, buf.data_ptr() + 8, need, k3._stream())
+    assert rc == 0, L.k3c_last_error()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    rc = L.k3c_q8_gemv_ws(y.data_ptr(), out, xd.data_ptr(), k3.K3C_BF16, in_, ntok, wq.data_ptr(), ws.data_ptr(),
+                          ldw, in_, out, buf.data_ptr(), need - 257, k3._stream())
+    assert rc == -1   # K3C_EINVAL
+    y2 = k3.q8_gemv(xd, wq, ws, ldw, in_, out, scratch=buf)
+    assert np.array_equal(y2.cpu().numpy().view(np.uint32), want.view(np.uint32))
