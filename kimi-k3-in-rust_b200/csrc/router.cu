@@ -240,28 +240,73 @@ __device__ __forceinline__ float sigmoid_score(double logit_d) {
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
 }
 
-// The tensor-core logit of (token, expert e) completed with the residual terms, or the
-// plain double dot product (the reference's own summation order) when either list overflowed.
-__device__ __noinline__ double rt_finish(const RtFix &fix, double logit, const uint16_t *xrow, int nx, int ex,
-                                         const int *s_xk, const float *s_xr, int e, int n_experts) {
-    const uint16_t *wrow = fix.W + (size_t)e * fix.H;
-    const int nw = fix.wcnt[e];
-    if (nx > fix.cap || nw > fix.cap) {
-        double acc = 0.0;
-        for (int k = 0; k < fix.H; k++)
-            acc += (double)bf16_bits_to_f32(wrow[k]) * (double)bf16_bits_to_f32(xrow[k]);
-        return acc;
+// The plain double dot product of token row x and expert row w (the reference's own order),
+// for a row whose residual list overflowed or that holds a NaN or an infinity.
+__device__ __noinline__ double rt_plain(const uint16_t *wrow, const uint16_t *xrow, int H) {
+    double acc = 0.0;
+    for (int k = 0; k < H; k++) acc += (double)bf16_bits_to_f32(wrow[k]) * (double)bf16_bits_to_f32(xrow[k]);
+    return acc;
+}
+
+// The tensor-core logits lg[u] of RU (token, expert) items completed with their residual
+// terms: c = sum_i rx_i * w[k_i] over the token's list, then + sum_j (x[k_j] - rx(x[k_j])) *
+// rw_j over the expert's list, in list order, and lg + c -- each item's own order, with the
+// items' loads interleaved so that their round trips overlap. Items with ok[u] false are
+// skipped; an item whose list overflowed gets the plain double dot product.
+template <int RU>
+__device__ __forceinline__ void rt_finish(const RtFix &fix, double (&lg)[RU], const bool (&ok)[RU],
+                                          const int (&tt)[RU], const int (&t)[RU], const int (&e)[RU],
+                                          const int *s_nx, const int *s_ex, const int (*s_xk)[RT_CAP],
+                                          const float (*s_xr)[RT_CAP], int n_experts) {
+    int nx[RU], nw[RU];
+    int nxm = 0, nwm = 0;
+#pragma unroll
+    for (int u = 0; u < RU; u++) {
+        nx[u] = ok[u] ? s_nx[tt[u]] : 0;
+        nw[u] = ok[u] ? fix.wcnt[e[u]] : 0;
     }
-    double c = 0.0;
-    for (int i = 0; i < nx; i++) c += (double)s_xr[i] * (double)bf16_bits_to_f32(wrow[s_xk[i]]);
-    for (int i = 0; i < nw; i++) {
-        const int k = fix.wk[(size_t)i * n_experts + e];
-        const float xv = bf16_bits_to_f32(xrow[k]);
-        int q0, q1, q2;
-        const float rx = rt_split(xv, ex, q0, q1, q2);
-        c += (double)(xv - rx) * (double)fix.wr[(size_t)i * n_experts + e];
+    bool plain[RU];
+    double c[RU];
+#pragma unroll
+    for (int u = 0; u < RU; u++) {
+        plain[u] = ok[u] && (nx[u] > fix.cap || nw[u] > fix.cap);
+        if (plain[u] || !ok[u]) nx[u] = nw[u] = 0;
+        nxm = max(nxm, nx[u]);
+        nwm = max(nwm, nw[u]);
+        c[u] = 0.0;
     }
-    return logit + c;
+    for (int i = 0; i < nxm; i++) {
+        float wv[RU];
+#pragma unroll
+        for (int u = 0; u < RU; u++)
+            wv[u] = i < nx[u] ? bf16_bits_to_f32(fix.W[(size_t)e[u] * fix.H + s_xk[tt[u]][i]]) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < RU; u++)
+            if (i < nx[u]) c[u] += (double)s_xr[tt[u]][i] * (double)wv[u];
+    }
+    for (int j = 0; j < nwm; j++) {
+        int k[RU];
+        float r[RU], xv[RU];
+#pragma unroll
+        for (int u = 0; u < RU; u++) {
+            k[u] = j < nw[u] ? fix.wk[(size_t)j * n_experts + e[u]] : 0;
+            r[u] = j < nw[u] ? fix.wr[(size_t)j * n_experts + e[u]] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < RU; u++) xv[u] = j < nw[u] ? bf16_bits_to_f32(fix.x[(size_t)t[u] * fix.H + k[u]]) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < RU; u++)
+            if (j < nw[u]) {
+                int q0, q1, q2;
+                const float rx = rt_split(xv[u], s_ex[tt[u]], q0, q1, q2);
+                c[u] += (double)(xv[u] - rx) * (double)r[u];
+            }
+    }
+#pragma unroll
+    for (int u = 0; u < RU; u++) {
+        if (plain[u]) lg[u] = rt_plain(fix.W + (size_t)e[u] * fix.H, fix.x + (size_t)t[u] * fix.H, fix.H);
+        else if (ok[u]) lg[u] = lg[u] + c[u];
+    }
 }
 
 // TPB tokens per block (1 for small batches, 8 for large ones). With `part`, all threads
@@ -300,31 +345,57 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
         }
         __syncthreads();
     }
-    for (int i = threadIdx.x; i < nt * n_experts; i += blockDim.x) {
-        const int tt = i / n_experts, e = i % n_experts, t = t0 + tt;
-        float v;
-        if (part) {
-            // chunks in order; up to 16 loads in flight per pass
-            double logit = 0.0;
-            for (int k0 = 0; k0 < nchunk; k0 += 16) {
-                double v16[16];
+    // RU items per thread per pass: their chunk loads and residual gathers are issued together
+    constexpr int RU = 4;
+    const int nitems = nt * n_experts;
+    for (int i0 = threadIdx.x; i0 < nitems; i0 += blockDim.x * RU) {
+        bool ok[RU];
+        int tt[RU], e[RU], t[RU];
 #pragma unroll
-                for (int k = 0; k < 16; k++)
-                    v16[k] = k0 + k < nchunk ? part[((size_t)(k0 + k) * ntok + t) * n_experts + e] : 0.0;
-#pragma unroll
-                for (int k = 0; k < 16; k++)
-                    if (k0 + k < nchunk) logit += v16[k];
-            }
-            if (fix.x)
-                logit = rt_finish(fix, logit, fix.x + (size_t)t * fix.H, s_nx[tt], s_ex[tt], s_xk[tt], s_xr[tt], e,
-                                  n_experts);
-            v = sigmoid_score(logit);
-            if (scores) scores[(size_t)t * n_experts + e] = v;
-        } else {
-            v = scores[(size_t)t * n_experts + e];
+        for (int u = 0; u < RU; u++) {
+            const int i = i0 + u * (int)blockDim.x;
+            ok[u] = i < nitems;
+            tt[u] = ok[u] ? i / n_experts : 0;
+            e[u] = ok[u] ? i % n_experts : 0;
+            t[u] = t0 + tt[u];
         }
-        ch[(size_t)(2 * tt + 1) * n_experts + e] = v;
-        ch[(size_t)(2 * tt) * n_experts + e] = __fadd_rn(v, bias ? bias[e] : 0.0f);
+        float v[RU];
+        if (part) {
+            // chunks in order; 16 loads in flight per pass (KL chunks of each item)
+            constexpr int KL = 16 / RU;
+            double lg[RU];
+#pragma unroll
+            for (int u = 0; u < RU; u++) lg[u] = 0.0;
+            for (int k0 = 0; k0 < nchunk; k0 += KL) {
+                double vk[RU][KL];
+#pragma unroll
+                for (int u = 0; u < RU; u++)
+#pragma unroll
+                    for (int k = 0; k < KL; k++)
+                        vk[u][k] = ok[u] && k0 + k < nchunk
+                                       ? part[((size_t)(k0 + k) * ntok + t[u]) * n_experts + e[u]] : 0.0;
+#pragma unroll
+                for (int u = 0; u < RU; u++)
+#pragma unroll
+                    for (int k = 0; k < KL; k++)
+                        if (k0 + k < nchunk) lg[u] += vk[u][k];
+            }
+            if (fix.x) rt_finish<RU>(fix, lg, ok, tt, t, e, s_nx, s_ex, s_xk, s_xr, n_experts);
+#pragma unroll
+            for (int u = 0; u < RU; u++) {
+                v[u] = sigmoid_score(lg[u]);
+                if (ok[u] && scores) scores[(size_t)t[u] * n_experts + e[u]] = v[u];
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < RU; u++) v[u] = ok[u] ? scores[(size_t)t[u] * n_experts + e[u]] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < RU; u++) {
+            if (!ok[u]) continue;
+            ch[(size_t)(2 * tt[u] + 1) * n_experts + e[u]] = v[u];
+            ch[(size_t)(2 * tt[u]) * n_experts + e[u]] = __fadd_rn(v[u], bias ? bias[e[u]] : 0.0f);
+        }
     }
     __syncthreads();
     if (warp >= nt) return;
@@ -398,40 +469,6 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
     }
 }
 
-static int launch_select(int *idx, float *w, float *scores, const double *part, int nchunk,
-                         const float *bias, int n_experts, int topk, int renorm, float routed_scale,
-                         int ntok, cudaStream_t s, RtFix fix = RtFix{}) {
-    if (n_experts <= 0 || topk <= 0 || topk > K3_MAX_TOPK || ntok < 0)
-        return set_error(K3C_EINVAL, "router_select: n_experts=%d topk=%d ntok=%d", n_experts,
-                         topk, ntok);
-    if (ntok == 0) return K3C_OK;
-    const size_t smem1 = (size_t)2 * n_experts * sizeof(float);
-    if (smem1 > 200 * 1024) return set_error(K3C_EINVAL, "router_select: n_experts=%d too large", n_experts);
-    // eight tokens per block for large batches (the top-k of each runs in its own warp)
-    if (ntok >= 256 && 8 * smem1 <= 200 * 1024) {
-        const size_t smem = 8 * smem1;
-        if (smem > 48 * 1024)
-            K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        count_launch();
-        K3C_TRY_CUDA(launch_pdl(k_router_select<8>, dim3((ntok + 7) / 8), dim3(256), smem, s, idx, w, scores, part,
-                                nchunk, bias, n_experts, topk, renorm, routed_scale, ntok, fix));
-        return K3C_OK;
-    }
-    if (smem1 > 48 * 1024)
-        K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_select<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
-    count_launch();
-    K3C_TRY_CUDA(launch_pdl(k_router_select<1>, dim3(ntok), dim3(256), smem1, s, idx, w, scores, part, nchunk, bias,
-                            n_experts, topk, renorm, routed_scale, ntok, fix));
-    return K3C_OK;
-}
-
-int launch_router_select(int *idx, float *w, const float *scores, const float *bias,
-                         int n_experts, int topk, int renorm, float routed_scale, int ntok,
-                         cudaStream_t s) {
-    return launch_select(idx, w, const_cast<float *>(scores), nullptr, 0, bias, n_experts, topk, renorm,
-                         routed_scale, ntok, s);
-}
-
 static int sm_count_rt() {
     static int n = 0;
     if (!n) {
@@ -442,6 +479,41 @@ static int sm_count_rt() {
     }
     return n;
 }
+
+static int launch_select(int *idx, float *w, float *scores, const double *part, int nchunk,
+                         const float *bias, int n_experts, int topk, int renorm, float routed_scale,
+                         int ntok, cudaStream_t s, RtFix fix = RtFix{}) {
+    if (n_experts <= 0 || topk <= 0 || topk > K3_MAX_TOPK || ntok < 0)
+        return set_error(K3C_EINVAL, "router_select: n_experts=%d topk=%d ntok=%d", n_experts,
+                         topk, ntok);
+    if (ntok == 0) return K3C_OK;
+    const size_t smem1 = (size_t)2 * n_experts * sizeof(float);
+    if (smem1 > 200 * 1024) return set_error(K3C_EINVAL, "router_select: n_experts=%d too large", n_experts);
+    // Tokens per block (the top-k of each runs in its own warp): the most that still gives every
+    // SM about six blocks, so that the logit phase's loads from many blocks overlap.
+    auto go = [&](auto kern, int tpb) -> int {
+        const size_t smem = (size_t)tpb * smem1;
+        if (smem > 48 * 1024)
+            K3C_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        count_launch();
+        K3C_TRY_CUDA(launch_pdl(kern, dim3((ntok + tpb - 1) / tpb), dim3(256), smem, s, idx, w, scores, part,
+                                nchunk, bias, n_experts, topk, renorm, routed_scale, ntok, fix));
+        return K3C_OK;
+    };
+    const long want = 6L * sm_count_rt();
+    if (ntok >= 8 * want && 8 * smem1 <= 200 * 1024) return go(k_router_select<8>, 8);
+    if (ntok >= 4 * want && 4 * smem1 <= 200 * 1024) return go(k_router_select<4>, 4);
+    if (ntok >= 2 * want && 2 * smem1 <= 200 * 1024) return go(k_router_select<2>, 2);
+    return go(k_router_select<1>, 1);
+}
+
+int launch_router_select(int *idx, float *w, const float *scores, const float *bias,
+                         int n_experts, int topk, int renorm, float routed_scale, int ntok,
+                         cudaStream_t s) {
+    return launch_select(idx, w, const_cast<float *>(scores), nullptr, 0, bias, n_experts, topk, renorm,
+                         routed_scale, ntok, s);
+}
+
 static int router_nparts(int hidden, int n_experts, int ntok);
 
 // Enough for either logit path (the operand dtypes are not known here).

@@ -29,20 +29,22 @@ namespace k3c {
 
 namespace {
 
-// grid (rows), 256 threads: digits, exponent and residual list of one bf16 row.
-// Digit j of row r goes to dig[j*rows*H + r*H + k]; list entry i of row r to
-// ek/er[r*rs + i*is]. Rows with a NaN or an infinity get zero digits and count cap+1.
+// grid (ceil(rows/8)), 256 threads, one warp per row: digits, exponent and residual list of a
+// bf16 row (H a multiple of 8). Digit j of row r goes to dig[j*rows*H + r*H + k]; list entry i
+// of row r to ek/er[r*rs + i*is], in k order. Rows with a NaN or an infinity get zero digits
+// and count cap+1. Warp-level reductions and scans only: a row is 28 loads of 16 bytes per lane
+// at H = 7168, too little work to amortise block-wide barriers.
 __global__ void __launch_bounds__(256) k_rt_digits(const uint16_t *__restrict__ src, int ld, int rows, int H,
                                                    int8_t *__restrict__ dig, int *__restrict__ exps,
                                                    int *__restrict__ cnt, int *__restrict__ ek,
                                                    float *__restrict__ er, int rs, int is, int cap) {
-    __shared__ float wmax[8];
-    __shared__ int wbad[8], wsum[8], s_base;
-    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (r >= rows) return;
     const uint16_t *row = src + (size_t)r * ld;
     float m = 0.0f;
     int bad = 0;
-    for (int k = threadIdx.x * 8; k < H; k += 256 * 8) {
+    for (int k = lane * 8; k < H; k += 32 * 8) {
         const uint4 u = *reinterpret_cast<const uint4 *>(row + k);
         const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -55,19 +57,14 @@ __global__ void __launch_bounds__(256) k_rt_digits(const uint16_t *__restrict__ 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     bad = __any_sync(0xffffffffu, bad);
-    if (lane == 0) { wmax[warp] = m; wbad[warp] = bad; }
-    if (threadIdx.x == 0) s_base = 0;
-    __syncthreads();
-    m = wmax[0];
-    bad = wbad[0];
-    for (int w = 1; w < 8; w++) { m = fmaxf(m, wmax[w]); bad |= wbad[w]; }
     int E = 0;
     if (!bad && m > 0.0f) frexpf(m, &E);                  // m < 2^E
-    if (threadIdx.x == 0) exps[r] = E;
+    if (lane == 0) exps[r] = E;
     const size_t dstride = (size_t)rows * H;
     int8_t *d0 = dig + (size_t)r * H;
-    for (int k0 = 0; k0 < H; k0 += 256 * 8) {
-        const int k = k0 + threadIdx.x * 8;
+    int base = 0;
+    for (int k0 = 0; k0 < H; k0 += 32 * 8) {
+        const int k = k0 + lane * 8;
         uint32_t q[3][2] = {{0, 0}, {0, 0}, {0, 0}};
         float res[8];
         int nres = 0;
@@ -87,20 +84,20 @@ __global__ void __launch_bounds__(256) k_rt_digits(const uint16_t *__restrict__ 
 #pragma unroll
             for (int j = 0; j < 3; j++)
                 *reinterpret_cast<uint2 *>(d0 + j * dstride + k) = make_uint2(q[j][0], q[j][1]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) res[i] = 0.0f;
         }
-        // list entries in k order: block-wide exclusive scan of the per-thread counts (most
-        // chunks of an ordinary row have none)
-        if (__syncthreads_count(nres) == 0) continue;
+        // list entries in k order: warp-wide exclusive scan of the per-lane counts (most chunks
+        // of an ordinary row have none)
+        if (!__any_sync(0xffffffffu, nres != 0)) continue;
         int incl = nres;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int v = __shfl_up_sync(0xffffffffu, incl, o);
             if (lane >= o) incl += v;
         }
-        if (lane == 31) wsum[warp] = incl;
-        __syncthreads();
-        int pos = s_base + incl - nres;
-        for (int w = 0; w < warp; w++) pos += wsum[w];
+        int pos = base + incl - nres;
         if (nres) {
 #pragma unroll
             for (int i = 0; i < 8; i++)
@@ -112,11 +109,9 @@ __global__ void __launch_bounds__(256) k_rt_digits(const uint16_t *__restrict__ 
                     pos++;
                 }
         }
-        __syncthreads();
-        if (threadIdx.x == 255) s_base = pos;   // the last thread's end is the running total
-        __syncthreads();
+        base += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (threadIdx.x == 0) cnt[r] = bad ? cap + 1 : s_base;
+    if (lane == 0) cnt[r] = bad ? cap + 1 : base;
 }
 
 // ------------------------------------------------------------------ the MMA kernel
@@ -345,9 +340,9 @@ int launch_router_tc(RtFix *fix, double **part, int *nslices, const void *x, con
     int *&err = err_of[cur_dev()];
     if (!err) K3C_TRY_CUDA(cudaGetSymbolAddress((void **)&err, g_rt_err));
     RtBufs b = carve_rt(scratch, H, E, T, S);
-    k_rt_digits<<<T, 256, 0, s>>>((const uint16_t *)x, H, T, H, b.xd, b.xexp, b.xcnt, b.xk, b.xr, RT_CAP, 1, RT_CAP);
+    k_rt_digits<<<(T + 7) / 8, 256, 0, s>>>((const uint16_t *)x, H, T, H, b.xd, b.xexp, b.xcnt, b.xk, b.xr, RT_CAP, 1, RT_CAP);
     K3C_CHECK_LAUNCH();
-    k_rt_digits<<<E, 256, 0, s>>>((const uint16_t *)W, H, E, H, b.wd, b.wexp, b.wcnt, b.wk, b.wr, 1, E, RT_CAP);
+    k_rt_digits<<<(E + 7) / 8, 256, 0, s>>>((const uint16_t *)W, H, E, H, b.wd, b.wexp, b.wcnt, b.wk, b.wr, 1, E, RT_CAP);
     K3C_CHECK_LAUNCH();
     CUtensorMap mx, mw;
     K3C_TRY(make_digit_map(&mx, b.xd, H, T, 128));
