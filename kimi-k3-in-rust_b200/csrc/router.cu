@@ -15,6 +15,8 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "rt_tc.cuh"
 
@@ -345,58 +347,63 @@ __global__ void __launch_bounds__(256) k_router_select(int *__restrict__ idx, fl
         }
         __syncthreads();
     }
-    // RU items per thread per pass: their chunk loads and residual gathers are issued together
-    constexpr int RU = 4;
-    const int nitems = nt * n_experts;
-    for (int i0 = threadIdx.x; i0 < nitems; i0 += blockDim.x * RU) {
-        bool ok[RU];
-        int tt[RU], e[RU], t[RU];
-#pragma unroll
-        for (int u = 0; u < RU; u++) {
-            const int i = i0 + u * (int)blockDim.x;
-            ok[u] = i < nitems;
-            tt[u] = ok[u] ? i / n_experts : 0;
-            e[u] = ok[u] ? i % n_experts : 0;
-            t[u] = t0 + tt[u];
-        }
-        float v[RU];
-        if (part) {
-            // chunks in order; 16 loads in flight per pass (KL chunks of each item)
-            constexpr int KL = 16 / RU;
-            double lg[RU];
-#pragma unroll
-            for (int u = 0; u < RU; u++) lg[u] = 0.0;
-            for (int k0 = 0; k0 < nchunk; k0 += KL) {
-                double vk[RU][KL];
-#pragma unroll
-                for (int u = 0; u < RU; u++)
-#pragma unroll
-                    for (int k = 0; k < KL; k++)
-                        vk[u][k] = ok[u] && k0 + k < nchunk
-                                       ? part[((size_t)(k0 + k) * ntok + t[u]) * n_experts + e[u]] : 0.0;
-#pragma unroll
-                for (int u = 0; u < RU; u++)
-#pragma unroll
-                    for (int k = 0; k < KL; k++)
-                        if (k0 + k < nchunk) lg[u] += vk[u][k];
-            }
-            if (fix.x) rt_finish<RU>(fix, lg, ok, tt, t, e, s_nx, s_ex, s_xk, s_xr, n_experts);
+    // RU items per thread per pass, KL chunk loads of each in flight: the tensor-core logits
+    // (one or a few K slices, residual gathers) interleave four items; the CUDA-core logits
+    // (dozens of K chunks) keep sixteen chunk loads of one item in flight.
+    auto logits = [&](auto ru, auto kl) {
+        constexpr int RU = decltype(ru)::value, KL = decltype(kl)::value;
+        const int nitems = nt * n_experts;
+        for (int i0 = threadIdx.x; i0 < nitems; i0 += blockDim.x * RU) {
+            bool ok[RU];
+            int tt[RU], e[RU], t[RU];
 #pragma unroll
             for (int u = 0; u < RU; u++) {
-                v[u] = sigmoid_score(lg[u]);
-                if (ok[u] && scores) scores[(size_t)t[u] * n_experts + e[u]] = v[u];
+                const int i = i0 + u * (int)blockDim.x;
+                ok[u] = i < nitems;
+                tt[u] = ok[u] ? i / n_experts : 0;
+                e[u] = ok[u] ? i % n_experts : 0;
+                t[u] = t0 + tt[u];
             }
-        } else {
+            float v[RU];
+            if (part) {
+                // chunks in order, KL loads of each item in flight per pass
+                double lg[RU];
 #pragma unroll
-            for (int u = 0; u < RU; u++) v[u] = ok[u] ? scores[(size_t)t[u] * n_experts + e[u]] : 0.0f;
-        }
+                for (int u = 0; u < RU; u++) lg[u] = 0.0;
+                for (int k0 = 0; k0 < nchunk; k0 += KL) {
+                    double vk[RU][KL];
 #pragma unroll
-        for (int u = 0; u < RU; u++) {
-            if (!ok[u]) continue;
-            ch[(size_t)(2 * tt[u] + 1) * n_experts + e[u]] = v[u];
-            ch[(size_t)(2 * tt[u]) * n_experts + e[u]] = __fadd_rn(v[u], bias ? bias[e[u]] : 0.0f);
+                    for (int u = 0; u < RU; u++)
+#pragma unroll
+                        for (int k = 0; k < KL; k++)
+                            vk[u][k] = ok[u] && k0 + k < nchunk
+                                           ? part[((size_t)(k0 + k) * ntok + t[u]) * n_experts + e[u]] : 0.0;
+#pragma unroll
+                    for (int u = 0; u < RU; u++)
+#pragma unroll
+                        for (int k = 0; k < KL; k++)
+                            if (k0 + k < nchunk) lg[u] += vk[u][k];
+                }
+                if (fix.x) rt_finish<RU>(fix, lg, ok, tt, t, e, s_nx, s_ex, s_xk, s_xr, n_experts);
+#pragma unroll
+                for (int u = 0; u < RU; u++) {
+                    v[u] = sigmoid_score(lg[u]);
+                    if (ok[u] && scores) scores[(size_t)t[u] * n_experts + e[u]] = v[u];
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < RU; u++) v[u] = ok[u] ? scores[(size_t)t[u] * n_experts + e[u]] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < RU; u++) {
+                if (!ok[u]) continue;
+                ch[(size_t)(2 * tt[u] + 1) * n_experts + e[u]] = v[u];
+                ch[(size_t)(2 * tt[u]) * n_experts + e[u]] = __fadd_rn(v[u], bias ? bias[e[u]] : 0.0f);
+            }
         }
-    }
+    };
+    if (nchunk > 4) logits(std::integral_constant<int, 1>{}, std::integral_constant<int, 16>{});
+    else logits(std::integral_constant<int, 4>{}, std::integral_constant<int, 4>{});
     __syncthreads();
     if (warp >= nt) return;
     const int t = t0 + warp;
