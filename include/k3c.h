@@ -471,6 +471,15 @@ int k3c_expert_upload(uint8_t *dev_run, const k3c_expert_run *r, const void *pay
  * k3_matmul_bf16 token by token. Int8 trunk rows run through k3c_q8_pack / k3c_q8_gemv. */
 int k3c_mmw(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int wdt,
             int in, int out, int accumulate, k3c_stream_t stream);
+/* The same product for many tokens on the tensor cores (tcgen05 kind::f16), bf16 W only: x
+ * enters as two bf16 terms (hi = bf16(x), lo = bf16(x - hi)), products accumulate in fp32.
+ * Not bit-exact with k3_matmul_bf16 (k3c_mmw is); error ~1e-6 of max|y|. in a multiple of 8,
+ * W 16-byte aligned; any ntok and out. scratch: k3c_mmw_tc_scratch(ntok, in) bytes of device
+ * memory for the activation terms. The latent layer takes this path for more than 32 tokens
+ * with a bf16 trunk (K3C_TRUNK_EXACT=1 keeps it on k3c_mmw). */
+size_t k3c_mmw_tc_scratch(int ntok, int in);
+int k3c_mmw_tc(float *y, int ldy, const float *x, int ldx, int ntok, const void *W, int in, int out,
+               int accumulate, void *scratch, size_t scratch_bytes, k3c_stream_t stream);
 /* k3_situ_glu (src/core/k3_ops.c:110-122) on ntok rows: gu [ntok][2n] (gate | up),
  * y [ntok][n]. */
 int k3c_situ_glu(float *y, const float *gu, int n, int ntok, float b1, float b2,

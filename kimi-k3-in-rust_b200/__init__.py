@@ -176,6 +176,8 @@ def lib():
         "k3c_q8_pack": ([vp, vp, i, vp, i, i, vp], i),
         "k3c_q8_gemv": ([vp, i, vp, i, i, i, vp, vp, i, i, i, vp], i),
         "k3c_q8_gemv_scratch": ([i, i, i], sz),
+        "k3c_mmw_tc_scratch": ([i, i], sz),
+        "k3c_mmw_tc": ([vp, i, vp, i, i, vp, i, i, i, vp, sz, vp], i),
         "k3c_q8_gemv_ws": ([vp, i, vp, i, i, i, vp, vp, i, i, i, vp, sz, vp], i),
         "k3c_router": ([vp, vp, vp, vp, i, vp, i, vp, i, i, i, i, f, i, vp], i),
         "k3c_router_select": ([vp, vp, vp, vp, i, i, i, f, i, vp], i),
@@ -827,6 +829,23 @@ def mmw(x, W, wdt, out=None, accumulate=False):
         out = torch.zeros((ntok, out_), dtype=torch.float32, device=x.device)
     _check(lib().k3c_mmw(_ptr(out), out.stride(0), _ptr(x), in_, ntok, _ptr(W), wdt, in_, out_,
                          1 if accumulate else 0, _stream()), "k3c_mmw")
+    return out
+
+
+def mmw_tc(x, W, out=None, accumulate=False, ldx=None):
+    """k3c_mmw_tc: y[t] = W x[t] on the tensor cores for any number of tokens, W [out][in] bf16
+    bit patterns (16-byte aligned, in a multiple of 8), x [ntok][>= in] fp32 (the first `in`
+    columns; ldx its row stride). Two bf16 terms of x, fp32 accumulation: not bit-exact."""
+    import torch
+    ntok = x.shape[0]
+    out_, in_ = W.shape
+    ldx = x.stride(0) if ldx is None else ldx
+    if out is None:
+        out = torch.zeros((ntok, out_), dtype=torch.float32, device=x.device)
+    n = int(lib().k3c_mmw_tc_scratch(ntok, in_))
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=x.device)
+    _check(lib().k3c_mmw_tc(_ptr(out), out.stride(0), _ptr(x), ldx, ntok, _ptr(W), in_, out_,
+                            1 if accumulate else 0, _ptr(ws), n, _stream()), "k3c_mmw_tc")
     return out
 
 

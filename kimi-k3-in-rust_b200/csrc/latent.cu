@@ -30,6 +30,11 @@
 
 namespace k3c {
 
+size_t mmw_tc_terms_bytes(int ntok, int in);
+bool mmw_tc_applies(const void *W, int in);
+int launch_mmw_tc_split(void *terms, const float *x, int ldx, int ntok, int in, cudaStream_t s);
+int launch_mmw_tc_gemm(float *y, int ldy, const void *terms, int ntok, const void *W, int in, int out,
+                       int accumulate, cudaStream_t s);
 int launch_router(int *idx, float *w, float *scores, const void *x, int x_dtype, const void *W, int w_dtype,
                   const float *bias, int hidden, int n_experts, int topk, int renorm, float routed_scale,
                   int ntok, double *part, cudaStream_t s);
@@ -374,6 +379,9 @@ constexpr int LAT_CHUNK = 32;
 // row each. Re-reading the weights per launch costs far less than that difference.
 constexpr int LAT_TRUNK_CHUNK = 16;
 constexpr int LAT_MAX_TOKENS = 65535;
+// bf16 trunk matrices for many tokens run on the tensor cores (trunk_tc.cu), this many tokens
+// per pass (bounds the shared branch's scratch; each pass reads every trunk matrix once)
+constexpr int LAT_TC_CHUNK = 2048;
 
 struct LatentBufs {
     double *rpart;     // router logit chunks
@@ -386,12 +394,15 @@ struct LatentBufs {
     float *wt;
     void *tc;          // tensor-core decode scratch
     size_t tc_bytes;
+    void *terms;       // bf16 activation terms of the tensor-core trunk (many tokens, bf16 trunk)
 };
 
 static bool carve_latent(Carve &cv, LatentBufs &b, const k3c_moe_latent_layer *L, int ntok) {
     const int SI = L->experts.inter * L->n_shared;
     const int Lw = L->experts.hidden;
-    const int C = ntok < LAT_CHUNK ? ntok : LAT_CHUNK;
+    const bool tc_trunk = ntok > LAT_CHUNK && L->wdt == K3C_WBF16;
+    const int C = tc_trunk ? (ntok < LAT_TC_CHUNK ? ntok : LAT_TC_CHUNK) : (ntok < LAT_CHUNK ? ntok : LAT_CHUNK);
+    const int kmax = L->hidden > SI ? (L->hidden > Lw ? L->hidden : Lw) : (SI > Lw ? SI : Lw);
     b.rpart = cv.take<double>(router_scratch_bytes(L->hidden, L->experts.n_experts, ntok) / sizeof(double) + 1);
     b.z = cv.take<float>((size_t)ntok * Lw);
     b.agg = cv.take<float>((size_t)ntok * Lw);
@@ -403,7 +414,8 @@ static bool carve_latent(Carve &cv, LatentBufs &b, const k3c_moe_latent_layer *L
     b.tc_bytes = ntok <= LAT_CHUNK ? moe_decode_tc_scratch(&L->experts, ntok)
                                    : moe_prefill_tc_scratch(&L->experts, ntok, true);
     b.tc = cv.take<char>(b.tc_bytes, 1024);
-    return b.rpart && b.z && b.agg && b.sgu && b.sact && b.sdn && b.idx && b.wt && b.tc;
+    b.terms = tc_trunk ? cv.take<char>(mmw_tc_terms_bytes(C, kmax), 256) : nullptr;
+    return b.rpart && b.z && b.agg && b.sgu && b.sact && b.sdn && b.idx && b.wt && b.tc && (b.terms || !tc_trunk);
 }
 
 static int check_latent(const k3c_moe_latent_layer *L, int ntok) {
@@ -462,6 +474,47 @@ int launch_moe_latent(float *out, const float *x, int ntok, const k3c_moe_latent
         stage_end(STAGE_ROUTER, s);
     }
     const bool sh = L->n_shared > 0;
+    if (b.terms && mmw_tc_applies(L->down, H) && mmw_tc_applies(L->up, Lw) &&
+        (!sh || (mmw_tc_applies(L->sh1, H) && mmw_tc_applies(L->sh3, H) && mmw_tc_applies(L->sh2, SI)))) {
+        // many tokens, bf16 trunk: every trunk matrix on the tensor cores, LAT_TC_CHUNK tokens
+        // per pass (the activations of a pass split once into their two bf16 terms and shared
+        // by the matrices that read them: down, sh1 and sh3 read x)
+        stage_begin(STAGE_Q8, s);
+        for (int t0 = 0; t0 < ntok; t0 += LAT_TC_CHUNK) {
+            const int c = ntok - t0 < LAT_TC_CHUNK ? ntok - t0 : LAT_TC_CHUNK;
+            K3C_TRY(launch_mmw_tc_split(b.terms, x + (size_t)t0 * H, H, c, H, s));
+            K3C_TRY(launch_mmw_tc_gemm(b.z + (size_t)t0 * Lw, Lw, b.terms, c, L->down, H, Lw, 0, s));
+            if (sh) {
+                K3C_TRY(launch_mmw_tc_gemm(b.sgu, 2 * SI, b.terms, c, L->sh1, H, SI, 0, s));
+                K3C_TRY(launch_mmw_tc_gemm(b.sgu + SI, 2 * SI, b.terms, c, L->sh3, H, SI, 0, s));
+                dim3 gs((SI + 255) / 256 < 148 ? (SI + 255) / 256 : 148, c);
+                k_situ_rows<<<gs, 256, 0, s>>>(b.sact, b.sgu, SI, L->situ_b1, L->situ_b2);
+                K3C_CHECK_LAUNCH();
+                K3C_TRY(launch_mmw_tc_split(b.terms, b.sact, SI, c, SI, s));
+                K3C_TRY(launch_mmw_tc_gemm(b.sdn + (size_t)t0 * H, H, b.terms, c, L->sh2, SI, H, 0, s));
+            }
+        }
+        stage_end(STAGE_Q8, s);
+        K3C_TRY(launch_moe_prefill_tc(b.agg, b.z, K3C_F32, ntok, &X, idx, wt, drops, b.tc, b.tc_bytes, s, true,
+                                      nullptr));
+        stage_begin(STAGE_Q8, s);
+        if (L->latent_norm_on) {
+            k_rmsnorm_rows<<<ntok, 256, 0, s>>>(b.agg, b.agg, L->latent_norm, Lw, L->rms_eps);
+            K3C_CHECK_LAUNCH();
+        }
+        for (int t0 = 0; t0 < ntok; t0 += LAT_TC_CHUNK) {
+            const int c = ntok - t0 < LAT_TC_CHUNK ? ntok - t0 : LAT_TC_CHUNK;
+            K3C_TRY(launch_mmw_tc_split(b.terms, b.agg + (size_t)t0 * Lw, Lw, c, Lw, s));
+            K3C_TRY(launch_mmw_tc_gemm(out + (size_t)t0 * H, H, b.terms, c, L->up, Lw, H, 0, s));
+        }
+        if (sh) {
+            const size_t n = (size_t)ntok * H;
+            k_add_f32<<<(unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, s>>>(out, b.sdn, n);
+            K3C_CHECK_LAUNCH();
+        }
+        stage_end(STAGE_Q8, s);
+        return K3C_OK;
+    }
     if (ntok > LAT_CHUNK) {
         // the same steps for many tokens: trunk matrices (and the shared branch) 16 tokens at
         // a time, the routed experts through the prefill kernels
