@@ -1015,8 +1015,10 @@ def run_latent(args, ws, rank, local):
         "metric": "K3 latent MoE-layer tokens/s", "value": B * args.steps / dt, "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": (f"experts mxfp4 x e4m3 ({args.terms} terms, tcgen05 kind::mxf8f6f4); trunk bf16 weights x fp32 "
-                  "activations, fp64 accumulate in the reference's order (bit-exact)"),
+        "dtype": (f"experts mxfp4 x e4m3 ({args.terms} terms, tcgen05 kind::mxf8f6f4); " +
+                  ("trunk bf16 weights x fp32 activations, fp64 accumulate in the reference's order (bit-exact)"
+                   if B <= 32 else
+                   "trunk bf16 weights x fp32 activations as two bf16 terms, fp32 accumulate (tcgen05 kind::f16)")),
         "data": "synthetic",
         "config": {"workload": LAT_WORKLOAD.replace("decode: B=16", f"{'decode' if B <= 32 else 'prefill'}: B={B}"),
                    "batch": B, "hidden": LH, "latent": LL, "inter": LI, "experts": LE,
@@ -1026,6 +1028,8 @@ def run_latent(args, ws, rank, local):
         "stages_ms_per_step": {"experts": exp_ms / args.steps, "router": ms_buf[1] / args.steps,
                                "trunk": trunk_ms / args.steps},
         "trunk_gbs": trunk_bytes * args.steps / (trunk_ms / 1e3) / 1e9 if trunk_ms > 0 else None,
+        "trunk_tflops": (2.0 * B * trunk_bytes / 2 * args.steps / (trunk_ms / 1e3) / 1e12
+                         if trunk_ms > 0 and B > 32 else None),
         "layer_hbm_gbs": (expert_bytes + args.steps * (trunk_bytes + LE * LH * 4)) / dt / 1e9,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm if achieved else None,
