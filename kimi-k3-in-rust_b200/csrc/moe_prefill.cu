@@ -1055,7 +1055,9 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     a.contrib[0] = b.contrib;   // one rank: the pair rows stay here ([T][topk+1][H])
     if (ep)                     // expert parallelism: each pair's row goes to its token's owner
         for (int q = 0; q < ep->world; q++) a.contrib[q] = ep->recv[q];
-    a.tmax = T;
+    // pair token g (of T = world * t_max under expert parallelism) is row g % tmax of rank
+    // g / tmax's receive buffer, which holds t_max rows
+    a.tmax = ep ? ep->t_max : T;
     a.kstride = K + 1;
     a.T = T;
     a.H = H;

@@ -171,3 +171,90 @@ def test_ep_fused_one_rank_equals_single_gpu():
         if ep is not None:
             ep.close()
         dist.destroy_process_group()
+
+
+def _emulated_ranks(k3, W_, H, I, E, K, counts, t_max, seed):
+    """W_ ranks of the peer-memory expert-parallel layer emulated on ONE GPU: every rank's
+    buffers are device tensors of cuda:0 and the three steps run for all ranks in turn on one
+    stream (step 1 of every rank, then step 2 of every rank, then step 3), which orders them
+    as the two barriers do. No kernel waits on another (the step-2 kernels read only x, idx
+    and wt, which step 2 never writes, and store into the receive buffers, which only step 3
+    reads). Returns each rank's output and the single-GPU layer's on the same tokens."""
+    import ctypes as C
+    import torch
+    dev = torch.device("cuda:0")
+    L = k3.lib()
+    g = k3.synth.rng(seed)
+    experts = [k3.synth.expert(g, H, I) for _ in range(E)]
+    shared = k3.synth.expert(g, H, I)
+    wf, _ = k3.synth.router_weights(g, E, H)
+    wb = k3.synth.bf16_bits((wf * 20).astype(np.float32))
+    Wr = torch.from_numpy(wb.view(np.int16)).to(dev).view(torch.bfloat16)
+    full = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in experts],
+                                k3.DeviceExpert.from_host(shared, dev), Wr, None, H, I, K, dev, terms=2)
+    owner = np.random.default_rng(seed).permutation(np.arange(E) % W_)     # scattered placement
+    expert_rank = torch.from_numpy(owner.astype(np.int32)).to(dev)
+    layers = []
+    for q in range(W_):
+        run_of = full.run_of.clone()
+        run_of[torch.from_numpy(owner != q).to(dev)] = -1
+        layers.append(k3.PoolMoeLayer(full.arena, E + 1, run_of, E, Wr, None, H, I, K, terms=2))
+    xb = [torch.zeros((t_max, H), dtype=torch.bfloat16, device=dev) for _ in range(W_)]
+    idx = [torch.zeros((t_max, K), dtype=torch.int32, device=dev) for _ in range(W_)]
+    wt = [torch.zeros((t_max, K), dtype=torch.float32, device=dev) for _ in range(W_)]
+    recv = [torch.zeros((t_max, K + 1, H), dtype=torch.int16, device=dev) for _ in range(W_)]
+    peers = []
+    for q in range(W_):
+        p = k3.EpPeersC()
+        p.world, p.rank, p.t_max = W_, q, t_max
+        p.x_dtype = k3._dtype_code(xb[0])
+        for r in range(W_):
+            p.ntok[r] = counts[r]
+            p.x[r], p.idx[r], p.wt[r], p.recv[r] = (xb[r].data_ptr(), idx[r].data_ptr(), wt[r].data_ptr(),
+                                                    recv[r].data_ptr())
+        peers.append(p)
+    xs = []
+    for q in range(W_):                                     # step 1: tokens and their routing
+        T = counts[q]
+        x = torch.from_numpy(k3.synth.bf16_bits(k3.synth.rng(900 + q).standard_normal((T, H)).astype(np.float32))
+                             .view(np.int16)).to(dev).view(torch.bfloat16)
+        xs.append(x)
+        xb[q][:T].copy_(x)
+        c = layers[q].c
+        rn = L.k3c_router_scratch(H, E, T)
+        rs = torch.empty(rn, dtype=torch.uint8, device=dev)
+        k3._check(L.k3c_router_ws(idx[q].data_ptr(), wt[q].data_ptr(), None, xb[q].data_ptr(), k3._dtype_code(xb[q]),
+                                  C.c_void_p(c.router_w), c.router_dtype, C.c_void_p(c.router_bias), H, E, K,
+                                  c.renorm, c.routed_scale, T, rs.data_ptr(), rn, k3._stream()), "k3c_router_ws")
+    keep = []
+    for q in range(W_):                                     # step 2: every rank's experts
+        c = layers[q].c
+        need = L.k3c_moe_prefill_ep_scratch(C.byref(c), C.byref(peers[q]))
+        assert need > 0, L.k3c_last_error()
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        keep.append(ws)
+        k3._check(L.k3c_moe_prefill_ep_experts(C.byref(c), C.byref(peers[q]), ws.data_ptr(), need, k3._stream()),
+                  "k3c_moe_prefill_ep_experts")
+    outs = []
+    for q in range(W_):                                     # step 3: each rank's combine
+        out = torch.empty((counts[q], H), dtype=torch.float32, device=dev)
+        k3._check(L.k3c_moe_ep_combine(out.data_ptr(), C.byref(peers[q]), H, K, expert_rank.data_ptr(), E, 1,
+                                       k3._stream()), "k3c_moe_ep_combine")
+        outs.append(out)
+    wants = [full.prefill(xs[q])[0] if counts[q] else torch.empty((0, H), device=dev) for q in range(W_)]
+    torch.cuda.synchronize()
+    return [o.cpu().numpy() for o in outs], [w.cpu().numpy() for w in wants]
+
+
+@pytest.mark.parametrize("W_,H,I,E,K,counts,t_max", [
+    (2, 256, 128, 8, 2, (200, 131), 256),
+    (4, 512, 256, 16, 4, (97, 300, 0, 1), 320),
+    (8, 256, 128, 16, 2, (40, 33, 64, 1, 17, 64, 5, 29), 64),
+])
+def test_ep_emulated_ranks_equal_single_gpu(k3, W_, H, I, E, K, counts, t_max):
+    """The multi-rank indexing of the peer-memory path (pair rows stored at row t % t_max of
+    rank t / t_max's receive buffer, token rows read from the owners' buffers, ragged and empty
+    ranks) on one GPU: every rank's output equals the single-GPU layer bit for bit."""
+    outs, wants = _emulated_ranks(k3, W_, H, I, E, K, list(counts), t_max, seed=40 + W_)
+    for q, (o, w) in enumerate(zip(outs, wants)):
+        assert np.array_equal(o, w), (q, np.abs(o - w).max() if o.size else 0)
