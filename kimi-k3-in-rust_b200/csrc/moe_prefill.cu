@@ -145,7 +145,8 @@ __global__ void __launch_bounds__(1024) k_pf_slots(int *__restrict__ n_slots, Sl
                                                    int *__restrict__ chunk_base, int *__restrict__ slot_base,
                                                    int *__restrict__ eoff, const int *__restrict__ cnt,
                                                    int nchunk, const int *__restrict__ run_of, int n_experts,
-                                                   int sh_base, int sh_n, int topk, int shared_run) {
+                                                   int sh_base, int sh_n, int topk, int shared_run,
+                                                   int *__restrict__ sh_row0) {
     __shared__ int2 warp_sum[32];
     int sbase = 0, rbase = 0;
     for (int e0 = 0; e0 < n_experts; e0 += blockDim.x) {
@@ -172,6 +173,7 @@ __global__ void __launch_bounds__(1024) k_pf_slots(int *__restrict__ n_slots, Sl
         sbase += ts;
         rbase += tr;
     }
+    if (threadIdx.x == 0) *sh_row0 = shared_run >= 0 ? rbase : -1;   // the shared rows follow the routed ones
     if (shared_run >= 0) {
         for (int t = threadIdx.x; t < sh_n; t += blockDim.x) {
             const size_t pos = (size_t)(sbase + t / PF_M) * PF_M + t % PF_M;
@@ -195,9 +197,11 @@ __global__ void __launch_bounds__(1024) k_pf_slots(int *__restrict__ n_slots, Sl
 }
 
 // Pair i of expert e goes to row r % 128 of slot slot_base[e] + r / 128, r its rank among all
-// pairs of e (chunk base + rank within the chunk).
+// pairs of e (chunk base + rank within the chunk); its compact A row is eoff[e] + r
+// (pair_row[i]; pairs that run nowhere here keep -1).
 __global__ void __launch_bounds__(1024) k_pf_scatter(int *__restrict__ pair_tok, int *__restrict__ pair_k,
-                                                     int *__restrict__ row_tok, const int *__restrict__ pe,
+                                                     int *__restrict__ row_tok, int *__restrict__ pair_row,
+                                                     const int *__restrict__ pe,
                                                      const int *__restrict__ rank, const int *__restrict__ chunk_base,
                                                      const int *__restrict__ slot_base, const int *__restrict__ eoff,
                                                      int P, int n_experts, int topk) {
@@ -210,6 +214,7 @@ __global__ void __launch_bounds__(1024) k_pf_scatter(int *__restrict__ pair_tok,
     pair_tok[pos] = i / topk;
     pair_k[pos] = i % topk;
     row_tok[eoff[e] + r] = i / topk;
+    pair_row[i] = eoff[e] + r;
 }
 
 // Scale atoms of the A operand per slot: sfa [slot][J][H/128][512] from the per-token scales
@@ -285,13 +290,16 @@ struct XSrc {
     const uint8_t *need;   // tokens to quantise (NULL: all)
 };
 
-// Token g's J terms, xq [J][T][H], and their block scales xsf [J][T][H/32]: every token once.
-// One thread per 32-element block.
+// Token g's J terms written straight into the compact A rows of its pairs (pair_row[g*topk+k],
+// and its shared-expert row sh_row0 + g - sh_base when g is one of the shared tokens), and its
+// block scales into xsf [J][T][H/32] (the slot scale atoms are built from them): every token
+// read and quantised once, no per-token staging copy. One thread per 32-element block.
 template <typename XT>
-__global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq, uint8_t *__restrict__ xsf,
-                                                       const XSrc src_x, int T, int H) {
+__global__ void __launch_bounds__(256) k_pf_quant_pairs(uint8_t *__restrict__ xq, uint8_t *__restrict__ xsf,
+                                                        const XSrc src_x, const int *__restrict__ pair_row,
+                                                        const int *__restrict__ sh_row0, int sh_base, int sh_n,
+                                                        int T, int H, int topk, int rows_cap) {
     const int nb = H / 32;
-    const int rows_cap = T;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int r = (int)(i / nb), blk = (int)(i % nb);
     if (r >= T) return;
@@ -328,25 +336,19 @@ __global__ void __launch_bounds__(256) k_pf_quant_rows(uint8_t *__restrict__ xq,
     uint32_t sf[PF_J];
     quant_row32(a, q, sf);
 #pragma unroll
-    for (int j = 0; j < PF_J; j++) {
-        uint4 *d = reinterpret_cast<uint4 *>(xq + ((size_t)j * rows_cap + r) * H + blk * 32);
-        d[0] = q[j][0];
-        d[1] = q[j][1];
-        xsf[((size_t)j * rows_cap + r) * nb + blk] = (uint8_t)sf[j];
-    }
-}
-
-// Compact row r of the A operand = token row_tok[r]'s terms: xq [J][rows_cap][H] copied from
-// tq [J][T][H] in 16-byte pieces (the token rows stay in L2; each is read topk+1 times).
-__global__ void __launch_bounds__(256) k_pf_gather_rows(uint8_t *__restrict__ xq, const uint8_t *__restrict__ tq,
-                                                        const int *__restrict__ row_tok,
-                                                        const int *__restrict__ n_rows, int rows_cap, int T, int H) {
-    const int j = blockIdx.y, h16 = H / 16;
-    const size_t n = (size_t)(*n_rows) * h16;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int r = (int)(i / h16), c = (int)(i % h16);
-        const uint4 v = *reinterpret_cast<const uint4 *>(tq + ((size_t)j * T + row_tok[r]) * H + 16 * c);
-        *reinterpret_cast<uint4 *>(xq + ((size_t)j * rows_cap + r) * H + 16 * c) = v;
+    for (int j = 0; j < PF_J; j++) xsf[((size_t)j * T + r) * nb + blk] = (uint8_t)sf[j];
+    const int sr0 = *sh_row0;
+    for (int k = 0; k <= topk; k++) {
+        int row;
+        if (k < topk) row = pair_row[(size_t)r * topk + k];
+        else row = (sr0 >= 0 && r >= sh_base && r < sh_base + sh_n) ? sr0 + (r - sh_base) : -1;
+        if (row < 0) continue;
+#pragma unroll
+        for (int j = 0; j < PF_J; j++) {
+            uint4 *d = reinterpret_cast<uint4 *>(xq + ((size_t)j * rows_cap + row) * H + blk * 32);
+            d[0] = q[j][0];
+            d[1] = q[j][1];
+        }
     }
 }
 
@@ -788,11 +790,11 @@ __global__ void __launch_bounds__(PT_THREADS) k_pf_tail(const __grid_constant__ 
 // ------------------------------------------------------------------ host side
 struct PfBufs {
     int *idx, *pe, *rank, *cnt, *chunk_base, *slot_base, *eoff, *n_slots, *n_rows, *err, *pair_tok, *pair_k,
-        *row_tok, *full_ids, *tail_ids, *n_full, *n_tail;
+        *row_tok, *full_ids, *tail_ids, *n_full, *n_tail, *pair_row, *sh_row0;
     float *wt;
     uint16_t *contrib;
     double *rpart;
-    uint8_t *dropped, *xq, *tq, *xsf, *sfa_x, *actq, *actsf;
+    uint8_t *dropped, *xq, *xsf, *sfa_x, *actq, *actsf;
     SlotPf *slots;
     int max_slots, nchunk, rows_cap;
 };
@@ -825,7 +827,8 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T, b
     b.pair_k = cv.take<int>((size_t)b.max_slots * PF_M);
     b.row_tok = cv.take<int>(b.rows_cap);
     b.xq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * H, 1024);
-    b.tq = cv.take<uint8_t>((size_t)PF_J * T * H, 256);
+    b.pair_row = cv.take<int>(P);
+    b.sh_row0 = cv.take<int>(1);
     b.xsf = cv.take<uint8_t>((size_t)PF_J * T * (H / 32));
     b.sfa_x = cv.take<uint8_t>((size_t)b.max_slots * PF_J * (H / 128) * 512);
     b.actq = cv.take<uint8_t>((size_t)PF_J * b.rows_cap * I, 1024);
@@ -834,7 +837,7 @@ static bool carve_pf(Carve &cv, PfBufs &b, const k3c_moe_pool_layer *L, int T, b
     return b.idx && b.wt && b.rpart && b.pe && b.rank && b.dropped && b.cnt && b.chunk_base && b.slot_base &&
            b.eoff && b.n_slots && b.n_rows && b.err && b.slots && b.full_ids && b.tail_ids && b.n_full && b.n_tail &&
            b.pair_tok && b.pair_k && b.row_tok && b.xq &&
-           b.tq && b.xsf && b.sfa_x && b.actq && b.actsf && b.contrib;
+           b.pair_row && b.sh_row0 && b.xsf && b.sfa_x && b.actq && b.actsf && b.contrib;
 }
 
 static char *const kPfSizing = reinterpret_cast<char *>(4096);
@@ -986,12 +989,14 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
     const int sh_base = ep ? ep->rank * ep->t_max : 0, sh_n = ep ? ep->ntok[ep->rank] : T;
     k_pf_slots<<<1, 1024, 0, s>>>(b.n_slots, b.slots, b.pair_tok, b.pair_k, b.row_tok, b.n_rows, b.chunk_base,
                                   b.slot_base, b.eoff, b.cnt, b.nchunk, L->run_of, E, sh_base, sh_n, K,
-                                  L->shared_run);
+                                  L->shared_run, b.sh_row0);
     K3C_CHECK_LAUNCH();
-    k_pf_scatter<<<b.nchunk, PF_CHUNK, 0, s>>>(b.pair_tok, b.pair_k, b.row_tok, b.pe, b.rank, b.chunk_base,
-                                               b.slot_base, b.eoff, P, E, K);
+    K3C_TRY_CUDA(cudaMemsetAsync(b.pair_row, 0xFF, (size_t)P * sizeof(int), s));   // -1: runs nowhere here
+    k_pf_scatter<<<b.nchunk, PF_CHUNK, 0, s>>>(b.pair_tok, b.pair_k, b.row_tok, b.pair_row, b.pe, b.rank,
+                                               b.chunk_base, b.slot_base, b.eoff, P, E, K);
     K3C_CHECK_LAUNCH();
-    // every token's terms once, the compact rows copied from them, each slot's scale atoms
+    // every token read and quantised once, its terms stored in its pairs' compact rows; each slot's
+    // scale atoms from the per-token scales
     const size_t nthr = (size_t)T * (H / 32);
     const unsigned qblocks = (unsigned)((nthr + 255) / 256);
     XSrc xs{};
@@ -1008,11 +1013,11 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         xs.tmax = T;
     }
     if (x_dtype == K3C_BF16)
-        k_pf_quant_rows<uint16_t><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, xs, T, H);
+        k_pf_quant_pairs<uint16_t><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, xs, b.pair_row, b.sh_row0, sh_base, sh_n, T, H,
+                                                            K, b.rows_cap);
     else
-        k_pf_quant_rows<float><<<qblocks, 256, 0, s>>>(b.tq, b.xsf, xs, T, H);
-    K3C_CHECK_LAUNCH();
-    k_pf_gather_rows<<<dim3(sm_count() * 16, PF_J), 256, 0, s>>>(b.xq, b.tq, b.row_tok, b.n_rows, b.rows_cap, T, H);
+        k_pf_quant_pairs<float><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, xs, b.pair_row, b.sh_row0, sh_base, sh_n, T, H,
+                                                         K, b.rows_cap);
     K3C_CHECK_LAUNCH();
     k_pf_slot_sf<<<dim3(b.max_slots, PF_J), 256, 0, s>>>(b.sfa_x, b.xsf, b.row_tok, b.n_slots, b.slots, b.n_rows, T, H);
     K3C_CHECK_LAUNCH();

@@ -128,21 +128,31 @@ struct WSlice {
     }
 };
 
-template <typename WT, typename XT, int NT>
-__global__ void __launch_bounds__(256, 2) k_router_partial(double *__restrict__ part, const XT *__restrict__ x,
-                                                        const WT *__restrict__ W, int hidden, int n_experts,
-                                                        int ntok, int vec_w, int vec_x, int cpb) {
-    extern __shared__ __align__(16) double rsm[];   // xs [RT_KC][NT], then red [8][NT][32]
+// EPT experts per lane (lane l of block b takes experts 32*EPT*b + l + 32*u, u < EPT): every
+// activation read from shared memory then feeds EPT x 2 FMAs, which keeps the FP64 pipe rather
+// than the shared-memory pipe the limit at 16 tokens per block. Each expert's sum keeps its
+// order (its own K slice per warp, warps in order, chunks in order), whatever EPT is.
+template <typename WT, typename XT, int NT, int EPT>
+__global__ void __launch_bounds__(256, EPT == 1 ? 2 : 1) k_router_partial(double *__restrict__ part,
+                                                                      const XT *__restrict__ x,
+                                                                      const WT *__restrict__ W, int hidden,
+                                                                      int n_experts, int ntok, int vec_w, int vec_x,
+                                                                      int cpb) {
+    extern __shared__ __align__(16) double rsm[];   // xs [RT_KC][NT], then red [8][NT][32*EPT]
     double *xs = rsm;
     double *red = rsm + RT_KC * NT;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     grid_dep_launch();   // the select kernel may be scheduled; it waits for this grid's end
     grid_dep_wait();     // x may come from the previous kernel
     const int t0 = blockIdx.z * NT, nt = min(NT, ntok - t0);
-    const int e = blockIdx.x * 32 + lane;
-    double acc[NT];
+    int e[EPT];
 #pragma unroll
-    for (int t = 0; t < NT; t++) acc[t] = 0.0;
+    for (int u = 0; u < EPT; u++) e[u] = blockIdx.x * 32 * EPT + 32 * u + lane;
+    double acc[EPT][NT];
+#pragma unroll
+    for (int u = 0; u < EPT; u++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[u][t] = 0.0;
     // this block adds chunks [cpb*y, cpb*y + cpb) in order; chunk c+1's activations and W
     // slices are loaded into registers while chunk c is multiplied
     const int nchunk = (hidden + RT_KC - 1) / RT_KC;
@@ -175,23 +185,31 @@ __global__ void __launch_bounds__(256, 2) k_router_partial(double *__restrict__ 
     };
     // every chunk full and rows 16-byte aligned: whole W slices, one round trip each
     const bool wfast = vec_w && hidden % RT_KC == 0;
-    const WT *wbase = W + (size_t)(e < n_experts ? e : 0) * hidden + warp * RT_KW;
-    WSlice<WT> wnext;
+    const WT *wbase[EPT];
+#pragma unroll
+    for (int u = 0; u < EPT; u++) wbase[u] = W + (size_t)(e[u] < n_experts ? e[u] : 0) * hidden + warp * RT_KW;
+    WSlice<WT> wnext[EPT];
     load_chunk(c_begin);
-    if (wfast) wnext.load(wbase + (size_t)c_begin * RT_KC);
+    if (wfast)
+#pragma unroll
+        for (int u = 0; u < EPT; u++) wnext[u].load(wbase[u] + (size_t)c_begin * RT_KC);
     for (int c = c_begin; c < c_end; c++) {
         const int k0 = c * RT_KC, kn = min(RT_KC, hidden - k0);
         if (c > c_begin) __syncthreads();   // every warp is done with the previous chunk
         store_chunk();
         __syncthreads();
-        const WSlice<WT> wcur = wnext;
+        WSlice<WT> wcur[EPT];
+#pragma unroll
+        for (int u = 0; u < EPT; u++) wcur[u] = wnext[u];
         if (c + 1 < c_end) {
             load_chunk(c + 1);
-            if (wfast) wnext.load(wbase + (size_t)(c + 1) * RT_KC);
+            if (wfast)
+#pragma unroll
+                for (int u = 0; u < EPT; u++) wnext[u].load(wbase[u] + (size_t)(c + 1) * RT_KC);
         }
         const int kw = warp * RT_KW, kwn = min(RT_KW, kn - kw);   // this warp's slice
-        // acc[t] += w[0..8) . x[kw+k .. kw+k+8)[t]
-        auto step = [&](const double (&w)[8], int k) {
+        // acc[u][t] += w[u][0..8) . x[kw+k .. kw+k+8)[t]
+        auto step = [&](const double (&w)[EPT][8], int k) {
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 const double *xp = xs + (kw + k + q) * NT;   // same address in every lane: broadcast
@@ -199,39 +217,50 @@ __global__ void __launch_bounds__(256, 2) k_router_partial(double *__restrict__ 
 #pragma unroll
                     for (int t2 = 0; t2 < NT / 2; t2++) {
                         const double2 xq = reinterpret_cast<const double2 *>(xp)[t2];
-                        acc[2 * t2] = fma(w[q], xq.x, acc[2 * t2]);
-                        acc[2 * t2 + 1] = fma(w[q], xq.y, acc[2 * t2 + 1]);
+#pragma unroll
+                        for (int u = 0; u < EPT; u++) {
+                            acc[u][2 * t2] = fma(w[u][q], xq.x, acc[u][2 * t2]);
+                            acc[u][2 * t2 + 1] = fma(w[u][q], xq.y, acc[u][2 * t2 + 1]);
+                        }
                     }
                 } else {
 #pragma unroll
-                    for (int t = 0; t < NT; t++) acc[t] = fma(w[q], xp[t], acc[t]);
+                    for (int t = 0; t < NT; t++)
+#pragma unroll
+                        for (int u = 0; u < EPT; u++) acc[u][t] = fma(w[u][q], xp[t], acc[u][t]);
                 }
             }
         };
         if (wfast) {
 #pragma unroll
             for (int g = 0; g < RT_KW / 8; g++) {
-                double w[8];
-                wcur.get(g, w);
+                double w[EPT][8];
+#pragma unroll
+                for (int u = 0; u < EPT; u++) wcur[u].get(g, w[u]);
                 step(w, 8 * g);
             }
         } else {
-            const WT *row = W + (size_t)(e < n_experts ? e : 0) * hidden + k0 + kw;
             for (int k = 0; k < kwn; k += 8) {
-                double w[8];
-                load_w8<WT>(row, k, kwn, vec_w != 0, w);
+                double w[EPT][8];
+#pragma unroll
+                for (int u = 0; u < EPT; u++)
+                    load_w8<WT>(W + (size_t)(e[u] < n_experts ? e[u] : 0) * hidden + k0 + kw, k, kwn, vec_w != 0,
+                                w[u]);
                 step(w, k);
             }
         }
     }
+    constexpr int EW = 32 * EPT;   // experts per block
 #pragma unroll
-    for (int t = 0; t < NT; t++) red[(warp * NT + t) * 32 + lane] = acc[t];
+    for (int u = 0; u < EPT; u++)
+#pragma unroll
+        for (int t = 0; t < NT; t++) red[(warp * NT + t) * EW + 32 * u + lane] = acc[u][t];
     __syncthreads();
-    for (int i = threadIdx.x; i < NT * 32; i += 256) {
-        const int t = i / 32, l = i % 32, ee = blockIdx.x * 32 + l;
-        double sum = red[t * 32 + l];
+    for (int i = threadIdx.x; i < NT * EW; i += 256) {
+        const int t = i / EW, l = i % EW, ee = blockIdx.x * EW + l;
+        double sum = red[t * EW + l];
 #pragma unroll
-        for (int w = 1; w < 8; w++) sum += red[(w * NT + t) * 32 + l];
+        for (int w = 1; w < 8; w++) sum += red[(w * NT + t) * EW + l];
         if (t < nt && ee < n_experts) part[((size_t)blockIdx.y * ntok + t0 + t) * n_experts + ee] = sum;
     }
 }
@@ -533,11 +562,16 @@ size_t router_scratch_bytes(int hidden, int n_experts, int ntok) {
     return b;
 }
 
+// Experts per lane: two for many tokens (the grid has blocks to spare and the FP64 pipe, not
+// shared memory, should be the limit), one for small batches (twice the blocks fill the SMs).
+static int router_ept(int ntok) { return ntok >= 64 ? 2 : 1; }
+
 // K chunks per block: 1 (most parallel) unless the grid would exceed about three waves,
 // in which case blocks take several chunks and the partial array shrinks accordingly.
 static int router_cpb(int hidden, int n_experts, int ntok) {
     const int nchunk = (hidden + RT_KC - 1) / RT_KC;
-    const long long blocks = (long long)((n_experts + 31) / 32) * nchunk * ((ntok + 15) / 16);
+    const int ew = 32 * router_ept(ntok);
+    const long long blocks = (long long)((n_experts + ew - 1) / ew) * nchunk * ((ntok + 15) / 16);
     const long long cap = 3LL * 3 * sm_count_rt();
     int cpb = (int)((blocks + cap - 1) / cap);
     return cpb < 1 ? 1 : (cpb > nchunk ? nchunk : cpb);
@@ -547,18 +581,29 @@ static int router_nparts(int hidden, int n_experts, int ntok) {
     return (nchunk + cpb - 1) / cpb;
 }
 
+template <typename WT, typename XT, int NT, int EPT>
+static int launch_partial_ept(double *part, const void *x, const void *W, int hidden, int n_experts, int ntok,
+                              int vec_w, int vec_x, cudaStream_t s) {
+    const int smem = (RT_KC * NT + 8 * NT * 32 * EPT) * (int)sizeof(double);
+    auto kern = k_router_partial<WT, XT, NT, EPT>;
+    if (smem > 48 * 1024)
+        K3C_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int cpb = router_cpb(hidden, n_experts, ntok);
+    const dim3 grid((n_experts + 32 * EPT - 1) / (32 * EPT), router_nparts(hidden, n_experts, ntok),
+                    (ntok + NT - 1) / NT);
+    count_launch();
+    K3C_TRY_CUDA(launch_pdl(kern, grid, dim3(256), smem, s, part, (const XT *)x, (const WT *)W, hidden, n_experts,
+                            ntok, vec_w, vec_x, cpb));
+    return K3C_OK;
+}
+
 template <typename WT, typename XT, int NT>
 static int launch_partial_nt(double *part, const void *x, const void *W, int hidden, int n_experts, int ntok,
                              int vec_w, int vec_x, cudaStream_t s) {
-    const int smem = (RT_KC * NT + 8 * NT * 32) * (int)sizeof(double);
-    if (smem > 48 * 1024)
-        K3C_TRY_CUDA(cudaFuncSetAttribute(k_router_partial<WT, XT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int cpb = router_cpb(hidden, n_experts, ntok);
-    const dim3 grid((n_experts + 31) / 32, router_nparts(hidden, n_experts, ntok), (ntok + NT - 1) / NT);
-    count_launch();
-    K3C_TRY_CUDA(launch_pdl(k_router_partial<WT, XT, NT>, grid, dim3(256), smem, s, part, (const XT *)x,
-                            (const WT *)W, hidden, n_experts, ntok, vec_w, vec_x, cpb));
-    return K3C_OK;
+    if constexpr (NT == 16)
+        if (router_ept(ntok) == 2)
+            return launch_partial_ept<WT, XT, NT, 2>(part, x, W, hidden, n_experts, ntok, vec_w, vec_x, s);
+    return launch_partial_ept<WT, XT, NT, 1>(part, x, W, hidden, n_experts, ntok, vec_w, vec_x, s);
 }
 
 template <typename WT, typename XT>
