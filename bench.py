@@ -426,7 +426,17 @@ def decode_line(args, ws, rank, local):
         c1.record()
         torch.cuda.synchronize()
         tb = maxed(c0.elapsed_time(c1) / 1e3)
-        batches[f"B{b}"] = {"tokens_per_s": ws * b * args.steps / tb, "ms_per_step": 1e3 * tb / args.steps}
+        # the distinct experts each of these steps streams (its routed ids + the shared expert)
+        nu = []
+        for i in range(args.steps):
+            layer.decode(xb[(args.warmup + i) % NB], out=ob, idx=ib, wt=wb)
+            nu.append(len(set(ib.cpu().numpy().ravel().tolist())) + 1)
+        step_bytes = float(np.mean(nu)) * run_bytes
+        batches[f"B{b}"] = {"tokens_per_s": ws * b * args.steps / tb, "ms_per_step": 1e3 * tb / args.steps,
+                            "distinct_experts_per_step": float(np.mean(nu)),
+                            "step_hbm_frac": step_bytes / (tb / args.steps) / 1e9 / hbm_peak,
+                            "how": "distinct experts' bytes / whole-step time / measured HBM peak"}
+    batches["config0_expert"] = expert_ffn_probe(k3, L, dev, rank, hbm_peak)
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -763,20 +773,13 @@ EX_WORKLOAD = "config[0] single MXFP4 expert SwiGLU FFN, 1 fp32 token per step (
               "E2M1 codes uniform, E8M0 uniform in [118,124]), fp32 accumulate"
 
 
-def run_expert(args, ws, rank, local):
-    """One step = one fp32 token through one expert (k3c_expert_ffn, the fp32-activation
-    CUDA-core path the 1e-5 tolerance calls for), rotating over 16 experts (374 MB, more than
-    L2) so every step streams its 23.4 MB from HBM."""
+def expert_ffn_setup(k3, L, dev, seed, NX=16):
+    """NX random experts in the reference's run layout (NX x 23.4 MB, more than L2 for NX=16),
+    NX fp32 tokens and a step function: one token through expert i % NX (k3c_expert_ffn)."""
     import ctypes as C
     import torch
-    import __graft_entry__ as ge
-    k3 = ge.load_package()
-    L = k3.lib()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    NX = 16
     g = torch.Generator(device=dev)
-    g.manual_seed(4242 + rank)
+    g.manual_seed(seed)
     lay, run = k3.expert_run_layout(H, I)
     blob = torch.empty(NX * run, dtype=torch.uint8, device=dev)
     b2 = blob.view(NX, run)
@@ -798,6 +801,51 @@ def run_expert(args, ws, rank, local):
         rc = L.k3c_expert_ffn(C.c_void_p(y.data_ptr()), C.c_void_p(xx.data_ptr()), 1, C.byref(q), H, I, 0,
                               C.c_void_p(scratch.data_ptr()), nbytes, k3._stream())
         assert rc == 0, L.k3c_last_error()
+
+    return step, run, xs, y, (blob, qs, scratch)
+
+
+def expert_ffn_probe(k3, L, dev, rank, hbm_peak, steps=160):
+    """config[0] beside the headline: one fp32 token through one expert, 16 experts rotated,
+    the calls replayed from a CUDA graph (the --workload expert measurement, shorter)."""
+    import torch
+    step, run, _, _, keep = expert_ffn_setup(k3, L, dev, 4242 + rank)
+    for i in range(16):
+        step(i)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    with torch.cuda.graph(gr, stream=cap):
+        for i in range(16):
+            step(i)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps // 16):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3 / (16 * (steps // 16))
+    del gr, keep
+    return {"us_per_token": 1e6 * dt, "hbm_frac": run / dt / 1e9 / hbm_peak,
+            "how": "k3c_expert_ffn, one fp32 token, 23.4 MB per token, graph replay (as --workload expert)"}
+
+
+def run_expert(args, ws, rank, local):
+    """One step = one fp32 token through one expert (k3c_expert_ffn, the fp32-activation
+    CUDA-core path the 1e-5 tolerance calls for), rotating over 16 experts (374 MB, more than
+    L2) so every step streams its 23.4 MB from HBM."""
+    import ctypes as C
+    import torch
+    import __graft_entry__ as ge
+    k3 = ge.load_package()
+    L = k3.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    NX = 16
+    step, run, xs, y, _keep = expert_ffn_setup(k3, L, dev, 4242 + rank, NX)
 
     for i in range(args.warmup):
         step(i)
