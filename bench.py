@@ -1197,6 +1197,22 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     for i in range(warmup):
         epl.forward(xs[i % 2], **fwd_kw)
     torch.cuda.synchronize()
+    graphs = None
+    if impl == "fused" and getattr(args, "ep_graph", False):
+        # the layer's launches (and its two barriers) captured once per input buffer and
+        # replayed: no host work between the kernels of a step
+        graphs = []
+        per_graph = 0
+        for i in range(2):
+            gr = torch.cuda.CUDAGraph()
+            l0 = L.k3c_launch_count()
+            with torch.cuda.graph(gr):
+                epl.forward(xs[i], **fwd_kw)
+            per_graph = L.k3c_launch_count() - l0
+            graphs.append(gr)
+        for i in range(2):
+            graphs[i].replay()
+        torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
     clk = Clocks(local)
@@ -1208,10 +1224,13 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(steps):
-        epl.forward(xs[i % 2], **fwd_kw)
+        if graphs:
+            graphs[i % 2].replay()
+        else:
+            epl.forward(xs[i % 2], **fwd_kw)
     e1.record()
     torch.cuda.synchronize()
-    launches = L.k3c_launch_count() - launches0
+    launches = L.k3c_launch_count() - launches0 if not graphs else per_graph * steps
     L.k3c_timing_enable(0)
     L.k3c_timing_read(ms_buf, n_buf, 4)
     stages = {name: ms_buf[j] / steps for j, name in enumerate(("experts", "router", "combine"))}
@@ -1219,10 +1238,17 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     phases = None
     if impl == "fused":
         epl.phase_timing(True)
+        if graphs:   # replayed steps record no stage events: take the stages from these steps
+            L.k3c_timing_enable(1)
+            L.k3c_timing_read(ms_buf, n_buf, 4)
         for i in range(3):
             epl.forward(xs[i % 2], **fwd_kw)
         phases = epl.phase_read()
         epl.phase_timing(False)
+        if graphs:
+            L.k3c_timing_enable(0)
+            L.k3c_timing_read(ms_buf, n_buf, 4)
+            stages = {name: ms_buf[j] / 3 for j, name in enumerate(("experts", "router", "combine"))}
         ph = torch.tensor([phases[k] for k in epl.PHASES], dtype=torch.float64, device=dev)
         if ws > 1:
             dist.all_reduce(ph, op=dist.ReduceOp.MAX)
@@ -1269,6 +1295,7 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     else:
         dt, rows_all, maxrel_all, idx_all = dt_local, remote_rows, maxrel, idx_ok
         pairs_all, exp_max, exp_mean = remote_pairs, stages["experts"], stages["experts"]
+    graphs = None   # graphs holding NCCL calls go before the process group does
     if impl == "fused":
         epl.close()
     if rank != 0:
@@ -1350,6 +1377,8 @@ def main():
                          "contiguous id ranges")
     ap.add_argument("--ep-impl", default="fused", choices=["fused", "a2a"],
                     help="ep workload: fused peer-memory exchange in the expert kernels, or NCCL all-to-all")
+    ap.add_argument("--ep-graph", action="store_true",
+                    help="ep: replay each step from a CUDA graph of the layer's launches (barriers included)")
     ap.add_argument("--ep-steps", type=int, default=10,
                     help="default line: timed steps of the config[3] expert-parallel layer (its 'ep' object)")
     ap.add_argument("--no-ep", action="store_true", help="default line without the 'ep' object")
