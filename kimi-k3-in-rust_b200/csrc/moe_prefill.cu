@@ -57,11 +57,14 @@ constexpr int PF_STAGE = PF_J * PF_A + PF_B + PF_SF;
 constexpr int PF_STAGES = 3;
 constexpr int PF_EPI_WARPS = 8;               // two per TMEM lane quadrant, each half the columns
 constexpr int PF_THREADS = 64 + 32 * PF_EPI_WARPS;
-constexpr int PF_BYTES = 1024 + PF_STAGES * PF_STAGE + PF_M * 4 + 256;
+constexpr int PF_STG = 32 * 64;                // D epilogue: a warp's 32 rows x 32 bf16 columns
+constexpr int PF_BYTES = 1024 + PF_STAGES * PF_STAGE + 256 + PF_EPI_WARPS * PF_STG;
 constexpr uint32_t PF_TMEM = 512;             // accumulator 256 columns + scale factors
 constexpr uint32_t PF_SF_COL = 256;
 constexpr uint32_t PF_TX = PF_J * PF_A + PF_N * 64 + PF_SF;   // E2M1 moves 4 bits per element
 static_assert(PF_STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
+static_assert(8 * (2 * PF_STAGES + 2) + 4 <= 256, "barrier area");
+static_assert(PF_BYTES <= 227 * 1024, "fits one CTA per SM");
 }  // namespace
 
 struct SlotPf {
@@ -364,7 +367,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
                                                        const __grid_constant__ CUtensorMap tmW, PfArgs p) {
     extern __shared__ uint8_t pf_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pf_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PF_STAGES * PF_STAGE);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PF_STAGES * PF_STAGE);   // 256 bytes, then staging
     uint64_t *full = bars, *empty = bars + PF_STAGES, *tfull = bars + 2 * PF_STAGES, *tempty = tfull + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -521,24 +524,42 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_moe(const __grid_constant__ C
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(tempty);
+                // This thread's row goes to its pair's row of the token owner's buffer (NULL: the
+                // row is past the slot's pairs). Each 32-column chunk is staged in shared memory
+                // and stored by four lanes per row, so a warp's store covers 8 rows x 64
+                // contiguous bytes instead of 32 rows x 16 bytes: the rows of a peer's buffer
+                // cross NVLink in 64-byte writes.
+                uint16_t *dst = nullptr;
                 if (ok && m < sl.ntok) {
                     const size_t pr = (size_t)s * PF_M + m;
                     const int g = p.pair_tok[pr];
-                    uint16_t *dst = p.contrib[g / p.tmax] + ((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H +
-                                    (size_t)nt * PF_N;
+                    dst = p.contrib[g / p.tmax] + ((size_t)(g % p.tmax) * p.kstride + p.pair_k[pr]) * p.H +
+                          (size_t)nt * PF_N + 32 * half * NC;
+                }
+                uint8_t *stg = smem + PF_STAGES * PF_STAGE + 256 + (warp - 2) * PF_STG;
+                const uint32_t sw = (lane >> 1) & 3;   // 16-byte chunk swizzle of this lane's row
 #pragma unroll
-                    for (int cc = 0; cc < NC; cc++) {
-                        uint4 *d4 = reinterpret_cast<uint4 *>(dst + 32 * (half * NC + cc));
+                for (int cc = 0; cc < NC; cc++) {
 #pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            uint32_t w[4];
+                    for (int i = 0; i < 4; i++) {
+                        uint32_t w[4];
 #pragma unroll
-                            for (int k = 0; k < 4; k++)
-                                w[k] = f32x2_to_bf16x2(__uint_as_float(v[cc][8 * i + 2 * k]),
-                                                       __uint_as_float(v[cc][8 * i + 2 * k + 1]));
-                            d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
-                        }
+                        for (int k = 0; k < 4; k++)
+                            w[k] = f32x2_to_bf16x2(__uint_as_float(v[cc][8 * i + 2 * k]),
+                                                   __uint_as_float(v[cc][8 * i + 2 * k + 1]));
+                        *reinterpret_cast<uint4 *>(stg + lane * 64 + 16 * (i ^ sw)) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int r = (lane >> 2) + 8 * i, c = lane & 3;
+                        const unsigned long long rd =
+                            __shfl_sync(0xffffffffu, (unsigned long long)(uintptr_t)dst, r);
+                        const uint4 val =
+                            *reinterpret_cast<const uint4 *>(stg + r * 64 + 16 * (c ^ ((r >> 1) & 3)));
+                        if (rd) *reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(rd) + cc * 64 + c * 16) = val;
+                    }
+                    __syncwarp();
                 }
             }
         }
