@@ -1184,11 +1184,17 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     if ws > 1:
         dist.broadcast(bias, 0)
     if place == "balanced" and ws > 1:
-        # expert placement from a routing sample (the sample the bias was fitted on, routed with
-        # it): an expert's GEMM time goes with its 128-row slots, so its load is its expected
-        # slot count at the full batch; greedy, heaviest expert to the least-loaded rank
-        sidx, _, _ = k3.router(sample, W, bias, K)
-        pairs = torch.bincount(sidx.reshape(-1).long(), minlength=E).double() * (EP_T / sample.shape[0])
+        # expert placement from routing statistics: a calibration batch of EP_T tokens drawn
+        # apart from the benchmark's tokens (the way a deployment places experts from past
+        # traffic), routed with the fitted bias. An expert's GEMM time goes with its 128-row
+        # slots, so its load is its slot count at the full batch; greedy, heaviest expert to
+        # the least-loaded rank.
+        gc = torch.Generator(device=dev)
+        gc.manual_seed(31337)
+        calib = torch.randn((EP_T, H), generator=gc, device=dev).to(torch.bfloat16)
+        sidx, _, _ = k3.router(calib, W, bias, K)
+        del calib
+        pairs = torch.bincount(sidx.reshape(-1).long(), minlength=E).double()
         load = torch.ceil(pairs / 128.0)
         dist.broadcast(load, 0)
         owner_l, lists = k3.ep.balanced_placement(load.cpu().tolist(), ws)
@@ -1207,7 +1213,7 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     T = EP_T // ws
     if impl == "fused":
         layer = k3.PoolMoeLayer(arena, per + 1, run_of, per, W, bias, H, I, K, terms=2)
-        epl = k3.ep.FusedExpertParallel(k3, layer, t_max=T)
+        epl = k3.ep.FusedExpertParallel(k3, layer, t_max=T, gather_x=not getattr(args, "ep_no_gather", False))
     else:
         lr = k3.PoolMoeLayer(arena, per + 1, run_of, -1, W, bias, H, I, K, terms=2)
         lsh = k3.PoolMoeLayer(arena, per + 1, none, per, W, bias, H, I, K, terms=2)
@@ -1240,9 +1246,9 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     torch.cuda.synchronize()
     clk = Clocks(local)
     L.k3c_timing_enable(1)
-    ms_buf = (C.c_double * 4)()
-    n_buf = (C.c_longlong * 4)()
-    L.k3c_timing_read(ms_buf, n_buf, 4)          # discard warm-up records
+    ms_buf = (C.c_double * 5)()
+    n_buf = (C.c_longlong * 5)()
+    L.k3c_timing_read(ms_buf, n_buf, 5)          # discard warm-up records
     launches0 = L.k3c_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -1255,29 +1261,31 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     torch.cuda.synchronize()
     launches = L.k3c_launch_count() - launches0 if not graphs else per_graph * steps
     L.k3c_timing_enable(0)
-    L.k3c_timing_read(ms_buf, n_buf, 4)
-    stages = {name: ms_buf[j] / steps for j, name in enumerate(("experts", "router", "combine"))}
+    L.k3c_timing_read(ms_buf, n_buf, 5)
+    stages = {name: ms_buf[j] / steps for j, name in enumerate(("experts", "router", "combine", "q8", "dispatch")) if name != "q8"}
     # the layer's phases, timed in separate steps after the timed region (events between them)
     phases = None
     if impl == "fused":
         epl.phase_timing(True)
         if graphs:   # replayed steps record no stage events: take the stages from these steps
             L.k3c_timing_enable(1)
-            L.k3c_timing_read(ms_buf, n_buf, 4)
+            L.k3c_timing_read(ms_buf, n_buf, 5)
         for i in range(3):
             epl.forward(xs[i % 2], **fwd_kw)
         phases = epl.phase_read()
         epl.phase_timing(False)
         if graphs:
             L.k3c_timing_enable(0)
-            L.k3c_timing_read(ms_buf, n_buf, 4)
-            stages = {name: ms_buf[j] / 3 for j, name in enumerate(("experts", "router", "combine"))}
+            L.k3c_timing_read(ms_buf, n_buf, 5)
+            stages = {name: ms_buf[j] / 3 for j, name in enumerate(("experts", "router", "combine", "q8", "dispatch")) if name != "q8"}
         ph = torch.tensor([phases[k] for k in epl.PHASES], dtype=torch.float64, device=dev)
         if ws > 1:
             dist.all_reduce(ph, op=dist.ReduceOp.MAX)
         phases = {"rank0": phases, "max_over_ranks": dict(zip(epl.PHASES, ph.tolist())),
                   "experts_call_parts_rank0": {"grouped_gemms": stages["experts"],
-                                               "plan_dispatch_other": phases["experts_call"] - stages["experts"]}}
+                                               "dispatch": stages["dispatch"],
+                                               "plan_other": phases["experts_call"] - stages["experts"]
+                                               - stages["dispatch"]}}
     dist.barrier()
     torch.cuda.synchronize()
     clocks = clk.stop()
@@ -1292,6 +1300,9 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     member.scatter_(1, dest, True)
     member[:, rank] = False
     remote_rows = float(member.sum().item())
+    gathered = impl == "fused" and getattr(epl, "gx", None) is not None
+    if gathered:   # every other rank's rows arrive through the all-gather
+        remote_rows = float((ws - 1) * T)
     remote_pairs = float((dest != rank).sum().item())
     # parity: 64 of this rank's tokens against the single-GPU layer over the full bank
     maxrel, idx_ok = 0.0, 1.0
@@ -1339,10 +1350,12 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
         "stages_ms_per_step_rank0": stages,
         "phases_ms": phases,
         "expert_stage_ms_max_over_ranks": exp_max, "expert_stage_ms_mean_over_ranks": exp_mean,
-        "nvlink_per_step": {"remote_token_rows_read": rows_all, "bytes_read": rows_all * H * 2,
+        "nvlink_per_step": {"remote_token_rows_received": rows_all, "bytes_received": rows_all * H * 2,
                             "pair_rows_written": pairs_all, "bytes_written": pairs_all * H * 2,
-                            "how": "bf16 token rows read by each rank that owns one of the token's experts; "
-                                   "one bf16 pair row stored at the token's owner per pair computed elsewhere"}
+                            "how": ("every rank's bf16 token rows all-gathered to every rank (NCCL, side stream, "
+                                    "during the router)" if gathered else
+                                    "bf16 token rows read by each rank that owns one of the token's experts")
+                                   + "; one bf16 pair row stored at the token's owner per pair computed elsewhere"}
         if impl == "fused" else None,
         "parity": {"tokens_per_rank": 64 if parity else 0, "maxrel_vs_single_gpu": maxrel_all if parity else None,
                    "indices_equal_single_gpu": bool(idx_all == 1.0) if parity else None,
@@ -1404,6 +1417,9 @@ def main():
                     help="ep: replay each step from a CUDA graph of the layer's launches (barriers included)")
     ap.add_argument("--ep-steps", type=int, default=10,
                     help="default line: timed steps of the config[3] expert-parallel layer (its 'ep' object)")
+    ap.add_argument("--ep-no-gather", action="store_true",
+                    help="ep workload: the quantisation pulls the other ranks' token rows after the barrier "
+                         "instead of an all-gather during the router")
     ap.add_argument("--no-ep", action="store_true", help="default line without the 'ep' object")
     ap.add_argument("--no-parity", action="store_true", help="ep: skip the parity check after the timed region")
     ap.add_argument("--workload", default="decode",

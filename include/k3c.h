@@ -122,7 +122,8 @@ const char *k3c_version(void);
  * launched since load. k3c_timing_enable(1) makes the k3c_* entry points record CUDA
  * events around their stages on the launching stream; k3c_timing_read sums and resets
  * the elapsed milliseconds and call counts per stage, in the order
- * {experts, router, combine, q8}. */
+ * {experts, router, combine, q8, dispatch} (dispatch: the prefill's token quantisation into
+ * its pairs' rows, which under expert parallelism reads the tokens of other ranks). */
 long long k3c_launch_count(void);
 void k3c_timing_enable(int on);
 int k3c_timing_read(double *ms, long long *count, int nstage);

@@ -30,8 +30,8 @@ struct StageTimer {
     std::mutex mu;
     bool on = false;
     std::vector<cudaEvent_t> pending[STAGE_N];  // begin,end,begin,end...
-    double ms[STAGE_N] = {0, 0, 0, 0};
-    long long n[STAGE_N] = {0, 0, 0, 0};
+    double ms[STAGE_N] = {};
+    long long n[STAGE_N] = {};
 };
 static StageTimer g_timer;
 

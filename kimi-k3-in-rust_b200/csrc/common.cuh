@@ -17,7 +17,7 @@ void clear_error();
 void count_launch();
 // Stage timing: when enabled, stage_begin/stage_end record CUDA events around a named
 // stage on the launching stream; k3c_timing_read() sums the elapsed times per stage.
-enum Stage { STAGE_EXPERTS = 0, STAGE_ROUTER = 1, STAGE_COMBINE = 2, STAGE_Q8 = 3, STAGE_N = 4 };
+enum Stage { STAGE_EXPERTS = 0, STAGE_ROUTER = 1, STAGE_COMBINE = 2, STAGE_Q8 = 3, STAGE_DISPATCH = 4, STAGE_N = 5 };
 void stage_begin(int stage, cudaStream_t s);
 void stage_end(int stage, cudaStream_t s);
 

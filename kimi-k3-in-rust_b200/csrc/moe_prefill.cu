@@ -1033,6 +1033,7 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         xs.ntok[0] = T;
         xs.tmax = T;
     }
+    stage_begin(STAGE_DISPATCH, s);
     if (x_dtype == K3C_BF16)
         k_pf_quant_pairs<uint16_t><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, xs, b.pair_row, b.sh_row0, sh_base, sh_n, T, H,
                                                             K, b.rows_cap);
@@ -1040,6 +1041,7 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         k_pf_quant_pairs<float><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, xs, b.pair_row, b.sh_row0, sh_base, sh_n, T, H,
                                                          K, b.rows_cap);
     K3C_CHECK_LAUNCH();
+    stage_end(STAGE_DISPATCH, s);
     k_pf_slot_sf<<<dim3(b.max_slots, PF_J), 256, 0, s>>>(b.sfa_x, b.xsf, b.row_tok, b.n_slots, b.slots, b.n_rows, T, H);
     K3C_CHECK_LAUNCH();
     // K3C_PF_TAIL=1: slots of at most PT_NMAX pairs on the weight-major kernel, the rest on the

@@ -132,9 +132,14 @@ class FusedExpertParallel:
 
     layer: a PoolMoeLayer whose run table marks the other ranks' experts -1 and whose shared
     run is the shared expert (each rank computes its own tokens' shared expert).
+
+    gather_x (more than one rank): every rank's token rows are gathered into a local buffer
+    by an NCCL all-gather on a side stream while the router runs (over NVSwitch each row
+    leaves its owner once), so the token quantisation of step 2 reads them from local memory
+    instead of pulling them from the owners over NVLink after the barrier.
     """
 
-    def __init__(self, k3, layer, t_max, x_dtype=None, group=None):
+    def __init__(self, k3, layer, t_max, x_dtype=None, group=None, gather_x=True):
         import torch
         import torch.distributed as dist
         self.k3, self.layer, self.group = k3, layer, group
@@ -189,6 +194,15 @@ class FusedExpertParallel:
                     p = ptr.value
                     self._opened.append(p)
                 getattr(self.peers, name)[q] = p
+        # every rank's token rows, ranks after one another: the quantisation reads the other
+        # ranks' tokens from here (this rank's own from x_buf)
+        self.gx = None
+        if gather_x and W_ > 1:
+            self.gx = torch.empty((W_ * T_, self.H), dtype=self.x_dtype, device=dev)
+            for q in range(W_):
+                if q != self.rank:
+                    self.peers.x[q] = self.gx[q * T_:(q + 1) * T_].data_ptr()
+            self._side = torch.cuda.Stream(device=dev)
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
         self._ntok = torch.zeros(W_, dtype=torch.int32, device=dev)
         self._scratch = torch.empty(0, dtype=torch.uint8, device=dev)
@@ -254,8 +268,14 @@ class FusedExpertParallel:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)]
             self._ph.append(ev)
         self._mark(ev, 0)
-        # 1. this rank's tokens and their routing into the shared buffers
+        # 1. this rank's tokens and their routing into the shared buffers; with gather_x the
+        # token rows of every rank are gathered on a side stream meanwhile
         self.x_buf[:T].copy_(x)
+        main = torch.cuda.current_stream()
+        if self.gx is not None:
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                dist.all_gather_into_tensor(self.gx, self.x_buf, group=self.group)
         if T:
             rneed = L.k3c_router_scratch(self.H, self.E, T)
             if self._rscratch.numel() < rneed:
@@ -265,6 +285,8 @@ class FusedExpertParallel:
                                       C.c_void_p(c.router_bias), self.H, self.E, self.K, c.renorm,
                                       c.routed_scale, T, k3._ptr(self._rscratch), self._rscratch.numel(),
                                       k3._stream()), "k3c_router_ws")
+        if self.gx is not None:
+            main.wait_stream(self._side)
         self._mark(ev, 1)
         self._barrier()
         self._mark(ev, 2)
