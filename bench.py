@@ -1117,9 +1117,11 @@ def run_latent(args, ws, rank, local):
 # ------------------------------------------------------------------ expert parallel (config[3])
 EP_T = 16384
 EP_WORKLOAD = "config[3] expert-parallel MoE prefill: 16384 bf16 tokens sharded over the GPUs, 384 " \
-              "MXFP4 experts (7168->2048->7168), 384/N per GPU (placement balanced on a routing sample) + a shared expert on " \
-              "each, top-8 under a Zipf(1.1) selection bias (popularity over a random permutation of " \
-              "the ids); dispatch and combine over NVLink peer memory inside the expert kernels (--ep-impl a2a: NCCL all-to-all)"
+              "MXFP4 experts (7168->2048->7168) sharded over the GPUs (the 16 hottest on every GPU, each running its " \
+              "own tokens' pairs of them; the rest (384-16)/N per GPU, placed by a balance of a calibration batch's " \
+              "slot counts) + a shared expert on each, top-8 under a Zipf(1.1) selection bias (popularity over a " \
+              "random permutation of the ids); token rows all-gathered during the router, pair rows stored at the " \
+              "tokens' owners over NVLink from the expert kernels (--ep-impl a2a: NCCL all-to-all)"
 
 
 def ep_init_group(ws, dev):
@@ -1195,14 +1197,29 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
         sidx, _, _ = k3.router(calib, W, bias, K)
         del calib
         pairs = torch.bincount(sidx.reshape(-1).long(), minlength=E).double()
-        load = torch.ceil(pairs / 128.0)
-        dist.broadcast(load, 0)
-        owner_l, lists = k3.ep.balanced_placement(load.cpu().tolist(), ws)
+        dist.broadcast(pairs, 0)
+        pl = pairs.cpu().tolist()
+        # the R hottest experts are held by every rank, each running its own tokens' pairs of
+        # them (their load splits evenly and their pair rows stay local); the rest are placed
+        nrep = max(0, getattr(args, "ep_replicate", 0) if impl == "fused" else 0)
+        while nrep and (E - nrep) % ws:
+            nrep -= 1
+        hot = sorted(sorted(range(E), key=lambda e: (-pl[e], e))[:nrep])
+        rest = [e for e in range(E) if e not in set(hot)]
+        own_r, lists_r = k3.ep.balanced_placement([float(np.ceil(pl[e] / 128.0)) for e in rest], ws)
+        owner_l = [0] * E
+        for i, e in enumerate(rest):
+            owner_l[e] = own_r[i]
+        lists = [sorted([rest[i] for i in lst] + hot) for lst in lists_r]
     else:
+        hot = []
         owner_l = [e // per for e in range(E)]
         lists = [list(range(q * per, (q + 1) * per)) for q in range(ws)]
     owner = torch.tensor(owner_l, dtype=torch.int64, device=dev)
+    hot_mask = torch.zeros(E, dtype=torch.bool, device=dev)
+    hot_mask[hot] = True
     mine = torch.tensor(lists[rank] + [E], dtype=torch.int64, device=dev)
+    per = len(lists[rank])
     if ws == 1:
         arena = arena_all
     else:
@@ -1296,6 +1313,7 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
     out_ep = epl.forward(xs[0], **fwd_kw)
     idx_ep = (epl.idx_buf[:T].clone() if impl == "fused" else k3.router(xs[0], W, bias, K)[0])
     dest = owner[idx_ep.long()]
+    dest[hot_mask[idx_ep.long()]] = rank          # replicated experts run at the token's owner
     member = torch.zeros((T, ws), dtype=torch.bool, device=dev)
     member.scatter_(1, dest, True)
     member[:, rank] = False
@@ -1344,7 +1362,8 @@ def ep_layer(args, k3, L, dev, ws, rank, local, steps, warmup, place="balanced",
         "workload": EP_WORKLOAD, "tokens": EP_T, "n_gpus": ws, "steps": steps, "warmup": warmup,
         "tokens_per_s": EP_T * steps / dt, "unit": UNIT, "ms_per_step": 1e3 * dt / steps,
         "scaling": "strong", "parallelism": f"ep{ws}",
-        "placement": place if ws > 1 else "all experts", "impl": impl,
+        "placement": (place + (f", the {len(hot)} hottest experts on every rank" if hot else "")) if ws > 1
+                     else "all experts", "impl": impl,
         "dtype": "mxfp4 x e4m3 (activations as 2 E4M3 terms), fp32 accumulate (tcgen05 kind::mxf8f6f4)",
         "useful_tflops": flop * steps / dt / 1e12,
         "stages_ms_per_step_rank0": stages,
@@ -1417,6 +1436,9 @@ def main():
                     help="ep: replay each step from a CUDA graph of the layer's launches (barriers included)")
     ap.add_argument("--ep-steps", type=int, default=10,
                     help="default line: timed steps of the config[3] expert-parallel layer (its 'ep' object)")
+    ap.add_argument("--ep-replicate", type=int, default=16,
+                    help="ep workload, balanced placement: the R hottest experts (calibration batch) held by every rank, "
+                         "each rank running its own tokens' pairs of them")
     ap.add_argument("--ep-no-gather", action="store_true",
                     help="ep workload: the quantisation pulls the other ranks' token rows after the barrier "
                          "instead of an all-gather during the router")

@@ -597,6 +597,11 @@ typedef struct {
     const int *idx[K3C_EP_MAX];   /* each rank's top-k ids [t_max][topk] */
     const float *wt[K3C_EP_MAX];  /* each rank's top-k weights [t_max][topk] */
     uint16_t *recv[K3C_EP_MAX];   /* each rank's pair rows [t_max][topk+1][hidden], bf16 */
+    /* Device [n_experts] or NULL. 1: every rank holds the expert (a hot expert replicated to
+     * spread its load) and each rank runs only its own tokens' pairs of it, so those pair rows
+     * never cross NVLink; 0: the pairs of all ranks' tokens run wherever the expert is
+     * resident. */
+    const unsigned char *local_only;
 } k3c_ep_peers;
 size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers);
 int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers,

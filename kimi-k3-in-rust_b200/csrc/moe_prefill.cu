@@ -937,9 +937,10 @@ size_t moe_prefill_tc_scratch(const k3c_moe_pool_layer *L, int T, bool own_contr
 }
 
 // Every rank's top-k ids, ranks after one another ([world*t_max][topk]); rows at or past a
-// rank's token count get -1 (no pair). need[g] = 1 when token g has a pair on this rank
-// (its expert resident here) or is this rank's own token with a shared expert: only those
-// tokens are quantised (read from their owner).
+// rank's token count get -1 (no pair), and so do the pairs of other ranks' tokens with an
+// expert every rank holds (ep.local_only: its owner runs them). need[g] = 1 when token g has a
+// pair on this rank (its expert resident here) or is this rank's own token with a shared
+// expert: only those tokens are quantised.
 __global__ void k_ep_gather_idx(int *__restrict__ all, uint8_t *__restrict__ need, k3c_ep_peers ep, int topk,
                                 const int *__restrict__ run_of, int n_experts, int has_shared) {
     const int n = ep.world * ep.t_max;
@@ -948,7 +949,8 @@ __global__ void k_ep_gather_idx(int *__restrict__ all, uint8_t *__restrict__ nee
         const bool live = t < ep.ntok[q];
         bool here = live && has_shared && q == ep.rank;
         for (int k = 0; k < topk; k++) {
-            const int e = live ? ep.idx[q][(size_t)t * topk + k] : -1;
+            int e = live ? ep.idx[q][(size_t)t * topk + k] : -1;
+            if (ep.local_only && q != ep.rank && e >= 0 && e < n_experts && ep.local_only[e]) e = -1;
             all[(size_t)g * topk + k] = e;
             here |= e >= 0 && e < n_experts && run_of[e] >= 0;
         }

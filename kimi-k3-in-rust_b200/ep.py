@@ -131,7 +131,9 @@ class FusedExpertParallel:
     after every rank has stored its pair rows.
 
     layer: a PoolMoeLayer whose run table marks the other ranks' experts -1 and whose shared
-    run is the shared expert (each rank computes its own tokens' shared expert).
+    run is the shared expert (each rank computes its own tokens' shared expert). An expert in
+    every rank's run table is a replicated hot expert: each rank runs only its own tokens'
+    pairs of it (k3c_ep_peers.local_only).
 
     gather_x (more than one rank): every rank's token rows are gathered into a local buffer
     by an NCCL all-gather on a side stream while the router runs (over NVSwitch each row
@@ -175,6 +177,10 @@ class FusedExpertParallel:
         for q in reversed(range(W_)):
             rank_of[every[q].bool()] = q
         self.expert_rank = rank_of
+        # experts every rank holds (hot experts replicated to spread their load): each rank
+        # runs only its own tokens' pairs of them, so their pair rows stay local
+        held = torch.stack([v.bool() for v in every]).all(0) if W_ > 1 else torch.zeros_like(mine, dtype=torch.bool)
+        self.local_only = held.to(torch.uint8) if bool(held.any()) else None
         torch.cuda.synchronize()
         everyone = [None] * W_
         dist.all_gather_object(everyone, handles, group=group)
@@ -182,6 +188,7 @@ class FusedExpertParallel:
         self.peers = k3.EpPeersC()
         self.peers.world, self.peers.rank, self.peers.t_max = W_, self.rank, T_
         self.peers.x_dtype = k3._dtype_code(torch.empty(0, dtype=self.x_dtype))
+        self.peers.local_only = self.local_only.data_ptr() if self.local_only is not None else None
         for q in range(W_):
             for name in sizes:
                 if q == self.rank:

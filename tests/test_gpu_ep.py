@@ -173,13 +173,15 @@ def test_ep_fused_one_rank_equals_single_gpu():
         dist.destroy_process_group()
 
 
-def _emulated_ranks(k3, W_, H, I, E, K, counts, t_max, seed):
+def _emulated_ranks(k3, W_, H, I, E, K, counts, t_max, seed, replicate=0):
     """W_ ranks of the peer-memory expert-parallel layer emulated on ONE GPU: every rank's
     buffers are device tensors of cuda:0 and the three steps run for all ranks in turn on one
     stream (step 1 of every rank, then step 2 of every rank, then step 3), which orders them
     as the two barriers do. No kernel waits on another (the step-2 kernels read only x, idx
     and wt, which step 2 never writes, and store into the receive buffers, which only step 3
-    reads). Returns each rank's output and the single-GPU layer's on the same tokens."""
+    reads). `replicate` experts are held by every rank with their pairs run by the tokens'
+    owners (k3c_ep_peers.local_only). Returns each rank's output and the single-GPU layer's on
+    the same tokens."""
     import ctypes as C
     import torch
     dev = torch.device("cuda:0")
@@ -193,11 +195,14 @@ def _emulated_ranks(k3, W_, H, I, E, K, counts, t_max, seed):
     full = k3.PoolMoeLayer.pack([k3.DeviceExpert.from_host(e, dev) for e in experts],
                                 k3.DeviceExpert.from_host(shared, dev), Wr, None, H, I, K, dev, terms=2)
     owner = np.random.default_rng(seed).permutation(np.arange(E) % W_)     # scattered placement
+    rep = np.zeros(E, bool)
+    rep[np.random.default_rng(seed + 1).permutation(E)[:replicate]] = True
     expert_rank = torch.from_numpy(owner.astype(np.int32)).to(dev)
+    local_only = torch.from_numpy(rep.astype(np.uint8)).to(dev)
     layers = []
     for q in range(W_):
         run_of = full.run_of.clone()
-        run_of[torch.from_numpy(owner != q).to(dev)] = -1
+        run_of[torch.from_numpy((owner != q) & ~rep).to(dev)] = -1
         layers.append(k3.PoolMoeLayer(full.arena, E + 1, run_of, E, Wr, None, H, I, K, terms=2))
     xb = [torch.zeros((t_max, H), dtype=torch.bfloat16, device=dev) for _ in range(W_)]
     idx = [torch.zeros((t_max, K), dtype=torch.int32, device=dev) for _ in range(W_)]
@@ -208,6 +213,7 @@ def _emulated_ranks(k3, W_, H, I, E, K, counts, t_max, seed):
         p = k3.EpPeersC()
         p.world, p.rank, p.t_max = W_, q, t_max
         p.x_dtype = k3._dtype_code(xb[0])
+        p.local_only = local_only.data_ptr() if replicate else None
         for r in range(W_):
             p.ntok[r] = counts[r]
             p.x[r], p.idx[r], p.wt[r], p.recv[r] = (xb[r].data_ptr(), idx[r].data_ptr(), wt[r].data_ptr(),
@@ -246,15 +252,18 @@ def _emulated_ranks(k3, W_, H, I, E, K, counts, t_max, seed):
     return [o.cpu().numpy() for o in outs], [w.cpu().numpy() for w in wants]
 
 
-@pytest.mark.parametrize("W_,H,I,E,K,counts,t_max", [
-    (2, 256, 128, 8, 2, (200, 131), 256),
-    (4, 512, 256, 16, 4, (97, 300, 0, 1), 320),
-    (8, 256, 128, 16, 2, (40, 33, 64, 1, 17, 64, 5, 29), 64),
+@pytest.mark.parametrize("W_,H,I,E,K,counts,t_max,replicate", [
+    (2, 256, 128, 8, 2, (200, 131), 256, 0),
+    (4, 512, 256, 16, 4, (97, 300, 0, 1), 320, 0),
+    (8, 256, 128, 16, 2, (40, 33, 64, 1, 17, 64, 5, 29), 64, 0),
+    (4, 512, 256, 16, 4, (97, 300, 0, 1), 320, 3),
+    (8, 256, 128, 16, 2, (40, 33, 64, 1, 17, 64, 5, 29), 64, 5),
 ])
-def test_ep_emulated_ranks_equal_single_gpu(k3, W_, H, I, E, K, counts, t_max):
+def test_ep_emulated_ranks_equal_single_gpu(k3, W_, H, I, E, K, counts, t_max, replicate):
     """The multi-rank indexing of the peer-memory path (pair rows stored at row t % t_max of
     rank t / t_max's receive buffer, token rows read from the owners' buffers, ragged and empty
-    ranks) on one GPU: every rank's output equals the single-GPU layer bit for bit."""
-    outs, wants = _emulated_ranks(k3, W_, H, I, E, K, list(counts), t_max, seed=40 + W_)
+    ranks, replicated experts whose pairs run at their tokens' owners) on one GPU: every rank's
+    output equals the single-GPU layer bit for bit."""
+    outs, wants = _emulated_ranks(k3, W_, H, I, E, K, list(counts), t_max, seed=40 + W_, replicate=replicate)
     for q, (o, w) in enumerate(zip(outs, wants)):
         assert np.array_equal(o, w), (q, np.abs(o - w).max() if o.size else 0)
