@@ -460,6 +460,7 @@ def decode_line(args, ws, rank, local):
                                    "from CUDA graphs of the layer call (one per input batch); "
                                    "ms_per_step_stream_launches: the same steps launched from the host"}
     batches["config0_expert"] = expert_ffn_probe(k3, L, dev, rank, hbm_peak)
+    batches["q8_alone"] = q8_probe(k3, L, dev, wq, wsc, q8_ws, hbm_peak)
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -826,6 +827,49 @@ def expert_ffn_setup(k3, L, dev, seed, NX=16):
         assert rc == 0, L.k3c_last_error()
 
     return step, run, xs, y, (blob, qs, scratch)
+
+
+def q8_probe(k3, L, dev, wq, wsc, ws_buf, hbm_peak, copies=16, reps=20):
+    """The INT8 trunk projection timed alone (in the step it shares the GPU with the layer's
+    router and experts): 16 bf16 tokens through 7168 x 7168, rotated over `copies` weight
+    matrices (822 MB, more than L2), calls replayed from a CUDA graph."""
+    import ctypes as C
+    import torch
+    B = 16
+    ws_ = [wq] + [wq.clone() for _ in range(copies - 1)]
+    x = torch.randn((B, H), device=dev).to(torch.bfloat16)
+    y = torch.empty((B, H), dtype=torch.float32, device=dev)
+
+    def call(w):
+        rc = L.k3c_q8_gemv_ws(C.c_void_p(y.data_ptr()), H, C.c_void_p(x.data_ptr()), k3.K3C_BF16, H, B,
+                              C.c_void_p(w.data_ptr()), C.c_void_p(wsc.data_ptr()), H, H, H,
+                              C.c_void_p(ws_buf.data_ptr()), ws_buf.numel(), k3._stream())
+        assert rc == 0, L.k3c_last_error()
+
+    for w in ws_:
+        call(w)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(gr, stream=cap):
+        for w in ws_:
+            call(w)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+    del gr, ws_
+    nbytes = H * H + 4 * H
+    return {"us_per_call": 1e6 * dt, "hbm_gbs": nbytes / dt / 1e9, "hbm_frac": nbytes / dt / 1e9 / hbm_peak,
+            "how": "k3c_q8_gemv_ws alone, 16 bf16 tokens x 7168x7168 int8, 16 weight copies rotated (> L2), "
+                   "graph replay"}
 
 
 def expert_ffn_probe(k3, L, dev, rank, hbm_peak, steps=160):
