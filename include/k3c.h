@@ -602,6 +602,10 @@ typedef struct {
      * never cross NVLink; 0: the pairs of all ranks' tokens run wherever the expert is
      * resident. */
     const unsigned char *local_only;
+    /* A cudaEvent_t or NULL: when the x[q] of other ranks are filled by a copy still in flight
+     * on another stream (an all-gather of the token rows), the event recorded after it; step 2
+     * plans first and makes the stream wait for it only before it reads those rows. */
+    void *x_ready;
 } k3c_ep_peers;
 size_t k3c_moe_prefill_ep_scratch(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers);
 int k3c_moe_prefill_ep_experts(const k3c_moe_pool_layer *L, const k3c_ep_peers *peers,

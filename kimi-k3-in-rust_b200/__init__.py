@@ -102,7 +102,8 @@ class EpPeersC(C.Structure):
 
     _fields_ = [("world", C.c_int), ("rank", C.c_int), ("t_max", C.c_int), ("x_dtype", C.c_int),
                 ("ntok", C.c_int * EP_MAX), ("x", C.c_void_p * EP_MAX), ("idx", C.c_void_p * EP_MAX),
-                ("wt", C.c_void_p * EP_MAX), ("recv", C.c_void_p * EP_MAX), ("local_only", C.c_void_p)]
+                ("wt", C.c_void_p * EP_MAX), ("recv", C.c_void_p * EP_MAX), ("local_only", C.c_void_p),
+                ("x_ready", C.c_void_p)]
 
 
 class K3CError(RuntimeError):

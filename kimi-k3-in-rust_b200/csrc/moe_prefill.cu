@@ -1035,6 +1035,8 @@ int launch_moe_prefill_tc(float *out, const void *x, int x_dtype, int T, const k
         xs.ntok[0] = T;
         xs.tmax = T;
     }
+    // expert parallelism: the other ranks' token rows may still be arriving on another stream
+    if (ep && ep->x_ready) K3C_TRY_CUDA(cudaStreamWaitEvent(s, (cudaEvent_t)ep->x_ready, 0));
     stage_begin(STAGE_DISPATCH, s);
     if (x_dtype == K3C_BF16)
         k_pf_quant_pairs<uint16_t><<<qblocks, 256, 0, s>>>(b.xq, b.xsf, xs, b.pair_row, b.sh_row0, sh_base, sh_n, T, H,

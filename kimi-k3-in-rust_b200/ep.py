@@ -138,7 +138,9 @@ class FusedExpertParallel:
     gather_x (more than one rank): every rank's token rows are gathered into a local buffer
     by an NCCL all-gather on a side stream while the router runs (over NVSwitch each row
     leaves its owner once), so the token quantisation of step 2 reads them from local memory
-    instead of pulling them from the owners over NVLink after the barrier.
+    instead of pulling them from the owners over NVLink after the barrier. The all-gather has
+    a communicator of its own, so it runs beside the first barrier, and step 2 waits for it
+    (k3c_ep_peers.x_ready) only after its planning, right before the quantisation.
     """
 
     def __init__(self, k3, layer, t_max, x_dtype=None, group=None, gather_x=True):
@@ -210,6 +212,9 @@ class FusedExpertParallel:
                 if q != self.rank:
                     self.peers.x[q] = self.gx[q * T_:(q + 1) * T_].data_ptr()
             self._side = torch.cuda.Stream(device=dev)
+            self._gx_group = dist.new_group(dist.get_process_group_ranks(group) if group is not None
+                                            else list(range(W_)))
+            self._gx_ready = torch.cuda.Event()
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
         self._ntok = torch.zeros(W_, dtype=torch.int32, device=dev)
         self._scratch = torch.empty(0, dtype=torch.uint8, device=dev)
@@ -282,7 +287,9 @@ class FusedExpertParallel:
         if self.gx is not None:
             self._side.wait_stream(main)
             with torch.cuda.stream(self._side):
-                dist.all_gather_into_tensor(self.gx, self.x_buf, group=self.group)
+                dist.all_gather_into_tensor(self.gx, self.x_buf, group=self._gx_group)
+                self._gx_ready.record(self._side)
+            self.peers.x_ready = self._gx_ready.cuda_event
         if T:
             rneed = L.k3c_router_scratch(self.H, self.E, T)
             if self._rscratch.numel() < rneed:
@@ -292,8 +299,6 @@ class FusedExpertParallel:
                                       C.c_void_p(c.router_bias), self.H, self.E, self.K, c.renorm,
                                       c.routed_scale, T, k3._ptr(self._rscratch), self._rscratch.numel(),
                                       k3._stream()), "k3c_router_ws")
-        if self.gx is not None:
-            main.wait_stream(self._side)
         self._mark(ev, 1)
         self._barrier()
         self._mark(ev, 2)
@@ -306,6 +311,8 @@ class FusedExpertParallel:
         k3._check(L.k3c_moe_prefill_ep_experts(C.byref(c), C.byref(self.peers), k3._ptr(self._scratch),
                                                self._scratch.numel(), k3._stream()),
                   "k3c_moe_prefill_ep_experts")
+        if self.gx is not None:
+            main.wait_stream(self._side)   # ordered through x_ready already; joins the streams
         self._mark(ev, 3)
         self._barrier()
         self._mark(ev, 4)

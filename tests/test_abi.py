@@ -83,12 +83,12 @@ def test_pool_and_ep_struct_layouts_match_header(k3):
 #include <stddef.h>
 #include "k3c.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n",
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\n",
          sizeof(k3c_moe_pool_layer), offsetof(k3c_moe_pool_layer, run_of),
          offsetof(k3c_moe_pool_layer, shared_run), offsetof(k3c_moe_pool_layer, terms),
          sizeof(k3c_ep_peers), offsetof(k3c_ep_peers, ntok), offsetof(k3c_ep_peers, x),
          offsetof(k3c_ep_peers, idx), offsetof(k3c_ep_peers, wt), offsetof(k3c_ep_peers, recv),
-         offsetof(k3c_ep_peers, local_only), sizeof(k3c_ipc_handle));
+         offsetof(k3c_ep_peers, local_only), offsetof(k3c_ep_peers, x_ready), sizeof(k3c_ipc_handle));
   return 0; }
 """
     with tempfile.TemporaryDirectory() as d:
@@ -100,7 +100,7 @@ int main(void) {
     P, E = k3.MoePoolLayerC, k3.EpPeersC
     want = [C.sizeof(P), P.run_of.offset, P.shared_run.offset, P.terms.offset,
             C.sizeof(E), E.ntok.offset, E.x.offset, E.idx.offset, E.wt.offset, E.recv.offset,
-            E.local_only.offset, C.sizeof(k3.IpcHandleC)]
+            E.local_only.offset, E.x_ready.offset, C.sizeof(k3.IpcHandleC)]
     assert got == want
 
 
